@@ -1,0 +1,468 @@
+"""Benchmark: GQA decode attention of the Qwen3-VL-2B text decoder at 4K context
+through the drop-in C-ABI library.
+
+One STEP = one decode step of attention for all 28 layers: for layer l, the split-KV
+kernel attends one new query (16 heads) over kv_len = 4097 + (i mod 512) cached rows of
+that layer (i = step index: the 512-step schedule of config 2 -- a cache prefilled to
+4,096 tokens, each step appending one).  The cache is BF16 (the FP32 cache is measured
+too, as `fp32_kv`).  28 layers x ~17 MB per step (~0.5 GB) exceeds the 126 MB L2, so no
+step finds the previous step's rows in L2.
+
+    value : device time / (decode steps summed over ranks), in us/step (lower is better).
+            Device-resident inputs, launches replayed from per-step CUDA graphs.
+    e2e   : the same metric through attention_decode_gqa with HOST (pinned) query and
+            output buffers, every call copying its query in and its output back.
+    --impl reference : the reference's own CPU attention (oracle/_ref, built from the
+            reference sources) on the host cores; one step = one layer's decode call
+            (a bounded sample), reported x28.
+
+Multi-GPU (torchrun): one independent sequence per GPU (request-level data
+parallelism, no collective on the data path); barrier + max over ranks for timing.
+"""
+
+import argparse
+import ctypes
+import importlib.util
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+PKG_DIR = ROOT / "typhoon-ocr-server_b200"
+METRIC = "GQA attn prefill tok/s & decode µs/step @4K ctx; % of HBM BW / tcgen05 peak"
+LAYERS = 28
+PREFILLED = 4096
+SCHEDULE = 512
+MAX_SEQ = PREFILLED + SCHEDULE
+HQ, HKV, D = 16, 8, 128
+
+
+def _pkg():
+    name = "typhoon_ocr_server_b200"
+    if name in sys.modules:
+        return sys.modules[name]
+    spec = importlib.util.spec_from_file_location(name, PKG_DIR / "__init__.py",
+                                                  submodule_search_locations=[str(PKG_DIR)])
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[name] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def kv_len_of(step):
+    return PREFILLED + 1 + (step % SCHEDULE)
+
+
+def step_bytes(step, elem_bytes):
+    """Algorithmic bytes of one step: K and V rows of every layer, plus q in / out."""
+    return LAYERS * (2 * kv_len_of(step) * HKV * D * elem_bytes + 2 * HQ * D * 4)
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+def profile_traffic(kind):
+    """DRAM bytes per decode launch from the committed ncu summary, if present."""
+    f = ROOT / "profiles" / "decode_split_kernel_config2.md"
+    if not f.exists():
+        return None
+    m = re.search(rf"traffic_bytes_per_launch_{kind}:\s*([0-9.eE+]+)", f.read_text())
+    return float(m.group(1)) if m else None
+
+
+class ClockSampler:
+    """nvidia-smi clocks + throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.file = None
+
+    def __enter__(self):
+        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "50"], stdout=self.file, stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc:
+            time.sleep(0.1)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        self.file.flush()
+        rows = []
+        for line in Path(self.file.name).read_text().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        os.unlink(self.file.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"], "samples": 0}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        smax = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ---------------------------------------------------------------------------------------
+# Our arm
+# ---------------------------------------------------------------------------------------
+
+class DecodeBench:
+    def __init__(self, pkg, lib, kv_dtype, device):
+        import torch
+        self.torch = torch
+        self.pkg, self.lib = pkg, lib
+        self.elem = 2 if kv_dtype == pkg.ATTN_KV_BF16 else 4
+        self.cache = lib.kv_cache_alloc_ex(MAX_SEQ, kv_dtype)
+        if not self.cache:
+            raise RuntimeError(pkg.last_error(lib))
+        gen = torch.Generator(device=device)
+        gen.manual_seed(2)
+        # Fill every layer's rows 0..MAX_SEQ-1 with N(0, 0.5^2) through the C-ABI.
+        buf_k = torch.empty((MAX_SEQ, HKV, D), dtype=torch.float32, device=device)
+        buf_v = torch.empty_like(buf_k)
+        cs = pkg.cache_struct(self.cache)
+        for layer in range(LAYERS):
+            buf_k.normal_(0.0, 0.5, generator=gen)
+            buf_v.normal_(0.0, 0.5, generator=gen)
+            cs.seq_len = 0
+            lib.kv_cache_append_prefill(self.cache, layer, ctypes.c_void_p(buf_k.data_ptr()),
+                                        ctypes.c_void_p(buf_v.data_ptr()), MAX_SEQ)
+            pkg.check(lib, "fill cache")
+        cs.seq_len = PREFILLED
+        del buf_k, buf_v
+        self.q = torch.empty((LAYERS, HQ, D), dtype=torch.float32, device=device).normal_(generator=gen)
+        self.out = torch.zeros((LAYERS, HQ, D), dtype=torch.float32, device=device)
+        self.scale = ctypes.c_float(pkg.SCALE)
+        self.graphs = {}
+        self.stream = torch.cuda.Stream(device=device)
+
+    def _launch_step(self, step):
+        kv = kv_len_of(step)
+        qp, op = self.q.data_ptr(), self.out.data_ptr()
+        for layer in range(LAYERS):
+            self.lib.attention_decode_gqa(ctypes.c_void_p(qp + layer * HQ * D * 4), self.cache,
+                                          ctypes.c_void_p(op + layer * HQ * D * 4), layer, kv, self.scale)
+
+    def capture(self):
+        torch = self.torch
+        self.lib.attn_set_stream(ctypes.c_void_p(self.stream.cuda_stream))
+        with torch.cuda.stream(self.stream):
+            self._launch_step(0)  # first launches set kernel attributes outside capture
+        self.stream.synchronize()
+        self.pkg.check(self.lib, "warm launch")
+        for s in range(SCHEDULE):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=self.stream):
+                self._launch_step(s)
+            self.graphs[s] = g
+        self.pkg.check(self.lib, "graph capture")
+
+    def run(self, first, n):
+        for i in range(first, first + n):
+            self.graphs[i % SCHEDULE].replay()
+
+    def close(self):
+        self.lib.attn_set_stream(None)
+        self.graphs.clear()
+        self.lib.kv_cache_free(self.cache)
+
+
+def time_device(bench, warmup, steps, dist_ctx):
+    torch = bench.torch
+    bench.run(0, warmup)
+    torch.cuda.synchronize()
+    dist_ctx.barrier()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record(bench.stream)
+    bench.run(warmup, steps)
+    end.record(bench.stream)
+    torch.cuda.synchronize()
+    dist_ctx.barrier()
+    return start.elapsed_time(end)  # ms
+
+
+def time_e2e(pkg, lib, cache, steps, device):
+    """attention_decode_gqa with pinned host q/output: each call copies q in, the output
+    back, and returns when done (the reference's blocking contract)."""
+    import torch
+    lib.attn_set_stream(None)
+    q = torch.empty((LAYERS, HQ, D), dtype=torch.float32).normal_().pin_memory()
+    out = torch.empty((LAYERS, HQ, D), dtype=torch.float32).pin_memory()
+    scale = ctypes.c_float(pkg.SCALE)
+    qp, op = q.data_ptr(), out.data_ptr()
+
+    def one(step):
+        kv = kv_len_of(step)
+        for layer in range(LAYERS):
+            lib.attention_decode_gqa(ctypes.c_void_p(qp + layer * HQ * D * 4), cache,
+                                     ctypes.c_void_p(op + layer * HQ * D * 4), layer, kv, scale)
+
+    for s in range(5):
+        one(s)
+    pkg.check(lib, "e2e warmup")
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for s in range(steps):
+        one(s)
+    t1 = time.perf_counter()
+    pkg.check(lib, "e2e")
+    return (t1 - t0) * 1e3, LAYERS * HQ * D * 4, LAYERS * HQ * D * 4
+
+
+class DistCtx:
+    def __init__(self, n):
+        self.n = n
+        self.dist = None
+        if n > 1:
+            import datetime
+            import torch.distributed as dist
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+            self.dist = dist
+
+    @property
+    def rank(self):
+        return self.dist.get_rank() if self.dist else 0
+
+    def barrier(self):
+        if self.dist:
+            self.dist.barrier()
+
+    def max(self, x):
+        if not self.dist:
+            return x
+        import torch
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self):
+        if self.dist:
+            self.dist.destroy_process_group()
+
+
+def cpu_reference_sample(budget_s=12.0, layers_cycle=LAYERS):
+    """The reference's attention_decode_gqa (oracle/_ref) -- or the C restatement when the
+    reference build is absent -- on the host cores, FP32 cache (the reference layout),
+    for config 2's schedule.  Returns (us per 28-layer step, cores, kind, sample text)."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import oracle as orc
+    threads = os.cpu_count() or 1
+    rng = np.random.default_rng(3)
+    q = rng.standard_normal((HQ, D), dtype=np.float32)
+    out = np.zeros((HQ, D), dtype=np.float32)
+    scale = ctypes.c_float(0.08838834764831843)
+    if orc.RefLib.available():
+        ref = orc.RefLib()
+        L = ref.lib
+        cache = L.kv_cache_alloc(MAX_SEQ)
+        rows = (0.5 * rng.standard_normal((MAX_SEQ, HKV, D), dtype=np.float32)).astype(np.float32)
+        for layer in range(layers_cycle):
+            L.kv_cache_append_prefill(cache, layer, rows.ctypes.data, rows.ctypes.data, MAX_SEQ)
+
+        def call(layer, kv):
+            L.attention_decode_gqa(q.ctypes.data, cache, out.ctypes.data, layer, kv, scale)
+        kind = "reference"
+        cleanup = lambda: L.kv_cache_free(cache)  # noqa: E731
+    else:
+        o = orc.Oracle()
+        ck = (0.5 * rng.standard_normal((HKV, MAX_SEQ, D), dtype=np.float32)).astype(np.float32)
+
+        def call(layer, kv):
+            o.lib.oracle_attention_decode(q.ctypes.data, ck.ctypes.data, ck.ctypes.data, MAX_SEQ,
+                                          out.ctypes.data, kv, scale)
+        kind = "port"
+        cleanup = lambda: None  # noqa: E731
+    call(0, kv_len_of(0))
+    n = 0
+    t0 = time.perf_counter()
+    while time.perf_counter() - t0 < budget_s:
+        call(n % layers_cycle, kv_len_of(n // layers_cycle))
+        n += 1
+    dt = time.perf_counter() - t0
+    cleanup()
+    per_layer_us = dt / n * 1e6
+    sample = (f"{n} single-layer decode calls over config 2's schedule (FP32 cache, kv_len from 4097), "
+              f"{threads} OpenMP threads, {dt:.1f} s; us/step = mean per-layer time x 28")
+    return per_layer_us * LAYERS, threads, kind, sample
+
+
+def run_reference_arm(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import oracle as orc
+    threads = os.cpu_count() or 1
+    if not orc.RefLib.available():
+        kind = "port"
+    else:
+        kind = "reference"
+    ref = orc.RefLib() if kind == "reference" else None
+    rng = np.random.default_rng(3)
+    q = rng.standard_normal((HQ, D), dtype=np.float32)
+    out = np.zeros((HQ, D), dtype=np.float32)
+    scale = ctypes.c_float(0.08838834764831843)
+    if ref:
+        L = ref.lib
+        cache = L.kv_cache_alloc(MAX_SEQ)
+        rows = (0.5 * rng.standard_normal((MAX_SEQ, HKV, D), dtype=np.float32)).astype(np.float32)
+        for layer in range(LAYERS):
+            L.kv_cache_append_prefill(cache, layer, rows.ctypes.data, rows.ctypes.data, MAX_SEQ)
+
+        def call(i):
+            L.attention_decode_gqa(q.ctypes.data, cache, out.ctypes.data, i % LAYERS, kv_len_of(i // LAYERS), scale)
+    else:
+        o = orc.Oracle()
+        ck = (0.5 * rng.standard_normal((HKV, MAX_SEQ, D), dtype=np.float32)).astype(np.float32)
+
+        def call(i):
+            o.lib.oracle_attention_decode(q.ctypes.data, ck.ctypes.data, ck.ctypes.data, MAX_SEQ, out.ctypes.data,
+                                          kv_len_of(i // LAYERS), scale)
+    for i in range(args.warmup):
+        call(i)
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        call(args.warmup + i)
+    dt = time.perf_counter() - t0
+    us_step = dt / args.steps * 1e6 * LAYERS
+    sample = (f"each step = one layer's decode call (config 2 schedule, FP32 cache), {args.steps} steps on "
+              f"{threads} OpenMP threads; value = mean per-layer time x 28 layers")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": us_step, "unit": "us/step", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": us_step / 1e3, "higher_is_better": False,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,0.5) K/V)",
+        "config": {"workload": "config2: 28-layer decode attention @4K ctx, batch 1", "kv_cache": "f32",
+                   "kv_len": "4097..4608 (512-step schedule)"},
+        "cpu_baseline": {"value": us_step, "unit": "us/step", "cores": threads, "kind": kind, "sample": sample},
+        "e2e": {"value": us_step, "unit": "us/step", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20000)
+    ap.add_argument("--warmup", type=int, default=512)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--e2e-steps", type=int, default=200)
+    ap.add_argument("--cpu-budget", type=float, default=12.0)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    if args.impl == "reference":
+        run_reference_arm(args)
+        return
+
+    import torch
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local_rank)
+    dctx = DistCtx(args.gpus)
+    pkg = _pkg()
+    lib = pkg.load_attention_lib()
+    hbm_peak, tc_peak, peak_src = peaks()
+
+    bf = DecodeBench(pkg, lib, pkg.ATTN_KV_BF16, f"cuda:{local_rank}")
+    bf.capture()
+    with ClockSampler(local_rank) as clk:
+        ms = time_device(bf, args.warmup, args.steps, dctx)
+    clocks = clk.summary()
+    ms_max = dctx.max(ms)
+    bytes_total = sum(step_bytes(args.warmup + i, 2) for i in range(args.steps))
+    e2e_ms, h2d, d2h = time_e2e(pkg, lib, bf.cache, args.e2e_steps, local_rank)
+    e2e_max = dctx.max(e2e_ms)
+    bf.close()
+
+    f32 = DecodeBench(pkg, lib, pkg.ATTN_KV_F32, f"cuda:{local_rank}")
+    f32.capture()
+    f32_steps = min(args.steps, 4096)
+    ms32 = dctx.max(time_device(f32, args.warmup, f32_steps, dctx))
+    bytes32 = sum(step_bytes(args.warmup + i, 4) for i in range(f32_steps))
+    f32.close()
+
+    cpu = None
+    if dctx.rank == 0:
+        us_cpu, cores, kind, sample = cpu_reference_sample(args.cpu_budget)
+        cpu = {"value": us_cpu, "unit": "us/step", "cores": cores, "kind": kind, "sample": sample}
+    dctx.close()
+    if dctx.rank != 0:
+        return
+
+    n = args.gpus
+    us_step_rank = ms_max * 1e3 / args.steps
+    achieved = bytes_total / (ms * 1e-3) / 1e9  # this rank's kernels, GB/s
+    launches = args.steps * LAYERS
+    line = {
+        "metric": METRIC,
+        "value": us_step_rank / n,
+        "unit": "us/step",
+        "n_gpus": n,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": us_step_rank / 1e3,
+        "higher_is_better": False,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded N(0,0.5) K/V, N(0,1) q; random, no checkpoint)",
+        "config": {
+            "workload": "config2: 28-layer decode attention @4K ctx, batch 1 per GPU",
+            "kv_cache": "bf16", "kv_len": "4097..4608 (512-step schedule, cycled)",
+            "parallelism": f"dp{n} (independent sequences, no collective)",
+            "l2": "inputs > L2: ~0.5 GB of K/V per step vs 126 MB L2",
+            "value_definition": "device time (max over ranks) / decode steps summed over ranks",
+            "launch": "per-step CUDA graph of 28 attention_decode_gqa calls",
+        },
+        "roofline": {
+            "bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+            "frac": achieved / hbm_peak, "traffic": profile_traffic("bf16"),
+            "kernel": "decode_split_kernel<bf16>",
+            "note": f"algorithmic bytes (K+V rows + q/out) / mean launch time incl. gaps; peak {peak_src}",
+        },
+        "e2e": {"value": e2e_max * 1e3 / args.e2e_steps, "unit": "us/step", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "steps": args.e2e_steps,
+                "path": "attention_decode_gqa x28 with pinned host q/output (blocking)"},
+        "fp32_kv": {"value": ms32 * 1e3 / f32_steps, "unit": "us/step", "steps": f32_steps,
+                    "achieved_gbs": bytes32 / (ms32 * 1e-3) / 1e9,
+                    "frac": bytes32 / (ms32 * 1e-3) / 1e9 / hbm_peak},
+        "cpu_baseline": cpu,
+        "clocks": clocks,
+        "gpu_launches": launches,
+    }
+    print(json.dumps(line))
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,125 @@
+"""The C-ABI boundary, checked without a GPU.
+
+* libtyphoon_attn.so loads and exports every function include/*.h declares, and the
+  Python binding declares exactly those.
+* The KVCache / DecoderScratch layouts are byte-identical to the reference headers
+  (kernel/kv_cache.h:11-26, kernel/scratch.h:17-34), so kernel/decoder.c can read
+  cache->seq_len / cache->rope_offset and the scratch fields in place.
+* The reference kernel/decoder.c compiles against include/ unchanged, and every
+  attention / kv_cache / scratch symbol it needs is exported by this library.
+* Entry points fail loudly, through attn_last_error(), when there is no usable GPU.
+"""
+
+import ctypes
+import re
+import shutil
+import subprocess
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+INCLUDE = ROOT / "include"
+REF_KERNEL = Path("/root/reference/kernel")
+CC = shutil.which("gcc", path="/usr/bin") or "gcc"
+
+
+def header_functions():
+    names = set()
+    for h in INCLUDE.glob("*.h"):
+        text = re.sub(r"/\*.*?\*/", "", h.read_text(), flags=re.S)
+        for m in re.finditer(r"^[A-Za-z_][\w \*]*?\b([a-z_][a-z0-9_]*)\s*\(", text, flags=re.M):
+            if not m.group(0).lstrip().startswith(("#", "typedef", "return")):
+                names.add(m.group(1))
+    return names
+
+
+def test_library_exports_every_declared_symbol(pkg):
+    lib = ctypes.CDLL(str(pkg.LIB_PATH))
+    declared = header_functions()
+    assert {"attention_decode_gqa", "attention_prefill_gqa", "attention_chunked_prefill_gqa",
+            "kv_cache_alloc", "decoder_scratch_alloc"} <= declared
+    missing = [n for n in sorted(declared) if not hasattr(lib, n)]
+    assert not missing, f"not exported: {missing}"
+    assert set(pkg.declared_symbols()) == declared
+
+
+def test_binding_loads_without_gpu(pkg):
+    lib = pkg.load_attention_lib()
+    assert lib.attn_last_error() is not None
+
+
+def _layout_program(include_dir):
+    src = r"""
+#include <stdio.h>
+#include <stddef.h>
+#include "kv_cache.h"
+#include "scratch.h"
+int main(void) {
+  printf("%zu %zu %zu %zu %zu %zu %zu %zu\n", sizeof(KVCache), offsetof(KVCache, seq_len),
+         offsetof(KVCache, max_seq_len), offsetof(KVCache, rope_offset), sizeof(DecoderScratch),
+         offsetof(DecoderScratch, q_hm), offsetof(DecoderScratch, o_hm),
+         offsetof(DecoderScratch, gate_up_fused));
+  return 0;
+}
+"""
+    return src
+
+
+def _run_layout(tmp_path, include_dir, tag):
+    c = tmp_path / f"layout_{tag}.c"
+    exe = tmp_path / f"layout_{tag}"
+    c.write_text(_layout_program(include_dir))
+    subprocess.run([CC, "-I", str(include_dir), str(c), "-o", str(exe)], check=True)
+    return subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split()
+
+
+def test_struct_layouts_match_reference(tmp_path, pkg):
+    ours = _run_layout(tmp_path, INCLUDE, "ours")
+    # sizeof(KVCache) = 28 layers x 8 heads x 2 pointers + 3 ints (+ tail padding)
+    assert int(ours[1]) == 28 * 8 * 2 * 8
+    assert ctypes.sizeof(pkg.KVCache) == int(ours[0])
+    assert pkg.KVCache.seq_len.offset == int(ours[1])
+    assert pkg.KVCache.rope_offset.offset == int(ours[3])
+    if not REF_KERNEL.exists():
+        pytest.skip("reference tree not present: layout checked against the ctypes mirror only")
+    assert ours == _run_layout(tmp_path, REF_KERNEL, "ref")
+
+
+@pytest.mark.skipif(not REF_KERNEL.exists(), reason="reference tree not present")
+def test_reference_decoder_compiles_and_links_against_include(tmp_path, pkg):
+    """Compile the reference decoder.c unchanged, with include/ supplying attention.h,
+    kv_cache.h and scratch.h (decoder.h/ops.h come from the reference), and check every
+    hot-path symbol it references is exported by libtyphoon_attn.so."""
+    work = tmp_path / "dropin"
+    work.mkdir()
+    for f in ("decoder.c", "decoder.h", "ops.h"):
+        shutil.copy(REF_KERNEL / f, work / f)
+    for f in ("attention.h", "kv_cache.h", "scratch.h"):
+        shutil.copy(INCLUDE / f, work / f)
+    obj = work / "decoder.o"
+    subprocess.run([CC, "-O2", "-fPIC", "-c", str(work / "decoder.c"), "-o", str(obj)], check=True)
+    nm = subprocess.run(["nm", "-u", str(obj)], capture_output=True, text=True, check=True).stdout.split()
+    needed = {s for s in nm if s.startswith(("attention_", "kv_cache_", "decoder_scratch_"))}
+    assert {"attention_decode_gqa", "attention_prefill_gqa", "attention_chunked_prefill_gqa",
+            "kv_cache_append", "kv_cache_append_prefill", "kv_cache_advance", "kv_cache_alloc",
+            "decoder_scratch_alloc"} <= needed
+    lib = ctypes.CDLL(str(pkg.LIB_PATH))
+    assert all(hasattr(lib, s) for s in needed)
+
+
+def test_entry_points_fail_loudly_without_gpu(pkg):
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present; the GPU tests cover the working path")
+    lib = pkg.load_attention_lib()
+    lib.attn_clear_error()
+    assert lib.kv_cache_alloc(64) is None
+    assert pkg.last_error(lib)
+    lib.attn_clear_error()
+    lib.attention_decode_gqa(None, None, None, 0, 1, ctypes.c_float(0.088))
+    assert "NULL" in pkg.last_error(lib)
+    lib.attn_clear_error()
+    assert lib.decoder_scratch_alloc(16) is None
+    assert pkg.last_error(lib)
+    lib.attn_clear_error()

@@ -1,0 +1,157 @@
+"""Split-KV decode kernel vs the oracle (kernel/attention.c:158-204 semantics), through
+the C-ABI entry points attention_decode_gqa and attention_decode_gqa_batched."""
+
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+from gpu_helpers import (TOL_BF16_MAX, TOL_BF16_REL, TOL_MAX, TOL_REL, bf16_round, check, dev, fill_layer,
+                         head_first, new_cache, vp)
+from oracle import max_abs, rel_l2
+
+pytestmark = pytest.mark.gpu
+SCALE = ctypes.c_float(0.08838834764831843)
+
+
+def _run_decode(pkg, lib, h, q, layer, kv_len, on_device):
+    if on_device:
+        qd = dev(q)
+        od = torch.zeros((16, 128), dtype=torch.float32, device="cuda")
+        lib.attention_decode_gqa(vp(qd), h, vp(od), layer, kv_len, SCALE)
+        assert lib.attn_sync() == 0, pkg.last_error(lib)
+        check(pkg, lib, "decode")
+        return od.cpu().numpy()
+    out = np.zeros((16, 128), dtype=np.float32)
+    lib.attention_decode_gqa(vp(q), h, vp(out), layer, kv_len, SCALE)
+    check(pkg, lib, "decode")
+    return out
+
+
+def test_golden_decode(pkg, lib, golden):
+    g = golden("decode_kv45.npz")
+    n = g["k_rows"].shape[0]
+    h = new_cache(pkg, lib, 64, pkg.ATTN_KV_F32)
+    try:
+        fill_layer(pkg, lib, h, 3, g["k_rows"], g["v_rows"])
+        out = _run_decode(pkg, lib, h, g["q"], 3, n, on_device=False)
+        assert max_abs(out, g["out"]) <= TOL_MAX and rel_l2(out, g["out"]) <= TOL_REL
+    finally:
+        lib.kv_cache_free(h)
+
+
+@pytest.mark.parametrize("kv_len", [1, 2, 15, 16, 17, 63, 64, 65, 127, 128, 129, 1000, 4097, 8192])
+@pytest.mark.parametrize("on_device", [False, True])
+def test_decode_fp32_vs_oracle(pkg, lib, oracle, kv_len, on_device):
+    rng = np.random.default_rng(kv_len)
+    max_seq = kv_len + 5
+    q = rng.standard_normal((16, 128), dtype=np.float32)
+    k = rng.standard_normal((max_seq, 8, 128), dtype=np.float32)
+    v = rng.standard_normal((max_seq, 8, 128), dtype=np.float32)
+    h = new_cache(pkg, lib, max_seq, pkg.ATTN_KV_F32)
+    try:
+        fill_layer(pkg, lib, h, 27, k, v)
+        out = _run_decode(pkg, lib, h, q, 27, kv_len, on_device)
+    finally:
+        lib.kv_cache_free(h)
+    want = oracle.decode(q, head_first(k), head_first(v), kv_len)
+    assert max_abs(out, want) <= TOL_MAX and rel_l2(out, want) <= TOL_REL
+
+
+@pytest.mark.parametrize("kv_len", [1, 33, 129, 4097])
+def test_decode_bf16_cache(pkg, lib, oracle, kv_len):
+    rng = np.random.default_rng(100 + kv_len)
+    q = rng.standard_normal((16, 128), dtype=np.float32)
+    k = rng.standard_normal((kv_len, 8, 128), dtype=np.float32)
+    v = rng.standard_normal((kv_len, 8, 128), dtype=np.float32)
+    h = new_cache(pkg, lib, kv_len, pkg.ATTN_KV_BF16)
+    try:
+        fill_layer(pkg, lib, h, 0, k, v)
+        out = _run_decode(pkg, lib, h, q, 0, kv_len, on_device=True)
+    finally:
+        lib.kv_cache_free(h)
+    # Same rows the kernel holds (bf16-rounded): the FP32 bar applies.
+    exact = oracle.decode(q, head_first(bf16_round(k)), head_first(bf16_round(v)), kv_len)
+    assert max_abs(out, exact) <= TOL_MAX and rel_l2(out, exact) <= TOL_REL
+    # Against the FP32 reference inputs: the stated BF16 KV tolerance.
+    ref32 = oracle.decode(q, head_first(k), head_first(v), kv_len)
+    assert max_abs(out, ref32) <= TOL_BF16_MAX and rel_l2(out, ref32) <= TOL_BF16_REL
+
+
+def test_decode_repeated_calls_reuse_workspace(pkg, lib, oracle):
+    """Split tickets must be left at zero: alternate long/short calls on one cache."""
+    rng = np.random.default_rng(7)
+    n = 3000
+    k = rng.standard_normal((n, 8, 128), dtype=np.float32)
+    v = rng.standard_normal((n, 8, 128), dtype=np.float32)
+    h = new_cache(pkg, lib, n, pkg.ATTN_KV_F32)
+    try:
+        fill_layer(pkg, lib, h, 1, k, v)
+        for kv_len in (3000, 40, 2999, 1, 1777, 3000):
+            q = rng.standard_normal((16, 128), dtype=np.float32)
+            out = _run_decode(pkg, lib, h, q, 1, kv_len, on_device=bool(kv_len % 2))
+            want = oracle.decode(q, head_first(k), head_first(v), kv_len)
+            assert max_abs(out, want) <= TOL_MAX, kv_len
+    finally:
+        lib.kv_cache_free(h)
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_decode_batched_ragged(pkg, lib, oracle, dtype):
+    rng = np.random.default_rng(11)
+    lens = [1, 17, 300, 1024, 2049, 5000]
+    kv_dt = pkg.ATTN_KV_F32 if dtype == "f32" else pkg.ATTN_KV_BF16
+    caches, rows = [], []
+    try:
+        for L in lens:
+            h = new_cache(pkg, lib, L + 8, kv_dt)
+            caches.append(h)
+            k = rng.standard_normal((L, 8, 128), dtype=np.float32)
+            v = rng.standard_normal((L, 8, 128), dtype=np.float32)
+            fill_layer(pkg, lib, h, 5, k, v)
+            rows.append((k, v))
+        q = rng.standard_normal((len(lens), 16, 128), dtype=np.float32)
+        out = np.zeros_like(q)
+        arr = (ctypes.c_void_p * len(lens))(*caches)
+        kvl = (ctypes.c_int * len(lens))(*lens)
+        rc = lib.attention_decode_gqa_batched(vp(q), arr, kvl, vp(out), len(lens), 5, SCALE)
+        assert rc == 0, pkg.last_error(lib)
+    finally:
+        for h in caches:
+            lib.kv_cache_free(h)
+    for b, (L, (k, v)) in enumerate(zip(lens, rows)):
+        if dtype == "bf16":
+            k, v = bf16_round(k), bf16_round(v)
+        want = oracle.decode(q[b], head_first(k), head_first(v), L)
+        assert max_abs(out[b], want) <= TOL_MAX and rel_l2(out[b], want) <= TOL_REL, (b, L)
+
+
+def test_decode_kv_len_zero_gives_zeros(pkg, lib):
+    h = new_cache(pkg, lib, 16, pkg.ATTN_KV_F32)
+    try:
+        out = np.full((16, 128), 7.0, dtype=np.float32)
+        q = np.ones((16, 128), dtype=np.float32)
+        lib.attention_decode_gqa(vp(q), h, vp(out), 0, 0, SCALE)
+        check(pkg, lib, "decode kv_len 0")
+        assert not out.any()
+    finally:
+        lib.kv_cache_free(h)
+
+
+def test_decode_rejects_bad_arguments(pkg, lib):
+    h = new_cache(pkg, lib, 16, pkg.ATTN_KV_F32)
+    try:
+        q = np.ones((16, 128), dtype=np.float32)
+        out = np.zeros((16, 128), dtype=np.float32)
+        for layer, kv_len in ((28, 4), (-1, 4), (0, 17), (0, -2)):
+            lib.attn_clear_error()
+            lib.attention_decode_gqa(vp(q), h, vp(out), layer, kv_len, SCALE)
+            assert pkg.last_error(lib), (layer, kv_len)
+        lib.attn_clear_error()
+        bogus = ctypes.create_string_buffer(8192)
+        lib.attention_decode_gqa(vp(q), ctypes.addressof(bogus), vp(out), 0, 1, SCALE)
+        assert "not allocated" in pkg.last_error(lib)
+        lib.attn_clear_error()
+    finally:
+        lib.kv_cache_free(h)

@@ -1,0 +1,244 @@
+/*
+ * attention.c -- the attention entry points of kernel/attention.h (typhoon-ocr-server),
+ * as host C that stages memory and launches the sm_100a kernels.
+ *
+ *   attention_decode_gqa          kernel/attention.c:194-204  -> decode.cu (split-KV)
+ *   attention_prefill_gqa         kernel/attention.c:364-381  -> prefill_simt.cu (FP32)
+ *   attention_chunked_prefill_gqa kernel/attention.c:527-543  -> prefill_simt.cu, K/V
+ *                                                                 from the device cache
+ *   attention_decode_gqa_batched  (new)                       -> decode.cu, many caches
+ *
+ * Host buffers are copied to the device on the library stream and results copied back,
+ * and then the call waits: the reference's calls block until done.  Device buffers are
+ * used in place and the call returns once the work is queued.
+ */
+#include <cuda_runtime_api.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include "attention.h"
+#include "attn_ext.h"
+#include "host_internal.h"
+
+static int check_layer(int layer, const char *what)
+{
+    if (layer < 0 || layer >= KV_NUM_LAYERS) {
+        tyb_set_error("%s: layer_idx %d out of range [0, %d)", what, layer, KV_NUM_LAYERS);
+        return 0;
+    }
+    return 1;
+}
+
+/* Device view of `p`: p itself if it is device memory, else `stage` after an H2D copy
+ * of `bytes` (stage == NULL: only report residency).  Returns NULL on error. */
+static const float *to_device(const float *p, float *stage, size_t bytes, int *is_dev, void *st,
+                              const char *what)
+{
+    int d = tyb_is_device_ptr(p);
+    if (d < 0) return NULL;
+    *is_dev = d;
+    if (d) return p;
+    if (bytes && !tyb_cuda_ok(cudaMemcpyAsync(stage, p, bytes, cudaMemcpyHostToDevice, (cudaStream_t)st), what))
+        return NULL;
+    return stage;
+}
+
+void attention_decode_gqa(const float *q, const KVCache *cache, float *output, int layer_idx,
+                          int kv_len, float scale)
+{
+    const char *what = "attention_decode_gqa";
+    tyb_cache *t = tyb_cache_from(cache);
+    if (!t || !check_layer(layer_idx, what)) return;
+    if (!q || !output) {
+        tyb_set_error("%s: NULL q/output", what);
+        return;
+    }
+    if (kv_len < 0 || kv_len > cache->max_seq_len) {
+        tyb_set_error("%s: kv_len %d out of range [0, %d]", what, kv_len, cache->max_seq_len);
+        return;
+    }
+    void *st = tyb_stream();
+    int q_dev = 0, o_dev = tyb_is_device_ptr(output);
+    if (o_dev < 0) return;
+    const float *dq = to_device(q, t->d_q, TYB_Q_FLOATS * sizeof(float), &q_dev, st, what);
+    if (!dq) return;
+    float *dout = o_dev ? output : t->d_out;
+    if (kv_len == 0) {
+        /* The reference's loops do not run and the output stays zeroed (:186-190). */
+        if (!tyb_cuda_ok(cudaMemsetAsync(dout, 0, TYB_Q_FLOATS * sizeof(float), (cudaStream_t)st), what)) return;
+    } else {
+        tyb_seq_kv one;
+        one.k = tyb_slab_head(t, t->k_slab, layer_idx, 0);
+        one.v = tyb_slab_head(t, t->v_slab, layer_idx, 0);
+        one.kv_len = kv_len;
+        one.row_capacity = cache->max_seq_len;
+        if (!tyb_cuda_ok(tyb_decode_launch(dq, dout, NULL, one, 1, kv_len, t->dtype, scale, t->d_partials,
+                                           t->d_counters, st),
+                         what))
+            return;
+    }
+    if (!o_dev) {
+        if (!tyb_cuda_ok(cudaMemcpyAsync(output, dout, TYB_Q_FLOATS * sizeof(float), cudaMemcpyDeviceToHost,
+                                         (cudaStream_t)st),
+                         what))
+            return;
+    }
+    if (!o_dev || !q_dev) tyb_finish(st, what);
+}
+
+void attention_prefill_gqa(const float *q, const float *k, const float *v, float *output, int Sq,
+                           int Sk, float scale, float *q_hm, float *k_hm, float *v_hm, float *o_hm)
+{
+    const char *what = "attention_prefill_gqa";
+    if (Sq < 0 || Sk < 0) {
+        tyb_set_error("%s: negative Sq/Sk (%d, %d)", what, Sq, Sk);
+        return;
+    }
+    if (Sq == 0) return;
+    if (!q || !k || !v || !output) {
+        tyb_set_error("%s: NULL q/k/v/output", what);
+        return;
+    }
+    void *st = tyb_stream();
+    /* Keys visible to any query are rows < min(Sk, Sq) (mask k_pos > q_pos, :293). */
+    const int kv_rows = Sk < Sq ? Sk : Sq;
+    const size_t qb = (size_t)Sq * TYB_Q_FLOATS * sizeof(float);
+    const size_t kb = (size_t)kv_rows * TYB_ROW_FLOATS * sizeof(float);
+
+    int qd = tyb_is_device_ptr(q), kd = tyb_is_device_ptr(k), vd = tyb_is_device_ptr(v),
+        od = tyb_is_device_ptr(output);
+    if (qd < 0 || kd < 0 || vd < 0 || od < 0) return;
+    /* Staging: the scratch's device slots when large enough, else the workspace. */
+    float *sq = NULL, *sk = NULL, *sv = NULL, *so = NULL;
+    if (!qd) sq = (q_hm && tyb_registry_size(q_hm) >= qb) ? q_hm : (float *)tyb_workspace(TYB_WS_Q, qb);
+    if (!kd) sk = (k_hm && tyb_registry_size(k_hm) >= kb) ? k_hm : (float *)tyb_workspace(TYB_WS_K, kb);
+    if (!vd) sv = (v_hm && tyb_registry_size(v_hm) >= kb) ? v_hm : (float *)tyb_workspace(TYB_WS_V, kb);
+    if (!od) so = (o_hm && tyb_registry_size(o_hm) >= qb) ? o_hm : (float *)tyb_workspace(TYB_WS_OUT, qb);
+    if ((!qd && !sq) || (!kd && !sk) || (!vd && !sv) || (!od && !so)) return;
+
+    const float *dq = to_device(q, sq, qb, &qd, st, what);
+    const float *dk = kv_rows ? to_device(k, sk, kb, &kd, st, what) : k;
+    const float *dv = kv_rows ? to_device(v, sv, kb, &vd, st, what) : v;
+    if (!dq || !dk || !dv) return;
+    float *dout = od ? output : so;
+    if (!tyb_cuda_ok(tyb_prefill_simt_launch(dq, dout, dk, dv, TYB_ROW_FLOATS, KV_HEAD_DIM, TYB_F32, Sq, Sk, 0,
+                                             scale, st),
+                     what))
+        return;
+    if (!od && !tyb_cuda_ok(cudaMemcpyAsync(output, dout, qb, cudaMemcpyDeviceToHost, (cudaStream_t)st), what))
+        return;
+    if (!qd || !kd || !vd || !od) tyb_finish(st, what);
+}
+
+void attention_chunked_prefill_gqa(const float *q, const KVCache *cache, float *output,
+                                   int layer_idx, int chunk_len, int pos_offset, float scale)
+{
+    const char *what = "attention_chunked_prefill_gqa";
+    tyb_cache *t = tyb_cache_from(cache);
+    if (!t || !check_layer(layer_idx, what)) return;
+    if (chunk_len < 0 || pos_offset < 0 || pos_offset + chunk_len > cache->max_seq_len) {
+        tyb_set_error("%s: rows [%d, %d) exceed max_seq_len %d", what, pos_offset, pos_offset + chunk_len,
+                      cache->max_seq_len);
+        return;
+    }
+    if (chunk_len == 0) return;
+    if (!q || !output) {
+        tyb_set_error("%s: NULL q/output", what);
+        return;
+    }
+    void *st = tyb_stream();
+    const size_t qb = (size_t)chunk_len * TYB_Q_FLOATS * sizeof(float);
+    int qd = tyb_is_device_ptr(q), od = tyb_is_device_ptr(output);
+    if (qd < 0 || od < 0) return;
+    float *sq = qd ? NULL : (float *)tyb_workspace(TYB_WS_Q, qb);
+    float *so = od ? NULL : (float *)tyb_workspace(TYB_WS_OUT, qb);
+    if ((!qd && !sq) || (!od && !so)) return;
+    const float *dq = to_device(q, sq, qb, &qd, st, what);
+    if (!dq) return;
+    float *dout = od ? output : so;
+    const void *kl = tyb_slab_head(t, t->k_slab, layer_idx, 0);
+    const void *vl = tyb_slab_head(t, t->v_slab, layer_idx, 0);
+    /* Head-first cache rows: row stride 128, head stride max_seq*128 (:425-427, :461). */
+    if (!tyb_cuda_ok(tyb_prefill_simt_launch(dq, dout, kl, vl, KV_HEAD_DIM,
+                                             (long long)cache->max_seq_len * KV_HEAD_DIM, t->dtype, chunk_len,
+                                             pos_offset + chunk_len, pos_offset, scale, st),
+                     what))
+        return;
+    if (!od && !tyb_cuda_ok(cudaMemcpyAsync(output, dout, qb, cudaMemcpyDeviceToHost, (cudaStream_t)st), what))
+        return;
+    if (!qd || !od) tyb_finish(st, what);
+}
+
+int attention_decode_gqa_batched(const float *q, const KVCache *const *caches, const int *kv_lens,
+                                 float *output, int batch, int layer_idx, float scale)
+{
+    const char *what = "attention_decode_gqa_batched";
+    if (batch <= 0 || !caches || !kv_lens || !q || !output) {
+        tyb_set_error("%s: need batch > 0 and non-NULL q/caches/kv_lens/output", what);
+        return 1;
+    }
+    if (!check_layer(layer_idx, what)) return 1;
+    tyb_seq_kv *descs = (tyb_seq_kv *)malloc(sizeof(tyb_seq_kv) * (size_t)batch);
+    if (!descs) {
+        tyb_set_error("%s: out of host memory", what);
+        return 1;
+    }
+    int dtype = -1, max_kv = 0, ok = 1;
+    for (int b = 0; b < batch && ok; b++) {
+        tyb_cache *t = tyb_cache_from(caches[b]);
+        if (!t) { ok = 0; break; }
+        if (dtype >= 0 && t->dtype != dtype) {
+            tyb_set_error("%s: caches mix element types", what);
+            ok = 0;
+            break;
+        }
+        dtype = t->dtype;
+        if (kv_lens[b] < 1 || kv_lens[b] > t->pub.max_seq_len) {
+            tyb_set_error("%s: kv_lens[%d] = %d out of range [1, %d]", what, b, kv_lens[b], t->pub.max_seq_len);
+            ok = 0;
+            break;
+        }
+        descs[b].k = tyb_slab_head(t, t->k_slab, layer_idx, 0);
+        descs[b].v = tyb_slab_head(t, t->v_slab, layer_idx, 0);
+        descs[b].kv_len = kv_lens[b];
+        descs[b].row_capacity = t->pub.max_seq_len;
+        if (kv_lens[b] > max_kv) max_kv = kv_lens[b];
+    }
+    if (!ok) {
+        free(descs);
+        return 1;
+    }
+    void *st = tyb_stream();
+    int chunk, nsplit;
+    tyb_decode_plan(batch, max_kv, dtype, &chunk, &nsplit);
+    const size_t qb = (size_t)batch * TYB_Q_FLOATS * sizeof(float);
+    tyb_seq_kv *ddesc = (tyb_seq_kv *)tyb_workspace(TYB_WS_DESC, sizeof(tyb_seq_kv) * (size_t)batch);
+    float *part = (float *)tyb_workspace(TYB_WS_PARTIALS, tyb_decode_partial_floats(batch, nsplit) * sizeof(float));
+    unsigned int *cnt =
+        (unsigned int *)tyb_workspace(TYB_WS_COUNTERS, sizeof(unsigned int) * (size_t)batch * KV_NUM_KV_HEADS);
+    int qd = tyb_is_device_ptr(q), od = tyb_is_device_ptr(output);
+    float *sq = (qd == 0) ? (float *)tyb_workspace(TYB_WS_Q, qb) : NULL;
+    float *so = (od == 0) ? (float *)tyb_workspace(TYB_WS_OUT, qb) : NULL;
+    if (!ddesc || !part || !cnt || qd < 0 || od < 0 || (!qd && !sq) || (!od && !so)) {
+        free(descs);
+        return 1;
+    }
+    /* The descriptor upload reads host memory: pageable copies are staged by the driver
+     * before cudaMemcpyAsync returns, so `descs` can be freed right after. */
+    ok = tyb_cuda_ok(cudaMemcpyAsync(ddesc, descs, sizeof(tyb_seq_kv) * (size_t)batch, cudaMemcpyHostToDevice,
+                                     (cudaStream_t)st),
+                     what);
+    free(descs);
+    if (!ok) return 1;
+    const float *dq = to_device(q, sq, qb, &qd, st, what);
+    if (!dq) return 1;
+    float *dout = od ? output : so;
+    tyb_seq_kv none;
+    memset(&none, 0, sizeof none);
+    if (!tyb_cuda_ok(tyb_decode_launch(dq, dout, ddesc, none, batch, max_kv, dtype, scale, part, cnt, st), what))
+        return 1;
+    if (!od && !tyb_cuda_ok(cudaMemcpyAsync(output, dout, qb, cudaMemcpyDeviceToHost, (cudaStream_t)st), what))
+        return 1;
+    if (!qd || !od) return tyb_finish(st, what) ? 0 : 1;
+    return 0;
+}

@@ -1,0 +1,76 @@
+/*
+ * attn_shim.h -- the thin C interface between the host C of this library
+ * (attention.c, kv_cache.c, scratch.c) and its sm_100a kernels (*.cu).
+ *
+ * Every launcher takes DEVICE pointers only, enqueues on `stream` (a
+ * cudaStream_t; NULL = the legacy default stream) and returns a cudaError_t
+ * value (0 = success).  Nothing here synchronises; the host C decides when the
+ * caller's contract needs a synchronous return.
+ */
+#ifndef TYB_ATTN_SHIM_H
+#define TYB_ATTN_SHIM_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Element type of KV-cache rows and of staged activations. */
+enum { TYB_F32 = 0, TYB_BF16 = 1 };
+
+/* Bits of the device status word (tyb_status_fetch). */
+#define TYB_STATUS_WAIT_TIMEOUT 0x1u /* an mbarrier wait ran past its time limit */
+#define TYB_STATUS_BAD_ARGUMENT 0x2u /* a kernel found an index outside its buffers */
+
+/* One sequence's K and V rows for ONE layer, head-first:
+ * element (kv_head h, row r, dim d) at base + ((size_t)h * row_capacity + r) * 128 + d. */
+typedef struct {
+    const void *k;
+    const void *v;
+    int kv_len;       /* rows attended: [0, kv_len) */
+    int row_capacity; /* rows allocated per head (the cache's max_seq_len) */
+} tyb_seq_kv;
+
+/* ---- split-KV flash decoding (decode.cu) ------------------------------------------ */
+
+/* Rows per split and split count the decode kernel will use for a batch whose
+ * longest sequence has max_kv_len rows. */
+void tyb_decode_plan(int batch, int max_kv_len, int kv_dtype, int *chunk_rows, int *nsplit);
+
+/* Floats of split workspace and counters needed for tyb_decode_launch. */
+size_t tyb_decode_partial_floats(int batch, int nsplit);
+
+/* q, out: [batch][16][128] fp32.  seqs_dev: device array of `batch` descriptors, or
+ * NULL with batch == 1 to use `one`.  partials: >= tyb_decode_partial_floats floats;
+ * counters: batch*8 zeroed words (the kernel leaves them zeroed). */
+int tyb_decode_launch(const float *q, float *out, const tyb_seq_kv *seqs_dev, tyb_seq_kv one,
+                      int batch, int max_kv_len, int kv_dtype, float scale, float *partials,
+                      unsigned int *counters, void *stream);
+
+/* ---- FP32 flash prefill on CUDA cores (prefill_simt.cu) --------------------------- */
+
+/* q/out token-major [Sq][16][128] fp32.  K/V element (row r, kv head h, dim d) at
+ * base + r*row_stride + h*head_stride + d (elements of kv_dtype).  Query i sits at
+ * absolute position pos_offset + i and sees keys r <= pos_offset + i, r < Sk. */
+int tyb_prefill_simt_launch(const float *q, float *out, const void *k, const void *v,
+                            long long row_stride, long long head_stride, int kv_dtype, int Sq,
+                            int Sk, int pos_offset, float scale, void *stream);
+
+/* ---- KV-cache row writes (kv_write.cu) -------------------------------------------- */
+
+/* Token-major fp32 rows [S][8][128] -> head-first cache rows [pos0, pos0+S) of one layer
+ * (layout of tyb_seq_kv), converting to the cache's element type. */
+int tyb_kv_scatter_launch(const float *k_src, const float *v_src, void *k_dst, void *v_dst,
+                          int row_capacity, int pos0, int S, int kv_dtype, void *stream);
+
+/* ---- status word -------------------------------------------------------------------- */
+
+/* Copy the status word to *bits after all work on `stream`, then clear it. */
+int tyb_status_fetch(unsigned int *bits, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

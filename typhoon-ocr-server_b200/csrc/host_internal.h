@@ -1,0 +1,71 @@
+/*
+ * host_internal.h -- shared declarations of the host C layer (runtime.c, kv_cache.c,
+ * scratch.c, attention.c).  Not part of the public interface.
+ */
+#ifndef TYB_HOST_INTERNAL_H
+#define TYB_HOST_INTERNAL_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include "attn_shim.h"
+#include "kv_cache.h"
+
+#define TYB_CACHE_MAGIC 0x54594243u /* "TYBC" */
+#define TYB_ROW_FLOATS (KV_NUM_KV_HEADS * KV_HEAD_DIM) /* 1024: one token of K or V */
+#define TYB_Q_FLOATS (16 * KV_HEAD_DIM)               /* 2048: one token of Q / output */
+
+/* Device cache.  `pub` is the first member, so the KVCache* handed to callers converts
+ * back to this struct; callers only ever touch pub's fields. */
+typedef struct {
+    KVCache pub;
+    uint32_t magic;
+    int dtype;               /* TYB_F32 / TYB_BF16 */
+    int device;              /* CUDA device current at allocation */
+    size_t elem_bytes;       /* 4 or 2 */
+    void *k_slab, *v_slab;   /* [28][8][max_seq][128] elements */
+    float *d_q;              /* [16][128] staging of a host query (decode) */
+    float *d_out;            /* [16][128] staging of a host output (decode) */
+    float *d_kv_stage;       /* [2][max_seq][8][128] fp32 staging of host K/V rows */
+    float *d_partials;       /* split-KV workspace of the decode kernel */
+    unsigned int *d_counters;/* [8] split tickets, kept zero between launches */
+} tyb_cache;
+
+/* The cache behind a KVCache*, or NULL (error set) if this library did not make it. */
+tyb_cache *tyb_cache_from(const KVCache *c);
+
+/* Device address of row 0 of (layer, head) in a slab. */
+static inline void *tyb_slab_head(const tyb_cache *c, void *slab, int layer, int head)
+{
+    size_t rows = (size_t)c->pub.max_seq_len;
+    return (char *)slab + (((size_t)layer * KV_NUM_KV_HEADS + head) * rows) * KV_HEAD_DIM * c->elem_bytes;
+}
+
+/* Errors: thread-local message, "" when none. */
+void tyb_set_error(const char *fmt, ...);
+/* 1 when err == 0 (cudaSuccess); otherwise records "<what>: <cuda error string>", returns 0. */
+int tyb_cuda_ok(int err, const char *what);
+
+/* The calling thread's stream (NULL = legacy default stream). */
+void *tyb_stream(void);
+
+/* 1 when p is device (or managed) memory usable by kernels, 0 when host memory,
+ * -1 on error (error set). */
+int tyb_is_device_ptr(const void *p);
+
+/* Process-wide device workspace slots, grown on demand; NULL on failure (error set). */
+enum { TYB_WS_Q, TYB_WS_K, TYB_WS_V, TYB_WS_OUT, TYB_WS_PARTIALS, TYB_WS_COUNTERS, TYB_WS_DESC,
+       TYB_WS_COUNT };
+void *tyb_workspace(int slot, size_t bytes);
+
+/* Device buffers handed out by decoder_scratch_alloc, so attention_prefill_gqa can tell
+ * whether a q_hm/k_hm/v_hm/o_hm pointer is ours and how large it is. */
+void   tyb_registry_add(const void *p, size_t bytes);
+void   tyb_registry_remove(const void *p);
+size_t tyb_registry_size(const void *p); /* 0 when unknown */
+
+/* Wait for `stream`, then check the device status word.  1 when all is well;
+ * otherwise 0 with the error set. */
+int tyb_finish(void *stream, const char *what);
+
+#endif

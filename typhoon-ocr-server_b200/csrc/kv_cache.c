@@ -1,0 +1,191 @@
+/*
+ * kv_cache.c -- the static KV cache of kernel/kv_cache.c (typhoon-ocr-server), resident
+ * in HBM.
+ *
+ * The reference mallocs 28 x 8 x 2 separate float[max_seq][128] arrays
+ * (kernel/kv_cache.c:15-34).  Here K and V are each ONE device slab
+ * [layer][kv_head][max_seq][128] (fp32 or bf16), and the KVHead pointers point into it,
+ * so a (layer, head) row block is contiguous exactly as in the reference and a decode
+ * split is one contiguous byte range for a bulk copy.  Row writes from host memory go
+ * through a device staging buffer and one scatter kernel (kv_write.cu).
+ */
+#include <cuda_runtime_api.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include "attn_ext.h"
+#include "host_internal.h"
+
+tyb_cache *tyb_cache_from(const KVCache *c)
+{
+    if (!c) {
+        tyb_set_error("KVCache is NULL");
+        return NULL;
+    }
+    tyb_cache *t = (tyb_cache *)c;
+    if (t->magic != TYB_CACHE_MAGIC) {
+        tyb_set_error("KVCache was not allocated by kv_cache_alloc of this library");
+        return NULL;
+    }
+    return t;
+}
+
+static void cache_release(tyb_cache *t)
+{
+    if (!t) return;
+    cudaFree(t->k_slab);
+    cudaFree(t->v_slab);
+    cudaFree(t->d_q);
+    cudaFree(t->d_out);
+    cudaFree(t->d_kv_stage);
+    cudaFree(t->d_partials);
+    cudaFree(t->d_counters);
+    t->magic = 0;
+    free(t);
+}
+
+KVCache *kv_cache_alloc_ex(int max_seq_len, int kv_dtype)
+{
+    if (max_seq_len <= 0) {
+        tyb_set_error("kv_cache_alloc: max_seq_len must be positive (got %d)", max_seq_len);
+        return NULL;
+    }
+    if (kv_dtype != ATTN_KV_F32 && kv_dtype != ATTN_KV_BF16) {
+        tyb_set_error("kv_cache_alloc_ex: unknown kv_dtype %d", kv_dtype);
+        return NULL;
+    }
+    tyb_cache *t = (tyb_cache *)calloc(1, sizeof(tyb_cache));
+    if (!t) {
+        tyb_set_error("kv_cache_alloc: out of host memory");
+        return NULL;
+    }
+    t->magic = TYB_CACHE_MAGIC;
+    t->dtype = kv_dtype == ATTN_KV_BF16 ? TYB_BF16 : TYB_F32;
+    t->elem_bytes = kv_dtype == ATTN_KV_BF16 ? 2 : 4;
+    t->pub.max_seq_len = max_seq_len;
+    t->pub.seq_len = 0;
+    t->pub.rope_offset = 0;
+    cudaGetDevice(&t->device);
+
+    const size_t slab = (size_t)KV_NUM_LAYERS * KV_NUM_KV_HEADS * max_seq_len * KV_HEAD_DIM * t->elem_bytes;
+    int chunk = 0, nsplit = 0;
+    /* Upper bound on splits for any kv_len <= max_seq_len: chunks are >= 16 rows. */
+    nsplit = (max_seq_len + 15) / 16 + 1;
+    (void)chunk;
+    const size_t part = tyb_decode_partial_floats(1, nsplit) * sizeof(float);
+
+    int ok = tyb_cuda_ok(cudaMalloc(&t->k_slab, slab), "kv_cache_alloc: K slab") &&
+             tyb_cuda_ok(cudaMalloc(&t->v_slab, slab), "kv_cache_alloc: V slab") &&
+             tyb_cuda_ok(cudaMalloc((void **)&t->d_q, TYB_Q_FLOATS * sizeof(float)), "kv_cache_alloc: q") &&
+             tyb_cuda_ok(cudaMalloc((void **)&t->d_out, TYB_Q_FLOATS * sizeof(float)), "kv_cache_alloc: out") &&
+             tyb_cuda_ok(cudaMalloc((void **)&t->d_kv_stage, 2 * (size_t)max_seq_len * TYB_ROW_FLOATS * sizeof(float)),
+                         "kv_cache_alloc: staging") &&
+             tyb_cuda_ok(cudaMalloc((void **)&t->d_partials, part), "kv_cache_alloc: decode workspace") &&
+             tyb_cuda_ok(cudaMalloc((void **)&t->d_counters, KV_NUM_KV_HEADS * sizeof(unsigned int)),
+                         "kv_cache_alloc: counters") &&
+             tyb_cuda_ok(cudaMemset(t->d_counters, 0, KV_NUM_KV_HEADS * sizeof(unsigned int)),
+                         "kv_cache_alloc: counters memset");
+    if (!ok) {
+        cache_release(t);
+        return NULL;
+    }
+    for (int l = 0; l < KV_NUM_LAYERS; l++)
+        for (int h = 0; h < KV_NUM_KV_HEADS; h++) {
+            t->pub.layers[l].heads[h].k = (float *)tyb_slab_head(t, t->k_slab, l, h);
+            t->pub.layers[l].heads[h].v = (float *)tyb_slab_head(t, t->v_slab, l, h);
+        }
+    return &t->pub;
+}
+
+KVCache *kv_cache_alloc(int max_seq_len) { return kv_cache_alloc_ex(max_seq_len, ATTN_KV_F32); }
+
+int kv_cache_dtype(const KVCache *c)
+{
+    tyb_cache *t = tyb_cache_from(c);
+    if (!t) return -1;
+    return t->dtype == TYB_BF16 ? ATTN_KV_BF16 : ATTN_KV_F32;
+}
+
+void kv_cache_free(KVCache *c)
+{
+    if (!c) return;
+    tyb_cache *t = tyb_cache_from(c);
+    if (!t) return;
+    cudaStreamSynchronize((cudaStream_t)tyb_stream());
+    cache_release(t);
+}
+
+void kv_cache_clear(KVCache *c)
+{
+    if (c) { c->seq_len = 0; c->rope_offset = 0; } /* kernel/kv_cache.c:48-51 */
+}
+
+/* Rows [pos, pos+S) of `layer` from token-major k_new/v_new [S][8][128] fp32. */
+static void append_rows(KVCache *c, int layer, const float *k_new, const float *v_new, int S,
+                        const char *what)
+{
+    tyb_cache *t = tyb_cache_from(c);
+    if (!t) return;
+    if (layer < 0 || layer >= KV_NUM_LAYERS) {
+        tyb_set_error("%s: layer %d out of range [0, %d)", what, layer, KV_NUM_LAYERS);
+        return;
+    }
+    const int pos = c->seq_len;
+    if (S < 0 || pos < 0 || pos + S > c->max_seq_len) {
+        tyb_set_error("%s: rows [%d, %d) exceed max_seq_len %d", what, pos, pos + S, c->max_seq_len);
+        return;
+    }
+    if (S == 0) return;
+    if (!k_new || !v_new) {
+        tyb_set_error("%s: NULL k_new/v_new", what);
+        return;
+    }
+    const int kd = tyb_is_device_ptr(k_new), vd = tyb_is_device_ptr(v_new);
+    if (kd < 0 || vd < 0) return;
+    void *st = tyb_stream();
+    const size_t bytes = (size_t)S * TYB_ROW_FLOATS * sizeof(float);
+    const float *ks = k_new, *vs = v_new;
+    if (!kd) {
+        if (!tyb_cuda_ok(cudaMemcpyAsync(t->d_kv_stage, k_new, bytes, cudaMemcpyHostToDevice, (cudaStream_t)st), what))
+            return;
+        ks = t->d_kv_stage;
+    }
+    if (!vd) {
+        float *dst = t->d_kv_stage + (size_t)c->max_seq_len * TYB_ROW_FLOATS;
+        if (!tyb_cuda_ok(cudaMemcpyAsync(dst, v_new, bytes, cudaMemcpyHostToDevice, (cudaStream_t)st), what))
+            return;
+        vs = dst;
+    }
+    void *kl = tyb_slab_head(t, t->k_slab, layer, 0), *vl = tyb_slab_head(t, t->v_slab, layer, 0);
+    if (!tyb_cuda_ok(tyb_kv_scatter_launch(ks, vs, kl, vl, c->max_seq_len, pos, S, t->dtype, st), what)) return;
+    /* Host sources: block until the rows are read, as the reference's memcpy does. */
+    if (!kd || !vd) tyb_finish(st, what);
+}
+
+void kv_cache_append(KVCache *c, int layer, const float *k_new, const float *v_new)
+{
+    append_rows(c, layer, k_new, v_new, 1, "kv_cache_append"); /* kernel/kv_cache.c:53-65 */
+}
+
+void kv_cache_append_prefill(KVCache *c, int layer, const float *k_new, const float *v_new,
+                             int seq_len)
+{
+    append_rows(c, layer, k_new, v_new, seq_len, "kv_cache_append_prefill"); /* :95-104 */
+}
+
+void kv_cache_advance(KVCache *c, int n)
+{
+    if (!c) return;
+    c->seq_len += n; /* kernel/kv_cache.c:106-110 */
+    if (c->rope_offset > 0) c->rope_offset += n;
+}
+
+const float *kv_cache_k(const KVCache *c, int layer, int head)
+{
+    return c->layers[layer].heads[head].k; /* kernel/kv_cache.c:112-115 */
+}
+
+const float *kv_cache_v(const KVCache *c, int layer, int head)
+{
+    return c->layers[layer].heads[head].v; /* kernel/kv_cache.c:117-120 */
+}

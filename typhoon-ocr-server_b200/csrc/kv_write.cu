@@ -1,0 +1,75 @@
+// kv_write.cu -- KV-cache row writes and the library status word.
+//
+// kv_cache_append (kernel/kv_cache.c:53-65) and kv_cache_append_prefill (:80-104) copy
+// token-major K/V rows [S][8][128] into the head-first cache [8][max_seq][128] of one
+// layer at rows seq_len.. .  On the device that is one scatter kernel: thread t moves
+// 8 contiguous elements (one 16-byte load per 4 fp32 values, one 16-byte store of bf16
+// or two of fp32), converting to the cache's element type on the way.
+#include "common.cuh"
+
+namespace tyb {
+
+__device__ unsigned int g_status = 0u;
+
+template <typename TDst>
+__global__ void kv_scatter_kernel(const float* __restrict__ k_src, const float* __restrict__ v_src,
+                                  TDst* __restrict__ k_dst, TDst* __restrict__ v_dst,
+                                  int row_capacity, int pos0, int S)
+{
+    // One thread per (tensor, token, head, 8-element group): 2 * S * 8 * 16 threads.
+    const long long n = 2LL * S * kHkv * (kD / 8);
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+         i += (long long)gridDim.x * blockDim.x) {
+        const int c = (int)(i % (kD / 8));
+        const long long th = i / (kD / 8);
+        const int h = (int)(th % kHkv);
+        const long long tt = th / kHkv;
+        const int t = (int)(tt % S);
+        const int which = (int)(tt / S);
+        const float* src = (which ? v_src : k_src) + ((size_t)t * kHkv + h) * kD + 8 * c;
+        TDst* dst = (which ? v_dst : k_dst) + ((size_t)h * row_capacity + pos0 + t) * kD + 8 * c;
+        float x[8];
+        load8(src, x);
+        store8(dst, x);
+    }
+}
+
+}  // namespace tyb
+
+using namespace tyb;
+
+extern "C" int tyb_kv_scatter_launch(const float* k_src, const float* v_src, void* k_dst,
+                                     void* v_dst, int row_capacity, int pos0, int S, int kv_dtype,
+                                     void* stream)
+{
+    if (S <= 0) return 0;
+    const long long n = 2LL * S * kHkv * (kD / 8);
+    const int threads = 256;
+    long long blocks = (n + threads - 1) / threads;
+    if (blocks > 148LL * 16) blocks = 148LL * 16;
+    if (kv_dtype == TYB_BF16)
+        kv_scatter_kernel<__nv_bfloat16><<<(unsigned)blocks, threads, 0, (cudaStream_t)stream>>>(
+            k_src, v_src, static_cast<__nv_bfloat16*>(k_dst), static_cast<__nv_bfloat16*>(v_dst),
+            row_capacity, pos0, S);
+    else
+        kv_scatter_kernel<float><<<(unsigned)blocks, threads, 0, (cudaStream_t)stream>>>(
+            k_src, v_src, static_cast<float*>(k_dst), static_cast<float*>(v_dst), row_capacity,
+            pos0, S);
+    return (int)cudaGetLastError();
+}
+
+extern "C" int tyb_status_fetch(unsigned int* bits, void* stream)
+{
+    cudaStream_t st = (cudaStream_t)stream;
+    cudaError_t e = cudaMemcpyFromSymbolAsync(bits, g_status, sizeof(unsigned int), 0,
+                                              cudaMemcpyDeviceToHost, st);
+    if (e != cudaSuccess) return (int)e;
+    e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) return (int)e;
+    if (*bits) {
+        const unsigned int zero = 0u;
+        e = cudaMemcpyToSymbolAsync(g_status, &zero, sizeof zero, 0, cudaMemcpyHostToDevice, st);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    }
+    return (int)e;
+}

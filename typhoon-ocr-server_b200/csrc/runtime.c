@@ -1,0 +1,149 @@
+/*
+ * runtime.c -- error reporting, stream selection, pointer residency, workspace and
+ * synchronisation for the host C layer.
+ *
+ * The reference's attention and append functions return void with no error channel
+ * (kernel/attention.h:11,26,39); here every entry point records failures in a
+ * thread-local message read through attn_last_error().
+ */
+#include <cuda_runtime_api.h>
+#include <pthread.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include "attn_ext.h"
+#include "host_internal.h"
+
+static _Thread_local char g_err[512];
+static _Thread_local void *g_stream; /* NULL: legacy default stream */
+
+void tyb_set_error(const char *fmt, ...)
+{
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_err, sizeof g_err, fmt, ap);
+    va_end(ap);
+}
+
+int tyb_cuda_ok(int err, const char *what)
+{
+    if (err == 0) return 1;
+    tyb_set_error("%s: %s", what, cudaGetErrorString((cudaError_t)err));
+    return 0;
+}
+
+const char *attn_last_error(void) { return g_err; }
+
+void attn_clear_error(void) { g_err[0] = '\0'; }
+
+void attn_set_stream(void *stream) { g_stream = stream; }
+
+void *tyb_stream(void) { return g_stream; }
+
+int tyb_is_device_ptr(const void *p)
+{
+    struct cudaPointerAttributes attr;
+    cudaError_t e = cudaPointerGetAttributes(&attr, p);
+    if (e != cudaSuccess) {
+        cudaGetLastError(); /* clear the sticky-free error state for later calls */
+        tyb_set_error("cudaPointerGetAttributes: %s", cudaGetErrorString(e));
+        return -1;
+    }
+    return attr.type == cudaMemoryTypeDevice || attr.type == cudaMemoryTypeManaged;
+}
+
+/* ---- workspace ------------------------------------------------------------------ */
+
+static pthread_mutex_t g_ws_lock = PTHREAD_MUTEX_INITIALIZER;
+static void *g_ws_ptr[TYB_WS_COUNT];
+static size_t g_ws_size[TYB_WS_COUNT];
+
+void *tyb_workspace(int slot, size_t bytes)
+{
+    void *p = NULL;
+    pthread_mutex_lock(&g_ws_lock);
+    if (g_ws_size[slot] >= bytes && g_ws_ptr[slot]) {
+        p = g_ws_ptr[slot];
+    } else {
+        if (g_ws_ptr[slot]) {
+            cudaDeviceSynchronize(); /* the old buffer may still be in use */
+            cudaFree(g_ws_ptr[slot]);
+            g_ws_ptr[slot] = NULL;
+            g_ws_size[slot] = 0;
+        }
+        size_t want = bytes < 4096 ? 4096 : bytes;
+        if (tyb_cuda_ok(cudaMalloc(&p, want), "workspace cudaMalloc")) {
+            /* Counters and tickets must start at zero. */
+            if (!tyb_cuda_ok(cudaMemset(p, 0, want), "workspace cudaMemset")) {
+                cudaFree(p);
+                p = NULL;
+            } else {
+                g_ws_ptr[slot] = p;
+                g_ws_size[slot] = want;
+            }
+        } else {
+            p = NULL;
+        }
+    }
+    pthread_mutex_unlock(&g_ws_lock);
+    return p;
+}
+
+/* ---- registry of scratch device buffers ------------------------------------------- */
+
+#define TYB_REG_MAX 256
+static pthread_mutex_t g_reg_lock = PTHREAD_MUTEX_INITIALIZER;
+static const void *g_reg_ptr[TYB_REG_MAX];
+static size_t g_reg_size[TYB_REG_MAX];
+
+void tyb_registry_add(const void *p, size_t bytes)
+{
+    pthread_mutex_lock(&g_reg_lock);
+    for (int i = 0; i < TYB_REG_MAX; i++)
+        if (!g_reg_ptr[i]) {
+            g_reg_ptr[i] = p;
+            g_reg_size[i] = bytes;
+            break;
+        }
+    pthread_mutex_unlock(&g_reg_lock);
+}
+
+void tyb_registry_remove(const void *p)
+{
+    pthread_mutex_lock(&g_reg_lock);
+    for (int i = 0; i < TYB_REG_MAX; i++)
+        if (g_reg_ptr[i] == p) {
+            g_reg_ptr[i] = NULL;
+            g_reg_size[i] = 0;
+        }
+    pthread_mutex_unlock(&g_reg_lock);
+}
+
+size_t tyb_registry_size(const void *p)
+{
+    size_t n = 0;
+    pthread_mutex_lock(&g_reg_lock);
+    for (int i = 0; i < TYB_REG_MAX; i++)
+        if (p && g_reg_ptr[i] == p) n = g_reg_size[i];
+    pthread_mutex_unlock(&g_reg_lock);
+    return n;
+}
+
+/* ---- synchronisation + status ----------------------------------------------------- */
+
+int tyb_finish(void *stream, const char *what)
+{
+    unsigned int bits = 0;
+    int e = tyb_status_fetch(&bits, stream);
+    if (!tyb_cuda_ok(e, what)) return 0;
+    if (bits) {
+        tyb_set_error("%s: device status 0x%x (%s%s)", what, bits,
+                      (bits & TYB_STATUS_WAIT_TIMEOUT) ? "wait timed out " : "",
+                      (bits & TYB_STATUS_BAD_ARGUMENT) ? "index check failed" : "");
+        return 0;
+    }
+    return 1;
+}
+
+int attn_sync(void) { return tyb_finish(g_stream, "attn_sync") ? 0 : 1; }
