@@ -189,8 +189,10 @@ class DecodeBench:
         self.pkg.check(self.lib, "graph capture")
 
     def run(self, first, n):
-        for i in range(first, first + n):
-            self.graphs[i % SCHEDULE].replay()
+        # replay() launches on the current stream: make it the stream the events time.
+        with self.torch.cuda.stream(self.stream):
+            for i in range(first, first + n):
+                self.graphs[i % SCHEDULE].replay()
 
     def close(self):
         self.lib.attn_set_stream(None)

@@ -4,27 +4,32 @@
 // KV head and its two query heads, scores = q.K*scale over kv_len rows, max, exp, sum,
 // normalise, out = sum p*V).  Here one CTA owns one (sequence, KV head, split of rows):
 //   1. one thread starts two bulk async copies (TMA, 1-D) of the split's K and V rows --
-//      contiguous in the head-first cache -- into shared memory, each completing on
-//      its own mbarrier, so the whole split is in flight before any math runs;
-//   2. the CTA computes both query heads' scores against K (16-byte vectors, 16 lanes
-//      per row, shuffle-xor reduction), then max and exp2 per head;
+//      contiguous in the head-first cache -- into shared memory, each completing on its
+//      own mbarrier.  The split count is chosen so the whole grid is resident at once
+//      (one wave), which puts every byte of the layer's K/V in flight together;
+//   2. scores of both query heads against K (16-byte vectors, 16 lanes per row,
+//      shuffle-xor reduction), then max and exp2 per head;
 //   3. once V has landed, p.V for both heads (K/V read once for the GQA pair);
-//   4. the split's (max, sum, unnormalised o) goes to a workspace and the last CTA of
-//      the (sequence, head) -- found with an atomic ticket -- merges all splits and
-//      writes the output.  No second launch.
+//   4. the split's (max, sum, unnormalised o) goes to a workspace record and the last
+//      CTA of the (sequence, head) -- found with an atomic ticket -- merges all records
+//      with parallel loads and writes the output.  No second launch.
+// Launched with programmatic dependent launch: the next kernel in the stream may start
+// its prologue while this grid drains; every global read of data produced by earlier
+// kernels happens after griddepcontrol.wait.
 // Bandwidth-bound: 2 * kv_len * 128 * sizeof(T) bytes per (sequence, KV head).
 #include "common.cuh"
 
 namespace tyb {
 
-constexpr int kDecThreads = 128;
-constexpr int kPartStride = 132;  // m, l, 2 pad, o[128]: keeps o 16-byte aligned
+constexpr int kDecThreads = 256;
+constexpr int kRowGroups = kDecThreads / 16;  // p.V row groups (16 lanes per row)
+constexpr int kRec = 4 + 2 * kD;              // record: m0 l0 m1 l1 | o0[128] | o1[128]
+constexpr int kRedBytes = kRowGroups * 2 * kD * (int)sizeof(float);
 
 template <typename T>
 struct DecodeTile {
-    // Rows per split are capped so K+V of one split stay <= 64 KB of shared memory,
-    // which leaves room for three CTAs per SM.
-    static constexpr int kMaxChunk = 65536 / (2 * kD * (int)sizeof(T));
+    // Rows per split: bounded so K+V of two CTAs fit in one SM's shared memory.
+    static constexpr int kMaxChunk = sizeof(T) == 2 ? 192 : 96;
 };
 
 struct DecodeArgs {
@@ -46,32 +51,50 @@ __device__ __forceinline__ float fast_exp2(float x)
     return y;
 }
 
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 template <typename T>
-__global__ void __launch_bounds__(kDecThreads) decode_split_kernel(const DecodeArgs a)
+__host__ __device__ constexpr size_t dec_kv_bytes(int chunk)
+{
+    return (size_t)chunk * kD * sizeof(T);
+}
+
+// Shared memory: [K (>= kRedBytes, reused for the p.V reduction and merge headers)]
+// [V (reused for merge weights)] [scores 2 x chunk] [stat 8] [2 mbarriers] [flag].
+template <typename T>
+__host__ __device__ constexpr size_t dec_k_region(int chunk)
+{
+    return dec_kv_bytes<T>(chunk) > (size_t)kRedBytes ? dec_kv_bytes<T>(chunk) : (size_t)kRedBytes;
+}
+
+template <typename T>
+__host__ __device__ constexpr size_t decode_smem_bytes(int chunk)
+{
+    return dec_k_region<T>(chunk) + dec_kv_bytes<T>(chunk) + sizeof(float) * (2 * chunk + 8) + 2 * sizeof(uint64_t) +
+           16;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kDecThreads, 2) decode_split_kernel(const DecodeArgs a)
 {
     extern __shared__ __align__(128) unsigned char smem[];
     const int s = blockIdx.x;
     const int kvh = blockIdx.y;
     const int b = blockIdx.z;
-    const tyb_seq_kv seq = a.seqs ? a.seqs[b] : a.one;
-    const int kv_len = seq.kv_len;
-    const int nsplit = (kv_len + a.chunk - 1) / a.chunk;
-    if (s >= nsplit) return;
-    const int r0 = s * a.chunk;
-    const int nrows = min(a.chunk, kv_len - r0);
-
-    T* Ks = reinterpret_cast<T*>(smem);
-    T* Vs = Ks + (size_t)a.chunk * kD;
-    float* sc = reinterpret_cast<float*>(Vs + (size_t)a.chunk * kD);  // [2][chunk]
-    float* red = sc + 2 * a.chunk;                                    // [8][2][128]
-    float* stat = red + 8 * 2 * kD;                                   // m0 m1 l0 l1
-    uint64_t* bars = reinterpret_cast<uint64_t*>(stat + 8);
-    int* last_flag = reinterpret_cast<int*>(bars + 2);
-
     const int tid = threadIdx.x;
     const int lane = tid & 31;
     const int warp = tid >> 5;
-    const size_t head_off = ((size_t)kvh * seq.row_capacity + r0) * kD;
+
+    unsigned char* kreg = smem;
+    unsigned char* vreg = smem + dec_k_region<T>(a.chunk);
+    T* Ks = reinterpret_cast<T*>(kreg);
+    T* Vs = reinterpret_cast<T*>(vreg);
+    float* sc = reinterpret_cast<float*>(vreg + dec_kv_bytes<T>(a.chunk));  // [2][chunk]
+    float* stat = sc + 2 * a.chunk;                                          // m0 m1 l0 l1 + scratch
+    uint64_t* bars = reinterpret_cast<uint64_t*>(stat + 8);
+    int* last_flag = reinterpret_cast<int*>(bars + 2);
+    float* red = reinterpret_cast<float*>(kreg);  // [16][2][128], after the scores
 
     if (tid == 0) {
         mbar_init(&bars[0], 1);
@@ -79,7 +102,19 @@ __global__ void __launch_bounds__(kDecThreads) decode_split_kernel(const DecodeA
         fence_barrier_init();
         fence_proxy_async_smem();
     }
+    // Everything below reads data earlier kernels wrote (descriptors, cache rows, q).
+    pdl_wait();
+    pdl_trigger();
     __syncthreads();
+
+    const tyb_seq_kv seq = a.seqs ? a.seqs[b] : a.one;
+    const int kv_len = seq.kv_len;
+    const int nsplit = (kv_len + a.chunk - 1) / a.chunk;
+    if (s >= nsplit) return;
+    const int r0 = s * a.chunk;
+    const int nrows = min(a.chunk, kv_len - r0);
+    const size_t head_off = ((size_t)kvh * seq.row_capacity + r0) * kD;
+
     if (tid == 0) {
         const uint32_t bytes = (uint32_t)nrows * kD * sizeof(T);
         mbar_arrive_expect_tx(&bars[0], bytes);
@@ -99,8 +134,7 @@ __global__ void __launch_bounds__(kDecThreads) decode_split_kernel(const DecodeA
     }
 
     // Every thread waits (bounded); the CTA leaves together if any wait ran out.
-    if (__syncthreads_or(!mbar_wait_bounded(&bars[0], 0, kWaitLimitNs, TYB_STATUS_WAIT_TIMEOUT)))
-        return;
+    if (__syncthreads_or(!mbar_wait_bounded(&bars[0], 0, kWaitLimitNs, TYB_STATUS_WAIT_TIMEOUT))) return;
 
     // Scores: each warp pass covers two rows (one per 16-lane half).
     const int half = lane >> 4;
@@ -148,17 +182,15 @@ __global__ void __launch_bounds__(kDecThreads) decode_split_kernel(const DecodeA
             stat[2 + warp] = l;
         }
     }
-    __syncthreads();
 
-    if (__syncthreads_or(!mbar_wait_bounded(&bars[1], 0, kWaitLimitNs, TYB_STATUS_WAIT_TIMEOUT)))
-        return;
+    if (__syncthreads_or(!mbar_wait_bounded(&bars[1], 0, kWaitLimitNs, TYB_STATUS_WAIT_TIMEOUT))) return;
 
-    // p.V: thread owns dims [8*g16, +8) of rows rg, rg+8, ...
+    // p.V: thread owns dims [8*g16, +8) of rows rg, rg+16, ...
     const int rg = tid >> 4;
     float o0[8], o1[8];
 #pragma unroll
     for (int j = 0; j < 8; j++) o0[j] = o1[j] = 0.f;
-    for (int r = rg; r < nrows; r += kDecThreads / 16) {
+    for (int r = rg; r < nrows; r += kRowGroups) {
         float v8[8];
         load8(Vs + (size_t)r * kD + g16 * 8, v8);
         const float p0 = sc[r], p1 = sc[a.chunk + r];
@@ -168,36 +200,28 @@ __global__ void __launch_bounds__(kDecThreads) decode_split_kernel(const DecodeA
             o1[j] = fmaf(p1, v8[j], o1[j]);
         }
     }
-    store8(red + ((size_t)rg * 2 + 0) * kD + g16 * 8, o0);
+    store8(red + ((size_t)rg * 2 + 0) * kD + g16 * 8, o0);  // K region is free now
     store8(red + ((size_t)rg * 2 + 1) * kD + g16 * 8, o1);
     __syncthreads();
 
-    // Thread t reduces dims (h = t / 64, d = 2*(t % 64) .. +1) over the 8 row groups.
-    const int h = tid >> 6;
-    const int d = 2 * (tid & 63);
-    float ox = 0.f, oy = 0.f;
+    // Thread t reduces output element (h = t / 128, d = t % 128) over the row groups.
+    const int h = tid >> 7;
+    const int d = tid & 127;
+    float acc = 0.f;
 #pragma unroll
-    for (int g = 0; g < 8; g++) {
-        const float2 v = *reinterpret_cast<const float2*>(red + ((size_t)g * 2 + h) * kD + d);
-        ox += v.x;
-        oy += v.y;
-    }
-    const size_t out_off = (size_t)b * kHq * kD + (size_t)(kGroup * kvh + h) * kD + d;
+    for (int g = 0; g < kRowGroups; g++) acc += red[((size_t)g * 2 + h) * kD + d];
+    const size_t out_head = (size_t)b * kHq * kD + (size_t)(kGroup * kvh) * kD;
 
     if (nsplit == 1) {
-        const float inv = 1.f / stat[2 + h];
-        *reinterpret_cast<float2*>(a.out + out_off) = make_float2(ox * inv, oy * inv);
+        a.out[out_head + (size_t)h * kD + d] = acc / stat[2 + h];
         return;
     }
 
-    float* part_base = a.partials + ((size_t)(b * kHkv + kvh) * a.nsplit_max) * 2 * kPartStride;
+    float* recs = a.partials + (size_t)(b * kHkv + kvh) * a.nsplit_max * kRec;
     {
-        float* mine = part_base + ((size_t)s * 2 + h) * kPartStride;
-        if ((tid & 63) == 0) {
-            mine[0] = stat[h];
-            mine[1] = stat[2 + h];
-        }
-        *reinterpret_cast<float2*>(mine + 4 + d) = make_float2(ox, oy);
+        float* mine = recs + (size_t)s * kRec;
+        if (tid == 0) *reinterpret_cast<float4*>(mine) = make_float4(stat[0], stat[2], stat[1], stat[3]);
+        mine[4 + h * kD + d] = acc;
     }
     __threadfence();
     __syncthreads();
@@ -209,77 +233,206 @@ __global__ void __launch_bounds__(kDecThreads) decode_split_kernel(const DecodeA
     if (!*last_flag) return;
     __threadfence();
 
-    // Last CTA of this (sequence, KV head): merge the splits.
-    float M = -INFINITY;
-    for (int j = 0; j < nsplit; j++) M = fmaxf(M, __ldcg(part_base + ((size_t)j * 2 + h) * kPartStride));
-    float L = 0.f, ax = 0.f, ay = 0.f;
-    for (int j = 0; j < nsplit; j++) {
-        const float* pj = part_base + ((size_t)j * 2 + h) * kPartStride;
-        const float w = fast_exp2(__ldcg(pj) - M);
-        L = fmaf(__ldcg(pj + 1), w, L);
-        const float2 o = __ldcg(reinterpret_cast<const float2*>(pj + 4 + d));
-        ax = fmaf(o.x, w, ax);
-        ay = fmaf(o.y, w, ay);
+    // ---- merge (last CTA of this sequence/KV head) -----------------------------------
+    // Headers of all splits in parallel -> shared memory (K region, after red is read).
+    __syncthreads();
+    float4* hdr = reinterpret_cast<float4*>(kreg);  // capacity checked by the host planner
+    float m0 = -INFINITY, m1 = -INFINITY;
+    for (int j = tid; j < nsplit; j += kDecThreads) {
+        const float4 hj = __ldcg(reinterpret_cast<const float4*>(recs + (size_t)j * kRec));
+        hdr[j] = hj;
+        m0 = fmaxf(m0, hj.x);
+        m1 = fmaxf(m1, hj.z);
     }
-    const float inv = 1.f / L;
-    *reinterpret_cast<float2*>(a.out + out_off) = make_float2(ax * inv, ay * inv);
+    float* wsc = reinterpret_cast<float*>(vreg);  // [nsplit][2] weights, V region is free
+    float Mh0, Mh1;
+    {
+        float v = m0;
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, off));
+        float w = m1;
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) w = fmaxf(w, __shfl_xor_sync(0xffffffffu, w, off));
+        __syncthreads();
+        if (lane == 0) {
+            sc[warp] = v;
+            sc[8 + warp] = w;
+        }
+        __syncthreads();
+        Mh0 = sc[0];
+        Mh1 = sc[8];
+#pragma unroll
+        for (int i = 1; i < kDecThreads / 32; i++) {
+            Mh0 = fmaxf(Mh0, sc[i]);
+            Mh1 = fmaxf(Mh1, sc[8 + i]);
+        }
+    }
+    float L0 = 0.f, L1 = 0.f;
+    for (int j = tid; j < nsplit; j += kDecThreads) {
+        const float4 hj = hdr[j];
+        const float w0 = fast_exp2(hj.x - Mh0), w1 = fast_exp2(hj.z - Mh1);
+        wsc[2 * j] = w0;
+        wsc[2 * j + 1] = w1;
+        L0 = fmaf(hj.y, w0, L0);
+        L1 = fmaf(hj.w, w1, L1);
+    }
+    {
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) {
+            L0 += __shfl_xor_sync(0xffffffffu, L0, off);
+            L1 += __shfl_xor_sync(0xffffffffu, L1, off);
+        }
+        __syncthreads();
+        if (lane == 0) {
+            sc[16 + warp] = L0;
+            sc[24 + warp] = L1;
+        }
+        __syncthreads();
+        L0 = 0.f;
+        L1 = 0.f;
+#pragma unroll
+        for (int i = 0; i < kDecThreads / 32; i++) {
+            L0 += sc[16 + i];
+            L1 += sc[24 + i];
+        }
+    }
+    // Outputs: 256 floats = 64 float4 slots; 4 split groups of 64 threads.
+    const int f = tid & 63;
+    const int grp = tid >> 6;
+    const int hh = f >> 5;
+    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+    const float* base = recs + 4 + (size_t)hh * kD + 4 * (f & 31);
+#pragma unroll 8
+    for (int j = grp; j < nsplit; j += 4) {
+        const float4 v = __ldcg(reinterpret_cast<const float4*>(base + (size_t)j * kRec));
+        const float w = wsc[2 * j + hh];
+        o.x = fmaf(v.x, w, o.x);
+        o.y = fmaf(v.y, w, o.y);
+        o.z = fmaf(v.z, w, o.z);
+        o.w = fmaf(v.w, w, o.w);
+    }
+    float4* red4 = reinterpret_cast<float4*>(kreg + 16 * ((nsplit + 3) / 4 * 4));  // after headers
+    __syncthreads();
+    red4[grp * 64 + f] = o;
+    __syncthreads();
+    if (tid < 64) {
+        float4 t = red4[tid];
+#pragma unroll
+        for (int g = 1; g < 4; g++) {
+            const float4 u = red4[g * 64 + tid];
+            t.x += u.x;
+            t.y += u.y;
+            t.z += u.z;
+            t.w += u.w;
+        }
+        const float inv = 1.f / (hh == 0 ? L0 : L1);
+        *reinterpret_cast<float4*>(a.out + out_head + (size_t)hh * kD + 4 * (f & 31)) =
+            make_float4(t.x * inv, t.y * inv, t.z * inv, t.w * inv);
+    }
     if (tid == 0) a.counters[b * kHkv + kvh] = 0u;
 }
 
-template <typename T>
-static size_t decode_smem_bytes(int chunk)
+// ---- host-side planning ----------------------------------------------------------------
+
+static int g_num_sms = 0;
+
+static int num_sms()
 {
-    return (size_t)2 * chunk * kD * sizeof(T) + sizeof(float) * (2 * chunk + 8 * 2 * kD + 8) +
-           2 * sizeof(uint64_t) + 16;
+    if (!g_num_sms) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        if (cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || g_num_sms <= 0)
+            g_num_sms = 148;
+    }
+    return g_num_sms;
+}
+
+template <typename T>
+static int blocks_per_sm(int chunk)
+{
+    // Cached per chunk size (multiples of 16 up to kMaxChunk).
+    static int cache[DecodeTile<T>::kMaxChunk / 16 + 1];
+    const int i = chunk / 16;
+    if (!cache[i]) {
+        int n = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, decode_split_kernel<T>, kDecThreads,
+                                                          decode_smem_bytes<T>(chunk)) != cudaSuccess ||
+            n <= 0)
+            n = 1;
+        cache[i] = n;
+    }
+    return cache[i];
+}
+
+template <typename T>
+static bool set_smem_attr()
+{
+    static bool done = false;
+    if (!done) {
+        if (cudaFuncSetAttribute(decode_split_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)decode_smem_bytes<T>(DecodeTile<T>::kMaxChunk)) != cudaSuccess)
+            return false;
+        done = true;
+    }
+    return true;
+}
+
+// Smallest chunk (multiple of 16) whose grid is resident in one wave; the largest chunk
+// when none is (then the grid runs in several waves, e.g. for large batches).
+template <typename T>
+static void plan(int batch, int max_kv_len, int* chunk_rows, int* nsplit)
+{
+    set_smem_attr<T>();
+    const long long slots_sms = num_sms();
+    int chosen = DecodeTile<T>::kMaxChunk;
+    for (int c = 16; c <= DecodeTile<T>::kMaxChunk; c += 16) {
+        const long long ctas = (long long)((max_kv_len + c - 1) / c) * kHkv * batch;
+        if (ctas <= slots_sms * blocks_per_sm<T>(c)) {
+            chosen = c;
+            break;
+        }
+    }
+    *chunk_rows = chosen;
+    *nsplit = max_kv_len > 0 ? (max_kv_len + chosen - 1) / chosen : 0;
 }
 
 template <typename T>
 static int launch_decode(const DecodeArgs& a, int batch, void* stream)
 {
-    const size_t smem = decode_smem_bytes<T>(a.chunk);
-    static bool attr_set = false;
-    if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(decode_split_kernel<T>,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)decode_smem_bytes<T>(DecodeTile<T>::kMaxChunk));
-        if (e != cudaSuccess) return (int)e;
-        attr_set = true;
-    }
-    dim3 grid(a.nsplit_max, kHkv, batch);
-    decode_split_kernel<T><<<grid, kDecThreads, smem, (cudaStream_t)stream>>>(a);
-    return (int)cudaGetLastError();
+    if (!set_smem_attr<T>()) return (int)cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(a.nsplit_max, kHkv, batch);
+    cfg.blockDim = dim3(kDecThreads);
+    cfg.dynamicSmemBytes = decode_smem_bytes<T>(a.chunk);
+    cfg.stream = (cudaStream_t)stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return (int)cudaLaunchKernelEx(&cfg, decode_split_kernel<T>, a);
 }
 
 }  // namespace tyb
 
 using namespace tyb;
 
-extern "C" void tyb_decode_plan(int batch, int max_kv_len, int kv_dtype, int* chunk_rows,
-                                int* nsplit)
+extern "C" void tyb_decode_plan(int batch, int max_kv_len, int kv_dtype, int* chunk_rows, int* nsplit)
 {
-    const int max_chunk =
-        kv_dtype == TYB_BF16 ? DecodeTile<__nv_bfloat16>::kMaxChunk : DecodeTile<float>::kMaxChunk;
-    // Aim for about four CTAs per SM across the grid (148 SMs), with at least 16 rows per
-    // split so each split's copies stay worth their setup.
-    const long long target_ctas = 4LL * 148;
-    long long per_seq_head = (target_ctas + (long long)batch * kHkv - 1) / ((long long)batch * kHkv);
-    if (per_seq_head < 1) per_seq_head = 1;
-    long long chunk = (max_kv_len + per_seq_head - 1) / per_seq_head;
-    chunk = (chunk + 15) / 16 * 16;
-    if (chunk < 16) chunk = 16;
-    if (chunk > max_chunk) chunk = max_chunk;
-    *chunk_rows = (int)chunk;
-    *nsplit = max_kv_len > 0 ? (int)((max_kv_len + chunk - 1) / chunk) : 0;
+    if (kv_dtype == TYB_BF16)
+        plan<__nv_bfloat16>(batch, max_kv_len, chunk_rows, nsplit);
+    else
+        plan<float>(batch, max_kv_len, chunk_rows, nsplit);
 }
 
 extern "C" size_t tyb_decode_partial_floats(int batch, int nsplit)
 {
-    return (size_t)batch * kHkv * (size_t)nsplit * 2 * kPartStride;
+    return (size_t)batch * kHkv * (size_t)nsplit * kRec;
 }
 
-extern "C" int tyb_decode_launch(const float* q, float* out, const tyb_seq_kv* seqs_dev,
-                                 tyb_seq_kv one, int batch, int max_kv_len, int kv_dtype,
-                                 float scale, float* partials, unsigned int* counters, void* stream)
+extern "C" int tyb_decode_launch(const float* q, float* out, const tyb_seq_kv* seqs_dev, tyb_seq_kv one,
+                                 int batch, int max_kv_len, int kv_dtype, float scale, float* partials,
+                                 unsigned int* counters, void* stream)
 {
     if (batch <= 0 || max_kv_len <= 0) return 0;
     DecodeArgs a;
@@ -294,6 +447,11 @@ extern "C" int tyb_decode_launch(const float* q, float* out, const tyb_seq_kv* s
     a.nsplit_max = nsplit;
     a.partials = partials;
     a.counters = counters;
+    // The merge keeps a 16-byte header per split plus a 4 KB reduction in the K region
+    // and two float weights per split in the V region.
+    const size_t kreg = kv_dtype == TYB_BF16 ? dec_k_region<__nv_bfloat16>(chunk) : dec_k_region<float>(chunk);
+    const size_t vreg = kv_dtype == TYB_BF16 ? dec_kv_bytes<__nv_bfloat16>(chunk) : dec_kv_bytes<float>(chunk);
+    if ((size_t)nsplit * 16 + 4096 > kreg || (size_t)nsplit * 8 > vreg) return (int)cudaErrorInvalidValue;
     if (kv_dtype == TYB_BF16) return launch_decode<__nv_bfloat16>(a, batch, stream);
     return launch_decode<float>(a, batch, stream);
 }

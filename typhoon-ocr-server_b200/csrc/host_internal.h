@@ -14,6 +14,9 @@
 #define TYB_CACHE_MAGIC 0x54594243u /* "TYBC" */
 #define TYB_ROW_FLOATS (KV_NUM_KV_HEADS * KV_HEAD_DIM) /* 1024: one token of K or V */
 #define TYB_Q_FLOATS (16 * KV_HEAD_DIM)               /* 2048: one token of Q / output */
+/* Longest cache: the decode merge keeps per-split state in shared memory, which bounds
+ * the split count (at most 2,816 splits of 96+ rows). */
+#define TYB_MAX_SEQ 262144
 
 /* Device cache.  `pub` is the first member, so the KVCache* handed to callers converts
  * back to this struct; callers only ever touch pub's fields. */

@@ -46,8 +46,8 @@ static void cache_release(tyb_cache *t)
 
 KVCache *kv_cache_alloc_ex(int max_seq_len, int kv_dtype)
 {
-    if (max_seq_len <= 0) {
-        tyb_set_error("kv_cache_alloc: max_seq_len must be positive (got %d)", max_seq_len);
+    if (max_seq_len <= 0 || max_seq_len > TYB_MAX_SEQ) {
+        tyb_set_error("kv_cache_alloc: max_seq_len must be in [1, %d] (got %d)", TYB_MAX_SEQ, max_seq_len);
         return NULL;
     }
     if (kv_dtype != ATTN_KV_F32 && kv_dtype != ATTN_KV_BF16) {
@@ -68,10 +68,8 @@ KVCache *kv_cache_alloc_ex(int max_seq_len, int kv_dtype)
     cudaGetDevice(&t->device);
 
     const size_t slab = (size_t)KV_NUM_LAYERS * KV_NUM_KV_HEADS * max_seq_len * KV_HEAD_DIM * t->elem_bytes;
-    int chunk = 0, nsplit = 0;
     /* Upper bound on splits for any kv_len <= max_seq_len: chunks are >= 16 rows. */
-    nsplit = (max_seq_len + 15) / 16 + 1;
-    (void)chunk;
+    const int nsplit = (max_seq_len + 15) / 16 + 1;
     const size_t part = tyb_decode_partial_floats(1, nsplit) * sizeof(float);
 
     int ok = tyb_cuda_ok(cudaMalloc(&t->k_slab, slab), "kv_cache_alloc: K slab") &&

@@ -60,16 +60,24 @@ extern "C" int tyb_kv_scatter_launch(const float* k_src, const float* v_src, voi
 
 extern "C" int tyb_status_fetch(unsigned int* bits, void* stream)
 {
+    // One pinned word per process receives the status copy, so the read is queued behind
+    // the caller's work and a single stream synchronisation covers both.
+    static unsigned int* pinned = nullptr;
+    if (!pinned) {
+        cudaError_t e = cudaHostAlloc(reinterpret_cast<void**>(&pinned), sizeof(unsigned int), cudaHostAllocDefault);
+        if (e != cudaSuccess) {
+            pinned = nullptr;
+            return (int)e;
+        }
+    }
     cudaStream_t st = (cudaStream_t)stream;
-    cudaError_t e = cudaMemcpyFromSymbolAsync(bits, g_status, sizeof(unsigned int), 0,
-                                              cudaMemcpyDeviceToHost, st);
+    cudaError_t e = cudaMemcpyFromSymbolAsync(pinned, g_status, sizeof(unsigned int), 0, cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
     if (e != cudaSuccess) return (int)e;
-    e = cudaStreamSynchronize(st);
-    if (e != cudaSuccess) return (int)e;
+    *bits = *pinned;
     if (*bits) {
         const unsigned int zero = 0u;
-        e = cudaMemcpyToSymbolAsync(g_status, &zero, sizeof zero, 0, cudaMemcpyHostToDevice, st);
-        if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+        e = cudaMemcpyToSymbol(g_status, &zero, sizeof zero);
     }
     return (int)e;
 }
