@@ -41,6 +41,27 @@ int attention_decode_gqa_batched(const float *q, const KVCache *const *caches,
                                  const int *kv_lens, float *output, int batch,
                                  int layer_idx, float scale);
 
+/* No counterpart in the reference.  Decode attention for one sequence and one layer that
+ * allocates no memory, for callers that cannot call cudaMalloc: a serving engine whose
+ * device memory is all reserved up front by its own caching allocator (an allocation behind
+ * its back can fail or fragment that pool), or a program that keeps a fixed, audited
+ * device-memory footprint.  Its scratch is a fixed array of about 2 MiB that exists on every
+ * GPU that loads this library until the process exits.
+ *   q, output       device [16][128] fp32
+ *   k_rows, v_rows  device, head-first [8][row_capacity][128] of kv_dtype (ATTN_KV_F32 or
+ *                   ATTN_KV_BF16), 16-byte aligned -- e.g. kv_cache_k(cache, layer, 0)
+ *   kv_len          rows attended, 1 <= kv_len <= row_capacity; at most 24,576 (F32) or
+ *                   49,152 (BF16) rows (256 splits); longer requests are rejected
+ *   stream          cudaStream_t (NULL = legacy default stream); the call only queues work
+ * The first call on each device looks up the array's device address (cudaGetSymbolAddress);
+ * make that first call before any stream capture.  All calls share the one array and it
+ * keeps the last call's contents: calls that overlap on the GPU (other streams, other
+ * threads) race, so serialise them, e.g. on one stream.  0 on success, else nonzero with
+ * attn_last_error() set. */
+int attention_decode_gqa_noalloc(const float *q, const void *k_rows, const void *v_rows,
+                                 int row_capacity, int kv_dtype, float *output, int kv_len,
+                                 float scale, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

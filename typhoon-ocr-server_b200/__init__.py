@@ -98,6 +98,8 @@ _SIGNATURES = {
     "attn_sync": (ctypes.c_int, []),
     "attention_decode_gqa_batched": (ctypes.c_int, [_VP, _VP, _VP, _VP, ctypes.c_int, ctypes.c_int,
                                                     ctypes.c_float]),
+    "attention_decode_gqa_noalloc": (ctypes.c_int, [_VP, _VP, _VP, ctypes.c_int, ctypes.c_int, _VP,
+                                                    ctypes.c_int, ctypes.c_float, _VP]),
 }
 
 

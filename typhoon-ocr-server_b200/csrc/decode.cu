@@ -17,7 +17,10 @@
 // its prologue while this grid drains; every global read of data produced by earlier
 // kernels happens after griddepcontrol.wait.
 // Bandwidth-bound: 2 * kv_len * 128 * sizeof(T) bytes per (sequence, KV head).
+#include <mutex>
+
 #include "common.cuh"
+#include "host_internal.h"
 
 namespace tyb {
 
@@ -454,4 +457,118 @@ extern "C" int tyb_decode_launch(const float* q, float* out, const tyb_seq_kv* s
     if ((size_t)nsplit * 16 + 4096 > kreg || (size_t)nsplit * 8 > vreg) return (int)cudaErrorInvalidValue;
     if (kv_dtype == TYB_BF16) return launch_decode<__nv_bfloat16>(a, batch, stream);
     return launch_decode<float>(a, batch, stream);
+}
+
+// ---- decode that allocates nothing ----------------------------------------------------------
+//
+// Some callers cannot call cudaMalloc: a serving engine whose device memory is all reserved
+// up front by its own caching allocator (an allocation behind its back can fail or fragment
+// that pool), or a host program that keeps a fixed, audited device-memory footprint.  For
+// them this entry point runs the same split-KV kernel with its split records and tickets in
+// a fixed file-scope device array instead of a cache's workspace.  The array (about 2 MiB)
+// exists on every GPU that loads this library until the process exits.
+
+namespace tyb {
+
+constexpr int kNoAllocMaxSplits = 256;
+constexpr int kNoAllocMaxDevices = 64;
+static __device__ __align__(256) float g_noalloc_records[kHkv * kNoAllocMaxSplits * kRec];
+static __device__ __align__(256) unsigned int g_noalloc_tickets[kHkv];
+
+// Device addresses of the two arrays, looked up once per device.  In host code the
+// arrays' names only stand in for the device symbols; kernels must get these addresses.
+static std::mutex g_noalloc_mu;
+static float* g_noalloc_records_addr[kNoAllocMaxDevices];
+static unsigned int* g_noalloc_tickets_addr[kNoAllocMaxDevices];
+
+static bool is_device_memory(const void* p)
+{
+    cudaPointerAttributes attr;
+    if (cudaPointerGetAttributes(&attr, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return attr.type == cudaMemoryTypeDevice || attr.type == cudaMemoryTypeManaged;
+}
+
+}  // namespace tyb
+
+extern "C" int attention_decode_gqa_noalloc(const float* q, const void* k_rows, const void* v_rows,
+                                            int row_capacity, int kv_dtype, float* output, int kv_len,
+                                            float scale, void* stream)
+{
+    const char* what = "attention_decode_gqa_noalloc";
+    if (!q || !k_rows || !v_rows || !output) {
+        tyb_set_error("%s: NULL q/k_rows/v_rows/output", what);
+        return 1;
+    }
+    if (kv_dtype != TYB_F32 && kv_dtype != TYB_BF16) {
+        tyb_set_error("%s: unknown kv_dtype %d", what, kv_dtype);
+        return 1;
+    }
+    if (row_capacity <= 0 || kv_len < 1 || kv_len > row_capacity) {
+        tyb_set_error("%s: need 1 <= kv_len (%d) <= row_capacity (%d)", what, kv_len, row_capacity);
+        return 1;
+    }
+    if ((reinterpret_cast<uintptr_t>(k_rows) | reinterpret_cast<uintptr_t>(v_rows)) & 15u) {
+        tyb_set_error("%s: k_rows and v_rows must be 16-byte aligned", what);
+        return 1;
+    }
+    if (!is_device_memory(q) || !is_device_memory(k_rows) || !is_device_memory(v_rows) ||
+        !is_device_memory(output)) {
+        tyb_set_error("%s: q, k_rows, v_rows and output must be device memory", what);
+        return 1;
+    }
+    int chunk = 0, nsplit = 0;
+    tyb_decode_plan(1, kv_len, kv_dtype, &chunk, &nsplit);
+    if (nsplit > kNoAllocMaxSplits) {
+        const int max_chunk =
+            kv_dtype == TYB_BF16 ? DecodeTile<__nv_bfloat16>::kMaxChunk : DecodeTile<float>::kMaxChunk;
+        tyb_set_error("%s: kv_len %d needs %d splits; the fixed scratch holds %d (kv_len <= %d for this "
+                      "element type)",
+                      what, kv_len, nsplit, kNoAllocMaxSplits, kNoAllocMaxSplits * max_chunk);
+        return 1;
+    }
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess || dev < 0 || dev >= kNoAllocMaxDevices) {
+        tyb_set_error("%s: no usable current device (%s)", what, cudaGetErrorString(e));
+        return 1;
+    }
+    float* records = nullptr;
+    unsigned int* tickets = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(g_noalloc_mu);
+        if (!g_noalloc_records_addr[dev]) {
+            void* r = nullptr;
+            void* t = nullptr;
+            e = cudaGetSymbolAddress(&r, g_noalloc_records);
+            if (e == cudaSuccess) e = cudaGetSymbolAddress(&t, g_noalloc_tickets);
+            if (e != cudaSuccess) {
+                tyb_set_error("%s: cudaGetSymbolAddress: %s", what, cudaGetErrorString(e));
+                return 1;
+            }
+            g_noalloc_records_addr[dev] = static_cast<float*>(r);
+            g_noalloc_tickets_addr[dev] = static_cast<unsigned int*>(t);
+        }
+        records = g_noalloc_records_addr[dev];
+        tickets = g_noalloc_tickets_addr[dev];
+    }
+    // The array keeps the previous call's contents: tickets must start at zero.
+    e = cudaMemsetAsync(tickets, 0, sizeof(unsigned int) * kHkv, (cudaStream_t)stream);
+    if (e != cudaSuccess) {
+        tyb_set_error("%s: cudaMemsetAsync: %s", what, cudaGetErrorString(e));
+        return 1;
+    }
+    tyb_seq_kv one;
+    one.k = k_rows;
+    one.v = v_rows;
+    one.kv_len = kv_len;
+    one.row_capacity = row_capacity;
+    const int rc = tyb_decode_launch(q, output, nullptr, one, 1, kv_len, kv_dtype, scale, records, tickets, stream);
+    if (rc != 0) {
+        tyb_set_error("%s: launch: %s", what, cudaGetErrorString((cudaError_t)rc));
+        return 1;
+    }
+    return 0;
 }

@@ -11,6 +11,10 @@
 #include "attn_shim.h"
 #include "kv_cache.h"
 
+#ifdef __cplusplus
+extern "C" {
+#endif
+
 #define TYB_CACHE_MAGIC 0x54594243u /* "TYBC" */
 #define TYB_ROW_FLOATS (KV_NUM_KV_HEADS * KV_HEAD_DIM) /* 1024: one token of K or V */
 #define TYB_Q_FLOATS (16 * KV_HEAD_DIM)               /* 2048: one token of Q / output */
@@ -71,4 +75,7 @@ size_t tyb_registry_size(const void *p); /* 0 when unknown */
  * otherwise 0 with the error set. */
 int tyb_finish(void *stream, const char *what);
 
+#ifdef __cplusplus
+}
+#endif
 #endif
