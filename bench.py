@@ -1,17 +1,20 @@
 """Benchmark: GQA decode attention of the Qwen3-VL-2B text decoder at 4K context
 through the drop-in C-ABI library.
 
-One STEP = one decode step of attention for all 28 layers: for layer l, the split-KV
-kernel attends one new query (16 heads) over kv_len = 4097 + (i mod 512) cached rows of
-that layer (i = step index: the 512-step schedule of config 2 -- a cache prefilled to
-4,096 tokens, each step appending one).  The cache is BF16 (the FP32 cache is measured
-too, as `fp32_kv`).  28 layers x ~17 MB per step (~0.5 GB) exceeds the 126 MB L2, so no
-step finds the previous step's rows in L2.
+One STEP = one decode step for all 28 layers, as kernel/decoder.c:97,104 runs it: for
+layer l, append the new token's K/V row at row 4096 + (i mod 512) and attend one new
+query (16 heads) over kv_len = 4097 + (i mod 512) rows of that layer (i = step index:
+the 512-step schedule of config 2 -- a cache prefilled to 4,096 tokens, each step
+appending one), through attention_decode_append_gqa.  The cache is BF16 (the FP32 cache
+is measured too, as `fp32_kv`; attention alone, without the append, as `attn_only`).
+28 layers x ~17 MB per step (~0.5 GB) exceeds the 126 MB L2, so no step finds the
+previous step's rows in L2.
 
     value : device time / (decode steps summed over ranks), in us/step (lower is better).
             Device-resident inputs, launches replayed from per-step CUDA graphs.
-    e2e   : the same metric through attention_decode_gqa with HOST (pinned) query and
-            output buffers, every call copying its query in and its output back.
+    e2e   : the same metric through attention_decode_append_gqa with HOST (pinned) q,
+            k_new, v_new and output buffers, every call copying its inputs in and its
+            output back and returning when done.
     --impl reference : the reference's own CPU attention (oracle/_ref, built from the
             reference sources) on the host cores; one step = one layer's decode call
             (a bounded sample), reported x28.
@@ -61,9 +64,12 @@ def kv_len_of(step):
     return PREFILLED + 1 + (step % SCHEDULE)
 
 
-def step_bytes(step, elem_bytes):
-    """Algorithmic bytes of one step: K and V rows of every layer, plus q in / out."""
-    return LAYERS * (2 * kv_len_of(step) * HKV * D * elem_bytes + 2 * HQ * D * 4)
+def step_bytes(step, elem_bytes, fused=True):
+    """Algorithmic bytes of one step: K and V rows of every layer, plus q in / out, plus
+    (fused append) the new K/V row read in fp32 and written in the cache's type."""
+    rows = kv_len_of(step) - (1 if fused else 0)
+    extra = 2 * HKV * D * (4 + elem_bytes) if fused else 0
+    return LAYERS * (2 * rows * HKV * D * elem_bytes + 2 * HQ * D * 4 + extra)
 
 
 def peaks():
@@ -138,7 +144,7 @@ class ClockSampler:
 # ---------------------------------------------------------------------------------------
 
 class DecodeBench:
-    def __init__(self, pkg, lib, kv_dtype, device):
+    def __init__(self, pkg, lib, kv_dtype, device, fused=True):
         import torch
         self.torch = torch
         self.pkg, self.lib = pkg, lib
@@ -161,7 +167,10 @@ class DecodeBench:
             pkg.check(lib, "fill cache")
         cs.seq_len = PREFILLED
         del buf_k, buf_v
+        self.fused = fused
         self.q = torch.empty((LAYERS, HQ, D), dtype=torch.float32, device=device).normal_(generator=gen)
+        self.k_new = torch.empty((LAYERS, HKV, D), dtype=torch.float32, device=device).normal_(0.0, 0.5, generator=gen)
+        self.v_new = torch.empty((LAYERS, HKV, D), dtype=torch.float32, device=device).normal_(0.0, 0.5, generator=gen)
         self.out = torch.zeros((LAYERS, HQ, D), dtype=torch.float32, device=device)
         self.scale = ctypes.c_float(pkg.SCALE)
         self.graphs = {}
@@ -170,9 +179,20 @@ class DecodeBench:
     def _launch_step(self, step):
         kv = kv_len_of(step)
         qp, op = self.q.data_ptr(), self.out.data_ptr()
+        kp, vp = self.k_new.data_ptr(), self.v_new.data_ptr()
+        cs = self.pkg.cache_struct(self.cache)
+        cs.seq_len = kv - 1
         for layer in range(LAYERS):
-            self.lib.attention_decode_gqa(ctypes.c_void_p(qp + layer * HQ * D * 4), self.cache,
-                                          ctypes.c_void_p(op + layer * HQ * D * 4), layer, kv, self.scale)
+            q_l = ctypes.c_void_p(qp + layer * HQ * D * 4)
+            o_l = ctypes.c_void_p(op + layer * HQ * D * 4)
+            if self.fused:
+                rc = self.lib.attention_decode_append_gqa(q_l, ctypes.c_void_p(kp + layer * HKV * D * 4),
+                                                          ctypes.c_void_p(vp + layer * HKV * D * 4), self.cache,
+                                                          o_l, layer, self.scale)
+                if rc:
+                    raise RuntimeError(self.pkg.last_error(self.lib))
+            else:
+                self.lib.attention_decode_gqa(q_l, self.cache, o_l, layer, kv, self.scale)
 
     def capture(self):
         torch = self.torch
@@ -216,20 +236,26 @@ def time_device(bench, warmup, steps, dist_ctx):
 
 
 def time_e2e(pkg, lib, cache, steps, device):
-    """attention_decode_gqa with pinned host q/output: each call copies q in, the output
-    back, and returns when done (the reference's blocking contract)."""
+    """attention_decode_append_gqa with pinned HOST q, k_new, v_new and output: each call
+    copies its inputs in, the output back, and returns when done (the reference's
+    blocking contract)."""
     import torch
     lib.attn_set_stream(None)
     q = torch.empty((LAYERS, HQ, D), dtype=torch.float32).normal_().pin_memory()
+    kn = torch.empty((LAYERS, HKV, D), dtype=torch.float32).normal_(0.0, 0.5).pin_memory()
+    vn = torch.empty((LAYERS, HKV, D), dtype=torch.float32).normal_(0.0, 0.5).pin_memory()
     out = torch.empty((LAYERS, HQ, D), dtype=torch.float32).pin_memory()
     scale = ctypes.c_float(pkg.SCALE)
-    qp, op = q.data_ptr(), out.data_ptr()
+    qp, op, kp, vp = q.data_ptr(), out.data_ptr(), kn.data_ptr(), vn.data_ptr()
+    cs = pkg.cache_struct(cache)
 
     def one(step):
-        kv = kv_len_of(step)
+        cs.seq_len = kv_len_of(step) - 1
         for layer in range(LAYERS):
-            lib.attention_decode_gqa(ctypes.c_void_p(qp + layer * HQ * D * 4), cache,
-                                     ctypes.c_void_p(op + layer * HQ * D * 4), layer, kv, scale)
+            lib.attention_decode_append_gqa(ctypes.c_void_p(qp + layer * HQ * D * 4),
+                                            ctypes.c_void_p(kp + layer * HKV * D * 4),
+                                            ctypes.c_void_p(vp + layer * HKV * D * 4), cache,
+                                            ctypes.c_void_p(op + layer * HQ * D * 4), layer, scale)
 
     for s in range(5):
         one(s)
@@ -240,7 +266,7 @@ def time_e2e(pkg, lib, cache, steps, device):
         one(s)
     t1 = time.perf_counter()
     pkg.check(lib, "e2e")
-    return (t1 - t0) * 1e3, LAYERS * HQ * D * 4, LAYERS * HQ * D * 4
+    return (t1 - t0) * 1e3, LAYERS * (HQ + 2 * HKV) * D * 4, LAYERS * HQ * D * 4
 
 
 class DistCtx:
@@ -407,6 +433,13 @@ def main():
     e2e_max = dctx.max(e2e_ms)
     bf.close()
 
+    ao = DecodeBench(pkg, lib, pkg.ATTN_KV_BF16, f"cuda:{local_rank}", fused=False)
+    ao.capture()
+    ao_steps = min(args.steps, 4096)
+    ms_ao = dctx.max(time_device(ao, args.warmup, ao_steps, dctx))
+    bytes_ao = sum(step_bytes(args.warmup + i, 2, fused=False) for i in range(ao_steps))
+    ao.close()
+
     f32 = DecodeBench(pkg, lib, pkg.ATTN_KV_F32, f"cuda:{local_rank}")
     f32.capture()
     f32_steps = min(args.steps, 4096)
@@ -445,17 +478,21 @@ def main():
             "parallelism": f"dp{n} (independent sequences, no collective)",
             "l2": "inputs > L2: ~0.5 GB of K/V per step vs 126 MB L2",
             "value_definition": "device time (max over ranks) / decode steps summed over ranks",
-            "launch": "per-step CUDA graph of 28 attention_decode_gqa calls",
+            "launch": "per-step CUDA graph of 28 attention_decode_append_gqa calls (append + attention)",
         },
         "roofline": {
             "bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
             "frac": achieved / hbm_peak, "traffic": profile_traffic("bf16"),
-            "kernel": "decode_split_kernel<bf16>",
+            "kernel": "decode_cluster_kernel<bf16>",
             "note": f"algorithmic bytes (K+V rows + q/out) / mean launch time incl. gaps; peak {peak_src}",
         },
         "e2e": {"value": e2e_max * 1e3 / args.e2e_steps, "unit": "us/step", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "steps": args.e2e_steps,
-                "path": "attention_decode_gqa x28 with pinned host q/output (blocking)"},
+                "path": "attention_decode_append_gqa x28 with pinned host q/k_new/v_new/output (blocking)"},
+        "attn_only": {"value": ms_ao * 1e3 / ao_steps, "unit": "us/step", "steps": ao_steps,
+                      "achieved_gbs": bytes_ao / (ms_ao * 1e-3) / 1e9,
+                      "frac": bytes_ao / (ms_ao * 1e-3) / 1e9 / hbm_peak,
+                      "path": "attention_decode_gqa x28 (no append)"},
         "fp32_kv": {"value": ms32 * 1e3 / f32_steps, "unit": "us/step", "steps": f32_steps,
                     "achieved_gbs": bytes32 / (ms32 * 1e-3) / 1e9,
                     "frac": bytes32 / (ms32 * 1e-3) / 1e9 / hbm_peak},

@@ -41,6 +41,18 @@ int attention_decode_gqa_batched(const float *q, const KVCache *const *caches,
                                  const int *kv_lens, float *output, int batch,
                                  int layer_idx, float scale);
 
+/* One decode step of one layer in one launch: kv_cache_append(cache, layer_idx, k_new, v_new)
+ * followed by attention_decode_gqa(q, cache, output, layer_idx, cache->seq_len + 1, scale)
+ * (kernel/kv_cache.c:53-65, kernel/attention.c:194-204; the pair kernel/decoder.c:97,104
+ * calls).  The new row is written to the cache and used directly, so the kernel can
+ * start streaming the older rows before the previous kernel in the stream finishes.
+ * seq_len is not advanced (kv_cache_advance does that, as in the reference).
+ * q, output [16][128]; k_new, v_new [8][128]; fp32, host or device.  0 on success.
+ * Rows of the cache are assumed to be written only through this library's calls (or by
+ * work that has completed before the call is made). */
+int attention_decode_append_gqa(const float *q, const float *k_new, const float *v_new,
+                                KVCache *cache, float *output, int layer_idx, float scale);
+
 /* No counterpart in the reference.  Decode attention for one sequence and one layer that
  * allocates no memory, for callers that cannot call cudaMalloc: a serving engine whose
  * device memory is all reserved up front by its own caching allocator (an allocation behind

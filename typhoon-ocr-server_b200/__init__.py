@@ -98,6 +98,7 @@ _SIGNATURES = {
     "attn_sync": (ctypes.c_int, []),
     "attention_decode_gqa_batched": (ctypes.c_int, [_VP, _VP, _VP, _VP, ctypes.c_int, ctypes.c_int,
                                                     ctypes.c_float]),
+    "attention_decode_append_gqa": (ctypes.c_int, [_VP, _VP, _VP, _VP, _VP, ctypes.c_int, ctypes.c_float]),
     "attention_decode_gqa_noalloc": (ctypes.c_int, [_VP, _VP, _VP, ctypes.c_int, ctypes.c_int, _VP,
                                                     ctypes.c_int, ctypes.c_float, _VP]),
 }
@@ -110,7 +111,7 @@ def declared_symbols():
 
 def load_attention_lib(path=None) -> ctypes.CDLL:
     """Load libtyphoon_attn.so and declare its entry points' types (no fallback)."""
-    p = Path(path) if path else LIB_PATH
+    p = Path(path or os.environ.get("TYB_ATTN_LIB") or LIB_PATH)
     if not p.exists():
         raise FileNotFoundError(f"{p} is missing: run __graft_entry__.build() (nvcc for sm_100a)")
     lib = ctypes.CDLL(str(p))

@@ -2,11 +2,13 @@
  * attention.c -- the attention entry points of kernel/attention.h (typhoon-ocr-server),
  * as host C that stages memory and launches the sm_100a kernels.
  *
- *   attention_decode_gqa          kernel/attention.c:194-204  -> decode.cu (split-KV)
+ *   attention_decode_gqa          kernel/attention.c:194-204  -> decode.cu
  *   attention_prefill_gqa         kernel/attention.c:364-381  -> prefill_simt.cu (FP32)
  *   attention_chunked_prefill_gqa kernel/attention.c:527-543  -> prefill_simt.cu, K/V
  *                                                                 from the device cache
  *   attention_decode_gqa_batched  (new)                       -> decode.cu, many caches
+ *   attention_decode_append_gqa   (new) kernel/kv_cache.c:53-65 + attention.c:194-204
+ *                                                             -> decode.cu, fused
  *
  * Host buffers are copied to the device on the library stream and results copied back,
  * and then the call waits: the reference's calls block until done.  Device buffers are
@@ -19,6 +21,15 @@
 #include "attention.h"
 #include "attn_ext.h"
 #include "host_internal.h"
+
+static int decode_launch(tyb_cache *t, const float *q, float *out, const tyb_seq_kv *seqs_dev, tyb_seq_kv one,
+                         int batch, int max_kv, int dtype, float scale, const float *k_new, const float *v_new,
+                         int prefetch_rows, float *partials, unsigned int *counters, void *st)
+{
+    (void)t;
+    return tyb_decode_launch_ex(q, out, seqs_dev, one, batch, max_kv, dtype, scale, partials, counters, k_new, v_new,
+                                prefetch_rows, st);
+}
 
 static int check_layer(int layer, const char *what)
 {
@@ -72,10 +83,12 @@ void attention_decode_gqa(const float *q, const KVCache *cache, float *output, i
         one.v = tyb_slab_head(t, t->v_slab, layer_idx, 0);
         one.kv_len = kv_len;
         one.row_capacity = cache->max_seq_len;
-        if (!tyb_cuda_ok(tyb_decode_launch(dq, dout, NULL, one, 1, kv_len, t->dtype, scale, t->d_partials,
-                                           t->d_counters, st),
+        const int early = tyb_prefetch_rows(cache, layer_idx, kv_len);
+        if (!tyb_cuda_ok(decode_launch(t, dq, dout, NULL, one, 1, kv_len, t->dtype, scale, NULL, NULL, early,
+                                       t->d_partials, t->d_counters, st),
                          what))
             return;
+        tyb_note_nowrite(st);
     }
     if (!o_dev) {
         if (!tyb_cuda_ok(cudaMemcpyAsync(output, dout, TYB_Q_FLOATS * sizeof(float), cudaMemcpyDeviceToHost,
@@ -125,6 +138,7 @@ void attention_prefill_gqa(const float *q, const float *k, const float *v, float
                                              scale, st),
                      what))
         return;
+    tyb_note_nowrite(st);
     if (!od && !tyb_cuda_ok(cudaMemcpyAsync(output, dout, qb, cudaMemcpyDeviceToHost, (cudaStream_t)st), what))
         return;
     if (!qd || !kd || !vd || !od) tyb_finish(st, what);
@@ -164,6 +178,7 @@ void attention_chunked_prefill_gqa(const float *q, const KVCache *cache, float *
                                              pos_offset + chunk_len, pos_offset, scale, st),
                      what))
         return;
+    tyb_note_nowrite(st);
     if (!od && !tyb_cuda_ok(cudaMemcpyAsync(output, dout, qb, cudaMemcpyDeviceToHost, (cudaStream_t)st), what))
         return;
     if (!qd || !od) tyb_finish(st, what);
@@ -209,17 +224,12 @@ int attention_decode_gqa_batched(const float *q, const KVCache *const *caches, c
         return 1;
     }
     void *st = tyb_stream();
-    int chunk, nsplit;
-    tyb_decode_plan(batch, max_kv, dtype, &chunk, &nsplit);
     const size_t qb = (size_t)batch * TYB_Q_FLOATS * sizeof(float);
     tyb_seq_kv *ddesc = (tyb_seq_kv *)tyb_workspace(TYB_WS_DESC, sizeof(tyb_seq_kv) * (size_t)batch);
-    float *part = (float *)tyb_workspace(TYB_WS_PARTIALS, tyb_decode_partial_floats(batch, nsplit) * sizeof(float));
-    unsigned int *cnt =
-        (unsigned int *)tyb_workspace(TYB_WS_COUNTERS, sizeof(unsigned int) * (size_t)batch * KV_NUM_KV_HEADS);
     int qd = tyb_is_device_ptr(q), od = tyb_is_device_ptr(output);
     float *sq = (qd == 0) ? (float *)tyb_workspace(TYB_WS_Q, qb) : NULL;
     float *so = (od == 0) ? (float *)tyb_workspace(TYB_WS_OUT, qb) : NULL;
-    if (!ddesc || !part || !cnt || qd < 0 || od < 0 || (!qd && !sq) || (!od && !so)) {
+    if (!ddesc || qd < 0 || od < 0 || (!qd && !sq) || (!od && !so)) {
         free(descs);
         return 1;
     }
@@ -235,10 +245,62 @@ int attention_decode_gqa_batched(const float *q, const KVCache *const *caches, c
     float *dout = od ? output : so;
     tyb_seq_kv none;
     memset(&none, 0, sizeof none);
-    if (!tyb_cuda_ok(tyb_decode_launch(dq, dout, ddesc, none, batch, max_kv, dtype, scale, part, cnt, st), what))
+    int chunk, nsplit;
+    tyb_decode_plan(batch, max_kv, dtype, &chunk, &nsplit);
+    float *part = (float *)tyb_workspace(TYB_WS_PARTIALS, tyb_decode_partial_floats(batch, nsplit) * sizeof(float));
+    unsigned int *cnt =
+        (unsigned int *)tyb_workspace(TYB_WS_COUNTERS, sizeof(unsigned int) * (size_t)batch * KV_NUM_KV_HEADS);
+    if (!part || !cnt) return 1;
+    if (!tyb_cuda_ok(decode_launch(NULL, dq, dout, ddesc, none, batch, max_kv, dtype, scale, NULL, NULL, 0, part, cnt,
+                                   st),
+                     what))
         return 1;
+    tyb_note_nowrite(st);
     if (!od && !tyb_cuda_ok(cudaMemcpyAsync(output, dout, qb, cudaMemcpyDeviceToHost, (cudaStream_t)st), what))
         return 1;
     if (!qd || !od) return tyb_finish(st, what) ? 0 : 1;
+    return 0;
+}
+
+int attention_decode_append_gqa(const float *q, const float *k_new, const float *v_new, KVCache *cache,
+                                float *output, int layer_idx, float scale)
+{
+    const char *what = "attention_decode_append_gqa";
+    tyb_cache *t = tyb_cache_from(cache);
+    if (!t || !check_layer(layer_idx, what)) return 1;
+    if (!q || !k_new || !v_new || !output) {
+        tyb_set_error("%s: NULL q/k_new/v_new/output", what);
+        return 1;
+    }
+    const int pos = cache->seq_len;
+    if (pos < 0 || pos >= cache->max_seq_len) {
+        tyb_set_error("%s: row %d exceeds max_seq_len %d", what, pos, cache->max_seq_len);
+        return 1;
+    }
+    void *st = tyb_stream();
+    int qd = 0, kd = 0, vd = 0, od = tyb_is_device_ptr(output);
+    if (od < 0) return 1;
+    const size_t row = TYB_ROW_FLOATS * sizeof(float);
+    const float *dq = to_device(q, t->d_q, TYB_Q_FLOATS * sizeof(float), &qd, st, what);
+    const float *dk = dq ? to_device(k_new, t->d_kv_stage, row, &kd, st, what) : NULL;
+    const float *dv = dk ? to_device(v_new, t->d_kv_stage + TYB_ROW_FLOATS, row, &vd, st, what) : NULL;
+    if (!dq || !dk || !dv) return 1;
+    float *dout = od ? output : t->d_out;
+    tyb_seq_kv one;
+    one.k = tyb_slab_head(t, t->k_slab, layer_idx, 0);
+    one.v = tyb_slab_head(t, t->v_slab, layer_idx, 0);
+    one.kv_len = pos + 1;
+    one.row_capacity = cache->max_seq_len;
+    const int early = tyb_prefetch_rows(cache, layer_idx, pos);
+    if (!tyb_cuda_ok(decode_launch(t, dq, dout, NULL, one, 1, pos + 1, t->dtype, scale, dk, dv, early, t->d_partials,
+                                   t->d_counters, st),
+                     what))
+        return 1;
+    tyb_note_write(cache, layer_idx, pos, st);
+    if (!od && !tyb_cuda_ok(cudaMemcpyAsync(output, dout, TYB_Q_FLOATS * sizeof(float), cudaMemcpyDeviceToHost,
+                                            (cudaStream_t)st),
+                            what))
+        return 1;
+    if (!qd || !kd || !vd || !od) return tyb_finish(st, what) ? 0 : 1;
     return 0;
 }

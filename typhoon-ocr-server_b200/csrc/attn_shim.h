@@ -49,6 +49,17 @@ int tyb_decode_launch(const float *q, float *out, const tyb_seq_kv *seqs_dev, ty
                       int batch, int max_kv_len, int kv_dtype, float scale, float *partials,
                       unsigned int *counters, void *stream);
 
+/* tyb_decode_launch plus the fused KV append and early streaming:
+ * k_new/v_new: NULL, or [batch][8][128] fp32 rows that are written at row kv_len-1 of each
+ * sequence's cache and attended to.
+ * prefetch_rows: cache rows [0, prefetch_rows) may be read before the kernel waits for the
+ * previous kernel in the stream (single-sequence form only; rows the previous launch
+ * wrote must lie at or above it). */
+int tyb_decode_launch_ex(const float *q, float *out, const tyb_seq_kv *seqs_dev, tyb_seq_kv one,
+                         int batch, int max_kv_len, int kv_dtype, float scale, float *partials,
+                         unsigned int *counters, const float *k_new, const float *v_new, int prefetch_rows,
+                         void *stream);
+
 /* ---- FP32 flash prefill on CUDA cores (prefill_simt.cu) --------------------------- */
 
 /* q/out token-major [Sq][16][128] fp32.  K/V element (row r, kv head h, dim d) at

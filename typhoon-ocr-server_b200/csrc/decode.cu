@@ -1,21 +1,23 @@
-// decode.cu -- split-KV flash decoding for one new token per sequence.
+// decode.cu -- split-KV flash decoding for one new token per sequence, optionally fused
+// with the KV append of that token.
 //
 // Replaces the reference's per-KV-head CPU worker (kernel/attention.c:158-204: for each
 // KV head and its two query heads, scores = q.K*scale over kv_len rows, max, exp, sum,
-// normalise, out = sum p*V).  Here one CTA owns one (sequence, KV head, split of rows):
+// normalise, out = sum p*V) and, fused, kernel/kv_cache.c:53-65 (the new row written at
+// row seq_len first).  One CTA owns one (sequence, KV head, split of rows):
 //   1. one thread starts two bulk async copies (TMA, 1-D) of the split's K and V rows --
-//      contiguous in the head-first cache -- into shared memory, each completing on its
-//      own mbarrier.  The split count is chosen so the whole grid is resident at once
-//      (one wave), which puts every byte of the layer's K/V in flight together;
-//   2. scores of both query heads against K (16-byte vectors, 16 lanes per row,
-//      shuffle-xor reduction), then max and exp2 per head;
-//   3. once V has landed, p.V for both heads (K/V read once for the GQA pair);
-//   4. the split's (max, sum, unnormalised o) goes to a workspace record and the last
-//      CTA of the (sequence, head) -- found with an atomic ticket -- merges all records
-//      with parallel loads and writes the output.  No second launch.
-// Launched with programmatic dependent launch: the next kernel in the stream may start
-// its prologue while this grid drains; every global read of data produced by earlier
-// kernels happens after griddepcontrol.wait.
+//      contiguous in the head-first cache -- into shared memory on two mbarriers.  The
+//      kernel is launched with programmatic dependent launch and the grid is planned to
+//      fill only half of the SM slots, so the next kernel's CTAs are resident early and
+//      request their rows BEFORE griddepcontrol.wait (only rows the host knows the
+//      previous launch did not write); the stream of K/V bytes continues across kernels;
+//   2. after the wait: the query (and the new row, written to the cache and into its
+//      slot), scores of both query heads (16-byte vectors, 16 lanes per row, shuffle-xor
+//      reduction), max and exp2 per head;
+//   3. p.V for both heads from the same V bytes (GQA pair read once);
+//   4. the split's (max, sum, unnormalised o) goes to a workspace record; the CTA that
+//      takes the last ticket merges all records, pulled into shared memory by bulk
+//      copies, and writes the output.  No second launch.
 // Bandwidth-bound: 2 * kv_len * 128 * sizeof(T) bytes per (sequence, KV head).
 #include <mutex>
 
@@ -40,9 +42,12 @@ struct DecodeArgs {
     float* out;
     const tyb_seq_kv* seqs;
     tyb_seq_kv one;
+    const float* k_new;  // [batch][8][128] fp32 rows appended at row kv_len-1, or NULL
+    const float* v_new;
     float scale_log2;
     int chunk;
     int nsplit_max;
+    int prefetch_rows;  // rows [0, prefetch_rows) may be requested before the dependency wait
     float* partials;
     unsigned int* counters;
 };
@@ -105,26 +110,49 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_split_kernel(const Deco
         fence_barrier_init();
         fence_proxy_async_smem();
     }
+    __syncthreads();
+
+    // Split geometry.  The new token's row (fused append) never comes from the cache.
+    int kv_len = 0, nsplit = 0, r0 = 0, nrows = 0, tma_rows = 0;
+    const T* kh = nullptr;
+    const T* vh = nullptr;
+    auto geometry = [&](const tyb_seq_kv& seq) {
+        kv_len = seq.kv_len;
+        nsplit = (kv_len + a.chunk - 1) / a.chunk;
+        r0 = s * a.chunk;
+        nrows = max(0, min(a.chunk, kv_len - r0));
+        tma_rows = max(0, min(nrows, (a.k_new ? kv_len - 1 : kv_len) - r0));
+        kh = static_cast<const T*>(seq.k) + (size_t)kvh * seq.row_capacity * kD;
+        vh = static_cast<const T*>(seq.v) + (size_t)kvh * seq.row_capacity * kD;
+    };
+    auto issue = [&]() {
+        const uint32_t bytes = (uint32_t)tma_rows * kD * sizeof(T);
+        if (bytes) {
+            mbar_arrive_expect_tx(&bars[0], bytes);
+            bulk_g2s(Ks, kh + (size_t)r0 * kD, bytes, &bars[0]);
+            mbar_arrive_expect_tx(&bars[1], bytes);
+            bulk_g2s(Vs, vh + (size_t)r0 * kD, bytes, &bars[1]);
+        } else {
+            mbar_arrive(&bars[0]);
+            mbar_arrive(&bars[1]);
+        }
+    };
+    // Single-sequence form: the geometry is in the parameters, so the split's rows are
+    // requested before waiting for the previous kernel when that kernel did not write them.
+    bool issued = false;
+    if (!a.seqs) {
+        geometry(a.one);
+        if (tid == 0 && s < nsplit && r0 + tma_rows <= a.prefetch_rows) {
+            issue();
+            issued = true;
+        }
+    }
     // Everything below reads data earlier kernels wrote (descriptors, cache rows, q).
     pdl_wait();
     pdl_trigger();
-    __syncthreads();
-
-    const tyb_seq_kv seq = a.seqs ? a.seqs[b] : a.one;
-    const int kv_len = seq.kv_len;
-    const int nsplit = (kv_len + a.chunk - 1) / a.chunk;
+    if (a.seqs) geometry(a.seqs[b]);
     if (s >= nsplit) return;
-    const int r0 = s * a.chunk;
-    const int nrows = min(a.chunk, kv_len - r0);
-    const size_t head_off = ((size_t)kvh * seq.row_capacity + r0) * kD;
-
-    if (tid == 0) {
-        const uint32_t bytes = (uint32_t)nrows * kD * sizeof(T);
-        mbar_arrive_expect_tx(&bars[0], bytes);
-        bulk_g2s(Ks, static_cast<const T*>(seq.k) + head_off, bytes, &bars[0]);
-        mbar_arrive_expect_tx(&bars[1], bytes);
-        bulk_g2s(Vs, static_cast<const T*>(seq.v) + head_off, bytes, &bars[1]);
-    }
+    if (tid == 0 && !issued) issue();
 
     // Query vectors of the two heads sharing this KV head: lane group g16 holds dims
     // [8*g16, 8*g16+8).
@@ -136,31 +164,65 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_split_kernel(const Deco
         load8(qb + kD, q1);
     }
 
+    // The new token's row (fused append): threads 0..15 write it to the cache and into its
+    // slot after the copied rows (K now, V once V has landed).
+    const bool has_new = a.k_new && kv_len - 1 >= r0 && kv_len - 1 < r0 + nrows;
+    float nk[8], nv[8];
+    if (has_new && tid < 16) {
+        const size_t off = ((size_t)b * kHkv + kvh) * kD + tid * 8;
+        load8(a.k_new + off, nk);
+        load8(a.v_new + off, nv);
+        store8(const_cast<T*>(kh) + (size_t)(kv_len - 1) * kD + tid * 8, nk);
+        store8(const_cast<T*>(vh) + (size_t)(kv_len - 1) * kD + tid * 8, nv);
+        store8(Ks + (size_t)(kv_len - 1 - r0) * kD + tid * 8, nk);
+    }
+
     // Every thread waits (bounded); the CTA leaves together if any wait ran out.
     if (__syncthreads_or(!mbar_wait_bounded(&bars[0], 0, kWaitLimitNs, TYB_STATUS_WAIT_TIMEOUT))) return;
 
-    // Scores: each warp pass covers two rows (one per 16-lane half).
+    // Scores: each warp pass covers two rows (one per 16-lane half); two passes are
+    // interleaved per iteration so their loads and shuffle chains overlap.
     const int half = lane >> 4;
-    for (int p = warp; 2 * p < nrows; p += kDecThreads / 32) {
-        const int r = 2 * p + half;
-        float d0 = 0.f, d1 = 0.f;
-        if (r < nrows) {
-            float k8[8];
-            load8(Ks + (size_t)r * kD + g16 * 8, k8);
+    constexpr int kPairStride = kDecThreads / 32;
+    for (int p = warp; 2 * p < nrows; p += 2 * kPairStride) {
+        const int ra = 2 * p + half, rb = 2 * (p + kPairStride) + half;
+        float ka[8], kb[8];
+        if (ra < nrows) {
+            load8(Ks + (size_t)ra * kD + g16 * 8, ka);
+        } else {
 #pragma unroll
-            for (int j = 0; j < 8; j++) {
-                d0 = fmaf(q0[j], k8[j], d0);
-                d1 = fmaf(q1[j], k8[j], d1);
-            }
+            for (int j = 0; j < 8; j++) ka[j] = 0.f;
+        }
+        if (rb < nrows) {
+            load8(Ks + (size_t)rb * kD + g16 * 8, kb);
+        } else {
+#pragma unroll
+            for (int j = 0; j < 8; j++) kb[j] = 0.f;
+        }
+        float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            a0 = fmaf(q0[j], ka[j], a0);
+            a1 = fmaf(q1[j], ka[j], a1);
+            b0 = fmaf(q0[j], kb[j], b0);
+            b1 = fmaf(q1[j], kb[j], b1);
         }
 #pragma unroll
         for (int off = 8; off >= 1; off >>= 1) {
-            d0 += __shfl_xor_sync(0xffffffffu, d0, off);
-            d1 += __shfl_xor_sync(0xffffffffu, d1, off);
+            a0 += __shfl_xor_sync(0xffffffffu, a0, off);
+            a1 += __shfl_xor_sync(0xffffffffu, a1, off);
+            b0 += __shfl_xor_sync(0xffffffffu, b0, off);
+            b1 += __shfl_xor_sync(0xffffffffu, b1, off);
         }
-        if (g16 == 0 && r < nrows) {
-            sc[r] = d0 * a.scale_log2;
-            sc[a.chunk + r] = d1 * a.scale_log2;
+        if (g16 == 0) {
+            if (ra < nrows) {
+                sc[ra] = a0 * a.scale_log2;
+                sc[a.chunk + ra] = a1 * a.scale_log2;
+            }
+            if (rb < nrows) {
+                sc[rb] = b0 * a.scale_log2;
+                sc[a.chunk + rb] = b1 * a.scale_log2;
+            }
         }
     }
     __syncthreads();
@@ -186,6 +248,7 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_split_kernel(const Deco
         }
     }
 
+    if (has_new && tid < 16) store8(Vs + (size_t)(kv_len - 1 - r0) * kD + tid * 8, nv);
     if (__syncthreads_or(!mbar_wait_bounded(&bars[1], 0, kWaitLimitNs, TYB_STATUS_WAIT_TIMEOUT))) return;
 
     // p.V: thread owns dims [8*g16, +8) of rows rg, rg+16, ...
@@ -226,112 +289,86 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_split_kernel(const Deco
         if (tid == 0) *reinterpret_cast<float4*>(mine) = make_float4(stat[0], stat[2], stat[1], stat[3]);
         mine[4 + h * kD + d] = acc;
     }
-    __threadfence();
+    // Publish the record, then take a ticket; the CTA that takes the last one merges.  One
+    // thread fences on behalf of the CTA (the barrier orders the other threads' writes
+    // before its fence).
     __syncthreads();
     if (tid == 0) {
+        __threadfence();
         const unsigned int ticket = atomicAdd(&a.counters[b * kHkv + kvh], 1u);
-        *last_flag = (ticket == (unsigned int)(nsplit - 1));
+        const int last = ticket == (unsigned int)(nsplit - 1);
+        if (last) {
+            __threadfence();
+            asm volatile("fence.proxy.async.global;" ::: "memory");  // records are read by TMA below
+        }
+        *last_flag = last;
     }
     __syncthreads();
     if (!*last_flag) return;
-    __threadfence();
 
     // ---- merge (last CTA of this sequence/KV head) -----------------------------------
-    // Headers of all splits in parallel -> shared memory (K region, after red is read).
-    __syncthreads();
-    float4* hdr = reinterpret_cast<float4*>(kreg);  // capacity checked by the host planner
-    float m0 = -INFINITY, m1 = -INFINITY;
-    for (int j = tid; j < nsplit; j += kDecThreads) {
-        const float4 hj = __ldcg(reinterpret_cast<const float4*>(recs + (size_t)j * kRec));
-        hdr[j] = hj;
-        m0 = fmaxf(m0, hj.x);
-        m1 = fmaxf(m1, hj.z);
-    }
-    float* wsc = reinterpret_cast<float*>(vreg);  // [nsplit][2] weights, V region is free
-    float Mh0, Mh1;
-    {
-        float v = m0;
-#pragma unroll
-        for (int off = 16; off >= 1; off >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, off));
-        float w = m1;
-#pragma unroll
-        for (int off = 16; off >= 1; off >>= 1) w = fmaxf(w, __shfl_xor_sync(0xffffffffu, w, off));
-        __syncthreads();
-        if (lane == 0) {
-            sc[warp] = v;
-            sc[8 + warp] = w;
+    // Records arrive in shared memory in batches by one bulk copy each; every thread then
+    // merges one output element (h, d) from shared memory, with an online max across batches.
+    float* region = reinterpret_cast<float*>(kreg);  // K and V regions are free now
+    const size_t region_bytes = dec_k_region<T>(a.chunk) + dec_kv_bytes<T>(a.chunk);
+    const int cap = (int)(region_bytes / (sizeof(float) * (kRec + 2)));
+    float* wts = region + (size_t)cap * kRec;  // [cap][2]
+    float run0 = -INFINITY, run1 = -INFINITY;  // running max of each head (uniform)
+    float L = 0.f, O = 0.f;                     // this thread's head h, element d
+    uint32_t phase = 1;                         // bars[0] completed phase 0 with the K rows
+    for (int j0 = 0; j0 < nsplit; j0 += cap) {
+        const int nb = min(cap, nsplit - j0);
+        __syncthreads();  // the previous batch is consumed
+        if (tid == 0) {
+            const uint32_t bytes = (uint32_t)nb * kRec * sizeof(float);
+            mbar_arrive_expect_tx(&bars[0], bytes);
+            bulk_g2s(region, recs + (size_t)j0 * kRec, bytes, &bars[0]);
         }
-        __syncthreads();
-        Mh0 = sc[0];
-        Mh1 = sc[8];
-#pragma unroll
-        for (int i = 1; i < kDecThreads / 32; i++) {
-            Mh0 = fmaxf(Mh0, sc[i]);
-            Mh1 = fmaxf(Mh1, sc[8 + i]);
+        if (__syncthreads_or(!mbar_wait_bounded(&bars[0], phase, kWaitLimitNs, TYB_STATUS_WAIT_TIMEOUT))) return;
+        phase ^= 1u;
+        // Batch maximum of each head: a block reduction over the records' headers.
+        float x0 = -INFINITY, x1 = -INFINITY;
+        for (int j = tid; j < nb; j += kDecThreads) {
+            x0 = fmaxf(x0, region[(size_t)j * kRec + 0]);
+            x1 = fmaxf(x1, region[(size_t)j * kRec + 2]);
         }
-    }
-    float L0 = 0.f, L1 = 0.f;
-    for (int j = tid; j < nsplit; j += kDecThreads) {
-        const float4 hj = hdr[j];
-        const float w0 = fast_exp2(hj.x - Mh0), w1 = fast_exp2(hj.z - Mh1);
-        wsc[2 * j] = w0;
-        wsc[2 * j + 1] = w1;
-        L0 = fmaf(hj.y, w0, L0);
-        L1 = fmaf(hj.w, w1, L1);
-    }
-    {
 #pragma unroll
         for (int off = 16; off >= 1; off >>= 1) {
-            L0 += __shfl_xor_sync(0xffffffffu, L0, off);
-            L1 += __shfl_xor_sync(0xffffffffu, L1, off);
+            x0 = fmaxf(x0, __shfl_xor_sync(0xffffffffu, x0, off));
+            x1 = fmaxf(x1, __shfl_xor_sync(0xffffffffu, x1, off));
         }
-        __syncthreads();
         if (lane == 0) {
-            sc[16 + warp] = L0;
-            sc[24 + warp] = L1;
+            sc[warp] = x0;
+            sc[16 + warp] = x1;
         }
         __syncthreads();
-        L0 = 0.f;
-        L1 = 0.f;
+        float n0 = run0, n1 = run1;
 #pragma unroll
-        for (int i = 0; i < kDecThreads / 32; i++) {
-            L0 += sc[16 + i];
-            L1 += sc[24 + i];
+        for (int w = 0; w < kDecThreads / 32; w++) {
+            n0 = fmaxf(n0, sc[w]);
+            n1 = fmaxf(n1, sc[16 + w]);
         }
-    }
-    // Outputs: 256 floats = 64 float4 slots; 4 split groups of 64 threads.
-    const int f = tid & 63;
-    const int grp = tid >> 6;
-    const int hh = f >> 5;
-    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-    const float* base = recs + 4 + (size_t)hh * kD + 4 * (f & 31);
-#pragma unroll 8
-    for (int j = grp; j < nsplit; j += 4) {
-        const float4 v = __ldcg(reinterpret_cast<const float4*>(base + (size_t)j * kRec));
-        const float w = wsc[2 * j + hh];
-        o.x = fmaf(v.x, w, o.x);
-        o.y = fmaf(v.y, w, o.y);
-        o.z = fmaf(v.z, w, o.z);
-        o.w = fmaf(v.w, w, o.w);
-    }
-    float4* red4 = reinterpret_cast<float4*>(kreg + 16 * ((nsplit + 3) / 4 * 4));  // after headers
-    __syncthreads();
-    red4[grp * 64 + f] = o;
-    __syncthreads();
-    if (tid < 64) {
-        float4 t = red4[tid];
-#pragma unroll
-        for (int g = 1; g < 4; g++) {
-            const float4 u = red4[g * 64 + tid];
-            t.x += u.x;
-            t.y += u.y;
-            t.z += u.z;
-            t.w += u.w;
+        // Weights of this batch's records against the new maxima.
+        for (int j = tid; j < nb; j += kDecThreads) {
+            wts[2 * j] = fast_exp2(region[(size_t)j * kRec + 0] - n0);
+            wts[2 * j + 1] = fast_exp2(region[(size_t)j * kRec + 2] - n1);
         }
-        const float inv = 1.f / (hh == 0 ? L0 : L1);
-        *reinterpret_cast<float4*>(a.out + out_head + (size_t)hh * kD + 4 * (f & 31)) =
-            make_float4(t.x * inv, t.y * inv, t.z * inv, t.w * inv);
+        __syncthreads();
+        const float alpha = fast_exp2((h ? run1 : run0) - (h ? n1 : n0));  // 0 on the first batch
+        L *= alpha;
+        O *= alpha;
+        const float* lp = region + 1 + 2 * h;
+        const float* op = region + 4 + (size_t)h * kD + d;
+#pragma unroll 4
+        for (int j = 0; j < nb; j++) {
+            const float w = wts[2 * j + h];
+            L = fmaf(lp[(size_t)j * kRec], w, L);
+            O = fmaf(op[(size_t)j * kRec], w, O);
+        }
+        run0 = n0;
+        run1 = n1;
     }
+    a.out[out_head + (size_t)h * kD + d] = O / L;
     if (tid == 0) a.counters[b * kHkv + kvh] = 0u;
 }
 
@@ -380,8 +417,10 @@ static bool set_smem_attr()
     return true;
 }
 
-// Smallest chunk (multiple of 16) whose grid is resident in one wave; the largest chunk
-// when none is (then the grid runs in several waves, e.g. for large batches).
+// Smallest chunk (multiple of 16) whose grid fits in HALF of the resident CTA slots, so
+// the grid is one wave and the next kernel in the stream (launched early by programmatic
+// dependent launch) finds room to start streaming its own rows meanwhile.  The largest
+// chunk when none fits (then the grid runs in several waves, e.g. for large batches).
 template <typename T>
 static void plan(int batch, int max_kv_len, int* chunk_rows, int* nsplit)
 {
@@ -390,7 +429,8 @@ static void plan(int batch, int max_kv_len, int* chunk_rows, int* nsplit)
     int chosen = DecodeTile<T>::kMaxChunk;
     for (int c = 16; c <= DecodeTile<T>::kMaxChunk; c += 16) {
         const long long ctas = (long long)((max_kv_len + c - 1) / c) * kHkv * batch;
-        if (ctas <= slots_sms * blocks_per_sm<T>(c)) {
+        const int half_slots = blocks_per_sm<T>(c) / 2 > 0 ? blocks_per_sm<T>(c) / 2 : 1;
+        if (ctas <= slots_sms * half_slots) {
             chosen = c;
             break;
         }
@@ -433,9 +473,10 @@ extern "C" size_t tyb_decode_partial_floats(int batch, int nsplit)
     return (size_t)batch * kHkv * (size_t)nsplit * kRec;
 }
 
-extern "C" int tyb_decode_launch(const float* q, float* out, const tyb_seq_kv* seqs_dev, tyb_seq_kv one,
-                                 int batch, int max_kv_len, int kv_dtype, float scale, float* partials,
-                                 unsigned int* counters, void* stream)
+extern "C" int tyb_decode_launch_ex(const float* q, float* out, const tyb_seq_kv* seqs_dev, tyb_seq_kv one,
+                                    int batch, int max_kv_len, int kv_dtype, float scale, float* partials,
+                                    unsigned int* counters, const float* k_new, const float* v_new,
+                                    int prefetch_rows, void* stream)
 {
     if (batch <= 0 || max_kv_len <= 0) return 0;
     DecodeArgs a;
@@ -443,20 +484,26 @@ extern "C" int tyb_decode_launch(const float* q, float* out, const tyb_seq_kv* s
     a.out = out;
     a.seqs = seqs_dev;
     a.one = one;
+    a.k_new = k_new;
+    a.v_new = v_new;
     a.scale_log2 = scale * kLog2e;
     int chunk, nsplit;
     tyb_decode_plan(batch, max_kv_len, kv_dtype, &chunk, &nsplit);
     a.chunk = chunk;
     a.nsplit_max = nsplit;
+    a.prefetch_rows = seqs_dev ? 0 : prefetch_rows;
     a.partials = partials;
     a.counters = counters;
-    // The merge keeps a 16-byte header per split plus a 4 KB reduction in the K region
-    // and two float weights per split in the V region.
-    const size_t kreg = kv_dtype == TYB_BF16 ? dec_k_region<__nv_bfloat16>(chunk) : dec_k_region<float>(chunk);
-    const size_t vreg = kv_dtype == TYB_BF16 ? dec_kv_bytes<__nv_bfloat16>(chunk) : dec_kv_bytes<float>(chunk);
-    if ((size_t)nsplit * 16 + 4096 > kreg || (size_t)nsplit * 8 > vreg) return (int)cudaErrorInvalidValue;
     if (kv_dtype == TYB_BF16) return launch_decode<__nv_bfloat16>(a, batch, stream);
     return launch_decode<float>(a, batch, stream);
+}
+
+extern "C" int tyb_decode_launch(const float* q, float* out, const tyb_seq_kv* seqs_dev, tyb_seq_kv one,
+                                 int batch, int max_kv_len, int kv_dtype, float scale, float* partials,
+                                 unsigned int* counters, void* stream)
+{
+    return tyb_decode_launch_ex(q, out, seqs_dev, one, batch, max_kv_len, kv_dtype, scale, partials, counters,
+                                nullptr, nullptr, 0, stream);
 }
 
 // ---- decode that allocates nothing ----------------------------------------------------------

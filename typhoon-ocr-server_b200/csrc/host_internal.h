@@ -18,8 +18,7 @@ extern "C" {
 #define TYB_CACHE_MAGIC 0x54594243u /* "TYBC" */
 #define TYB_ROW_FLOATS (KV_NUM_KV_HEADS * KV_HEAD_DIM) /* 1024: one token of K or V */
 #define TYB_Q_FLOATS (16 * KV_HEAD_DIM)               /* 2048: one token of Q / output */
-/* Longest cache: the decode merge keeps per-split state in shared memory, which bounds
- * the split count (at most 2,816 splits of 96+ rows). */
+/* Longest cache accepted (sizes the per-cache decode split workspace). */
 #define TYB_MAX_SEQ 262144
 
 /* Device cache.  `pub` is the first member, so the KVCache* handed to callers converts
@@ -70,6 +69,19 @@ void *tyb_workspace(int slot, size_t bytes);
 void   tyb_registry_add(const void *p, size_t bytes);
 void   tyb_registry_remove(const void *p);
 size_t tyb_registry_size(const void *p); /* 0 when unknown */
+
+/* Which cache rows the most recent launch of this thread wrote.  A kernel may read rows
+ * before waiting on its predecessor (programmatic dependent launch) only if that
+ * predecessor did not write them: every launch of this library waits on its own
+ * predecessor before it lets the next one start, so writes two or more launches back
+ * are complete.
+ *   tyb_note_write: the launch just queued wrote rows >= lo of (cache, layer).
+ *   tyb_note_nowrite: the launch just queued wrote no cache rows.
+ *   tyb_prefetch_rows: how many leading rows of (cache, layer) the next launch may read
+ *                      early (at most `rows`). */
+void tyb_note_write(const void *cache, int layer, int lo, void *stream);
+void tyb_note_nowrite(void *stream);
+int  tyb_prefetch_rows(const void *cache, int layer, int rows);
 
 /* Wait for `stream`, then check the device status word.  1 when all is well;
  * otherwise 0 with the error set. */

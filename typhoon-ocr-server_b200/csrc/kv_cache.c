@@ -156,6 +156,7 @@ static void append_rows(KVCache *c, int layer, const float *k_new, const float *
     }
     void *kl = tyb_slab_head(t, t->k_slab, layer, 0), *vl = tyb_slab_head(t, t->v_slab, layer, 0);
     if (!tyb_cuda_ok(tyb_kv_scatter_launch(ks, vs, kl, vl, c->max_seq_len, pos, S, t->dtype, st), what)) return;
+    tyb_note_write(c, layer, pos, st);
     /* Host sources: block until the rows are read, as the reference's memcpy does. */
     if (!kd || !vd) tyb_finish(st, what);
 }

@@ -130,6 +130,37 @@ size_t tyb_registry_size(const void *p)
     return n;
 }
 
+/* ---- rows written by the previous launch ------------------------------------------ */
+
+static _Thread_local struct {
+    const void *cache;
+    int layer;
+    int lo;
+    void *stream;
+    int valid;
+} g_last_write;
+
+void tyb_note_write(const void *cache, int layer, int lo, void *stream)
+{
+    g_last_write.cache = cache;
+    g_last_write.layer = layer;
+    g_last_write.lo = lo;
+    g_last_write.stream = stream;
+    g_last_write.valid = 1;
+}
+
+void tyb_note_nowrite(void *stream)
+{
+    if (g_last_write.stream == stream) g_last_write.valid = 0;
+}
+
+int tyb_prefetch_rows(const void *cache, int layer, int rows)
+{
+    if (g_last_write.valid && g_last_write.cache == cache && g_last_write.layer == layer)
+        return g_last_write.lo < rows ? g_last_write.lo : rows;
+    return rows;
+}
+
 /* ---- synchronisation + status ----------------------------------------------------- */
 
 int tyb_finish(void *stream, const char *what)
@@ -137,6 +168,7 @@ int tyb_finish(void *stream, const char *what)
     unsigned int bits = 0;
     int e = tyb_status_fetch(&bits, stream);
     if (!tyb_cuda_ok(e, what)) return 0;
+    if (g_last_write.stream == stream) g_last_write.valid = 0; /* everything queued is done */
     if (bits) {
         tyb_set_error("%s: device status 0x%x (%s%s)", what, bits,
                       (bits & TYB_STATUS_WAIT_TIMEOUT) ? "wait timed out " : "",
