@@ -235,6 +235,64 @@ def time_device(bench, warmup, steps, dist_ctx):
     return start.elapsed_time(end)  # ms
 
 
+def time_prefill(pkg, lib, device, pages, warmup, seq=4096):
+    """one page = 4,096 tokens (3,600 vision tokens on a 60x60 M-RoPE grid
+    + 496 text tokens) through all 28 layers of attention_prefill_fused_gqa (QK-RMSNorm +
+    M-RoPE fused, K/V appended to a BF16 cache, causal attention on the tensor cores), BF16
+    activations.  Returns (ms per page, causal FLOPs per page, kernel launches per page)."""
+    import torch
+    wl = importlib.import_module(pkg.__name__ + ".workloads")
+    pos = wl.config3_positions()
+    assert pos.shape[1] == seq
+    gen = torch.Generator(device=device)
+    gen.manual_seed(3)
+    q = (0.5 * torch.randn((LAYERS, seq, HQ, D), generator=gen, device=device)).to(torch.bfloat16)
+    k = (0.5 * torch.randn((LAYERS, seq, HKV, D), generator=gen, device=device)).to(torch.bfloat16)
+    v = (0.5 * torch.randn((LAYERS, seq, HKV, D), generator=gen, device=device)).to(torch.bfloat16)
+    qn = 1.0 + 0.02 * torch.randn((LAYERS, D), generator=gen, device=device)
+    kn = 1.0 + 0.02 * torch.randn((LAYERS, D), generator=gen, device=device)
+    # Per-token cos/sin of the interleaved M-RoPE (sections [24,20,20], theta 5e6).
+    j = torch.arange(D // 2, device=device)
+    inv_freq = 1.0 / (5000000.0 ** (2.0 * j.double() / D))
+    sect = torch.where(j < 60, j % 3, torch.zeros_like(j))
+    p3 = torch.from_numpy(pos).to(device).double()
+    ang = p3[sect, :].T * inv_freq[None, :]
+    cos, sin = torch.cos(ang).float().contiguous(), torch.sin(ang).float().contiguous()
+    out = torch.empty((seq, HQ, D), dtype=torch.bfloat16, device=device)
+    cache = lib.kv_cache_alloc_ex(seq, pkg.ATTN_KV_BF16)
+    if not cache:
+        raise RuntimeError(pkg.last_error(lib))
+    cs = pkg.cache_struct(cache)
+    scale, eps = ctypes.c_float(pkg.SCALE), ctypes.c_float(pkg.RMS_EPS)
+    lib.attn_set_stream(None)
+
+    def page():
+        cs.seq_len = 0
+        for layer in range(LAYERS):
+            rc = lib.attention_prefill_fused_gqa(
+                ctypes.c_void_p(q[layer].data_ptr()), ctypes.c_void_p(k[layer].data_ptr()),
+                ctypes.c_void_p(v[layer].data_ptr()), pkg.ATTN_DT_BF16, ctypes.c_void_p(qn[layer].data_ptr()),
+                ctypes.c_void_p(kn[layer].data_ptr()), ctypes.c_void_p(cos.data_ptr()),
+                ctypes.c_void_p(sin.data_ptr()), cache, layer, ctypes.c_void_p(out.data_ptr()), pkg.ATTN_DT_BF16,
+                seq, scale, eps)
+            if rc:
+                raise RuntimeError(pkg.last_error(lib))
+
+    for _ in range(warmup):
+        page()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(pages):
+        page()
+    end.record()
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(end) / pages
+    lib.kv_cache_free(cache)
+    flops = LAYERS * 4.0 * D * HQ * seq * (seq + 1) / 2  # causal (q, k) pairs only
+    return ms, flops, 2 * LAYERS
+
+
 def time_e2e(pkg, lib, cache, steps, device):
     """attention_decode_append_gqa with pinned HOST q, k_new, v_new and output: each call
     copies its inputs in, the output back, and returns when done (the reference's
@@ -407,6 +465,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=200)
     ap.add_argument("--cpu-budget", type=float, default=12.0)
+    ap.add_argument("--prefill-pages", type=int, default=20)
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -446,6 +505,13 @@ def main():
     ms32 = dctx.max(time_device(f32, args.warmup, f32_steps, dctx))
     bytes32 = sum(step_bytes(args.warmup + i, 4) for i in range(f32_steps))
     f32.close()
+
+    pf_ms, pf_flops, pf_launches = time_prefill(pkg, lib, f"cuda:{local_rank}", pages=args.prefill_pages, warmup=2)
+    pf_ms_max = dctx.max(pf_ms)
+    tc_sustained = tc_peak
+    pk = ROOT / "MEASURED_PEAKS.json"
+    if pk.exists():
+        tc_sustained = float(json.loads(pk.read_text()).get("bf16_tflops_sustained", tc_peak))
 
     cpu = None
     if dctx.rank == 0:
@@ -496,6 +562,15 @@ def main():
         "fp32_kv": {"value": ms32 * 1e3 / f32_steps, "unit": "us/step", "steps": f32_steps,
                     "achieved_gbs": bytes32 / (ms32 * 1e-3) / 1e9,
                     "frac": bytes32 / (ms32 * 1e-3) / 1e9 / hbm_peak},
+        "prefill": {"value": 4096 * n / (pf_ms_max * 1e-3), "unit": "tok/s", "ms_per_page": pf_ms_max,
+                    "pages": args.prefill_pages,
+                    "tflops": pf_flops / (pf_ms * 1e-3) / 1e12, "peak_tflops": tc_sustained,
+                    "frac": pf_flops / (pf_ms * 1e-3) / 1e12 / tc_sustained,
+                    "workload": "config3: 4096-token page (3600 vision 60x60 + 496 text), 28 layers, bf16, "
+                                "QK-RMSNorm + M-RoPE fused, K/V appended to the cache",
+                    "path": "attention_prefill_fused_gqa x28 (kv_prep + prefill_tc_kernel per layer)",
+                    "flops_definition": "4*128*16*S*(S+1)/2 per layer (causal pairs)",
+                    "peak_note": "bf16 cuBLAS sustained, measured"},
         "cpu_baseline": cpu,
         "clocks": clocks,
         "gpu_launches": launches,

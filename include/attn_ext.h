@@ -41,6 +41,25 @@ int attention_decode_gqa_batched(const float *q, const KVCache *const *caches,
                                  const int *kv_lens, float *output, int batch,
                                  int layer_idx, float scale);
 
+/* Element types of the fused prefill's activations. */
+#define ATTN_DT_F32  0
+#define ATTN_DT_BF16 1
+
+/* One layer of the multimodal prefill chain of kernel/decoder.c:73-117 in two launches, on
+ * the tensor cores: RMSNorm of q and k with q_norm/k_norm (eps), rotate_half M-RoPE with the
+ * per-token tables token_cos/token_sin [seq_len][64] (from decoder_build_rope_3d), K/V
+ * appended to the cache at rows cache->seq_len.., then causal attention of the seq_len new
+ * queries over cache rows [0, cache->seq_len + seq_len) -- query i at position
+ * cache->seq_len + i (a fresh cache gives the plain prefill; a filled one, chunked prefill).
+ * q_raw [seq_len][16][128], k_raw/v_raw [seq_len][8][128] in `in_dtype`; output
+ * [seq_len][16][128] in `out_dtype`; q_norm/k_norm [128] fp32.  All DEVICE memory; the cache
+ * must be ATTN_KV_BF16.  BF16 operands, FP32 accumulation (tolerance of the BF16 path).
+ * seq_len is not advanced.  0 on success. */
+int attention_prefill_fused_gqa(const void *q_raw, const void *k_raw, const void *v_raw, int in_dtype,
+                                const float *q_norm, const float *k_norm, const float *token_cos,
+                                const float *token_sin, KVCache *cache, int layer_idx, void *output,
+                                int out_dtype, int seq_len, float scale, float eps);
+
 /* One decode step of one layer in one launch: kv_cache_append(cache, layer_idx, k_new, v_new)
  * followed by attention_decode_gqa(q, cache, output, layer_idx, cache->seq_len + 1, scale)
  * (kernel/kv_cache.c:53-65, kernel/attention.c:194-204; the pair kernel/decoder.c:97,104

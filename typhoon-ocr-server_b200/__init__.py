@@ -26,6 +26,8 @@ MROPE_THETA = 5000000.0
 
 ATTN_KV_F32 = 0
 ATTN_KV_BF16 = 1
+ATTN_DT_F32 = 0
+ATTN_DT_BF16 = 1
 
 PKG_DIR = Path(__file__).resolve().parent
 LIB_PATH = PKG_DIR / "libtyphoon_attn.so"
@@ -98,6 +100,8 @@ _SIGNATURES = {
     "attn_sync": (ctypes.c_int, []),
     "attention_decode_gqa_batched": (ctypes.c_int, [_VP, _VP, _VP, _VP, ctypes.c_int, ctypes.c_int,
                                                     ctypes.c_float]),
+    "attention_prefill_fused_gqa": (ctypes.c_int, [_VP, _VP, _VP, ctypes.c_int, _VP, _VP, _VP, _VP, _VP, ctypes.c_int,
+                                                   _VP, ctypes.c_int, ctypes.c_int, ctypes.c_float, ctypes.c_float]),
     "attention_decode_append_gqa": (ctypes.c_int, [_VP, _VP, _VP, _VP, _VP, ctypes.c_int, ctypes.c_float]),
     "attention_decode_gqa_noalloc": (ctypes.c_int, [_VP, _VP, _VP, ctypes.c_int, ctypes.c_int, _VP,
                                                     ctypes.c_int, ctypes.c_float, _VP]),

@@ -304,3 +304,50 @@ int attention_decode_append_gqa(const float *q, const float *k_new, const float 
     if (!qd || !kd || !vd || !od) return tyb_finish(st, what) ? 0 : 1;
     return 0;
 }
+
+int attention_prefill_fused_gqa(const void *q_raw, const void *k_raw, const void *v_raw, int in_dtype,
+                                const float *q_norm, const float *k_norm, const float *token_cos,
+                                const float *token_sin, KVCache *cache, int layer_idx, void *output, int out_dtype,
+                                int seq_len, float scale, float eps)
+{
+    const char *what = "attention_prefill_fused_gqa";
+    tyb_cache *t = tyb_cache_from(cache);
+    if (!t || !check_layer(layer_idx, what)) return 1;
+    if (t->dtype != TYB_BF16) {
+        tyb_set_error("%s: the cache must hold BF16 rows (kv_cache_alloc_ex(.., ATTN_KV_BF16))", what);
+        return 1;
+    }
+    if ((in_dtype != ATTN_DT_F32 && in_dtype != ATTN_DT_BF16) || (out_dtype != ATTN_DT_F32 && out_dtype != ATTN_DT_BF16)) {
+        tyb_set_error("%s: unknown element type", what);
+        return 1;
+    }
+    const int pos0 = cache->seq_len;
+    if (seq_len < 0 || pos0 < 0 || pos0 + seq_len > cache->max_seq_len) {
+        tyb_set_error("%s: rows [%d, %d) exceed max_seq_len %d", what, pos0, pos0 + seq_len, cache->max_seq_len);
+        return 1;
+    }
+    if (seq_len == 0) return 0;
+    const void *ptrs[9] = {q_raw, k_raw, v_raw, q_norm, k_norm, token_cos, token_sin, output, NULL};
+    for (int i = 0; i < 8; i++) {
+        const int d = ptrs[i] ? tyb_is_device_ptr(ptrs[i]) : 0;
+        if (d < 0) return 1;
+        if (!d) {
+            tyb_set_error("%s: argument %d must be device memory", what, i);
+            return 1;
+        }
+    }
+    void *st = tyb_stream();
+    void *kl = tyb_slab_head(t, t->k_slab, layer_idx, 0), *vl = tyb_slab_head(t, t->v_slab, layer_idx, 0);
+    if (!tyb_cuda_ok(tyb_kv_prep_launch(k_raw, v_raw, in_dtype == ATTN_DT_BF16, k_norm, token_cos, token_sin, kl, vl,
+                                        cache->max_seq_len, pos0, seq_len, eps, st),
+                     what))
+        return 1;
+    tyb_note_write(cache, layer_idx, pos0, st);
+    if (!tyb_cuda_ok(tyb_prefill_tc_launch(q_raw, in_dtype == ATTN_DT_BF16, q_norm, token_cos, token_sin, kl, vl,
+                                           cache->max_seq_len, output, out_dtype == ATTN_DT_BF16, seq_len, pos0, scale,
+                                           eps, st),
+                     what))
+        return 1;
+    tyb_note_nowrite(st);
+    return 0;
+}

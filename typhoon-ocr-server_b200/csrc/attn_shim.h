@@ -69,6 +69,22 @@ int tyb_prefill_simt_launch(const float *q, float *out, const void *k, const voi
                             long long row_stride, long long head_stride, int kv_dtype, int Sq,
                             int Sk, int pos_offset, float scale, void *stream);
 
+/* ---- tensor-core prefill (prefill_tc.cu) ---------------------------------------------- */
+
+/* Raw K/V rows [S][8][128] (fp32, or bf16 when in_bf16) -> BF16 cache rows [pos0, pos0+S) of
+ * one layer (layout of tyb_seq_kv): K through RMSNorm(k_norm) and rotate_half M-RoPE with the
+ * per-token cos/sin [S][64]; V as is. */
+int tyb_kv_prep_launch(const void *k_raw, const void *v_raw, int in_bf16, const float *k_norm, const float *cos,
+                       const float *sin, void *k_dst, void *v_dst, int row_capacity, int pos0, int S, float eps,
+                       void *stream);
+
+/* Causal attention of Sq raw queries [Sq][16][128] (fp32 or bf16; RMSNorm(q_norm) + M-RoPE
+ * applied on load) over BF16 cache rows [0, pos_offset + Sq) of one layer; query i sits at
+ * position pos_offset + i.  Output [Sq][16][128], fp32 or bf16. */
+int tyb_prefill_tc_launch(const void *q, int q_bf16, const float *q_norm, const float *cos, const float *sin,
+                          const void *k_cache, const void *v_cache, int row_capacity, void *out, int out_bf16,
+                          int Sq, int pos_offset, float scale, float eps, void *stream);
+
 /* ---- KV-cache row writes (kv_write.cu) -------------------------------------------- */
 
 /* Token-major fp32 rows [S][8][128] -> head-first cache rows [pos0, pos0+S) of one layer

@@ -1,0 +1,601 @@
+// prefill_tc.cu -- causal GQA flash attention for prefill on the 5th-generation tensor
+// cores (tcgen05 + TMEM), BF16 operands, FP32 accumulation, with QK-RMSNorm and M-RoPE
+// fused into the query load, plus the KV-cache append kernel that normalises and rotates K.
+//
+// Reference semantics: kernel/decoder.c:73-117 for one layer -- per-head RMSNorm of q and k
+// with q_norm/k_norm (kernel/ops.c:22-62), rotate_half M-RoPE with per-token cos/sin
+// (kernel/ops.c:297-343), K/V appended to the cache at rows seq_len.. (kernel/kv_cache.c:
+// 80-104), then causal attention of the new queries over cache rows [0, seq_len + S) with
+// query i at position seq_len + i (kernel/attention.c:413-543; seq_len = 0 is the plain
+// prefill of :252-381).
+//
+// Work item = 128 query tokens x the 2 query heads of one KV head (the GQA pair folded into
+// the tile: one K/V tile feeds both heads).  Per item:
+//   * all 8 softmax warps load the raw queries, RMSNorm + rotate them in registers and store
+//     them as BF16 into shared memory in the 128-byte-swizzled K-major layout the tensor core
+//     reads (Q0, Q1: 128 x 128 each);
+//   * one thread of warp 8 streams K and V tiles (128 keys x 128 dims, BF16) from the cache
+//     with TMA tensor copies (SWIZZLE_128B; rows past the attended length are zero-filled) and
+//     issues the MMAs: S_h = Q_h . K^T into TMEM, later O_h += P_h . V into TMEM;
+//   * softmax warp w owns TMEM lane (row) 32*(w%4)+lane of head w/4: it reads its S row with
+//     tcgen05.ld, applies the causal mask and the online softmax (base 2), rescales its O row
+//     in TMEM, and writes P as BF16 into shared memory (same swizzled layout) for the P.V MMA;
+//   * the epilogue reads O, divides by the row sum and writes the output rows.
+// TMEM: S0 | S1 | O0 | O1, 128 columns each (all 512).  Shared memory: Q0 Q1 P0 P1 K V, 32 KB
+// each.  Every mbarrier wait is bounded; a timed-out CTA raises the status word, leaves its
+// loops, frees its TMEM and returns.
+#include <cuda.h>
+
+#include "common.cuh"
+
+namespace tyb {
+
+constexpr int kPtRows = 128;            // query tokens per item (= tensor-core M)
+constexpr int kPtKeys = 128;            // keys per tile (= N of S, K of P.V)
+constexpr int kPtSoftmaxThreads = 256;  // warps 0-7
+constexpr int kPtThreads = kPtSoftmaxThreads + 32;  // + warp 8: TMA + MMA issue
+constexpr int kPtTile = 128 * 128 * 2;  // one 128x128 BF16 operand tile: 32 KB
+constexpr int kPtBox = 128 * 128;       // one 128-row x 64-column swizzled box: 16 KB
+
+struct PrefillTcArgs {
+    const void* q;        // [Sq][16][128] raw queries, fp32 (q_bf16 = 0) or bf16
+    int q_bf16;
+    const float* q_norm;  // [128]
+    const float* cos;     // [Sq][64]
+    const float* sin;     // [Sq][64]
+    void* out;            // [Sq][16][128], fp32 (out_bf16 = 0) or bf16
+    int out_bf16;
+    int Sq;
+    int pos_offset;       // absolute position of query 0 (rows already in the cache)
+    int total_kv;         // pos_offset + Sq: rows attended by the last query
+    int n_qtiles;
+    float scale_log2;
+    float eps;
+};
+
+// ---- tcgen05 / TMA primitives ---------------------------------------------------------
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tc_commit(uint64_t* bar)
+{
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+// D[tmem] (+)= A[smem desc] . B[smem desc]^T, kind::f16 (BF16 in, FP32 accumulate).
+__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                       uint32_t accumulate)
+{
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0)
+        : "memory");
+}
+
+// 32 consecutive 32-bit TMEM columns of this thread's lane.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32])
+{
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+#pragma unroll
+    for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32])
+{
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+        "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])),
+        "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])),
+        "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+        "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+        "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])),
+        "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])),
+        "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
+        "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])),
+        "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
+        "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+        : "memory");
+}
+
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// TMA tensor copy: 3-D box {64 dims, 128 rows, 1 head} -> shared memory, on `bar`.
+__device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* map, int c0, int c1, int c2,
+                                            uint64_t* bar)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::
+            "r"(smem_u32(smem_dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// Shared-memory matrix descriptor (sm_100 format, version 1) for a 128-byte-swizzled tile.
+//   K-major operands (Q, K, P): 8-row core groups 1024 B apart (SBO); LBO unused (1).
+//   MN-major operand (V): 64-element atoms along N are `lbo` bytes apart; SBO = 1024 B.
+__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo_bytes)
+{
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+    d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFF) << 16;
+    d |= (uint64_t)((1024 >> 4) & 0x3FFF) << 32;
+    d |= (uint64_t)1 << 46;  // version
+    d |= (uint64_t)2 << 61;  // SWIZZLE_128B
+    return d;
+}
+
+// Instruction descriptor, kind::f16: BF16 A/B, FP32 D, M = 128, N = 128.
+__host__ __device__ constexpr uint32_t umma_idesc(bool b_mn_major)
+{
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((b_mn_major ? 1u : 0u) << 16) | ((128u >> 3) << 17) |
+           ((128u >> 4) << 24);
+}
+
+// Byte offset of element (row r, column c) of a 128x128 BF16 operand tile stored as two
+// 128-row x 64-column boxes, 128-byte rows, 16-byte chunks XOR-swizzled by r % 8 -- the
+// layout TMA writes with SWIZZLE_128B and the tensor core reads through umma_desc.
+__device__ __forceinline__ uint32_t sw128_offset(int r, int c)
+{
+    return (uint32_t)((c >> 6) * kPtBox + r * 128 + ((((c & 63) >> 3) ^ (r & 7)) << 4) + ((c & 7) << 1));
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi)
+{
+    __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+
+__device__ __forceinline__ float pt_exp2(float x)
+{
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+__global__ void __launch_bounds__(kPtThreads, 1)
+    prefill_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
+                      const PrefillTcArgs a)
+{
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    // 1024-byte alignment is required by the 128-byte swizzle atoms.
+    unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    unsigned char* sQ = smem;                  // Q0, Q1
+    unsigned char* sP = smem + 2 * kPtTile;    // P0, P1
+    unsigned char* sK = smem + 4 * kPtTile;
+    unsigned char* sV = smem + 5 * kPtTile;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 6 * kPtTile);
+    uint64_t* k_full = bars + 0;
+    uint64_t* v_full = bars + 1;
+    uint64_t* k_free = bars + 2;   // QK of the current tile has finished reading K
+    uint64_t* s_full = bars + 3;   // S of the current tile is in TMEM
+    uint64_t* p_full = bars + 4;   // P written, O rescaled (256 arrivals)
+    uint64_t* pv_done = bars + 5;  // P.V of the current tile has finished (O final, P and V free)
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 8);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    // Longest items first: q-tile index descends with blockIdx.
+    const int item = blockIdx.x;
+    const int qt = a.n_qtiles - 1 - item / kHkv;
+    const int kvh = item % kHkv;
+    const int t0 = qt * kPtRows;
+    const int ntok = min(kPtRows, a.Sq - t0);
+    const int last_pos = a.pos_offset + t0 + ntok - 1;
+    const int ntiles = last_pos / kPtKeys + 1;
+
+    if (warp == 8) {
+        if (lane == 0) {
+            mbar_init(k_full, 1);
+            mbar_init(v_full, 1);
+            mbar_init(k_free, 1);
+            mbar_init(s_full, 1);
+            mbar_init(p_full, kPtSoftmaxThreads);
+            mbar_init(pv_done, 1);
+            fence_barrier_init();
+            fence_proxy_async_smem();
+        }
+        __syncwarp();
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_u32(tmem_slot))
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+
+    // ---- queries: RMSNorm(q_norm) + rotate_half M-RoPE, BF16, swizzled into Q0/Q1 ----------
+    if (warp < 8) {
+        float w4[4];
+        {
+            const float4 w = *reinterpret_cast<const float4*>(a.q_norm + 4 * lane);
+            w4[0] = w.x; w4[1] = w.y; w4[2] = w.z; w4[3] = w.w;
+        }
+        const int jr = 4 * (lane & 15);  // rotary frequency index of this lane's first dim
+        for (int i = 0; i < 32; i++) {
+            const int row = warp * 32 + i;  // 0..255: head = row / 128, token = row % 128
+            const int h = row >> 7, r = row & 127;
+            const int tok = t0 + r;
+            float x[4] = {0.f, 0.f, 0.f, 0.f};
+            if (tok < a.Sq) {
+                const size_t off = ((size_t)tok * kHq + kGroup * kvh + h) * kD + 4 * lane;
+                if (a.q_bf16) {
+                    const uint2 u = *reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(a.q) + off);
+                    const __nv_bfloat162* hv = reinterpret_cast<const __nv_bfloat162*>(&u);
+                    const float2 f0 = __bfloat1622float2(hv[0]), f1 = __bfloat1622float2(hv[1]);
+                    x[0] = f0.x; x[1] = f0.y; x[2] = f1.x; x[3] = f1.y;
+                } else {
+                    const float4 f = *reinterpret_cast<const float4*>(static_cast<const float*>(a.q) + off);
+                    x[0] = f.x; x[1] = f.y; x[2] = f.z; x[3] = f.w;
+                }
+            }
+            float ss = x[0] * x[0] + x[1] * x[1] + x[2] * x[2] + x[3] * x[3];
+#pragma unroll
+            for (int o = 16; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+            const float rs = rsqrtf(ss * (1.f / kD) + a.eps);
+            float y[4];
+#pragma unroll
+            for (int e = 0; e < 4; e++) y[e] = x[e] * rs * w4[e];
+            // rotate_half: lane l < 16 holds dims [4l, 4l+4), lane l+16 the partner dims + 64.
+            float partner[4];
+#pragma unroll
+            for (int e = 0; e < 4; e++) partner[e] = __shfl_xor_sync(0xffffffffu, y[e], 16);
+            float c4[4] = {1.f, 1.f, 1.f, 1.f}, s4[4] = {0.f, 0.f, 0.f, 0.f};
+            if (tok < a.Sq) {
+                const float4 c = *reinterpret_cast<const float4*>(a.cos + (size_t)tok * 64 + jr);
+                const float4 s = *reinterpret_cast<const float4*>(a.sin + (size_t)tok * 64 + jr);
+                c4[0] = c.x; c4[1] = c.y; c4[2] = c.z; c4[3] = c.w;
+                s4[0] = s.x; s4[1] = s.y; s4[2] = s.z; s4[3] = s.w;
+            }
+            float z[4];
+#pragma unroll
+            for (int e = 0; e < 4; e++)
+                z[e] = lane < 16 ? y[e] * c4[e] - partner[e] * s4[e]   // x[j] c - x[j+64] s
+                                 : y[e] * c4[e] + partner[e] * s4[e];  // x[j+64] c + x[j] s
+            const uint2 packed = make_uint2(pack_bf16x2(z[0], z[1]), pack_bf16x2(z[2], z[3]));
+            *reinterpret_cast<uint2*>(sQ + h * kPtTile + sw128_offset(r, 4 * lane)) = packed;
+        }
+        fence_proxy_async_smem();  // Q is read by the tensor core (async proxy)
+    }
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    const uint32_t idesc_qk = umma_idesc(false);
+    const uint32_t idesc_pv = umma_idesc(true);
+
+    if (warp == 8) {
+        // ---- TMA + MMA issue (one thread) ------------------------------------------------
+        if (lane == 0) {
+            bool ok = true;
+            auto load_k = [&](int j) {
+                mbar_arrive_expect_tx(k_full, kPtTile);
+                tma_load_3d(sK, &tmap_k, 0, j * kPtKeys, kvh, k_full);
+                tma_load_3d(sK + kPtBox, &tmap_k, 64, j * kPtKeys, kvh, k_full);
+            };
+            auto load_v = [&](int j) {
+                mbar_arrive_expect_tx(v_full, kPtTile);
+                tma_load_3d(sV, &tmap_v, 0, j * kPtKeys, kvh, v_full);
+                tma_load_3d(sV + kPtBox, &tmap_v, 64, j * kPtKeys, kvh, v_full);
+            };
+            load_k(0);
+            load_v(0);
+            const uint32_t q_base = smem_u32(sQ), p_base = smem_u32(sP);
+            const uint32_t k_base = smem_u32(sK), v_base = smem_u32(sV);
+            for (int j = 0; j < ntiles && ok; j++) {
+                const uint32_t par = (uint32_t)j & 1u;
+                ok = mbar_wait_bounded(k_full, par, kWaitLimitNs, TYB_STATUS_WAIT_TIMEOUT);
+                if (!ok) break;
+                tc_fence_after();
+                // S_h = Q_h . K^T: 8 steps of K = 16 dims (32 bytes) along the swizzled rows.
+                for (int h = 0; h < 2; h++)
+#pragma unroll
+                    for (int kk = 0; kk < 8; kk++) {
+                        const uint32_t off = (kk >> 2) * kPtBox + (kk & 3) * 32;
+                        tc_mma(tmem + h * 128, umma_desc(q_base + h * kPtTile + off, 16),
+                               umma_desc(k_base + off, 16), idesc_qk, kk > 0);
+                    }
+                tc_commit(s_full);
+                tc_commit(k_free);
+                // Next K tile once this QK has read the current one.
+                ok = mbar_wait_bounded(k_free, par, kWaitLimitNs, TYB_STATUS_WAIT_TIMEOUT);
+                if (!ok) break;
+                if (j + 1 < ntiles) load_k(j + 1);
+                // P of this tile ready (and O rescaled) -> O_h += P_h . V.
+                ok = mbar_wait_bounded(p_full, par, kWaitLimitNs, TYB_STATUS_WAIT_TIMEOUT) &&
+                     mbar_wait_bounded(v_full, par, kWaitLimitNs, TYB_STATUS_WAIT_TIMEOUT);
+                if (!ok) break;
+                tc_fence_after();
+                for (int h = 0; h < 2; h++)
+#pragma unroll
+                    for (int kk = 0; kk < 8; kk++) {
+                        // P: K-major, keys [16kk, 16kk+16) of the swizzled rows.
+                        const uint32_t poff = (kk >> 2) * kPtBox + (kk & 3) * 32;
+                        // V: MN-major, 16 key rows of 128 bytes per step; the two 64-dim boxes
+                        // are kPtBox apart.
+                        tc_mma(tmem + 256 + h * 128, umma_desc(p_base + h * kPtTile + poff, 16),
+                               umma_desc(v_base + kk * 16 * 128, kPtBox), idesc_pv, (j > 0 || kk > 0));
+                    }
+                tc_commit(pv_done);
+                // Next V tile once this P.V has read the current one.
+                ok = mbar_wait_bounded(pv_done, par, kWaitLimitNs, TYB_STATUS_WAIT_TIMEOUT);
+                if (!ok) break;
+                if (j + 1 < ntiles) load_v(j + 1);
+            }
+        }
+        __syncwarp();
+    } else {
+        // ---- softmax + epilogue: one TMEM lane (row) per thread -----------------------------
+        const int h = warp >> 2;
+        const int r = 32 * (warp & 3) + lane;  // row = TMEM lane = token t0 + r
+        const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
+        const uint32_t s_addr = tmem + lane_base + h * 128;
+        const uint32_t o_addr = tmem + lane_base + 256 + h * 128;
+        const int qpos = a.pos_offset + t0 + r;
+        float m_run = -INFINITY, l_run = 0.f;
+        bool ok = true;
+        // A wait that runs out of time ends the loop for the whole warp (the TMEM loads below are
+        // warp-collective).
+        auto warp_wait = [&](uint64_t* bar, uint32_t parity) {
+            return !__any_sync(0xffffffffu, !mbar_wait_bounded(bar, parity, kWaitLimitNs, TYB_STATUS_WAIT_TIMEOUT));
+        };
+        unsigned char* prow = sP + h * kPtTile;
+        for (int j = 0; j < ntiles; j++) {
+            const uint32_t par = (uint32_t)j & 1u;
+            if (!warp_wait(s_full, par)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            // Causal mask: key k is visible to query qpos iff k <= qpos (and k < total_kv).
+            const int k0 = j * kPtKeys;
+            const int vis = min(qpos, a.total_kv - 1) - k0 + 1;  // keys [k0, k0 + vis) visible
+            // Pass 1: row maximum of the scaled scores.
+            float mx = -INFINITY;
+#pragma unroll
+            for (int c = 0; c < 4; c++) {
+                float v[32];
+                tmem_ld32(s_addr + c * 32, v);
+                tmem_wait_ld();
+#pragma unroll
+                for (int i = 0; i < 32; i++)
+                    if (c * 32 + i < vis) mx = fmaxf(mx, v[i] * a.scale_log2);
+            }
+            const float m_new = fmaxf(m_run, mx);
+            const float alpha = pt_exp2(m_run - m_new);  // 0 on the first tile
+            // O of the previous tile must be final before it is rescaled and P overwritten.
+            if (j > 0) {
+                if (!warp_wait(pv_done, par ^ 1u)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+#pragma unroll
+                for (int c = 0; c < 4; c++) {
+                    float v[32];
+                    tmem_ld32(o_addr + c * 32, v);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int i = 0; i < 32; i++) v[i] *= alpha;
+                    tmem_st32(o_addr + c * 32, v);
+                }
+                tmem_wait_st();
+            }
+            // Pass 2: p = exp2(s - m), summed, packed to BF16 and stored into P's swizzled row.
+            float rowsum = 0.f;
+#pragma unroll
+            for (int c = 0; c < 4; c++) {
+                float v[32];
+                tmem_ld32(s_addr + c * 32, v);
+                tmem_wait_ld();
+                uint32_t pk[16];
+#pragma unroll
+                for (int i = 0; i < 32; i += 2) {
+                    const float p0 = (c * 32 + i < vis) ? pt_exp2(v[i] * a.scale_log2 - m_new) : 0.f;
+                    const float p1 = (c * 32 + i + 1 < vis) ? pt_exp2(v[i + 1] * a.scale_log2 - m_new) : 0.f;
+                    rowsum += p0 + p1;
+                    pk[i >> 1] = pack_bf16x2(p0, p1);
+                }
+#pragma unroll
+                for (int q4 = 0; q4 < 4; q4++)
+                    *reinterpret_cast<uint4*>(prow + sw128_offset(r, c * 32 + 8 * q4)) =
+                        make_uint4(pk[4 * q4], pk[4 * q4 + 1], pk[4 * q4 + 2], pk[4 * q4 + 3]);
+            }
+            l_run = l_run * alpha + rowsum;
+            m_run = m_new;
+            fence_proxy_async_smem();
+            tc_fence_before();
+            mbar_arrive(p_full);
+        }
+        // Epilogue: O / l for this row.
+        if (ok && warp_wait(pv_done, (uint32_t)(ntiles - 1) & 1u)) {
+            tc_fence_after();
+            const int tok = t0 + r;
+            const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+            const size_t ooff = ((size_t)tok * kHq + kGroup * kvh + h) * kD;
+#pragma unroll
+            for (int c = 0; c < 4; c++) {
+                float v[32];
+                tmem_ld32(o_addr + c * 32, v);
+                tmem_wait_ld();
+                if (tok < a.Sq) {
+                    if (a.out_bf16) {
+                        __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(a.out) + ooff + c * 32;
+#pragma unroll
+                        for (int i = 0; i < 32; i += 8) {
+                            const uint4 u = make_uint4(pack_bf16x2(v[i] * inv, v[i + 1] * inv),
+                                                       pack_bf16x2(v[i + 2] * inv, v[i + 3] * inv),
+                                                       pack_bf16x2(v[i + 4] * inv, v[i + 5] * inv),
+                                                       pack_bf16x2(v[i + 6] * inv, v[i + 7] * inv));
+                            *reinterpret_cast<uint4*>(dst + i) = u;
+                        }
+                    } else {
+                        float* dst = static_cast<float*>(a.out) + ooff + c * 32;
+#pragma unroll
+                        for (int i = 0; i < 32; i += 4)
+                            *reinterpret_cast<float4*>(dst + i) =
+                                make_float4(v[i] * inv, v[i + 1] * inv, v[i + 2] * inv, v[i + 3] * inv);
+                    }
+                }
+            }
+        }
+        tc_fence_before();
+    }
+    __syncthreads();
+    if (warp == 8) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem) : "memory");
+    }
+}
+
+// ---- K/V append with QK-RMSNorm + M-RoPE on K ------------------------------------------------
+// One warp per (token, KV head): RMSNorm(k_norm) + rotate_half with the token's cos/sin, K and V
+// written as BF16 into cache rows pos0 + t (layout of tyb_seq_kv).
+__global__ void kv_prep_kernel(const void* __restrict__ k_raw, const void* __restrict__ v_raw, int in_bf16,
+                               const float* __restrict__ k_norm, const float* __restrict__ cosv,
+                               const float* __restrict__ sinv, __nv_bfloat16* __restrict__ k_dst,
+                               __nv_bfloat16* __restrict__ v_dst, int row_capacity, int pos0, int S, float eps)
+{
+    const int lane = threadIdx.x & 31;
+    const long long nwarps = (long long)gridDim.x * (blockDim.x >> 5);
+    const float4 w = *reinterpret_cast<const float4*>(k_norm + 4 * lane);
+    const float w4[4] = {w.x, w.y, w.z, w.w};
+    const int jr = 4 * (lane & 15);
+    for (long long wi = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); wi < (long long)S * kHkv;
+         wi += nwarps) {
+        const int t = (int)(wi / kHkv), hh = (int)(wi % kHkv);
+        const size_t off = ((size_t)t * kHkv + hh) * kD + 4 * lane;
+        float x[4], v4[4];
+        if (in_bf16) {
+            const uint2 uk = *reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(k_raw) + off);
+            const uint2 uv = *reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(v_raw) + off);
+            const __nv_bfloat162* hk = reinterpret_cast<const __nv_bfloat162*>(&uk);
+            const __nv_bfloat162* hv = reinterpret_cast<const __nv_bfloat162*>(&uv);
+            float2 a0 = __bfloat1622float2(hk[0]), a1 = __bfloat1622float2(hk[1]);
+            float2 b0 = __bfloat1622float2(hv[0]), b1 = __bfloat1622float2(hv[1]);
+            x[0] = a0.x; x[1] = a0.y; x[2] = a1.x; x[3] = a1.y;
+            v4[0] = b0.x; v4[1] = b0.y; v4[2] = b1.x; v4[3] = b1.y;
+        } else {
+            const float4 fk = *reinterpret_cast<const float4*>(static_cast<const float*>(k_raw) + off);
+            const float4 fv = *reinterpret_cast<const float4*>(static_cast<const float*>(v_raw) + off);
+            x[0] = fk.x; x[1] = fk.y; x[2] = fk.z; x[3] = fk.w;
+            v4[0] = fv.x; v4[1] = fv.y; v4[2] = fv.z; v4[3] = fv.w;
+        }
+        float ss = x[0] * x[0] + x[1] * x[1] + x[2] * x[2] + x[3] * x[3];
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        const float rs = rsqrtf(ss * (1.f / kD) + eps);
+        float y[4], partner[4];
+#pragma unroll
+        for (int e = 0; e < 4; e++) y[e] = x[e] * rs * w4[e];
+#pragma unroll
+        for (int e = 0; e < 4; e++) partner[e] = __shfl_xor_sync(0xffffffffu, y[e], 16);
+        const float4 c = *reinterpret_cast<const float4*>(cosv + (size_t)t * 64 + jr);
+        const float4 s = *reinterpret_cast<const float4*>(sinv + (size_t)t * 64 + jr);
+        const float c4[4] = {c.x, c.y, c.z, c.w}, s4[4] = {s.x, s.y, s.z, s.w};
+        float z[4];
+#pragma unroll
+        for (int e = 0; e < 4; e++)
+            z[e] = lane < 16 ? y[e] * c4[e] - partner[e] * s4[e] : y[e] * c4[e] + partner[e] * s4[e];
+        const size_t doff = ((size_t)hh * row_capacity + pos0 + t) * kD + 4 * lane;
+        *reinterpret_cast<uint2*>(k_dst + doff) = make_uint2(pack_bf16x2(z[0], z[1]), pack_bf16x2(z[2], z[3]));
+        *reinterpret_cast<uint2*>(v_dst + doff) = make_uint2(pack_bf16x2(v4[0], v4[1]), pack_bf16x2(v4[2], v4[3]));
+    }
+}
+
+// ---- host ---------------------------------------------------------------------------------
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn()
+{
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    }
+    return fn;
+}
+
+// Rows [0, rows) of the 8 heads of one layer's BF16 cache as a 3-D tensor {128, rows, 8};
+// rows past `rows` read as zeros.
+static bool make_kv_map(CUtensorMap* map, const void* base, int rows, int row_capacity)
+{
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return false;
+    const cuuint64_t dims[3] = {(cuuint64_t)kD, (cuuint64_t)rows, (cuuint64_t)kHkv};
+    const cuuint64_t strides[2] = {(cuuint64_t)kD * 2, (cuuint64_t)row_capacity * kD * 2};
+    const cuuint32_t box[3] = {64, (cuuint32_t)kPtKeys, 1};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+constexpr size_t kPtSmemBytes = 6 * (size_t)kPtTile + 128 + 1024;  // tiles + barriers + alignment slack
+
+}  // namespace tyb
+
+using namespace tyb;
+
+extern "C" int tyb_kv_prep_launch(const void* k_raw, const void* v_raw, int in_bf16, const float* k_norm,
+                                  const float* cos, const float* sin, void* k_dst, void* v_dst, int row_capacity,
+                                  int pos0, int S, float eps, void* stream)
+{
+    if (S <= 0) return 0;
+    const int threads = 256;
+    long long blocks = ((long long)S * kHkv + threads / 32 - 1) / (threads / 32);
+    if (blocks > 148LL * 16) blocks = 148LL * 16;
+    kv_prep_kernel<<<(unsigned)blocks, threads, 0, (cudaStream_t)stream>>>(
+        k_raw, v_raw, in_bf16, k_norm, cos, sin, static_cast<__nv_bfloat16*>(k_dst), static_cast<__nv_bfloat16*>(v_dst),
+        row_capacity, pos0, S, eps);
+    return (int)cudaGetLastError();
+}
+
+extern "C" int tyb_prefill_tc_launch(const void* q, int q_bf16, const float* q_norm, const float* cos,
+                                     const float* sin, const void* k_cache, const void* v_cache, int row_capacity,
+                                     void* out, int out_bf16, int Sq, int pos_offset, float scale, float eps,
+                                     void* stream)
+{
+    if (Sq <= 0) return 0;
+    static bool attr = false;
+    if (!attr) {
+        cudaError_t e =
+            cudaFuncSetAttribute(prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPtSmemBytes);
+        if (e != cudaSuccess) return (int)e;
+        attr = true;
+    }
+    PrefillTcArgs a;
+    a.q = q;
+    a.q_bf16 = q_bf16;
+    a.q_norm = q_norm;
+    a.cos = cos;
+    a.sin = sin;
+    a.out = out;
+    a.out_bf16 = out_bf16;
+    a.Sq = Sq;
+    a.pos_offset = pos_offset;
+    a.total_kv = pos_offset + Sq;
+    a.n_qtiles = (Sq + kPtRows - 1) / kPtRows;
+    a.scale_log2 = scale * kLog2e;
+    a.eps = eps;
+    CUtensorMap mk, mv;
+    if (!make_kv_map(&mk, k_cache, a.total_kv, row_capacity) || !make_kv_map(&mv, v_cache, a.total_kv, row_capacity))
+        return (int)cudaErrorInvalidValue;
+    prefill_tc_kernel<<<a.n_qtiles * kHkv, kPtThreads, kPtSmemBytes, (cudaStream_t)stream>>>(mk, mv, a);
+    return (int)cudaGetLastError();
+}
