@@ -32,8 +32,18 @@ namespace tyb {
 
 constexpr int kPtRows = 128;            // query tokens per item (= tensor-core M)
 constexpr int kPtKeys = 128;            // keys per tile (= N of S, K of P.V)
-constexpr int kPtSoftmaxThreads = 256;  // warps 0-7
-constexpr int kPtThreads = kPtSoftmaxThreads + 32;  // + warp 8: TMA + MMA issue
+constexpr int kPtSoftmaxThreads = 256;  // warpgroups 0, 1 (warps 0-3 head 0, 4-7 head 1)
+constexpr int kPtThreads = kPtSoftmaxThreads + 128;  // + warpgroup 2: warp 8 MMA issue, warp 9 TMA
+// Register split (setmaxnreg): the kernel is compiled for kPtLaunchRegs per thread, the
+// issue warpgroup gives registers back and the softmax warpgroups take them, so that a
+// softmax thread holds its whole 128-column S row.  The shares add up to no more than the
+// launch's total (checked on the host against the compiled count before every launch).
+constexpr int kPtLaunchRegs = 168;
+constexpr int kPtIssueRegs = 56;
+constexpr int kPtSoftmaxRegs = 216;
+static_assert(kPtSoftmaxThreads * kPtSoftmaxRegs + 128 * kPtIssueRegs <= kPtThreads * kPtLaunchRegs,
+              "register split exceeds the launch allocation");
+static_assert(2 * kPtSoftmaxRegs + kPtIssueRegs <= 512, "one warp of each warpgroup shares a sub-partition");
 constexpr int kPtTile = 128 * 128 * 2;  // one 128x128 BF16 operand tile: 32 KB
 constexpr int kPtBox = 128 * 128;       // one 128-row x 64-column swizzled box: 16 KB
 
@@ -76,20 +86,51 @@ __device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t a_desc, uint64_
         : "memory");
 }
 
-// 32 consecutive 32-bit TMEM columns of this thread's lane.
+// 32 / 64 consecutive 32-bit TMEM columns of this thread's lane.  The wait for the load is
+// part of the same asm statement, so no use of the results can be scheduled before it.
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32])
 {
     uint32_t r[32];
     asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-        : "r"(taddr));
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr)
+        : "memory");
 #pragma unroll
     for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, float (&v)[64])
+{
+    uint32_t r[64];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x64.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%64];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]), "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]), "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]), "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]), "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
+        : "r"(taddr)
+        : "memory");
+#pragma unroll
+    for (int i = 0; i < 64; i++) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tmem_ld128(uint32_t taddr, float (&v)[128])
+{
+    uint32_t r[128];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x128.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63,%64,%65,%66,%67,%68,%69,%70,%71,%72,%73,%74,%75,%76,%77,%78,%79,%80,%81,%82,%83,%84,%85,%86,%87,%88,%89,%90,%91,%92,%93,%94,%95,%96,%97,%98,%99,%100,%101,%102,%103,%104,%105,%106,%107,%108,%109,%110,%111,%112,%113,%114,%115,%116,%117,%118,%119,%120,%121,%122,%123,%124,%125,%126,%127}, [%128];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]), "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]), "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]), "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]), "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63]), "=r"(r[64]), "=r"(r[65]), "=r"(r[66]), "=r"(r[67]), "=r"(r[68]), "=r"(r[69]), "=r"(r[70]), "=r"(r[71]), "=r"(r[72]), "=r"(r[73]), "=r"(r[74]), "=r"(r[75]), "=r"(r[76]), "=r"(r[77]), "=r"(r[78]), "=r"(r[79]), "=r"(r[80]), "=r"(r[81]), "=r"(r[82]), "=r"(r[83]), "=r"(r[84]), "=r"(r[85]), "=r"(r[86]), "=r"(r[87]), "=r"(r[88]), "=r"(r[89]), "=r"(r[90]), "=r"(r[91]), "=r"(r[92]), "=r"(r[93]), "=r"(r[94]), "=r"(r[95]), "=r"(r[96]), "=r"(r[97]), "=r"(r[98]), "=r"(r[99]), "=r"(r[100]), "=r"(r[101]), "=r"(r[102]), "=r"(r[103]), "=r"(r[104]), "=r"(r[105]), "=r"(r[106]), "=r"(r[107]), "=r"(r[108]), "=r"(r[109]), "=r"(r[110]), "=r"(r[111]), "=r"(r[112]), "=r"(r[113]), "=r"(r[114]), "=r"(r[115]), "=r"(r[116]), "=r"(r[117]), "=r"(r[118]), "=r"(r[119]), "=r"(r[120]), "=r"(r[121]), "=r"(r[122]), "=r"(r[123]), "=r"(r[124]), "=r"(r[125]), "=r"(r[126]), "=r"(r[127])
+        : "r"(taddr)
+        : "memory");
+#pragma unroll
+    for (int i = 0; i < 128; i++) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tmem_st64(uint32_t taddr, const float (&v)[64])
+{
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x64.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63,%64};" ::"r"(taddr), "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])), "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])), "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])), "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])), "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])), "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])), "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])), "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31])), "r"(__float_as_uint(v[32])), "r"(__float_as_uint(v[33])), "r"(__float_as_uint(v[34])), "r"(__float_as_uint(v[35])), "r"(__float_as_uint(v[36])), "r"(__float_as_uint(v[37])), "r"(__float_as_uint(v[38])), "r"(__float_as_uint(v[39])), "r"(__float_as_uint(v[40])), "r"(__float_as_uint(v[41])), "r"(__float_as_uint(v[42])), "r"(__float_as_uint(v[43])), "r"(__float_as_uint(v[44])), "r"(__float_as_uint(v[45])), "r"(__float_as_uint(v[46])), "r"(__float_as_uint(v[47])), "r"(__float_as_uint(v[48])), "r"(__float_as_uint(v[49])), "r"(__float_as_uint(v[50])), "r"(__float_as_uint(v[51])), "r"(__float_as_uint(v[52])), "r"(__float_as_uint(v[53])), "r"(__float_as_uint(v[54])), "r"(__float_as_uint(v[55])), "r"(__float_as_uint(v[56])), "r"(__float_as_uint(v[57])), "r"(__float_as_uint(v[58])), "r"(__float_as_uint(v[59])), "r"(__float_as_uint(v[60])), "r"(__float_as_uint(v[61])), "r"(__float_as_uint(v[62])), "r"(__float_as_uint(v[63]))
+                 : "memory");
 }
 
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32])
@@ -110,7 +151,6 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32])
         : "memory");
 }
 
-__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // TMA tensor copy: 3-D box {64 dims, 128 rows, 1 head} -> shared memory, on `bar`.
@@ -166,7 +206,62 @@ __device__ __forceinline__ float pt_exp2(float x)
     return y;
 }
 
-__global__ void __launch_bounds__(kPtThreads, 1)
+__device__ __forceinline__ float fmax3(float a, float b, float c)
+{
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+
+// Largest visible score of a row: columns [0, lim) (all 128 when the tile needs no mask).
+template <bool kMask>
+__device__ __forceinline__ float row_max(const float (&s)[kPtKeys], int lim)
+{
+    float m[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+    for (int c = 0; c < kPtKeys; c += 2) {
+        const float a = (!kMask || c < lim) ? s[c] : -INFINITY;
+        const float b = (!kMask || c + 1 < lim) ? s[c + 1] : -INFINITY;
+        m[(c >> 1) & 3] = fmax3(m[(c >> 1) & 3], a, b);
+    }
+    return fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3]));
+}
+
+// p = exp2(s * scale_log2 + neg_m) on the visible columns (0 on the others), written as BF16
+// into this row of the swizzled P tile; returns the FP32 sum of the row's p.  The affine step
+// and the sum run two columns per instruction (f32x2).
+template <bool kMask>
+__device__ __forceinline__ float row_exp(const float (&s)[kPtKeys], int lim, float scale_log2, float neg_m,
+                                         unsigned char* prow, int r)
+{
+    const float2 sc = make_float2(scale_log2, scale_log2), nm = make_float2(neg_m, neg_m);
+    float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int c = 0; c < kPtKeys; c += 8) {
+        float e[8];
+#pragma unroll
+        for (int i = 0; i < 8; i += 2) {
+            float2 x = __ffma2_rn(make_float2(s[c + i], s[c + i + 1]), sc, nm);
+            if (kMask) {
+                if (c + i >= lim) x.x = -INFINITY;
+                if (c + i + 1 >= lim) x.y = -INFINITY;
+            }
+            e[i] = pt_exp2(x.x);
+            e[i + 1] = pt_exp2(x.y);
+        }
+        acc0 = __fadd2_rn(acc0, make_float2(e[0], e[1]));
+        acc1 = __fadd2_rn(acc1, make_float2(e[2], e[3]));
+        acc0 = __fadd2_rn(acc0, make_float2(e[4], e[5]));
+        acc1 = __fadd2_rn(acc1, make_float2(e[6], e[7]));
+        *reinterpret_cast<uint4*>(prow + sw128_offset(r, c)) =
+            make_uint4(pack_bf16x2(e[0], e[1]), pack_bf16x2(e[2], e[3]), pack_bf16x2(e[4], e[5]),
+                       pack_bf16x2(e[6], e[7]));
+    }
+    return (acc0.x + acc0.y) + (acc1.x + acc1.y);
+}
+
+// 384 threads (3 warpgroups) launched at 168 registers each, split 216 / 216 / 56 by setmaxnreg.
+__global__ void __maxnreg__(kPtLaunchRegs)
     prefill_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
                       const PrefillTcArgs a)
 {
@@ -176,15 +271,16 @@ __global__ void __launch_bounds__(kPtThreads, 1)
     unsigned char* sQ = smem;                  // Q0, Q1
     unsigned char* sP = smem + 2 * kPtTile;    // P0, P1
     unsigned char* sK = smem + 4 * kPtTile;
-    unsigned char* sV = smem + 5 * kPtTile;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 6 * kPtTile);
-    uint64_t* k_full = bars + 0;
-    uint64_t* v_full = bars + 1;
-    uint64_t* k_free = bars + 2;   // QK of the current tile has finished reading K
-    uint64_t* s_full = bars + 3;   // S of the current tile is in TMEM
-    uint64_t* p_full = bars + 4;   // P written, O rescaled (256 arrivals)
-    uint64_t* pv_done = bars + 5;  // P.V of the current tile has finished (O final, P and V free)
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 8);
+    unsigned char* sV = smem + 5 * kPtTile;    // V stages 0, 1
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 7 * kPtTile);
+    uint64_t* v_full = bars + 0;    // [2] V stage landed
+    uint64_t* v_free = bars + 2;    // [2] both P.Vs of the tile in that stage have read it
+    uint64_t* k_full = bars + 4;
+    uint64_t* k_free = bars + 5;    // both QKs of the tile have read K
+    uint64_t* s_full = bars + 6;    // [2] per head: S of the tile is in TMEM
+    uint64_t* p_full = bars + 8;    // [2] per head: P written, O rescaled (128 arrivals)
+    uint64_t* pv_done = bars + 10;  // [2] per head: P.V of the tile finished
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     // Longest items first: q-tile index descends with blockIdx.
@@ -198,12 +294,15 @@ __global__ void __launch_bounds__(kPtThreads, 1)
 
     if (warp == 8) {
         if (lane == 0) {
+            for (int i = 0; i < 2; i++) {
+                mbar_init(&v_full[i], 1);
+                mbar_init(&v_free[i], 1);
+                mbar_init(&s_full[i], 1);
+                mbar_init(&p_full[i], kPtSoftmaxThreads / 2);
+                mbar_init(&pv_done[i], 1);
+            }
             mbar_init(k_full, 1);
-            mbar_init(v_full, 1);
             mbar_init(k_free, 1);
-            mbar_init(s_full, 1);
-            mbar_init(p_full, kPtSoftmaxThreads);
-            mbar_init(pv_done, 1);
             fence_barrier_init();
             fence_proxy_async_smem();
         }
@@ -273,67 +372,94 @@ __global__ void __launch_bounds__(kPtThreads, 1)
     const uint32_t idesc_qk = umma_idesc(false);
     const uint32_t idesc_pv = umma_idesc(true);
 
-    if (warp == 8) {
-        // ---- TMA + MMA issue (one thread) ------------------------------------------------
+    if (warp >= 8) asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kPtIssueRegs));
+    else asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kPtSoftmaxRegs));
+
+    if (warp == 9) {
+        // ---- TMA producer (one thread): K single-buffered (refilled as soon as both QKs of
+        // a tile have read it, well before the next QK), V double-buffered (its next tile is
+        // needed right after the current P.Vs, so it is requested one tile ahead).
         if (lane == 0) {
-            bool ok = true;
-            auto load_k = [&](int j) {
+            for (int j = 0; j < ntiles; j++) {
+                const int st = j & 1;
+                if (j >= 1 && !mbar_wait_bounded(k_free, (uint32_t)(j - 1) & 1u, kWaitLimitNs, TYB_STATUS_WAIT_TIMEOUT))
+                    break;
                 mbar_arrive_expect_tx(k_full, kPtTile);
                 tma_load_3d(sK, &tmap_k, 0, j * kPtKeys, kvh, k_full);
                 tma_load_3d(sK + kPtBox, &tmap_k, 64, j * kPtKeys, kvh, k_full);
-            };
-            auto load_v = [&](int j) {
-                mbar_arrive_expect_tx(v_full, kPtTile);
-                tma_load_3d(sV, &tmap_v, 0, j * kPtKeys, kvh, v_full);
-                tma_load_3d(sV + kPtBox, &tmap_v, 64, j * kPtKeys, kvh, v_full);
-            };
-            load_k(0);
-            load_v(0);
-            const uint32_t q_base = smem_u32(sQ), p_base = smem_u32(sP);
-            const uint32_t k_base = smem_u32(sK), v_base = smem_u32(sV);
-            for (int j = 0; j < ntiles && ok; j++) {
-                const uint32_t par = (uint32_t)j & 1u;
-                ok = mbar_wait_bounded(k_full, par, kWaitLimitNs, TYB_STATUS_WAIT_TIMEOUT);
-                if (!ok) break;
-                tc_fence_after();
-                // S_h = Q_h . K^T: 8 steps of K = 16 dims (32 bytes) along the swizzled rows.
-                for (int h = 0; h < 2; h++)
-#pragma unroll
-                    for (int kk = 0; kk < 8; kk++) {
-                        const uint32_t off = (kk >> 2) * kPtBox + (kk & 3) * 32;
-                        tc_mma(tmem + h * 128, umma_desc(q_base + h * kPtTile + off, 16),
-                               umma_desc(k_base + off, 16), idesc_qk, kk > 0);
-                    }
-                tc_commit(s_full);
-                tc_commit(k_free);
-                // Next K tile once this QK has read the current one.
-                ok = mbar_wait_bounded(k_free, par, kWaitLimitNs, TYB_STATUS_WAIT_TIMEOUT);
-                if (!ok) break;
-                if (j + 1 < ntiles) load_k(j + 1);
-                // P of this tile ready (and O rescaled) -> O_h += P_h . V.
-                ok = mbar_wait_bounded(p_full, par, kWaitLimitNs, TYB_STATUS_WAIT_TIMEOUT) &&
-                     mbar_wait_bounded(v_full, par, kWaitLimitNs, TYB_STATUS_WAIT_TIMEOUT);
-                if (!ok) break;
-                tc_fence_after();
-                for (int h = 0; h < 2; h++)
-#pragma unroll
-                    for (int kk = 0; kk < 8; kk++) {
-                        // P: K-major, keys [16kk, 16kk+16) of the swizzled rows.
-                        const uint32_t poff = (kk >> 2) * kPtBox + (kk & 3) * 32;
-                        // V: MN-major, 16 key rows of 128 bytes per step; the two 64-dim boxes
-                        // are kPtBox apart.
-                        tc_mma(tmem + 256 + h * 128, umma_desc(p_base + h * kPtTile + poff, 16),
-                               umma_desc(v_base + kk * 16 * 128, kPtBox), idesc_pv, (j > 0 || kk > 0));
-                    }
-                tc_commit(pv_done);
-                // Next V tile once this P.V has read the current one.
-                ok = mbar_wait_bounded(pv_done, par, kWaitLimitNs, TYB_STATUS_WAIT_TIMEOUT);
-                if (!ok) break;
-                if (j + 1 < ntiles) load_v(j + 1);
+                if (j >= 2 && !mbar_wait_bounded(&v_free[st], (uint32_t)((j - 2) >> 1) & 1u, kWaitLimitNs,
+                                                 TYB_STATUS_WAIT_TIMEOUT))
+                    break;
+                mbar_arrive_expect_tx(&v_full[st], kPtTile);
+                tma_load_3d(sV + st * kPtTile, &tmap_v, 0, j * kPtKeys, kvh, &v_full[st]);
+                tma_load_3d(sV + st * kPtTile + kPtBox, &tmap_v, 64, j * kPtKeys, kvh, &v_full[st]);
             }
         }
         __syncwarp();
-    } else {
+    } else if (warp == 8) {
+        // ---- MMA issue (one thread); the two heads ping-pong so that one head's softmax
+        // overlaps the other head's tensor-core work.
+        if (lane == 0) {
+            // Descriptors of the operand tiles, built once; a K step of 16 columns within a
+            // 128-byte swizzle atom (32 bytes) or the next 64-column box adds to the start
+            // address field (16-byte units; shared addresses stay below 2^18, so no carry).
+            const uint64_t dq0 = umma_desc(smem_u32(sQ), 16), dq1 = umma_desc(smem_u32(sQ) + kPtTile, 16);
+            const uint64_t dp0 = umma_desc(smem_u32(sP), 16), dp1 = umma_desc(smem_u32(sP) + kPtTile, 16);
+            const uint64_t dk = umma_desc(smem_u32(sK), 16);
+            const uint64_t dv0 = umma_desc(smem_u32(sV), kPtBox), dv1 = umma_desc(smem_u32(sV) + kPtTile, kPtBox);
+            auto qk = [&](int h, int j) {  // S_h = Q_h . K(j)^T
+                const uint64_t dq = h ? dq1 : dq0;
+#pragma unroll
+                for (int kk = 0; kk < 8; kk++) {
+                    const uint32_t off = ((kk >> 2) * kPtBox + (kk & 3) * 32) >> 4;
+                    tc_mma(tmem + h * 128, dq + off, dk + off, idesc_qk, kk > 0);
+                }
+                tc_commit(&s_full[h]);
+            };
+            auto pv = [&](int h, int j) {  // O_h += P_h . V(j)
+                const uint64_t dp = h ? dp1 : dp0;
+                const uint64_t dv = (j & 1) ? dv1 : dv0;
+#pragma unroll
+                for (int kk = 0; kk < 8; kk++) {
+                    const uint32_t poff = ((kk >> 2) * kPtBox + (kk & 3) * 32) >> 4;
+                    tc_mma(tmem + 256 + h * 128, dp + poff, dv + ((kk * 16 * 128) >> 4), idesc_pv, (j > 0 || kk > 0));
+                }
+                tc_commit(&pv_done[h]);
+            };
+            auto wait = [&](uint64_t* bar, uint32_t parity) {
+                const bool ok = mbar_wait_bounded(bar, parity, kWaitLimitNs, TYB_STATUS_WAIT_TIMEOUT);
+                tc_fence_after();
+                return ok;
+            };
+            bool ok = wait(k_full, 0);
+            if (ok) {
+                qk(0, 0);
+                qk(1, 0);
+                tc_commit(k_free);
+            }
+            for (int j = 0; j < ntiles && ok; j++) {
+                const uint32_t par = (uint32_t)j & 1u;
+                const bool more = j + 1 < ntiles;
+                ok = wait(&p_full[0], par) && wait(&v_full[j & 1], (uint32_t)(j >> 1) & 1u);
+                if (!ok) break;
+                pv(0, j);
+                if (more) {
+                    ok = wait(k_full, (uint32_t)(j + 1) & 1u);
+                    if (!ok) break;
+                    qk(0, j + 1);
+                }
+                ok = wait(&p_full[1], par);
+                if (!ok) break;
+                pv(1, j);
+                tc_commit(&v_free[j & 1]);
+                if (more) {
+                    qk(1, j + 1);
+                    tc_commit(k_free);
+                }
+            }
+        }
+        __syncwarp();
+    } else if (warp < 8) {
         // ---- softmax + epilogue: one TMEM lane (row) per thread -----------------------------
         const int h = warp >> 2;
         const int r = 32 * (warp & 3) + lane;  // row = TMEM lane = token t0 + r
@@ -341,6 +467,7 @@ __global__ void __launch_bounds__(kPtThreads, 1)
         const uint32_t s_addr = tmem + lane_base + h * 128;
         const uint32_t o_addr = tmem + lane_base + 256 + h * 128;
         const int qpos = a.pos_offset + t0 + r;
+        const int qmin = a.pos_offset + t0;  // first query position of the item
         float m_run = -INFINITY, l_run = 0.f;
         bool ok = true;
         // A wait that runs out of time ends the loop for the whole warp (the TMEM loads below are
@@ -351,73 +478,58 @@ __global__ void __launch_bounds__(kPtThreads, 1)
         unsigned char* prow = sP + h * kPtTile;
         for (int j = 0; j < ntiles; j++) {
             const uint32_t par = (uint32_t)j & 1u;
-            if (!warp_wait(s_full, par)) {
+            if (!warp_wait(&s_full[h], par)) {
                 ok = false;
                 break;
             }
             tc_fence_after();
-            // Causal mask: key k is visible to query qpos iff k <= qpos (and k < total_kv).
+            float sv[kPtKeys];  // this row of S
+            tmem_ld128(s_addr, sv);
+            // Causal mask (key k visible to query qpos iff k <= qpos, and k < total_kv) --
+            // only tiles that reach past the item's first query or the attended length need it.
             const int k0 = j * kPtKeys;
-            const int vis = min(qpos, a.total_kv - 1) - k0 + 1;  // keys [k0, k0 + vis) visible
-            // Pass 1: row maximum of the scaled scores.
-            float mx = -INFINITY;
-#pragma unroll
-            for (int c = 0; c < 4; c++) {
-                float v[32];
-                tmem_ld32(s_addr + c * 32, v);
-                tmem_wait_ld();
-#pragma unroll
-                for (int i = 0; i < 32; i++)
-                    if (c * 32 + i < vis) mx = fmaxf(mx, v[i] * a.scale_log2);
-            }
-            const float m_new = fmaxf(m_run, mx);
-            const float alpha = pt_exp2(m_run - m_new);  // 0 on the first tile
-            // O of the previous tile must be final before it is rescaled and P overwritten.
+            const bool masked = k0 + kPtKeys - 1 > qmin || k0 + kPtKeys > a.total_kv;
+            const int lim = masked ? min(qpos, a.total_kv - 1) - k0 + 1 : kPtKeys;  // columns [0, lim) visible
+            const float m_tile = (masked ? row_max<true>(sv, lim) : row_max<false>(sv, lim)) * a.scale_log2;
+            // The running maximum moves only when the tile's exceeds it by more than 2^8; below
+            // that the stale one stays (P <= 256: exact in BF16's range and harmless to the FP32
+            // sums), which spares the O rescale on almost every tile.
+            const bool move = m_tile > m_run + 8.f;
+            const float m_new = move ? m_tile : m_run;
+            const float alpha = move ? pt_exp2(m_run - m_new) : 1.f;  // 0 on the first tile
+            const float neg_m = m_new == -INFINITY ? 0.f : -m_new;
+            // P.V of the previous tile has finished by now (the tensor pipe ran it before this
+            // tile's S); the wait orders the P overwrite and the O rescale after it.
             if (j > 0) {
-                if (!warp_wait(pv_done, par ^ 1u)) {
+                if (!warp_wait(&pv_done[h], par ^ 1u)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
+            }
+            const float rowsum = masked ? row_exp<true>(sv, lim, a.scale_log2, neg_m, prow, r)
+                                        : row_exp<false>(sv, lim, a.scale_log2, neg_m, prow, r);
+            // O rescale: the TMEM accesses are warp-collective, so the warp takes the branch if
+            // any of its rows moved (the others multiply by 1).
+            if (j > 0 && __any_sync(0xffffffffu, move)) {
 #pragma unroll
-                for (int c = 0; c < 4; c++) {
-                    float v[32];
-                    tmem_ld32(o_addr + c * 32, v);
-                    tmem_wait_ld();
+                for (int q4 = 0; q4 < 4; q4++) {
+                    float ov[32];
+                    tmem_ld32(o_addr + q4 * 32, ov);
 #pragma unroll
-                    for (int i = 0; i < 32; i++) v[i] *= alpha;
-                    tmem_st32(o_addr + c * 32, v);
+                    for (int c = 0; c < 32; c++) ov[c] *= alpha;
+                    tmem_st32(o_addr + q4 * 32, ov);
                 }
                 tmem_wait_st();
-            }
-            // Pass 2: p = exp2(s - m), summed, packed to BF16 and stored into P's swizzled row.
-            float rowsum = 0.f;
-#pragma unroll
-            for (int c = 0; c < 4; c++) {
-                float v[32];
-                tmem_ld32(s_addr + c * 32, v);
-                tmem_wait_ld();
-                uint32_t pk[16];
-#pragma unroll
-                for (int i = 0; i < 32; i += 2) {
-                    const float p0 = (c * 32 + i < vis) ? pt_exp2(v[i] * a.scale_log2 - m_new) : 0.f;
-                    const float p1 = (c * 32 + i + 1 < vis) ? pt_exp2(v[i + 1] * a.scale_log2 - m_new) : 0.f;
-                    rowsum += p0 + p1;
-                    pk[i >> 1] = pack_bf16x2(p0, p1);
-                }
-#pragma unroll
-                for (int q4 = 0; q4 < 4; q4++)
-                    *reinterpret_cast<uint4*>(prow + sw128_offset(r, c * 32 + 8 * q4)) =
-                        make_uint4(pk[4 * q4], pk[4 * q4 + 1], pk[4 * q4 + 2], pk[4 * q4 + 3]);
             }
             l_run = l_run * alpha + rowsum;
             m_run = m_new;
             fence_proxy_async_smem();
             tc_fence_before();
-            mbar_arrive(p_full);
+            mbar_arrive(&p_full[h]);
         }
         // Epilogue: O / l for this row.
-        if (ok && warp_wait(pv_done, (uint32_t)(ntiles - 1) & 1u)) {
+        if (ok && warp_wait(&pv_done[h], (uint32_t)(ntiles - 1) & 1u)) {
             tc_fence_after();
             const int tok = t0 + r;
             const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
@@ -426,7 +538,6 @@ __global__ void __launch_bounds__(kPtThreads, 1)
             for (int c = 0; c < 4; c++) {
                 float v[32];
                 tmem_ld32(o_addr + c * 32, v);
-                tmem_wait_ld();
                 if (tok < a.Sq) {
                     if (a.out_bf16) {
                         __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(a.out) + ooff + c * 32;
@@ -546,7 +657,7 @@ static bool make_kv_map(CUtensorMap* map, const void* base, int rows, int row_ca
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-constexpr size_t kPtSmemBytes = 6 * (size_t)kPtTile + 128 + 1024;  // tiles + barriers + alignment slack
+constexpr size_t kPtSmemBytes = 7 * (size_t)kPtTile + 128 + 1024;  // tiles + barriers + alignment slack
 
 }  // namespace tyb
 
@@ -572,12 +683,22 @@ extern "C" int tyb_prefill_tc_launch(const void* q, int q_bf16, const float* q_n
                                      void* stream)
 {
     if (Sq <= 0) return 0;
-    static bool attr = false;
-    if (!attr) {
-        cudaError_t e =
-            cudaFuncSetAttribute(prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPtSmemBytes);
+    // Once per device: the shared-memory opt-in, and a check that the kernel was compiled with
+    // the register count its setmaxnreg split was sized for (a split above the launch's
+    // registers would never be granted).
+    static bool ready[64];
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return (int)e;
+    if (dev < 0 || dev >= 64) return (int)cudaErrorInvalidDevice;
+    if (!ready[dev]) {
+        cudaFuncAttributes fa;
+        e = cudaFuncGetAttributes(&fa, prefill_tc_kernel);
         if (e != cudaSuccess) return (int)e;
-        attr = true;
+        if (fa.numRegs != kPtLaunchRegs || fa.maxThreadsPerBlock < kPtThreads) return (int)cudaErrorInvalidConfiguration;
+        e = cudaFuncSetAttribute(prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPtSmemBytes);
+        if (e != cudaSuccess) return (int)e;
+        ready[dev] = true;
     }
     PrefillTcArgs a;
     a.q = q;
