@@ -33,17 +33,7 @@ namespace tyb {
 constexpr int kPtRows = 128;            // query tokens per item (= tensor-core M)
 constexpr int kPtKeys = 128;            // keys per tile (= N of S, K of P.V)
 constexpr int kPtSoftmaxThreads = 256;  // warpgroups 0, 1 (warps 0-3 head 0, 4-7 head 1)
-constexpr int kPtThreads = kPtSoftmaxThreads + 128;  // + warpgroup 2: warp 8 MMA issue, warp 9 TMA
-// Register split (setmaxnreg): the kernel is compiled for kPtLaunchRegs per thread, the
-// issue warpgroup gives registers back and the softmax warpgroups take them, so that a
-// softmax thread holds its whole 128-column S row.  The shares add up to no more than the
-// launch's total (checked on the host against the compiled count before every launch).
-constexpr int kPtLaunchRegs = 168;
-constexpr int kPtIssueRegs = 56;
-constexpr int kPtSoftmaxRegs = 216;
-static_assert(kPtSoftmaxThreads * kPtSoftmaxRegs + 128 * kPtIssueRegs <= kPtThreads * kPtLaunchRegs,
-              "register split exceeds the launch allocation");
-static_assert(2 * kPtSoftmaxRegs + kPtIssueRegs <= 512, "one warp of each warpgroup shares a sub-partition");
+constexpr int kPtThreads = kPtSoftmaxThreads + 64;  // + warp 8: MMA issue, warp 9: TMA
 constexpr int kPtTile = 128 * 128 * 2;  // one 128x128 BF16 operand tile: 32 KB
 constexpr int kPtBox = 128 * 128;       // one 128-row x 64-column swizzled box: 16 KB
 
@@ -83,6 +73,19 @@ __device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t a_desc, uint64_
         "setp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(d_tmem),
         "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0)
+        : "memory");
+}
+
+// D[tmem] (+)= A[tmem] . B[smem desc], kind::f16: A (M rows = TMEM lanes, K = 16 BF16 values
+// packed two per 32-bit column, the lower column index in the low half) read from TMEM.
+__device__ __forceinline__ void tc_mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                          uint32_t accumulate)
+{
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0)
         : "memory");
 }
 
@@ -149,6 +152,18 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32])
         "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
         "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
         : "memory");
+}
+
+__device__ __forceinline__ void tmem_st32u(uint32_t taddr, const uint32_t (&v)[32])
+{
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr), "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_st16u(uint32_t taddr, const uint32_t (&v)[16])
+{
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr), "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+                 : "memory");
 }
 
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
@@ -227,41 +242,45 @@ __device__ __forceinline__ float row_max(const float (&s)[kPtKeys], int lim)
     return fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3]));
 }
 
-// p = exp2(s * scale_log2 + neg_m) on the visible columns (0 on the others), written as BF16
-// into this row of the swizzled P tile; returns the FP32 sum of the row's p.  The affine step
-// and the sum run two columns per instruction (f32x2).
+// p = exp2(s * scale_log2 + neg_m) on the visible columns (0 on the others), packed as BF16
+// pairs into TMEM columns [p_addr, p_addr + 64) of this row (column c / 2 holds keys c, c + 1);
+// returns the FP32 sum of the row's p.  The affine step and the sum run two columns per
+// instruction (f32x2).  The stores are waited for before returning.
 template <bool kMask>
 __device__ __forceinline__ float row_exp(const float (&s)[kPtKeys], int lim, float scale_log2, float neg_m,
-                                         unsigned char* prow, int r)
+                                         uint32_t p_addr)
 {
     const float2 sc = make_float2(scale_log2, scale_log2), nm = make_float2(neg_m, neg_m);
     float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
 #pragma unroll
-    for (int c = 0; c < kPtKeys; c += 8) {
-        float e[8];
+    for (int hf = 0; hf < 4; hf++) {
+        uint32_t pk[16];
 #pragma unroll
-        for (int i = 0; i < 8; i += 2) {
-            float2 x = __ffma2_rn(make_float2(s[c + i], s[c + i + 1]), sc, nm);
+        for (int c = 0; c < 32; c += 4) {
+            const int k = hf * 32 + c;
+            float2 x0 = __ffma2_rn(make_float2(s[k], s[k + 1]), sc, nm);
+            float2 x1 = __ffma2_rn(make_float2(s[k + 2], s[k + 3]), sc, nm);
             if (kMask) {
-                if (c + i >= lim) x.x = -INFINITY;
-                if (c + i + 1 >= lim) x.y = -INFINITY;
+                if (k >= lim) x0.x = -INFINITY;
+                if (k + 1 >= lim) x0.y = -INFINITY;
+                if (k + 2 >= lim) x1.x = -INFINITY;
+                if (k + 3 >= lim) x1.y = -INFINITY;
             }
-            e[i] = pt_exp2(x.x);
-            e[i + 1] = pt_exp2(x.y);
+            const float2 e0 = make_float2(pt_exp2(x0.x), pt_exp2(x0.y));
+            const float2 e1 = make_float2(pt_exp2(x1.x), pt_exp2(x1.y));
+            acc0 = __fadd2_rn(acc0, e0);
+            acc1 = __fadd2_rn(acc1, e1);
+            pk[c / 2] = pack_bf16x2(e0.x, e0.y);
+            pk[c / 2 + 1] = pack_bf16x2(e1.x, e1.y);
         }
-        acc0 = __fadd2_rn(acc0, make_float2(e[0], e[1]));
-        acc1 = __fadd2_rn(acc1, make_float2(e[2], e[3]));
-        acc0 = __fadd2_rn(acc0, make_float2(e[4], e[5]));
-        acc1 = __fadd2_rn(acc1, make_float2(e[6], e[7]));
-        *reinterpret_cast<uint4*>(prow + sw128_offset(r, c)) =
-            make_uint4(pack_bf16x2(e[0], e[1]), pack_bf16x2(e[2], e[3]), pack_bf16x2(e[4], e[5]),
-                       pack_bf16x2(e[6], e[7]));
+        tmem_st16u(p_addr + hf * 16, pk);
     }
+    tmem_wait_st();
     return (acc0.x + acc0.y) + (acc1.x + acc1.y);
 }
 
-// 384 threads (3 warpgroups) launched at 168 registers each, split 216 / 216 / 56 by setmaxnreg.
-__global__ void __maxnreg__(kPtLaunchRegs)
+// 320 threads (10 warps: three share a sub-partition's 16K registers) -> at most 168 registers.
+__global__ void __launch_bounds__(kPtThreads, 1)
     prefill_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
                       const PrefillTcArgs a)
 {
@@ -269,18 +288,17 @@ __global__ void __maxnreg__(kPtLaunchRegs)
     // 1024-byte alignment is required by the 128-byte swizzle atoms.
     unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     unsigned char* sQ = smem;                  // Q0, Q1
-    unsigned char* sP = smem + 2 * kPtTile;    // P0, P1
-    unsigned char* sK = smem + 4 * kPtTile;
-    unsigned char* sV = smem + 5 * kPtTile;    // V stages 0, 1
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 7 * kPtTile);
+    unsigned char* sK = smem + 2 * kPtTile;    // K stages 0, 1
+    unsigned char* sV = smem + 4 * kPtTile;    // V stages 0, 1
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 6 * kPtTile);
     uint64_t* v_full = bars + 0;    // [2] V stage landed
     uint64_t* v_free = bars + 2;    // [2] both P.Vs of the tile in that stage have read it
-    uint64_t* k_full = bars + 4;
-    uint64_t* k_free = bars + 5;    // both QKs of the tile have read K
-    uint64_t* s_full = bars + 6;    // [2] per head: S of the tile is in TMEM
-    uint64_t* p_full = bars + 8;    // [2] per head: P written, O rescaled (128 arrivals)
-    uint64_t* pv_done = bars + 10;  // [2] per head: P.V of the tile finished
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+    uint64_t* k_full = bars + 4;    // [2] K stage landed
+    uint64_t* k_free = bars + 6;    // [2] both QKs of the tile in that stage have read it
+    uint64_t* s_full = bars + 8;    // [2] per head: S of the tile is in TMEM
+    uint64_t* p_full = bars + 10;   // [2] per head: P written, O rescaled (128 arrivals)
+    uint64_t* pv_done = bars + 12;  // [2] per head: P.V of the tile finished
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     // Longest items first: q-tile index descends with blockIdx.
@@ -300,9 +318,9 @@ __global__ void __maxnreg__(kPtLaunchRegs)
                 mbar_init(&s_full[i], 1);
                 mbar_init(&p_full[i], kPtSoftmaxThreads / 2);
                 mbar_init(&pv_done[i], 1);
+                mbar_init(&k_full[i], 1);
+                mbar_init(&k_free[i], 1);
             }
-            mbar_init(k_full, 1);
-            mbar_init(k_free, 1);
             fence_barrier_init();
             fence_proxy_async_smem();
         }
@@ -372,24 +390,18 @@ __global__ void __maxnreg__(kPtLaunchRegs)
     const uint32_t idesc_qk = umma_idesc(false);
     const uint32_t idesc_pv = umma_idesc(true);
 
-    if (warp >= 8) asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kPtIssueRegs));
-    else asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kPtSoftmaxRegs));
-
     if (warp == 9) {
-        // ---- TMA producer (one thread): K single-buffered (refilled as soon as both QKs of
-        // a tile have read it, well before the next QK), V double-buffered (its next tile is
-        // needed right after the current P.Vs, so it is requested one tile ahead).
+        // ---- TMA producer (one thread): K and V double-buffered, each stage refilled as soon
+        // as the MMAs of the tile two back have read it.
         if (lane == 0) {
             for (int j = 0; j < ntiles; j++) {
                 const int st = j & 1;
-                if (j >= 1 && !mbar_wait_bounded(k_free, (uint32_t)(j - 1) & 1u, kWaitLimitNs, TYB_STATUS_WAIT_TIMEOUT))
-                    break;
-                mbar_arrive_expect_tx(k_full, kPtTile);
-                tma_load_3d(sK, &tmap_k, 0, j * kPtKeys, kvh, k_full);
-                tma_load_3d(sK + kPtBox, &tmap_k, 64, j * kPtKeys, kvh, k_full);
-                if (j >= 2 && !mbar_wait_bounded(&v_free[st], (uint32_t)((j - 2) >> 1) & 1u, kWaitLimitNs,
-                                                 TYB_STATUS_WAIT_TIMEOUT))
-                    break;
+                const uint32_t fpar = (uint32_t)((j - 2) >> 1) & 1u;
+                if (j >= 2 && !mbar_wait_bounded(&k_free[st], fpar, kWaitLimitNs, TYB_STATUS_WAIT_TIMEOUT)) break;
+                mbar_arrive_expect_tx(&k_full[st], kPtTile);
+                tma_load_3d(sK + st * kPtTile, &tmap_k, 0, j * kPtKeys, kvh, &k_full[st]);
+                tma_load_3d(sK + st * kPtTile + kPtBox, &tmap_k, 64, j * kPtKeys, kvh, &k_full[st]);
+                if (j >= 2 && !mbar_wait_bounded(&v_free[st], fpar, kWaitLimitNs, TYB_STATUS_WAIT_TIMEOUT)) break;
                 mbar_arrive_expect_tx(&v_full[st], kPtTile);
                 tma_load_3d(sV + st * kPtTile, &tmap_v, 0, j * kPtKeys, kvh, &v_full[st]);
                 tma_load_3d(sV + st * kPtTile + kPtBox, &tmap_v, 64, j * kPtKeys, kvh, &v_full[st]);
@@ -400,15 +412,15 @@ __global__ void __maxnreg__(kPtLaunchRegs)
         // ---- MMA issue (one thread); the two heads ping-pong so that one head's softmax
         // overlaps the other head's tensor-core work.
         if (lane == 0) {
-            // Descriptors of the operand tiles, built once; a K step of 16 columns within a
-            // 128-byte swizzle atom (32 bytes) or the next 64-column box adds to the start
-            // address field (16-byte units; shared addresses stay below 2^18, so no carry).
+            // Descriptors of the shared-memory operand tiles, built once; a K step of 16 columns
+            // within a 128-byte swizzle atom (32 bytes) or the next 64-column box adds to the
+            // start address field (16-byte units; shared addresses stay below 2^18: no carry).
             const uint64_t dq0 = umma_desc(smem_u32(sQ), 16), dq1 = umma_desc(smem_u32(sQ) + kPtTile, 16);
-            const uint64_t dp0 = umma_desc(smem_u32(sP), 16), dp1 = umma_desc(smem_u32(sP) + kPtTile, 16);
-            const uint64_t dk = umma_desc(smem_u32(sK), 16);
+            const uint64_t dk0 = umma_desc(smem_u32(sK), 16), dk1 = umma_desc(smem_u32(sK) + kPtTile, 16);
             const uint64_t dv0 = umma_desc(smem_u32(sV), kPtBox), dv1 = umma_desc(smem_u32(sV) + kPtTile, kPtBox);
             auto qk = [&](int h, int j) {  // S_h = Q_h . K(j)^T
                 const uint64_t dq = h ? dq1 : dq0;
+                const uint64_t dk = (j & 1) ? dk1 : dk0;
 #pragma unroll
                 for (int kk = 0; kk < 8; kk++) {
                     const uint32_t off = ((kk >> 2) * kPtBox + (kk & 3) * 32) >> 4;
@@ -416,14 +428,12 @@ __global__ void __maxnreg__(kPtLaunchRegs)
                 }
                 tc_commit(&s_full[h]);
             };
-            auto pv = [&](int h, int j) {  // O_h += P_h . V(j)
-                const uint64_t dp = h ? dp1 : dp0;
+            auto pv = [&](int h, int j) {  // O_h += P_h . V(j), P_h (BF16) in S_h's first 64 columns
                 const uint64_t dv = (j & 1) ? dv1 : dv0;
 #pragma unroll
-                for (int kk = 0; kk < 8; kk++) {
-                    const uint32_t poff = ((kk >> 2) * kPtBox + (kk & 3) * 32) >> 4;
-                    tc_mma(tmem + 256 + h * 128, dp + poff, dv + ((kk * 16 * 128) >> 4), idesc_pv, (j > 0 || kk > 0));
-                }
+                for (int kk = 0; kk < 8; kk++)
+                    tc_mma_ts(tmem + 256 + h * 128, tmem + h * 128 + kk * 8, dv + ((kk * 16 * 128) >> 4), idesc_pv,
+                              (j > 0 || kk > 0));
                 tc_commit(&pv_done[h]);
             };
             auto wait = [&](uint64_t* bar, uint32_t parity) {
@@ -431,20 +441,23 @@ __global__ void __maxnreg__(kPtLaunchRegs)
                 tc_fence_after();
                 return ok;
             };
-            bool ok = wait(k_full, 0);
+            // The tensor pipe runs this thread's MMAs in issue order: P_h of tile j (in S_h's
+            // columns) is read by P.V(h, j) before QK(h, j + 1) overwrites S_h.
+            bool ok = wait(&k_full[0], 0);
             if (ok) {
                 qk(0, 0);
                 qk(1, 0);
-                tc_commit(k_free);
+                tc_commit(&k_free[0]);
             }
             for (int j = 0; j < ntiles && ok; j++) {
                 const uint32_t par = (uint32_t)j & 1u;
                 const bool more = j + 1 < ntiles;
+                const int nst = (j + 1) & 1;
                 ok = wait(&p_full[0], par) && wait(&v_full[j & 1], (uint32_t)(j >> 1) & 1u);
                 if (!ok) break;
                 pv(0, j);
                 if (more) {
-                    ok = wait(k_full, (uint32_t)(j + 1) & 1u);
+                    ok = wait(&k_full[nst], (uint32_t)((j + 1) >> 1) & 1u);
                     if (!ok) break;
                     qk(0, j + 1);
                 }
@@ -454,7 +467,7 @@ __global__ void __maxnreg__(kPtLaunchRegs)
                 tc_commit(&v_free[j & 1]);
                 if (more) {
                     qk(1, j + 1);
-                    tc_commit(k_free);
+                    tc_commit(&k_free[nst]);
                 }
             }
         }
@@ -475,7 +488,6 @@ __global__ void __maxnreg__(kPtLaunchRegs)
         auto warp_wait = [&](uint64_t* bar, uint32_t parity) {
             return !__any_sync(0xffffffffu, !mbar_wait_bounded(bar, parity, kWaitLimitNs, TYB_STATUS_WAIT_TIMEOUT));
         };
-        unsigned char* prow = sP + h * kPtTile;
         for (int j = 0; j < ntiles; j++) {
             const uint32_t par = (uint32_t)j & 1u;
             if (!warp_wait(&s_full[h], par)) {
@@ -507,8 +519,8 @@ __global__ void __maxnreg__(kPtLaunchRegs)
                 }
                 tc_fence_after();
             }
-            const float rowsum = masked ? row_exp<true>(sv, lim, a.scale_log2, neg_m, prow, r)
-                                        : row_exp<false>(sv, lim, a.scale_log2, neg_m, prow, r);
+            const float rowsum = masked ? row_exp<true>(sv, lim, a.scale_log2, neg_m, s_addr)
+                                        : row_exp<false>(sv, lim, a.scale_log2, neg_m, s_addr);
             // O rescale: the TMEM accesses are warp-collective, so the warp takes the branch if
             // any of its rows moved (the others multiply by 1).
             if (j > 0 && __any_sync(0xffffffffu, move)) {
@@ -524,7 +536,6 @@ __global__ void __maxnreg__(kPtLaunchRegs)
             }
             l_run = l_run * alpha + rowsum;
             m_run = m_new;
-            fence_proxy_async_smem();
             tc_fence_before();
             mbar_arrive(&p_full[h]);
         }
@@ -657,7 +668,7 @@ static bool make_kv_map(CUtensorMap* map, const void* base, int rows, int row_ca
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-constexpr size_t kPtSmemBytes = 7 * (size_t)kPtTile + 128 + 1024;  // tiles + barriers + alignment slack
+constexpr size_t kPtSmemBytes = 6 * (size_t)kPtTile + 128 + 1024;  // tiles + barriers + alignment slack
 
 }  // namespace tyb
 
@@ -683,19 +694,13 @@ extern "C" int tyb_prefill_tc_launch(const void* q, int q_bf16, const float* q_n
                                      void* stream)
 {
     if (Sq <= 0) return 0;
-    // Once per device: the shared-memory opt-in, and a check that the kernel was compiled with
-    // the register count its setmaxnreg split was sized for (a split above the launch's
-    // registers would never be granted).
+    // Once per device: the shared-memory opt-in.
     static bool ready[64];
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return (int)e;
     if (dev < 0 || dev >= 64) return (int)cudaErrorInvalidDevice;
     if (!ready[dev]) {
-        cudaFuncAttributes fa;
-        e = cudaFuncGetAttributes(&fa, prefill_tc_kernel);
-        if (e != cudaSuccess) return (int)e;
-        if (fa.numRegs != kPtLaunchRegs || fa.maxThreadsPerBlock < kPtThreads) return (int)cudaErrorInvalidConfiguration;
         e = cudaFuncSetAttribute(prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPtSmemBytes);
         if (e != cudaSuccess) return (int)e;
         ready[dev] = true;
