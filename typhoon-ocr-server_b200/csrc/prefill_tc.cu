@@ -221,6 +221,37 @@ __device__ __forceinline__ float pt_exp2(float x)
     return y;
 }
 
+// Softmax weight split between the two exp2 units: of every four column pairs of an unmasked
+// tile, kPtEmuPairs are evaluated on the FMA pipe (exp2_fma2) and the rest on the MUFU.
+constexpr int kPtEmuPairs = 0;
+// BF16 packing of P by integer round-half-up (IADD + PRMT) instead of the conversion unit.
+constexpr bool kPtIntPack = false;
+
+// Two BF16 values (round to nearest, ties away from zero) from non-negative finite floats.
+__device__ __forceinline__ uint32_t pack_bf16x2_rna(float lo, float hi)
+{
+    return __byte_perm(__float_as_uint(lo) + 0x8000u, __float_as_uint(hi) + 0x8000u, 0x7632);
+}
+
+// 2^x of two values on the FMA pipe, for x <= 8 (x below -120 is taken as -120: 2^-120 is
+// far below any row sum here).  x = j + f, j = round(x) by the 1.5 * 2^23 shifter, f in
+// [-1/2, 1/2]; 2^f by a cubic fitted to minimise the relative error on that interval
+// (Lawson's iteratively reweighted least squares, max relative error 7.5e-5 after FP32
+// rounding, well inside BF16's 2^-9); 2^j enters through the exponent field.
+__device__ __forceinline__ float2 exp2_fma2(float2 x)
+{
+    x.x = fmaxf(x.x, -120.f);
+    x.y = fmaxf(x.y, -120.f);
+    const float2 t = __fadd2_rn(x, make_float2(12582912.f, 12582912.f));
+    const float2 j = __fadd2_rn(t, make_float2(-12582912.f, -12582912.f));
+    const float2 f = __ffma2_rn(j, make_float2(-1.f, -1.f), x);
+    float2 p = __ffma2_rn(make_float2(0.055171434f, 0.055171434f), f, make_float2(0.24261081f, 0.24261081f));
+    p = __ffma2_rn(p, f, make_float2(0.69326097f, 0.69326097f));
+    p = __ffma2_rn(p, f, make_float2(0.99992812f, 0.99992812f));
+    return make_float2(__int_as_float(__float_as_int(p.x) + (__float_as_int(t.x) << 23)),
+                       __int_as_float(__float_as_int(p.y) + (__float_as_int(t.y) << 23)));
+}
+
 __device__ __forceinline__ float fmax3(float a, float b, float c)
 {
     float d;
@@ -246,12 +277,14 @@ __device__ __forceinline__ float row_max(const float (&s)[kPtKeys], int lim)
 // pairs into TMEM columns [p_addr, p_addr + 64) of this row (column c / 2 holds keys c, c + 1);
 // returns the FP32 sum of the row's p.  The affine step and the sum run two columns per
 // instruction (f32x2).  The stores are waited for before returning.
-template <bool kMask>
+// With kTrack, *xmax receives the largest exponent s * scale_log2 + neg_m of the row.
+template <bool kMask, bool kTrack>
 __device__ __forceinline__ float row_exp(const float (&s)[kPtKeys], int lim, float scale_log2, float neg_m,
-                                         uint32_t p_addr)
+                                         uint32_t p_addr, float* xmax)
 {
     const float2 sc = make_float2(scale_log2, scale_log2), nm = make_float2(neg_m, neg_m);
     float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
+    float xm0 = -INFINITY, xm1 = -INFINITY;
 #pragma unroll
     for (int hf = 0; hf < 4; hf++) {
         uint32_t pk[16];
@@ -266,17 +299,83 @@ __device__ __forceinline__ float row_exp(const float (&s)[kPtKeys], int lim, flo
                 if (k + 2 >= lim) x1.x = -INFINITY;
                 if (k + 3 >= lim) x1.y = -INFINITY;
             }
-            const float2 e0 = make_float2(pt_exp2(x0.x), pt_exp2(x0.y));
-            const float2 e1 = make_float2(pt_exp2(x1.x), pt_exp2(x1.y));
+            if (kTrack) {
+                xm0 = fmax3(xm0, x0.x, x0.y);
+                xm1 = fmax3(xm1, x1.x, x1.y);
+            }
+            const int pair = (c >> 1) & 3;  // pairs c/2, c/2 + 1 of the group of four
+            const float2 e0 = (!kMask && pair < kPtEmuPairs) ? exp2_fma2(x0)
+                                                            : make_float2(pt_exp2(x0.x), pt_exp2(x0.y));
+            const float2 e1 = (!kMask && pair + 1 < kPtEmuPairs) ? exp2_fma2(x1)
+                                                                : make_float2(pt_exp2(x1.x), pt_exp2(x1.y));
             acc0 = __fadd2_rn(acc0, e0);
             acc1 = __fadd2_rn(acc1, e1);
-            pk[c / 2] = pack_bf16x2(e0.x, e0.y);
-            pk[c / 2 + 1] = pack_bf16x2(e1.x, e1.y);
+            pk[c / 2] = kPtIntPack ? pack_bf16x2_rna(e0.x, e0.y) : pack_bf16x2(e0.x, e0.y);
+            pk[c / 2 + 1] = kPtIntPack ? pack_bf16x2_rna(e1.x, e1.y) : pack_bf16x2(e1.x, e1.y);
         }
         tmem_st16u(p_addr + hf * 16, pk);
     }
     tmem_wait_st();
+    if (kTrack) *xmax = fmaxf(xm0, xm1);
     return (acc0.x + acc0.y) + (acc1.x + acc1.y);
+}
+
+// Query rows of one item into shared memory: RMSNorm(q_norm) + rotate_half M-RoPE, rounded to
+// BF16, in the 128-byte-swizzled K-major layout of the QK MMA.  Warp w handles head w / 4 and
+// tokens 32 (w % 4) .. +32; lane l holds dims [4l, 4l + 4) mod 64 of the lower (l < 16) or
+// upper half.  All loads of eight rows go out before any is used (rows past Sq read row Sq - 1
+// and are zeroed), so that their latencies overlap.
+template <bool kBf16>
+__device__ __forceinline__ void load_queries(const PrefillTcArgs& a, unsigned char* sQ, int t0, int kvh, int warp,
+                                             int lane)
+{
+    const int h = warp >> 2;
+    const float4 w = *reinterpret_cast<const float4*>(a.q_norm + 4 * lane);
+    const int jr = 4 * (lane & 15);  // rotary frequency index of this lane's first dim
+#pragma unroll 1
+    for (int i0 = 0; i0 < 32; i0 += 8) {
+        float x[8][4];
+        float4 cv[8], sn[8];
+#pragma unroll
+        for (int u = 0; u < 8; u++) {
+            const int tok = min(t0 + 32 * (warp & 3) + i0 + u, a.Sq - 1);
+            const size_t off = ((size_t)tok * kHq + kGroup * kvh + h) * kD + 4 * lane;
+            if (kBf16) {
+                const uint2 q2 = __ldg(reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(a.q) + off));
+                const float2 f0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&q2.x));
+                const float2 f1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&q2.y));
+                x[u][0] = f0.x; x[u][1] = f0.y; x[u][2] = f1.x; x[u][3] = f1.y;
+            } else {
+                const float4 f = __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(a.q) + off));
+                x[u][0] = f.x; x[u][1] = f.y; x[u][2] = f.z; x[u][3] = f.w;
+            }
+            cv[u] = __ldg(reinterpret_cast<const float4*>(a.cos + (size_t)tok * 64 + jr));
+            sn[u] = __ldg(reinterpret_cast<const float4*>(a.sin + (size_t)tok * 64 + jr));
+        }
+#pragma unroll
+        for (int u = 0; u < 8; u++) {
+            const int r = 32 * (warp & 3) + i0 + u;
+            const bool live = t0 + r < a.Sq;
+            float ss = x[u][0] * x[u][0] + x[u][1] * x[u][1] + x[u][2] * x[u][2] + x[u][3] * x[u][3];
+#pragma unroll
+            for (int o = 16; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+            const float rs = live ? rsqrtf(ss * (1.f / kD) + a.eps) : 0.f;
+            const float y[4] = {x[u][0] * rs * w.x, x[u][1] * rs * w.y, x[u][2] * rs * w.z, x[u][3] * rs * w.w};
+            // rotate_half: lane l < 16 holds dims [4l, 4l+4), lane l+16 the partner dims + 64.
+            float partner[4];
+#pragma unroll
+            for (int e = 0; e < 4; e++) partner[e] = __shfl_xor_sync(0xffffffffu, y[e], 16);
+            const float c4[4] = {cv[u].x, cv[u].y, cv[u].z, cv[u].w};
+            const float s4[4] = {sn[u].x, sn[u].y, sn[u].z, sn[u].w};
+            float z[4];
+#pragma unroll
+            for (int e = 0; e < 4; e++)
+                z[e] = lane < 16 ? y[e] * c4[e] - partner[e] * s4[e]   // x[j] c - x[j+64] s
+                                 : y[e] * c4[e] + partner[e] * s4[e];  // x[j+64] c + x[j] s
+            const uint2 packed = make_uint2(pack_bf16x2(z[0], z[1]), pack_bf16x2(z[2], z[3]));
+            *reinterpret_cast<uint2*>(sQ + h * kPtTile + sw128_offset(r, 4 * lane)) = packed;
+        }
+    }
 }
 
 // 320 threads (10 warps: three share a sub-partition's 16K registers) -> at most 168 registers.
@@ -298,7 +397,8 @@ __global__ void __launch_bounds__(kPtThreads, 1)
     uint64_t* s_full = bars + 8;    // [2] per head: S of the tile is in TMEM
     uint64_t* p_full = bars + 10;   // [2] per head: P written, O rescaled (128 arrivals)
     uint64_t* pv_done = bars + 12;  // [2] per head: P.V of the tile finished
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
+    uint64_t* q_full = bars + 14;   // Q0, Q1 written (256 arrivals)
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 15);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     // Longest items first: q-tile index descends with blockIdx.
@@ -321,6 +421,7 @@ __global__ void __launch_bounds__(kPtThreads, 1)
                 mbar_init(&k_full[i], 1);
                 mbar_init(&k_free[i], 1);
             }
+            mbar_init(q_full, kPtSoftmaxThreads);
             fence_barrier_init();
             fence_proxy_async_smem();
         }
@@ -328,64 +429,22 @@ __global__ void __launch_bounds__(kPtThreads, 1)
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_u32(tmem_slot))
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+        tc_fence_before();
     }
 
-    // ---- queries: RMSNorm(q_norm) + rotate_half M-RoPE, BF16, swizzled into Q0/Q1 ----------
-    if (warp < 8) {
-        float w4[4];
-        {
-            const float4 w = *reinterpret_cast<const float4*>(a.q_norm + 4 * lane);
-            w4[0] = w.x; w4[1] = w.y; w4[2] = w.z; w4[3] = w.w;
-        }
-        const int jr = 4 * (lane & 15);  // rotary frequency index of this lane's first dim
-        for (int i = 0; i < 32; i++) {
-            const int row = warp * 32 + i;  // 0..255: head = row / 128, token = row % 128
-            const int h = row >> 7, r = row & 127;
-            const int tok = t0 + r;
-            float x[4] = {0.f, 0.f, 0.f, 0.f};
-            if (tok < a.Sq) {
-                const size_t off = ((size_t)tok * kHq + kGroup * kvh + h) * kD + 4 * lane;
-                if (a.q_bf16) {
-                    const uint2 u = *reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(a.q) + off);
-                    const __nv_bfloat162* hv = reinterpret_cast<const __nv_bfloat162*>(&u);
-                    const float2 f0 = __bfloat1622float2(hv[0]), f1 = __bfloat1622float2(hv[1]);
-                    x[0] = f0.x; x[1] = f0.y; x[2] = f1.x; x[3] = f1.y;
-                } else {
-                    const float4 f = *reinterpret_cast<const float4*>(static_cast<const float*>(a.q) + off);
-                    x[0] = f.x; x[1] = f.y; x[2] = f.z; x[3] = f.w;
-                }
-            }
-            float ss = x[0] * x[0] + x[1] * x[1] + x[2] * x[2] + x[3] * x[3];
-#pragma unroll
-            for (int o = 16; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-            const float rs = rsqrtf(ss * (1.f / kD) + a.eps);
-            float y[4];
-#pragma unroll
-            for (int e = 0; e < 4; e++) y[e] = x[e] * rs * w4[e];
-            // rotate_half: lane l < 16 holds dims [4l, 4l+4), lane l+16 the partner dims + 64.
-            float partner[4];
-#pragma unroll
-            for (int e = 0; e < 4; e++) partner[e] = __shfl_xor_sync(0xffffffffu, y[e], 16);
-            float c4[4] = {1.f, 1.f, 1.f, 1.f}, s4[4] = {0.f, 0.f, 0.f, 0.f};
-            if (tok < a.Sq) {
-                const float4 c = *reinterpret_cast<const float4*>(a.cos + (size_t)tok * 64 + jr);
-                const float4 s = *reinterpret_cast<const float4*>(a.sin + (size_t)tok * 64 + jr);
-                c4[0] = c.x; c4[1] = c.y; c4[2] = c.z; c4[3] = c.w;
-                s4[0] = s.x; s4[1] = s.y; s4[2] = s.z; s4[3] = s.w;
-            }
-            float z[4];
-#pragma unroll
-            for (int e = 0; e < 4; e++)
-                z[e] = lane < 16 ? y[e] * c4[e] - partner[e] * s4[e]   // x[j] c - x[j+64] s
-                                 : y[e] * c4[e] + partner[e] * s4[e];  // x[j+64] c + x[j] s
-            const uint2 packed = make_uint2(pack_bf16x2(z[0], z[1]), pack_bf16x2(z[2], z[3]));
-            *reinterpret_cast<uint2*>(sQ + h * kPtTile + sw128_offset(r, 4 * lane)) = packed;
-        }
-        fence_proxy_async_smem();  // Q is read by the tensor core (async proxy)
-    }
-    __syncthreads();
+    __syncthreads();  // barriers initialised, TMEM allocated
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+
+    // ---- queries: RMSNorm(q_norm) + rotate_half M-RoPE, BF16, swizzled into Q0/Q1 ----------
+    // Warps 0-7 (warp w: head w / 4, tokens 32 (w % 4) ..+32), while the producer already
+    // streams the first K/V tiles.
+    if (warp < 8) {
+        if (a.q_bf16) load_queries<true>(a, sQ, t0, kvh, warp, lane);
+        else load_queries<false>(a, sQ, t0, kvh, warp, lane);
+        fence_proxy_async_smem();  // Q is read by the tensor core (async proxy)
+        mbar_arrive(q_full);
+    }
 
     const uint32_t idesc_qk = umma_idesc(false);
     const uint32_t idesc_pv = umma_idesc(true);
@@ -443,7 +502,7 @@ __global__ void __launch_bounds__(kPtThreads, 1)
             };
             // The tensor pipe runs this thread's MMAs in issue order: P_h of tile j (in S_h's
             // columns) is read by P.V(h, j) before QK(h, j + 1) overwrites S_h.
-            bool ok = wait(&k_full[0], 0);
+            bool ok = wait(q_full, 0) && wait(&k_full[0], 0);
             if (ok) {
                 qk(0, 0);
                 qk(1, 0);
@@ -502,40 +561,44 @@ __global__ void __launch_bounds__(kPtThreads, 1)
             const int k0 = j * kPtKeys;
             const bool masked = k0 + kPtKeys - 1 > qmin || k0 + kPtKeys > a.total_kv;
             const int lim = masked ? min(qpos, a.total_kv - 1) - k0 + 1 : kPtKeys;  // columns [0, lim) visible
-            const float m_tile = (masked ? row_max<true>(sv, lim) : row_max<false>(sv, lim)) * a.scale_log2;
-            // The running maximum moves only when the tile's exceeds it by more than 2^8; below
-            // that the stale one stays (P <= 256: exact in BF16's range and harmless to the FP32
-            // sums), which spares the O rescale on almost every tile.
-            const bool move = m_tile > m_run + 8.f;
-            const float m_new = move ? m_tile : m_run;
-            const float alpha = move ? pt_exp2(m_run - m_new) : 1.f;  // 0 on the first tile
-            const float neg_m = m_new == -INFINITY ? 0.f : -m_new;
-            // P.V of the previous tile has finished by now (the tensor pipe ran it before this
-            // tile's S); the wait orders the P overwrite and the O rescale after it.
-            if (j > 0) {
-                if (!warp_wait(&pv_done[h], par ^ 1u)) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
-            }
-            const float rowsum = masked ? row_exp<true>(sv, lim, a.scale_log2, neg_m, s_addr)
-                                        : row_exp<false>(sv, lim, a.scale_log2, neg_m, s_addr);
-            // O rescale: the TMEM accesses are warp-collective, so the warp takes the branch if
-            // any of its rows moved (the others multiply by 1).
-            if (j > 0 && __any_sync(0xffffffffu, move)) {
+            // P of this tile overwrites P of the previous one in TMEM: the previous P.V has
+            // completed, since the commit that signalled this S tracks every earlier MMA.
+            if (j == 0) {
+                // First tile: the row maximum starts the running one (every row sees key 0).
+                m_run = (masked ? row_max<true>(sv, lim) : row_max<false>(sv, lim)) * a.scale_log2;
+                const float neg_m = m_run == -INFINITY ? 0.f : -m_run;
+                l_run = masked ? row_exp<true, false>(sv, lim, a.scale_log2, neg_m, s_addr, nullptr)
+                               : row_exp<false, false>(sv, lim, a.scale_log2, neg_m, s_addr, nullptr);
+            } else {
+                // Later tiles: one pass against the running maximum m, tracking the tile's largest
+                // exponent.  The maximum stays stale while no score exceeds it by more than 2^8
+                // (P <= 256: exact in BF16's range and harmless to the FP32 sums); a row that
+                // goes past that takes its new maximum -- P rewritten, O and l rescaled.
+                float xmax;
+                float rowsum = masked ? row_exp<true, true>(sv, lim, a.scale_log2, -m_run, s_addr, &xmax)
+                                      : row_exp<false, true>(sv, lim, a.scale_log2, -m_run, s_addr, &xmax);
+                // The TMEM accesses are warp-collective: the whole warp takes the branch, rows
+                // that keep their maximum rewrite the same P and scale by 1.
+                if (__any_sync(0xffffffffu, xmax > 8.f)) {
+                    const bool move = xmax > 8.f;
+                    const float m_new = move ? m_run + xmax : m_run;
+                    const float alpha = move ? pt_exp2(-xmax) : 1.f;
+                    rowsum = masked ? row_exp<true, false>(sv, lim, a.scale_log2, -m_new, s_addr, nullptr)
+                                    : row_exp<false, false>(sv, lim, a.scale_log2, -m_new, s_addr, nullptr);
 #pragma unroll
-                for (int q4 = 0; q4 < 4; q4++) {
-                    float ov[32];
-                    tmem_ld32(o_addr + q4 * 32, ov);
+                    for (int q4 = 0; q4 < 4; q4++) {
+                        float ov[32];
+                        tmem_ld32(o_addr + q4 * 32, ov);
 #pragma unroll
-                    for (int c = 0; c < 32; c++) ov[c] *= alpha;
-                    tmem_st32(o_addr + q4 * 32, ov);
+                        for (int c = 0; c < 32; c++) ov[c] *= alpha;
+                        tmem_st32(o_addr + q4 * 32, ov);
+                    }
+                    tmem_wait_st();
+                    l_run *= alpha;
+                    m_run = m_new;
                 }
-                tmem_wait_st();
+                l_run += rowsum;
             }
-            l_run = l_run * alpha + rowsum;
-            m_run = m_new;
             tc_fence_before();
             mbar_arrive(&p_full[h]);
         }
