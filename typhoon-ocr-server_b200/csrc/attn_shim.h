@@ -96,6 +96,8 @@ int tyb_kv_scatter_launch(const float *k_src, const float *v_src, void *k_dst, v
 
 /* Copy the status word to *bits after all work on `stream`, then clear it. */
 int tyb_status_fetch(unsigned int *bits, void *stream);
+/* Device address of the status word on the current device (NULL on failure). */
+unsigned int *tyb_status_word(void);
 
 #ifdef __cplusplus
 }

@@ -22,9 +22,13 @@ constexpr float kLog2e = 1.4426950408889634f;
 // Status word shared by every kernel of this library.  Kernels never trap: a wait
 // that runs out of time or an index that fails a check sets a bit here and the
 // kernel returns; the host reads it back (attn_sync, synchronous entry points).
+// Relocatable translation units name the symbol; a whole-program one (TYB_WHOLE_PROGRAM)
+// receives its address (tyb_status_word) as a kernel argument.
+#ifndef TYB_WHOLE_PROGRAM
 extern __device__ unsigned int g_status;
 
 __device__ __forceinline__ void raise_status(unsigned int bits) { atomicOr(&g_status, bits); }
+#endif
 
 __device__ __forceinline__ uint64_t globaltimer_ns()
 {
@@ -132,20 +136,58 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t pari
 }
 
 // Wait for phase `parity` of an mbarrier, giving up after `limit_ns` of wall time.
-// Returns false (and raises `status_bit`) when the limit ran out.
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
-                                                  uint64_t limit_ns, unsigned int status_bit)
+// Returns false (and sets `status_bit` in *status) when the limit ran out.
+__device__ __forceinline__ bool mbar_wait_bounded_to(uint64_t* bar, uint32_t parity, uint64_t limit_ns,
+                                                     unsigned int status_bit, unsigned int* status)
 {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
     while (true) {
         if (mbar_try_wait_sleep(bar, parity, 2000u)) return true;
         if (globaltimer_ns() - t0 > limit_ns) {
-            raise_status(status_bit);
+            atomicOr(status, status_bit);
             return false;
         }
     }
 }
+
+// Non-blocking test of phase `parity`.
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity)
+{
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Like mbar_wait_bounded_to, but polling without suspending: for a single latency-critical
+// thread (it reacts within a few cycles of the phase completing, at the price of issue slots).
+__device__ __forceinline__ bool mbar_spin_bounded_to(uint64_t* bar, uint32_t parity, uint64_t limit_ns,
+                                                     unsigned int status_bit, unsigned int* status)
+{
+    if (mbar_test_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t n = 1;; n++) {
+        if (mbar_test_wait(bar, parity)) return true;
+        if ((n & 255u) == 0 && globaltimer_ns() - t0 > limit_ns) {
+            atomicOr(status, status_bit);
+            return false;
+        }
+    }
+}
+
+#ifndef TYB_WHOLE_PROGRAM
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
+                                                  uint64_t limit_ns, unsigned int status_bit)
+{
+    return mbar_wait_bounded_to(bar, parity, limit_ns, status_bit, &g_status);
+}
+#endif
 
 // 1-D bulk copy global -> this CTA's shared memory, completing on `bar`.
 // Both addresses 16-byte aligned, bytes a multiple of 16.

@@ -58,6 +58,20 @@ extern "C" int tyb_kv_scatter_launch(const float* k_src, const float* v_src, voi
     return (int)cudaGetLastError();
 }
 
+extern "C" unsigned int* tyb_status_word(void)
+{
+    // Device address of the status word on the current device (looked up once per device).
+    static unsigned int* addr[64];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    if (!addr[dev]) {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_status) != cudaSuccess) return nullptr;
+        addr[dev] = static_cast<unsigned int*>(p);
+    }
+    return addr[dev];
+}
+
 extern "C" int tyb_status_fetch(unsigned int* bits, void* stream)
 {
     // One pinned word per process receives the status copy, so the read is queued behind

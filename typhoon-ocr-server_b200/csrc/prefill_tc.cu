@@ -26,6 +26,7 @@
 // loops, frees its TMEM and returns.
 #include <cuda.h>
 
+#define TYB_WHOLE_PROGRAM
 #include "common.cuh"
 
 namespace tyb {
@@ -33,7 +34,18 @@ namespace tyb {
 constexpr int kPtRows = 128;            // query tokens per item (= tensor-core M)
 constexpr int kPtKeys = 128;            // keys per tile (= N of S, K of P.V)
 constexpr int kPtSoftmaxThreads = 256;  // warpgroups 0, 1 (warps 0-3 head 0, 4-7 head 1)
-constexpr int kPtThreads = kPtSoftmaxThreads + 64;  // + warp 8: MMA issue, warp 9: TMA
+constexpr int kPtThreads = kPtSoftmaxThreads + 128;  // + warpgroup 2: warp 8 MMA issue, warp 9 TMA
+// Register split (setmaxnreg): the kernel is launched at kPtLaunchRegs per thread; the issue
+// warpgroup drops to kPtIssueRegs and the two softmax warpgroups rise to kPtSoftmaxRegs, so
+// that a softmax thread keeps its 128-column S row in registers with room to spare.  The
+// shares fit the launch's registers (checked against the compiled count before launching),
+// and a warp of each warpgroup shares every sub-partition's 512 registers per lane.
+constexpr int kPtLaunchRegs = 168;
+constexpr int kPtIssueRegs = 96;
+constexpr int kPtSoftmaxRegs = 200;
+static_assert(kPtSoftmaxThreads * kPtSoftmaxRegs + 128 * kPtIssueRegs <= kPtThreads * kPtLaunchRegs,
+              "register split exceeds the launch allocation");
+static_assert(2 * kPtSoftmaxRegs + kPtIssueRegs <= 512, "register split exceeds a sub-partition");
 constexpr int kPtTile = 128 * 128 * 2;  // one 128x128 BF16 operand tile: 32 KB
 constexpr int kPtBox = 128 * 128;       // one 128-row x 64-column swizzled box: 16 KB
 
@@ -51,6 +63,7 @@ struct PrefillTcArgs {
     int n_qtiles;
     float scale_log2;
     float eps;
+    unsigned int* status;  // the library's status word (tyb_status_word)
 };
 
 // ---- tcgen05 / TMA primitives ---------------------------------------------------------
@@ -378,7 +391,7 @@ __device__ __forceinline__ void load_queries(const PrefillTcArgs& a, unsigned ch
     }
 }
 
-// 320 threads (10 warps: three share a sub-partition's 16K registers) -> at most 168 registers.
+// 384 threads (3 warpgroups) launched at 168 registers, split 200 / 200 / 96 by setmaxnreg.
 __global__ void __launch_bounds__(kPtThreads, 1)
     prefill_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
                       const PrefillTcArgs a)
@@ -398,7 +411,8 @@ __global__ void __launch_bounds__(kPtThreads, 1)
     uint64_t* p_full = bars + 10;   // [2] per head: P written, O rescaled (128 arrivals)
     uint64_t* pv_done = bars + 12;  // [2] per head: P.V of the tile finished
     uint64_t* q_full = bars + 14;   // Q0, Q1 written (256 arrivals)
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 15);
+    uint64_t* e_done = bars + 15;   // [2] per head: exponentials of the tile done (128 arrivals)
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     // Longest items first: q-tile index descends with blockIdx.
@@ -422,6 +436,8 @@ __global__ void __launch_bounds__(kPtThreads, 1)
                 mbar_init(&k_free[i], 1);
             }
             mbar_init(q_full, kPtSoftmaxThreads);
+            mbar_init(&e_done[0], kPtSoftmaxThreads / 2);
+            mbar_init(&e_done[1], kPtSoftmaxThreads / 2);
             fence_barrier_init();
             fence_proxy_async_smem();
         }
@@ -436,102 +452,106 @@ __global__ void __launch_bounds__(kPtThreads, 1)
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    // ---- queries: RMSNorm(q_norm) + rotate_half M-RoPE, BF16, swizzled into Q0/Q1 ----------
-    // Warps 0-7 (warp w: head w / 4, tokens 32 (w % 4) ..+32), while the producer already
-    // streams the first K/V tiles.
-    if (warp < 8) {
-        if (a.q_bf16) load_queries<true>(a, sQ, t0, kvh, warp, lane);
-        else load_queries<false>(a, sQ, t0, kvh, warp, lane);
-        fence_proxy_async_smem();  // Q is read by the tensor core (async proxy)
-        mbar_arrive(q_full);
-    }
-
     const uint32_t idesc_qk = umma_idesc(false);
     const uint32_t idesc_pv = umma_idesc(true);
 
-    if (warp == 9) {
-        // ---- TMA producer (one thread): K and V double-buffered, each stage refilled as soon
-        // as the MMAs of the tile two back have read it.
-        if (lane == 0) {
-            for (int j = 0; j < ntiles; j++) {
-                const int st = j & 1;
-                const uint32_t fpar = (uint32_t)((j - 2) >> 1) & 1u;
-                if (j >= 2 && !mbar_wait_bounded(&k_free[st], fpar, kWaitLimitNs, TYB_STATUS_WAIT_TIMEOUT)) break;
-                mbar_arrive_expect_tx(&k_full[st], kPtTile);
-                tma_load_3d(sK + st * kPtTile, &tmap_k, 0, j * kPtKeys, kvh, &k_full[st]);
-                tma_load_3d(sK + st * kPtTile + kPtBox, &tmap_k, 64, j * kPtKeys, kvh, &k_full[st]);
-                if (j >= 2 && !mbar_wait_bounded(&v_free[st], fpar, kWaitLimitNs, TYB_STATUS_WAIT_TIMEOUT)) break;
-                mbar_arrive_expect_tx(&v_full[st], kPtTile);
-                tma_load_3d(sV + st * kPtTile, &tmap_v, 0, j * kPtKeys, kvh, &v_full[st]);
-                tma_load_3d(sV + st * kPtTile + kPtBox, &tmap_v, 64, j * kPtKeys, kvh, &v_full[st]);
-            }
-        }
-        __syncwarp();
-    } else if (warp == 8) {
-        // ---- MMA issue (one thread); the two heads ping-pong so that one head's softmax
-        // overlaps the other head's tensor-core work.
-        if (lane == 0) {
-            // Descriptors of the shared-memory operand tiles, built once; a K step of 16 columns
-            // within a 128-byte swizzle atom (32 bytes) or the next 64-column box adds to the
-            // start address field (16-byte units; shared addresses stay below 2^18: no carry).
-            const uint64_t dq0 = umma_desc(smem_u32(sQ), 16), dq1 = umma_desc(smem_u32(sQ) + kPtTile, 16);
-            const uint64_t dk0 = umma_desc(smem_u32(sK), 16), dk1 = umma_desc(smem_u32(sK) + kPtTile, 16);
-            const uint64_t dv0 = umma_desc(smem_u32(sV), kPtBox), dv1 = umma_desc(smem_u32(sV) + kPtTile, kPtBox);
-            auto qk = [&](int h, int j) {  // S_h = Q_h . K(j)^T
-                const uint64_t dq = h ? dq1 : dq0;
-                const uint64_t dk = (j & 1) ? dk1 : dk0;
-#pragma unroll
-                for (int kk = 0; kk < 8; kk++) {
-                    const uint32_t off = ((kk >> 2) * kPtBox + (kk & 3) * 32) >> 4;
-                    tc_mma(tmem + h * 128, dq + off, dk + off, idesc_qk, kk > 0);
+    if (warp >= 8) {
+        asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kPtIssueRegs));
+        if (warp == 9) {
+            // ---- TMA producer (one thread): K and V double-buffered, each stage refilled as soon
+            // as the MMAs of the tile two back have read it.
+            if (lane == 0) {
+                for (int j = 0; j < ntiles; j++) {
+                    const int st = j & 1;
+                    const uint32_t fpar = (uint32_t)((j - 2) >> 1) & 1u;
+                    if (j >= 2 && !mbar_wait_bounded_to(&k_free[st], fpar, kWaitLimitNs, TYB_STATUS_WAIT_TIMEOUT, a.status)) break;
+                    mbar_arrive_expect_tx(&k_full[st], kPtTile);
+                    tma_load_3d(sK + st * kPtTile, &tmap_k, 0, j * kPtKeys, kvh, &k_full[st]);
+                    tma_load_3d(sK + st * kPtTile + kPtBox, &tmap_k, 64, j * kPtKeys, kvh, &k_full[st]);
+                    if (j >= 2 && !mbar_wait_bounded_to(&v_free[st], fpar, kWaitLimitNs, TYB_STATUS_WAIT_TIMEOUT, a.status)) break;
+                    mbar_arrive_expect_tx(&v_full[st], kPtTile);
+                    tma_load_3d(sV + st * kPtTile, &tmap_v, 0, j * kPtKeys, kvh, &v_full[st]);
+                    tma_load_3d(sV + st * kPtTile + kPtBox, &tmap_v, 64, j * kPtKeys, kvh, &v_full[st]);
                 }
-                tc_commit(&s_full[h]);
-            };
-            auto pv = [&](int h, int j) {  // O_h += P_h . V(j), P_h (BF16) in S_h's first 64 columns
-                const uint64_t dv = (j & 1) ? dv1 : dv0;
-#pragma unroll
-                for (int kk = 0; kk < 8; kk++)
-                    tc_mma_ts(tmem + 256 + h * 128, tmem + h * 128 + kk * 8, dv + ((kk * 16 * 128) >> 4), idesc_pv,
-                              (j > 0 || kk > 0));
-                tc_commit(&pv_done[h]);
-            };
-            auto wait = [&](uint64_t* bar, uint32_t parity) {
-                const bool ok = mbar_wait_bounded(bar, parity, kWaitLimitNs, TYB_STATUS_WAIT_TIMEOUT);
-                tc_fence_after();
-                return ok;
-            };
-            // The tensor pipe runs this thread's MMAs in issue order: P_h of tile j (in S_h's
-            // columns) is read by P.V(h, j) before QK(h, j + 1) overwrites S_h.
-            bool ok = wait(q_full, 0) && wait(&k_full[0], 0);
-            if (ok) {
-                qk(0, 0);
-                qk(1, 0);
-                tc_commit(&k_free[0]);
             }
-            for (int j = 0; j < ntiles && ok; j++) {
-                const uint32_t par = (uint32_t)j & 1u;
-                const bool more = j + 1 < ntiles;
-                const int nst = (j + 1) & 1;
-                ok = wait(&p_full[0], par) && wait(&v_full[j & 1], (uint32_t)(j >> 1) & 1u);
-                if (!ok) break;
-                pv(0, j);
-                if (more) {
-                    ok = wait(&k_full[nst], (uint32_t)((j + 1) >> 1) & 1u);
+            __syncwarp();
+        } else if (warp == 8) {
+            // ---- MMA issue (one thread); the two heads ping-pong so that one head's softmax
+            // overlaps the other head's tensor-core work.
+            if (lane == 0) {
+                // Descriptors of the shared-memory operand tiles, built once; a K step of 16 columns
+                // within a 128-byte swizzle atom (32 bytes) or the next 64-column box adds to the
+                // start address field (16-byte units; shared addresses stay below 2^18: no carry).
+                const uint64_t dq0 = umma_desc(smem_u32(sQ), 16), dq1 = umma_desc(smem_u32(sQ) + kPtTile, 16);
+                const uint64_t dk0 = umma_desc(smem_u32(sK), 16), dk1 = umma_desc(smem_u32(sK) + kPtTile, 16);
+                const uint64_t dv0 = umma_desc(smem_u32(sV), kPtBox), dv1 = umma_desc(smem_u32(sV) + kPtTile, kPtBox);
+                auto qk = [&](int h, int j) {  // S_h = Q_h . K(j)^T
+                    const uint64_t dq = h ? dq1 : dq0;
+                    const uint64_t dk = (j & 1) ? dk1 : dk0;
+    #pragma unroll
+                    for (int kk = 0; kk < 8; kk++) {
+                        const uint32_t off = ((kk >> 2) * kPtBox + (kk & 3) * 32) >> 4;
+                        tc_mma(tmem + h * 128, dq + off, dk + off, idesc_qk, kk > 0);
+                    }
+                    tc_commit(&s_full[h]);
+                };
+                auto pv = [&](int h, int j) {  // O_h += P_h . V(j), P_h (BF16) in S_h's first 64 columns
+                    const uint64_t dv = (j & 1) ? dv1 : dv0;
+    #pragma unroll
+                    for (int kk = 0; kk < 8; kk++)
+                        tc_mma_ts(tmem + 256 + h * 128, tmem + h * 128 + kk * 8, dv + ((kk * 16 * 128) >> 4), idesc_pv,
+                                  (j > 0 || kk > 0));
+                    tc_commit(&pv_done[h]);
+                };
+                auto wait = [&](uint64_t* bar, uint32_t parity) {
+                    const bool ok = mbar_wait_bounded_to(bar, parity, kWaitLimitNs, TYB_STATUS_WAIT_TIMEOUT, a.status);
+                    tc_fence_after();
+                    return ok;
+                };
+                // The tensor pipe runs this thread's MMAs in issue order: P_h of tile j (in S_h's
+                // columns) is read by P.V(h, j) before QK(h, j + 1) overwrites S_h.
+                bool ok = wait(q_full, 0) && wait(&k_full[0], 0);
+                if (ok) {
+                    qk(0, 0);
+                    qk(1, 0);
+                    tc_commit(&k_free[0]);
+                }
+                for (int j = 0; j < ntiles && ok; j++) {
+                    const uint32_t par = (uint32_t)j & 1u;
+                    const bool more = j + 1 < ntiles;
+                    const int nst = (j + 1) & 1;
+                    ok = wait(&p_full[0], par) && wait(&v_full[j & 1], (uint32_t)(j >> 1) & 1u);
                     if (!ok) break;
-                    qk(0, j + 1);
-                }
-                ok = wait(&p_full[1], par);
-                if (!ok) break;
-                pv(1, j);
-                tc_commit(&v_free[j & 1]);
-                if (more) {
-                    qk(1, j + 1);
-                    tc_commit(&k_free[nst]);
+                    pv(0, j);
+                    if (more) {
+                        ok = wait(&k_full[nst], (uint32_t)((j + 1) >> 1) & 1u);
+                        if (!ok) break;
+                        qk(0, j + 1);
+                    }
+                    ok = wait(&p_full[1], par);
+                    if (!ok) break;
+                    pv(1, j);
+                    tc_commit(&v_free[j & 1]);
+                    if (more) {
+                        qk(1, j + 1);
+                        tc_commit(&k_free[nst]);
+                    }
                 }
             }
+            __syncwarp();
         }
-        __syncwarp();
-    } else if (warp < 8) {
+    } else {
+        asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kPtSoftmaxRegs));
+        // ---- queries: RMSNorm(q_norm) + rotate_half M-RoPE, BF16, swizzled into Q0/Q1 ----------
+        // Warps 0-7 (warp w: head w / 4, tokens 32 (w % 4) ..+32), while the producer already
+        // streams the first K/V tiles.
+        {
+            if (a.q_bf16) load_queries<true>(a, sQ, t0, kvh, warp, lane);
+            else load_queries<false>(a, sQ, t0, kvh, warp, lane);
+            fence_proxy_async_smem();  // Q is read by the tensor core (async proxy)
+            mbar_arrive(q_full);
+        }
+
         // ---- softmax + epilogue: one TMEM lane (row) per thread -----------------------------
         const int h = warp >> 2;
         const int r = 32 * (warp & 3) + lane;  // row = TMEM lane = token t0 + r
@@ -545,7 +565,8 @@ __global__ void __launch_bounds__(kPtThreads, 1)
         // A wait that runs out of time ends the loop for the whole warp (the TMEM loads below are
         // warp-collective).
         auto warp_wait = [&](uint64_t* bar, uint32_t parity) {
-            return !__any_sync(0xffffffffu, !mbar_wait_bounded(bar, parity, kWaitLimitNs, TYB_STATUS_WAIT_TIMEOUT));
+            return !__any_sync(0xffffffffu,
+                               !mbar_wait_bounded_to(bar, parity, kWaitLimitNs, TYB_STATUS_WAIT_TIMEOUT, a.status));
         };
         for (int j = 0; j < ntiles; j++) {
             const uint32_t par = (uint32_t)j & 1u;
@@ -561,6 +582,15 @@ __global__ void __launch_bounds__(kPtThreads, 1)
             const int k0 = j * kPtKeys;
             const bool masked = k0 + kPtKeys - 1 > qmin || k0 + kPtKeys > a.total_kv;
             const int lim = masked ? min(qpos, a.total_kv - 1) - k0 + 1 : kPtKeys;  // columns [0, lim) visible
+            // The two heads take turns on the exponential unit (a warp of each shares every
+            // sub-partition): head 0 runs tile j after head 1's tile j - 1, head 1 after head
+            // 0's tile j, so that each pass has the unit to itself.
+            if (h == 1 || j > 0) {
+                if (!warp_wait(&e_done[h ^ 1], (uint32_t)(h == 0 ? j - 1 : j) & 1u)) {
+                    ok = false;
+                    break;
+                }
+            }
             // P of this tile overwrites P of the previous one in TMEM: the previous P.V has
             // completed, since the commit that signalled this S tracks every earlier MMA.
             if (j == 0) {
@@ -570,21 +600,18 @@ __global__ void __launch_bounds__(kPtThreads, 1)
                 l_run = masked ? row_exp<true, false>(sv, lim, a.scale_log2, neg_m, s_addr, nullptr)
                                : row_exp<false, false>(sv, lim, a.scale_log2, neg_m, s_addr, nullptr);
             } else {
-                // Later tiles: one pass against the running maximum m, tracking the tile's largest
-                // exponent.  The maximum stays stale while no score exceeds it by more than 2^8
-                // (P <= 256: exact in BF16's range and harmless to the FP32 sums); a row that
-                // goes past that takes its new maximum -- P rewritten, O and l rescaled.
-                float xmax;
-                float rowsum = masked ? row_exp<true, true>(sv, lim, a.scale_log2, -m_run, s_addr, &xmax)
-                                      : row_exp<false, true>(sv, lim, a.scale_log2, -m_run, s_addr, &xmax);
-                // The TMEM accesses are warp-collective: the whole warp takes the branch, rows
-                // that keep their maximum rewrite the same P and scale by 1.
-                if (__any_sync(0xffffffffu, xmax > 8.f)) {
-                    const bool move = xmax > 8.f;
-                    const float m_new = move ? m_run + xmax : m_run;
-                    const float alpha = move ? pt_exp2(-xmax) : 1.f;
-                    rowsum = masked ? row_exp<true, false>(sv, lim, a.scale_log2, -m_new, s_addr, nullptr)
-                                    : row_exp<false, false>(sv, lim, a.scale_log2, -m_new, s_addr, nullptr);
+                // Later tiles: the running maximum moves only when the tile's exceeds it by more
+                // than 2^8; below that the stale one stays (P <= 256: exact in BF16's range and
+                // harmless to the FP32 sums), which spares the O rescale on almost every tile.
+                const float m_tile = (masked ? row_max<true>(sv, lim) : row_max<false>(sv, lim)) * a.scale_log2;
+                const bool move = m_tile > m_run + 8.f;
+                const float m_new = move ? m_tile : m_run;
+                const float alpha = move ? pt_exp2(m_run - m_new) : 1.f;
+                const float rowsum = masked ? row_exp<true, false>(sv, lim, a.scale_log2, -m_new, s_addr, nullptr)
+                                            : row_exp<false, false>(sv, lim, a.scale_log2, -m_new, s_addr, nullptr);
+                // O rescale: the TMEM accesses are warp-collective, so the warp takes the branch
+                // if any of its rows moved (the others multiply by 1).
+                if (__any_sync(0xffffffffu, move)) {
 #pragma unroll
                     for (int q4 = 0; q4 < 4; q4++) {
                         float ov[32];
@@ -594,11 +621,11 @@ __global__ void __launch_bounds__(kPtThreads, 1)
                         tmem_st32(o_addr + q4 * 32, ov);
                     }
                     tmem_wait_st();
-                    l_run *= alpha;
-                    m_run = m_new;
                 }
-                l_run += rowsum;
+                l_run = l_run * alpha + rowsum;
+                m_run = m_new;
             }
+            mbar_arrive(&e_done[h]);
             tc_fence_before();
             mbar_arrive(&p_full[h]);
         }
@@ -731,7 +758,7 @@ static bool make_kv_map(CUtensorMap* map, const void* base, int rows, int row_ca
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-constexpr size_t kPtSmemBytes = 6 * (size_t)kPtTile + 128 + 1024;  // tiles + barriers + alignment slack
+constexpr size_t kPtSmemBytes = 6 * (size_t)kPtTile + 256 + 1024;  // tiles + barriers + alignment slack
 
 }  // namespace tyb
 
@@ -757,13 +784,19 @@ extern "C" int tyb_prefill_tc_launch(const void* q, int q_bf16, const float* q_n
                                      void* stream)
 {
     if (Sq <= 0) return 0;
-    // Once per device: the shared-memory opt-in.
+    // Once per device: the shared-memory opt-in, and a check that the kernel was compiled
+    // for the launch register count its setmaxnreg split is sized against (a split above
+    // the launch's registers would never be granted).
     static bool ready[64];
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return (int)e;
     if (dev < 0 || dev >= 64) return (int)cudaErrorInvalidDevice;
     if (!ready[dev]) {
+        cudaFuncAttributes fa;
+        e = cudaFuncGetAttributes(&fa, prefill_tc_kernel);
+        if (e != cudaSuccess) return (int)e;
+        if (fa.numRegs != kPtLaunchRegs || fa.maxThreadsPerBlock < kPtThreads) return (int)cudaErrorInvalidConfiguration;
         e = cudaFuncSetAttribute(prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPtSmemBytes);
         if (e != cudaSuccess) return (int)e;
         ready[dev] = true;
@@ -782,6 +815,8 @@ extern "C" int tyb_prefill_tc_launch(const void* q, int q_bf16, const float* q_n
     a.n_qtiles = (Sq + kPtRows - 1) / kPtRows;
     a.scale_log2 = scale * kLog2e;
     a.eps = eps;
+    a.status = tyb_status_word();
+    if (!a.status) return (int)cudaErrorInvalidSymbol;
     CUtensorMap mk, mv;
     if (!make_kv_map(&mk, k_cache, a.total_kv, row_capacity) || !make_kv_map(&mv, v_cache, a.total_kv, row_capacity))
         return (int)cudaErrorInvalidValue;
