@@ -457,6 +457,59 @@ def run_reference_arm(args):
     print(json.dumps(line))
 
 
+def run_case(case):
+    """Small, fixed invocations of one hot kernel for profiler captures (ncu): no timing.
+      decode-small   4 decode steps of config 2 (28 layers, BF16 cache filled to 4,096 rows, 470 MB
+                     of K/V: larger than L2) through attention_decode_append_gqa, device buffers
+      prefill-small  4 passes of one config-3 layer (4,096 tokens) through attention_prefill_fused_gqa
+    """
+    import torch
+    pkg = _pkg()
+    lib = pkg.load_attention_lib()
+    vp = lambda t: ctypes.c_void_p(t.data_ptr())
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(1)
+    if case == "decode-small":
+        h = lib.kv_cache_alloc_ex(PREFILLED + 64, pkg.ATTN_KV_BF16)
+        cs = pkg.cache_struct(h)
+        rows = (0.5 * torch.randn((PREFILLED, HKV, D), generator=gen, device="cuda")).float()
+        for layer in range(LAYERS):
+            cs.seq_len = 0
+            lib.kv_cache_append_prefill(h, layer, vp(rows), vp(rows), PREFILLED)
+        q = torch.randn((HQ, D), generator=gen, device="cuda")
+        kn = torch.randn((HKV, D), generator=gen, device="cuda")
+        vn = torch.randn((HKV, D), generator=gen, device="cuda")
+        out = torch.empty((HQ, D), device="cuda")
+        for _ in range(4):
+            cs.seq_len = PREFILLED
+            for layer in range(LAYERS):
+                if lib.attention_decode_append_gqa(vp(q), vp(kn), vp(vn), h, vp(out), layer, ctypes.c_float(pkg.SCALE)):
+                    raise RuntimeError(pkg.last_error(lib))
+    elif case == "prefill-small":
+        S = 4096
+        q = (0.5 * torch.randn((S, HQ, D), generator=gen, device="cuda")).bfloat16()
+        k = (0.5 * torch.randn((S, HKV, D), generator=gen, device="cuda")).bfloat16()
+        v = (0.5 * torch.randn((S, HKV, D), generator=gen, device="cuda")).bfloat16()
+        qn, kn = torch.ones(D, device="cuda"), torch.ones(D, device="cuda")
+        ang = torch.arange(S, device="cuda", dtype=torch.float32)[:, None] * torch.ones(64, device="cuda")[None, :]
+        cos, sin = torch.cos(ang).contiguous(), torch.sin(ang).contiguous()
+        out = torch.empty((S, HQ, D), device="cuda", dtype=torch.bfloat16)
+        h = lib.kv_cache_alloc_ex(S, pkg.ATTN_KV_BF16)
+        cs = pkg.cache_struct(h)
+        for _ in range(4):
+            cs.seq_len = 0
+            if lib.attention_prefill_fused_gqa(vp(q), vp(k), vp(v), pkg.ATTN_DT_BF16, vp(qn), vp(kn), vp(cos), vp(sin),
+                                               h, 0, vp(out), pkg.ATTN_DT_BF16, S, ctypes.c_float(pkg.SCALE),
+                                               ctypes.c_float(pkg.RMS_EPS)):
+                raise RuntimeError(pkg.last_error(lib))
+    else:
+        raise SystemExit(f"unknown case {case}")
+    if lib.attn_sync():
+        raise RuntimeError(pkg.last_error(lib))
+    lib.kv_cache_free(h)
+    print(json.dumps({"case": case, "status": "ok"}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -466,7 +519,12 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=200)
     ap.add_argument("--cpu-budget", type=float, default=12.0)
     ap.add_argument("--prefill-pages", type=int, default=20)
+    ap.add_argument("--case", choices=["decode-small", "prefill-small"],
+                    help="run a small fixed invocation of one kernel (for profiler captures) and exit")
     args = ap.parse_args()
+    if args.case:
+        run_case(args.case)
+        return
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     if args.impl == "reference":
@@ -549,7 +607,7 @@ def main():
         "roofline": {
             "bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
             "frac": achieved / hbm_peak, "traffic": profile_traffic("bf16"),
-            "kernel": "decode_cluster_kernel<bf16>",
+            "kernel": "decode_split_kernel<bf16>",
             "note": f"algorithmic bytes (K+V rows + q/out) / mean launch time incl. gaps; peak {peak_src}",
         },
         "e2e": {"value": e2e_max * 1e3 / args.e2e_steps, "unit": "us/step", "h2d_bytes_per_step": h2d,

@@ -258,3 +258,73 @@ def test_decode_long_context_bf16(pkg, lib, oracle):
         lib.kv_cache_free(h)
     want = oracle.decode(q, head_first(bf16_round(k)), head_first(bf16_round(v)), kv_len)
     assert max_abs(out, want) <= TOL_MAX and rel_l2(out, want) <= TOL_REL
+
+
+def _pinned(a):
+    """A page-locked host copy of `a` (the decode entry points read and write such buffers in
+    place through their device mapping instead of copying them)."""
+    t = torch.from_numpy(np.ascontiguousarray(a)).pin_memory()
+    assert t.is_pinned()
+    return t
+
+
+@pytest.mark.parametrize("kv_len", [0, 1, 129, 4097])
+def test_decode_pinned_host_buffers(pkg, lib, oracle, kv_len):
+    rng = np.random.default_rng(5000 + kv_len)
+    max_seq = kv_len + 3
+    q = rng.standard_normal((16, 128), dtype=np.float32)
+    k = rng.standard_normal((max_seq, 8, 128), dtype=np.float32)
+    v = rng.standard_normal((max_seq, 8, 128), dtype=np.float32)
+    h = new_cache(pkg, lib, max_seq, pkg.ATTN_KV_F32)
+    try:
+        fill_layer(pkg, lib, h, 11, k, v)
+        qp, op = _pinned(q), _pinned(np.full((16, 128), 3.0, dtype=np.float32))
+        lib.attention_decode_gqa(vp(qp), h, vp(op), 11, kv_len, SCALE)
+        check(pkg, lib, "decode pinned")
+        out_pinned = op.numpy().copy()
+        # page-locked input with a pageable output, and the reverse
+        out_mixed = np.zeros((16, 128), dtype=np.float32)
+        lib.attention_decode_gqa(vp(qp), h, vp(out_mixed), 11, kv_len, SCALE)
+        check(pkg, lib, "decode pinned q")
+        op2 = _pinned(np.zeros((16, 128), dtype=np.float32))
+        lib.attention_decode_gqa(vp(q), h, vp(op2), 11, kv_len, SCALE)
+        check(pkg, lib, "decode pinned out")
+    finally:
+        lib.kv_cache_free(h)
+    if kv_len == 0:
+        want = np.zeros((16, 128), dtype=np.float32)
+        assert not out_pinned.any() and not out_mixed.any() and not op2.numpy().any()
+        return
+    want = oracle.decode(q, head_first(k), head_first(v), kv_len)
+    for got in (out_pinned, out_mixed, op2.numpy()):
+        assert max_abs(got, want) <= TOL_MAX and rel_l2(got, want) <= TOL_REL
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+@pytest.mark.parametrize("pos", [0, 700, 4096])
+def test_decode_append_pinned_host_buffers(pkg, lib, oracle, dtype, pos):
+    kv_dt = pkg.ATTN_KV_F32 if dtype == "f32" else pkg.ATTN_KV_BF16
+    rng = np.random.default_rng(7000 + pos)
+    rows = pos + 1
+    k = rng.standard_normal((rows, 8, 128), dtype=np.float32)
+    v = rng.standard_normal((rows, 8, 128), dtype=np.float32)
+    q = rng.standard_normal((16, 128), dtype=np.float32)
+    h = new_cache(pkg, lib, rows + 2, kv_dt)
+    try:
+        if pos:
+            fill_layer(pkg, lib, h, 7, k[:pos], v[:pos])
+        pkg.cache_struct(h).seq_len = pos
+        qp, kp, vp_, op = _pinned(q), _pinned(k[pos]), _pinned(v[pos]), _pinned(np.zeros((16, 128), np.float32))
+        rc = lib.attention_decode_append_gqa(vp(qp), vp(kp), vp(vp_), h, vp(op), 7, SCALE)
+        assert rc == 0, pkg.last_error(lib)
+        out = op.numpy().copy()
+        # the appended row reads back from the cache as written
+        rc = lib.attention_decode_append_gqa(vp(q), vp(k[pos]), vp(v[pos]), h, vp(op), 7, SCALE)
+        assert rc == 0, pkg.last_error(lib)
+        again = op.numpy().copy()
+    finally:
+        lib.kv_cache_free(h)
+    kk, vv = (bf16_round(k), bf16_round(v)) if dtype == "bf16" else (k, v)
+    want = oracle.decode(q, head_first(kk), head_first(vv), rows)
+    assert max_abs(out, want) <= TOL_MAX and rel_l2(out, want) <= TOL_REL
+    assert np.array_equal(out, again)

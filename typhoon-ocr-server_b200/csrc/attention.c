@@ -54,6 +54,23 @@ static const float *to_device(const float *p, float *stage, size_t bytes, int *i
     return stage;
 }
 
+/* Device view of a small per-call buffer: device memory in place, page-locked host memory
+ * through its device mapping (the kernel reads or writes it over the bus: no copy to queue
+ * and wait for), pageable host memory through `stage` after an H2D copy of `bytes` (stage
+ * == NULL: a result buffer, copied back by the caller).  *kind receives TYB_MEM_*.  NULL on
+ * error. */
+static float *small_view(const float *p, float *stage, size_t bytes, int *kind, void *st, const char *what)
+{
+    void *view = NULL;
+    const int k = tyb_residency(p, &view);
+    *kind = k;
+    if (k < 0) return NULL;
+    if (k != TYB_MEM_HOST) return (float *)view;
+    if (stage && !tyb_cuda_ok(cudaMemcpyAsync(stage, p, bytes, cudaMemcpyHostToDevice, (cudaStream_t)st), what))
+        return NULL;
+    return stage;
+}
+
 void attention_decode_gqa(const float *q, const KVCache *cache, float *output, int layer_idx,
                           int kv_len, float scale)
 {
@@ -69,14 +86,20 @@ void attention_decode_gqa(const float *q, const KVCache *cache, float *output, i
         return;
     }
     void *st = tyb_stream();
-    int q_dev = 0, o_dev = tyb_is_device_ptr(output);
-    if (o_dev < 0) return;
-    const float *dq = to_device(q, t->d_q, TYB_Q_FLOATS * sizeof(float), &q_dev, st, what);
+    int qk = 0, ok = 0;
+    const float *dq = small_view(q, t->d_q, TYB_Q_FLOATS * sizeof(float), &qk, st, what);
     if (!dq) return;
-    float *dout = o_dev ? output : t->d_out;
+    float *dout = small_view(output, NULL, 0, &ok, st, what);
+    if (ok < 0 || (ok == TYB_MEM_DEVICE && !dout)) return;
+    if (ok == TYB_MEM_HOST) dout = t->d_out;
     if (kv_len == 0) {
         /* The reference's loops do not run and the output stays zeroed (:186-190). */
-        if (!tyb_cuda_ok(cudaMemsetAsync(dout, 0, TYB_Q_FLOATS * sizeof(float), (cudaStream_t)st), what)) return;
+        if (ok == TYB_MEM_PINNED) {
+            memset(output, 0, TYB_Q_FLOATS * sizeof(float));
+            dout = NULL;
+        } else if (!tyb_cuda_ok(cudaMemsetAsync(dout, 0, TYB_Q_FLOATS * sizeof(float), (cudaStream_t)st), what)) {
+            return;
+        }
     } else {
         tyb_seq_kv one;
         one.k = tyb_slab_head(t, t->k_slab, layer_idx, 0);
@@ -90,13 +113,14 @@ void attention_decode_gqa(const float *q, const KVCache *cache, float *output, i
             return;
         tyb_note_nowrite(st);
     }
-    if (!o_dev) {
+    if (ok == TYB_MEM_HOST) {
         if (!tyb_cuda_ok(cudaMemcpyAsync(output, dout, TYB_Q_FLOATS * sizeof(float), cudaMemcpyDeviceToHost,
                                          (cudaStream_t)st),
                          what))
             return;
     }
-    if (!o_dev || !q_dev) tyb_finish(st, what);
+    /* Host buffers (pageable or page-locked): the call returns once the result is there. */
+    if (ok != TYB_MEM_DEVICE || qk != TYB_MEM_DEVICE) tyb_finish(st, what);
 }
 
 void attention_prefill_gqa(const float *q, const float *k, const float *v, float *output, int Sq,
@@ -278,14 +302,15 @@ int attention_decode_append_gqa(const float *q, const float *k_new, const float 
         return 1;
     }
     void *st = tyb_stream();
-    int qd = 0, kd = 0, vd = 0, od = tyb_is_device_ptr(output);
-    if (od < 0) return 1;
+    int qk = 0, kk = 0, vk = 0, ok = 0;
     const size_t row = TYB_ROW_FLOATS * sizeof(float);
-    const float *dq = to_device(q, t->d_q, TYB_Q_FLOATS * sizeof(float), &qd, st, what);
-    const float *dk = dq ? to_device(k_new, t->d_kv_stage, row, &kd, st, what) : NULL;
-    const float *dv = dk ? to_device(v_new, t->d_kv_stage + TYB_ROW_FLOATS, row, &vd, st, what) : NULL;
+    const float *dq = small_view(q, t->d_q, TYB_Q_FLOATS * sizeof(float), &qk, st, what);
+    const float *dk = dq ? small_view(k_new, t->d_kv_stage, row, &kk, st, what) : NULL;
+    const float *dv = dk ? small_view(v_new, t->d_kv_stage + TYB_ROW_FLOATS, row, &vk, st, what) : NULL;
     if (!dq || !dk || !dv) return 1;
-    float *dout = od ? output : t->d_out;
+    float *dout = small_view(output, NULL, 0, &ok, st, what);
+    if (ok < 0 || (ok != TYB_MEM_HOST && !dout)) return 1;
+    if (ok == TYB_MEM_HOST) dout = t->d_out;
     tyb_seq_kv one;
     one.k = tyb_slab_head(t, t->k_slab, layer_idx, 0);
     one.v = tyb_slab_head(t, t->v_slab, layer_idx, 0);
@@ -297,11 +322,13 @@ int attention_decode_append_gqa(const float *q, const float *k_new, const float 
                      what))
         return 1;
     tyb_note_write(cache, layer_idx, pos, st);
-    if (!od && !tyb_cuda_ok(cudaMemcpyAsync(output, dout, TYB_Q_FLOATS * sizeof(float), cudaMemcpyDeviceToHost,
-                                            (cudaStream_t)st),
-                            what))
+    if (ok == TYB_MEM_HOST && !tyb_cuda_ok(cudaMemcpyAsync(output, dout, TYB_Q_FLOATS * sizeof(float),
+                                                           cudaMemcpyDeviceToHost, (cudaStream_t)st),
+                                           what))
         return 1;
-    if (!qd || !kd || !vd || !od) return tyb_finish(st, what) ? 0 : 1;
+    /* Host buffers (pageable or page-locked): the call returns once the result is there. */
+    if (qk != TYB_MEM_DEVICE || kk != TYB_MEM_DEVICE || vk != TYB_MEM_DEVICE || ok != TYB_MEM_DEVICE)
+        return tyb_finish(st, what) ? 0 : 1;
     return 0;
 }
 

@@ -98,6 +98,12 @@ int tyb_kv_scatter_launch(const float *k_src, const float *v_src, void *k_dst, v
 int tyb_status_fetch(unsigned int *bits, void *stream);
 /* Device address of the status word on the current device (NULL on failure). */
 unsigned int *tyb_status_word(void);
+/* Status mirror (a page-locked host word that kernels flag when they raise a status bit):
+ * set up for the current device (0 or a cudaError_t); its host view, or NULL when the
+ * current device has none; its device view, or NULL. */
+int tyb_status_mirror_setup(void);
+unsigned int *tyb_status_mirror_host(void);
+unsigned int *tyb_status_mirror_device(void);
 
 #ifdef __cplusplus
 }

@@ -24,10 +24,29 @@ constexpr float kLog2e = 1.4426950408889634f;
 // kernel returns; the host reads it back (attn_sync, synchronous entry points).
 // Relocatable translation units name the symbol; a whole-program one (TYB_WHOLE_PROGRAM)
 // receives its address (tyb_status_word) as a kernel argument.
+//
+// A raised bit also flags a page-locked host word (the mirror, NULL until the host sets it
+// up), so that a blocking call learns that nothing went wrong from a stream synchronisation
+// alone and reads the status word back only when the mirror is set.
 #ifndef TYB_WHOLE_PROGRAM
 extern __device__ unsigned int g_status;
+extern __device__ unsigned int* g_status_mirror;
 
-__device__ __forceinline__ void raise_status(unsigned int bits) { atomicOr(&g_status, bits); }
+__device__ __forceinline__ void flag_mirror(unsigned int* mirror)
+{
+    if (mirror) *reinterpret_cast<volatile unsigned int*>(mirror) = 1u;
+}
+
+__device__ __forceinline__ void raise_status(unsigned int bits)
+{
+    atomicOr(&g_status, bits);
+    flag_mirror(g_status_mirror);
+}
+#else
+__device__ __forceinline__ void flag_mirror(unsigned int* mirror)
+{
+    if (mirror) *reinterpret_cast<volatile unsigned int*>(mirror) = 1u;
+}
 #endif
 
 __device__ __forceinline__ uint64_t globaltimer_ns()
@@ -138,7 +157,8 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t pari
 // Wait for phase `parity` of an mbarrier, giving up after `limit_ns` of wall time.
 // Returns false (and sets `status_bit` in *status) when the limit ran out.
 __device__ __forceinline__ bool mbar_wait_bounded_to(uint64_t* bar, uint32_t parity, uint64_t limit_ns,
-                                                     unsigned int status_bit, unsigned int* status)
+                                                     unsigned int status_bit, unsigned int* status,
+                                                     unsigned int* mirror)
 {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
@@ -146,6 +166,7 @@ __device__ __forceinline__ bool mbar_wait_bounded_to(uint64_t* bar, uint32_t par
         if (mbar_try_wait_sleep(bar, parity, 2000u)) return true;
         if (globaltimer_ns() - t0 > limit_ns) {
             atomicOr(status, status_bit);
+            flag_mirror(mirror);
             return false;
         }
     }
@@ -168,7 +189,8 @@ __device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity)
 // Like mbar_wait_bounded_to, but polling without suspending: for a single latency-critical
 // thread (it reacts within a few cycles of the phase completing, at the price of issue slots).
 __device__ __forceinline__ bool mbar_spin_bounded_to(uint64_t* bar, uint32_t parity, uint64_t limit_ns,
-                                                     unsigned int status_bit, unsigned int* status)
+                                                     unsigned int status_bit, unsigned int* status,
+                                                     unsigned int* mirror)
 {
     if (mbar_test_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
@@ -176,6 +198,7 @@ __device__ __forceinline__ bool mbar_spin_bounded_to(uint64_t* bar, uint32_t par
         if (mbar_test_wait(bar, parity)) return true;
         if ((n & 255u) == 0 && globaltimer_ns() - t0 > limit_ns) {
             atomicOr(status, status_bit);
+            flag_mirror(mirror);
             return false;
         }
     }
@@ -185,7 +208,7 @@ __device__ __forceinline__ bool mbar_spin_bounded_to(uint64_t* bar, uint32_t par
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
                                                   uint64_t limit_ns, unsigned int status_bit)
 {
-    return mbar_wait_bounded_to(bar, parity, limit_ns, status_bit, &g_status);
+    return mbar_wait_bounded_to(bar, parity, limit_ns, status_bit, &g_status, g_status_mirror);
 }
 #endif
 

@@ -59,6 +59,15 @@ void *tyb_stream(void);
  * -1 on error (error set). */
 int tyb_is_device_ptr(const void *p);
 
+/* Where p lives, for the calls that take host or device buffers:
+ *   TYB_MEM_DEVICE  device or managed memory: *view = p
+ *   TYB_MEM_PINNED  page-locked host memory mapped into the device's address space: *view is
+ *                   the device-side address (kernels read and write it over the bus)
+ *   TYB_MEM_HOST    pageable host memory: *view = NULL, the data must be copied
+ * Returns -1 on error (error set). */
+enum { TYB_MEM_HOST = 0, TYB_MEM_DEVICE = 1, TYB_MEM_PINNED = 2 };
+int tyb_residency(const void *p, void **view);
+
 /* Process-wide device workspace slots, grown on demand; NULL on failure (error set). */
 enum { TYB_WS_Q, TYB_WS_K, TYB_WS_V, TYB_WS_OUT, TYB_WS_PARTIALS, TYB_WS_COUNTERS, TYB_WS_DESC,
        TYB_WS_COUNT };

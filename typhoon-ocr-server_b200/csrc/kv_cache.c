@@ -66,6 +66,9 @@ KVCache *kv_cache_alloc_ex(int max_seq_len, int kv_dtype)
     t->pub.seq_len = 0;
     t->pub.rope_offset = 0;
     cudaGetDevice(&t->device);
+    /* Kernels on this device may flag the status mirror from now on; without one (setup
+     * failed) the blocking calls read the status word back each time instead. */
+    if (tyb_status_mirror_setup() != 0) cudaGetLastError();
 
     const size_t slab = (size_t)KV_NUM_LAYERS * KV_NUM_KV_HEADS * max_seq_len * KV_HEAD_DIM * t->elem_bytes;
     /* Upper bound on splits for any kv_len <= max_seq_len: chunks are >= 16 rows. */

@@ -10,6 +10,7 @@
 namespace tyb {
 
 __device__ unsigned int g_status = 0u;
+__device__ unsigned int* g_status_mirror = nullptr;
 
 template <typename TDst>
 __global__ void kv_scatter_kernel(const float* __restrict__ k_src, const float* __restrict__ v_src,
@@ -56,6 +57,53 @@ extern "C" int tyb_kv_scatter_launch(const float* k_src, const float* v_src, voi
             k_src, v_src, static_cast<float*>(k_dst), static_cast<float*>(v_dst), row_capacity,
             pos0, S);
     return (int)cudaGetLastError();
+}
+
+// The status mirror: one page-locked, device-mapped host word for the process, its device
+// address stored in g_status_mirror on each device once (tyb_status_mirror_setup, called
+// where caches are allocated).  Until then kernels flag nothing and the host always reads
+// the status word back.
+static unsigned int* g_mirror_host = nullptr;
+static unsigned int* g_mirror_dev[64];
+static bool g_mirror_ready[64];
+
+extern "C" int tyb_status_mirror_setup(void)
+{
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return (int)e;
+    if (dev < 0 || dev >= 64) return (int)cudaErrorInvalidDevice;
+    if (g_mirror_ready[dev]) return 0;
+    if (!g_mirror_host) {
+        void* p = nullptr;
+        e = cudaHostAlloc(&p, sizeof(unsigned int), cudaHostAllocMapped | cudaHostAllocPortable);
+        if (e != cudaSuccess) return (int)e;
+        g_mirror_host = static_cast<unsigned int*>(p);
+        *g_mirror_host = 0u;
+    }
+    void* d = nullptr;
+    e = cudaHostGetDevicePointer(&d, g_mirror_host, 0);
+    if (e != cudaSuccess) return (int)e;
+    unsigned int* dp = static_cast<unsigned int*>(d);
+    e = cudaMemcpyToSymbol(g_status_mirror, &dp, sizeof dp);
+    if (e != cudaSuccess) return (int)e;
+    g_mirror_dev[dev] = dp;
+    g_mirror_ready[dev] = true;
+    return 0;
+}
+
+extern "C" unsigned int* tyb_status_mirror_host(void)
+{
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64 || !g_mirror_ready[dev]) return nullptr;
+    return g_mirror_host;
+}
+
+extern "C" unsigned int* tyb_status_mirror_device(void)
+{
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64 || !g_mirror_ready[dev]) return nullptr;
+    return g_mirror_dev[dev];
 }
 
 extern "C" unsigned int* tyb_status_word(void)

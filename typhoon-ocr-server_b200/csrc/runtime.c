@@ -53,6 +53,28 @@ int tyb_is_device_ptr(const void *p)
     return attr.type == cudaMemoryTypeDevice || attr.type == cudaMemoryTypeManaged;
 }
 
+int tyb_residency(const void *p, void **view)
+{
+    struct cudaPointerAttributes attr;
+    cudaError_t e = cudaPointerGetAttributes(&attr, p);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        tyb_set_error("cudaPointerGetAttributes: %s", cudaGetErrorString(e));
+        return -1;
+    }
+    if (attr.type == cudaMemoryTypeDevice || attr.type == cudaMemoryTypeManaged) {
+        *view = (void *)p;
+        return TYB_MEM_DEVICE;
+    }
+    if (attr.type == cudaMemoryTypeHost && attr.devicePointer) {
+        /* devicePointer is the mapping of the allocation's base view; keep p's offset. */
+        *view = (char *)attr.devicePointer + ((const char *)p - (const char *)attr.hostPointer);
+        return TYB_MEM_PINNED;
+    }
+    *view = NULL;
+    return TYB_MEM_HOST;
+}
+
 /* ---- workspace ------------------------------------------------------------------ */
 
 static pthread_mutex_t g_ws_lock = PTHREAD_MUTEX_INITIALIZER;
@@ -166,6 +188,17 @@ int tyb_prefetch_rows(const void *cache, int layer, int rows)
 int tyb_finish(void *stream, const char *what)
 {
     unsigned int bits = 0;
+    volatile unsigned int *mirror = tyb_status_mirror_host();
+    if (mirror) {
+        /* Kernels flag the mirror whenever they raise a status bit: an unflagged mirror after
+         * the synchronisation means the status word is clear, with no read-back. */
+        if (!tyb_cuda_ok(cudaStreamSynchronize((cudaStream_t)stream), what)) return 0;
+        if (*mirror == 0u) {
+            if (g_last_write.stream == stream) g_last_write.valid = 0;
+            return 1;
+        }
+        *mirror = 0u;
+    }
     int e = tyb_status_fetch(&bits, stream);
     if (!tyb_cuda_ok(e, what)) return 0;
     if (g_last_write.stream == stream) g_last_write.valid = 0; /* everything queued is done */
