@@ -29,7 +29,8 @@ namespace tyb {
 constexpr int kDecThreads = 256;
 constexpr int kRowGroups = kDecThreads / 16;  // p.V row groups (16 lanes per row)
 constexpr int kRec = 4 + 2 * kD;              // record: m0 l0 m1 l1 | o0[128] | o1[128]
-constexpr int kRedBytes = kRowGroups * 2 * kD * (int)sizeof(float);
+// p.V reduction area: [16 row groups][2 heads][128] partial outputs + [16][2] partial sums.
+constexpr int kRedBytes = (kRowGroups * 2 * kD + kRowGroups * 2) * (int)sizeof(float);
 
 template <typename T>
 struct DecodeTile {
@@ -69,7 +70,7 @@ __host__ __device__ constexpr size_t dec_kv_bytes(int chunk)
 }
 
 // Shared memory: [K (>= kRedBytes, reused for the p.V reduction and merge headers)]
-// [V (reused for merge weights)] [scores 2 x chunk] [stat 8] [2 mbarriers] [flag].
+// [V (reused for merge weights)] [scores 2 x chunk] [stat 24] [2 mbarriers] [flag].
 template <typename T>
 __host__ __device__ constexpr size_t dec_k_region(int chunk)
 {
@@ -79,7 +80,7 @@ __host__ __device__ constexpr size_t dec_k_region(int chunk)
 template <typename T>
 __host__ __device__ constexpr size_t decode_smem_bytes(int chunk)
 {
-    return dec_k_region<T>(chunk) + dec_kv_bytes<T>(chunk) + sizeof(float) * (2 * chunk + 8) + 2 * sizeof(uint64_t) +
+    return dec_k_region<T>(chunk) + dec_kv_bytes<T>(chunk) + sizeof(float) * (2 * chunk + 24) + 2 * sizeof(uint64_t) +
            16;
 }
 
@@ -99,8 +100,8 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_split_kernel(const Deco
     T* Ks = reinterpret_cast<T*>(kreg);
     T* Vs = reinterpret_cast<T*>(vreg);
     float* sc = reinterpret_cast<float*>(vreg + dec_kv_bytes<T>(a.chunk));  // [2][chunk]
-    float* stat = sc + 2 * a.chunk;                                          // m0 m1 l0 l1 + scratch
-    uint64_t* bars = reinterpret_cast<uint64_t*>(stat + 8);
+    float* stat = sc + 2 * a.chunk;  // m0 m1 l0 l1, then [8 warps][2] score maxima
+    uint64_t* bars = reinterpret_cast<uint64_t*>(stat + 24);
     int* last_flag = reinterpret_cast<int*>(bars + 2);
     float* red = reinterpret_cast<float*>(kreg);  // [16][2][128], after the scores
 
@@ -154,14 +155,17 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_split_kernel(const Deco
     if (s >= nsplit) return;
     if (tid == 0 && !issued) issue();
 
-    // Query vectors of the two heads sharing this KV head: lane group g16 holds dims
-    // [8*g16, 8*g16+8).
+    // Query vectors of the two heads sharing this KV head, for the scores: 8 lanes per row,
+    // lane part p holds dims [8p, 8p+8) and [64+8p, 64+8p+8).
     const int g16 = lane & 15;
-    float q0[8], q1[8];
+    const int part = lane & 7;
+    float q0[16], q1[16];
     {
-        const float* qb = a.q + (size_t)b * kHq * kD + (size_t)(kGroup * kvh) * kD + g16 * 8;
-        load8(qb, q0);
-        load8(qb + kD, q1);
+        const float* qb = a.q + (size_t)b * kHq * kD + (size_t)(kGroup * kvh) * kD + part * 8;
+        load8(qb, *reinterpret_cast<float(*)[8]>(&q0[0]));
+        load8(qb + 64, *reinterpret_cast<float(*)[8]>(&q0[8]));
+        load8(qb + kD, *reinterpret_cast<float(*)[8]>(&q1[0]));
+        load8(qb + kD + 64, *reinterpret_cast<float(*)[8]>(&q1[8]));
     }
 
     // The new token's row (fused append): threads 0..15 write it to the cache and into its
@@ -180,71 +184,90 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_split_kernel(const Deco
     // Every thread waits (bounded); the CTA leaves together if any wait ran out.
     if (__syncthreads_or(!mbar_wait_bounded(&bars[0], 0, kWaitLimitNs, TYB_STATUS_WAIT_TIMEOUT))) return;
 
-    // Scores: each warp pass covers two rows (one per 16-lane half); two passes are
-    // interleaved per iteration so their loads and shuffle chains overlap.
-    const int half = lane >> 4;
-    constexpr int kPairStride = kDecThreads / 32;
-    for (int p = warp; 2 * p < nrows; p += 2 * kPairStride) {
-        const int ra = 2 * p + half, rb = 2 * (p + kPairStride) + half;
-        float ka[8], kb[8];
-        if (ra < nrows) {
-            load8(Ks + (size_t)ra * kD + g16 * 8, ka);
-        } else {
+    // Scores: 8 lanes per row (each 16-byte chunk of a 128-byte line read by one lane: no
+    // bank conflicts), 4 rows per warp pass, two passes 32 rows apart interleaved; a 3-level
+    // shuffle-xor sum.  Each warp keeps the maximum of its rows per head.
+    float* wmax = stat + 4;  // [8 warps][2] -> after the scores, stat[4..] is scratch
+    {
+        const int rsub = lane >> 3;
+        float m0 = -INFINITY, m1 = -INFINITY;
+        for (int base = warp * 4; base < nrows; base += 64) {
+            const int ra = base + rsub, rb = base + 32 + rsub;
+            const int ra_c = min(ra, nrows - 1), rb_c = min(rb, nrows - 1);
+            float ka[16], kb[16];
+            load8(Ks + (size_t)ra_c * kD + part * 8, *reinterpret_cast<float(*)[8]>(&ka[0]));
+            load8(Ks + (size_t)ra_c * kD + 64 + part * 8, *reinterpret_cast<float(*)[8]>(&ka[8]));
+            load8(Ks + (size_t)rb_c * kD + part * 8, *reinterpret_cast<float(*)[8]>(&kb[0]));
+            load8(Ks + (size_t)rb_c * kD + 64 + part * 8, *reinterpret_cast<float(*)[8]>(&kb[8]));
+            float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f, a2 = 0.f, a3 = 0.f, b2 = 0.f, b3 = 0.f;
 #pragma unroll
-            for (int j = 0; j < 8; j++) ka[j] = 0.f;
-        }
-        if (rb < nrows) {
-            load8(Ks + (size_t)rb * kD + g16 * 8, kb);
-        } else {
-#pragma unroll
-            for (int j = 0; j < 8; j++) kb[j] = 0.f;
-        }
-        float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f;
-#pragma unroll
-        for (int j = 0; j < 8; j++) {
-            a0 = fmaf(q0[j], ka[j], a0);
-            a1 = fmaf(q1[j], ka[j], a1);
-            b0 = fmaf(q0[j], kb[j], b0);
-            b1 = fmaf(q1[j], kb[j], b1);
-        }
-#pragma unroll
-        for (int off = 8; off >= 1; off >>= 1) {
-            a0 += __shfl_xor_sync(0xffffffffu, a0, off);
-            a1 += __shfl_xor_sync(0xffffffffu, a1, off);
-            b0 += __shfl_xor_sync(0xffffffffu, b0, off);
-            b1 += __shfl_xor_sync(0xffffffffu, b1, off);
-        }
-        if (g16 == 0) {
-            if (ra < nrows) {
-                sc[ra] = a0 * a.scale_log2;
-                sc[a.chunk + ra] = a1 * a.scale_log2;
+            for (int j = 0; j < 8; j++) {
+                a0 = fmaf(q0[j], ka[j], a0);
+                a1 = fmaf(q1[j], ka[j], a1);
+                b0 = fmaf(q0[j], kb[j], b0);
+                b1 = fmaf(q1[j], kb[j], b1);
+                a2 = fmaf(q0[8 + j], ka[8 + j], a2);
+                a3 = fmaf(q1[8 + j], ka[8 + j], a3);
+                b2 = fmaf(q0[8 + j], kb[8 + j], b2);
+                b3 = fmaf(q1[8 + j], kb[8 + j], b3);
             }
-            if (rb < nrows) {
-                sc[rb] = b0 * a.scale_log2;
-                sc[a.chunk + rb] = b1 * a.scale_log2;
+            a0 += a2;
+            a1 += a3;
+            b0 += b2;
+            b1 += b3;
+#pragma unroll
+            for (int off = 4; off >= 1; off >>= 1) {
+                a0 += __shfl_xor_sync(0xffffffffu, a0, off);
+                a1 += __shfl_xor_sync(0xffffffffu, a1, off);
+                b0 += __shfl_xor_sync(0xffffffffu, b0, off);
+                b1 += __shfl_xor_sync(0xffffffffu, b1, off);
             }
+            if (part == 0) {
+                if (ra < nrows) {
+                    const float x0 = a0 * a.scale_log2, x1 = a1 * a.scale_log2;
+                    sc[ra] = x0;
+                    sc[a.chunk + ra] = x1;
+                    m0 = fmaxf(m0, x0);
+                    m1 = fmaxf(m1, x1);
+                }
+                if (rb < nrows) {
+                    const float x0 = b0 * a.scale_log2, x1 = b1 * a.scale_log2;
+                    sc[rb] = x0;
+                    sc[a.chunk + rb] = x1;
+                    m0 = fmaxf(m0, x0);
+                    m1 = fmaxf(m1, x1);
+                }
+            }
+        }
+#pragma unroll
+        for (int off = 8; off <= 16; off <<= 1) {
+            m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, off));
+            m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, off));
+        }
+        if (lane == 0) {
+            wmax[2 * warp] = m0;
+            wmax[2 * warp + 1] = m1;
         }
     }
     __syncthreads();
 
-    // Max and exp2 per head: warp 0 takes head 0, warp 1 head 1.
-    if (warp < 2) {
-        float* row = sc + warp * a.chunk;
-        float m = -INFINITY;
-        for (int r = lane; r < nrows; r += 32) m = fmaxf(m, row[r]);
+    // exp2 of every score against its head's maximum, all threads at once.
+    {
+        float M0 = -INFINITY, M1 = -INFINITY;
 #pragma unroll
-        for (int off = 16; off >= 1; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
-        float l = 0.f;
-        for (int r = lane; r < nrows; r += 32) {
-            const float e = fast_exp2(row[r] - m);
-            row[r] = e;
-            l += e;
+        for (int w = 0; w < kDecThreads / 32; w++) {
+            M0 = fmaxf(M0, wmax[2 * w]);
+            M1 = fmaxf(M1, wmax[2 * w + 1]);
         }
-#pragma unroll
-        for (int off = 16; off >= 1; off >>= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
-        if (lane == 0) {
-            stat[warp] = m;
-            stat[2 + warp] = l;
+        for (int i = tid; i < 2 * nrows; i += kDecThreads) {
+            const int hh = i >= nrows;
+            float* x = sc + hh * a.chunk + (i - hh * nrows);
+            *x = fast_exp2(*x - (hh ? M1 : M0));
+        }
+        __syncthreads();  // every thread has read wmax: stat[0..1] may take the maxima
+        if (tid == 0) {
+            stat[0] = M0;
+            stat[1] = M1;
         }
     }
 
@@ -254,12 +277,15 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_split_kernel(const Deco
     // p.V: thread owns dims [8*g16, +8) of rows rg, rg+16, ...
     const int rg = tid >> 4;
     float o0[8], o1[8];
+    float l0 = 0.f, l1 = 0.f;  // this row group's weight sums (used from lane g16 == 0)
 #pragma unroll
     for (int j = 0; j < 8; j++) o0[j] = o1[j] = 0.f;
     for (int r = rg; r < nrows; r += kRowGroups) {
         float v8[8];
         load8(Vs + (size_t)r * kD + g16 * 8, v8);
         const float p0 = sc[r], p1 = sc[a.chunk + r];
+        l0 += p0;
+        l1 += p1;
 #pragma unroll
         for (int j = 0; j < 8; j++) {
             o0[j] = fmaf(p0, v8[j], o0[j]);
@@ -268,7 +294,22 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_split_kernel(const Deco
     }
     store8(red + ((size_t)rg * 2 + 0) * kD + g16 * 8, o0);  // K region is free now
     store8(red + ((size_t)rg * 2 + 1) * kD + g16 * 8, o1);
+    float* lred = red + kRowGroups * 2 * kD;  // [16][2]
+    if (g16 == 0) {
+        lred[2 * rg] = l0;
+        lred[2 * rg + 1] = l1;
+    }
     __syncthreads();
+    if (tid == 0) {
+        float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+        for (int g = 0; g < kRowGroups; g++) {
+            s0 += lred[2 * g];
+            s1 += lred[2 * g + 1];
+        }
+        stat[2] = s0;
+        stat[3] = s1;
+    }
 
     // Thread t reduces output element (h = t / 128, d = t % 128) over the row groups.
     const int h = tid >> 7;
@@ -276,6 +317,7 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_split_kernel(const Deco
     float acc = 0.f;
 #pragma unroll
     for (int g = 0; g < kRowGroups; g++) acc += red[((size_t)g * 2 + h) * kD + d];
+    __syncthreads();  // stat[2..3] (the sums) are written
     const size_t out_head = (size_t)b * kHq * kD + (size_t)(kGroup * kvh) * kD;
 
     if (nsplit == 1) {
