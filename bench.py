@@ -293,6 +293,113 @@ def time_prefill(pkg, lib, device, pages, warmup, seq=4096):
     return ms, flops, 2 * LAYERS
 
 
+def _rope_tables(pos, device):
+    """Per-token cos/sin [S][64] of the interleaved M-RoPE (sections [24,20,20], theta 5e6)."""
+    import torch
+    j = torch.arange(D // 2, device=device)
+    inv_freq = 1.0 / (5000000.0 ** (2.0 * j.double() / D))
+    sect = torch.where(j < 60, j % 3, torch.zeros_like(j))
+    p3 = torch.from_numpy(pos).to(device).double()
+    ang = p3[sect, :].T * inv_freq[None, :]
+    return torch.cos(ang).float().contiguous(), torch.sin(ang).float().contiguous()
+
+
+def time_long_context(pkg, lib, dctx, device, decode_steps=16):
+    """one 32,768-token sequence (30,000 vision tokens on a 150x200 M-RoPE
+    grid + 2,768 text tokens), 28 layers, BF16, sharded by KV head over the ranks (8/N heads
+    each): per layer attention_prefill_fused_gqa_heads -> NCCL all-gather of the head-major
+    shards -> attn_heads_to_tokens; then decode steps at 32K context the same way
+    (attention_decode_append_gqa_heads + all-gather of the [2n][128] shard).  CUDA events on
+    the compute stream, max over ranks; one warm-up pass first."""
+    import torch
+    shard = importlib.import_module(pkg.__name__ + ".shard")
+    wl = importlib.import_module(pkg.__name__ + ".workloads")
+    world = dctx.n
+    h0, n = shard.kv_head_range(dctx.rank, world)
+    pos = wl.config5_positions()
+    S = pos.shape[1]
+    gen = torch.Generator(device=device)
+    gen.manual_seed(5)
+    q = (0.5 * torch.randn((S, HQ, D), generator=gen, device=device)).to(torch.bfloat16)
+    k = (0.5 * torch.randn((S, HKV, D), generator=gen, device=device)).to(torch.bfloat16)
+    v = (0.5 * torch.randn((S, HKV, D), generator=gen, device=device)).to(torch.bfloat16)
+    qn = 1.0 + 0.02 * torch.randn((D,), generator=gen, device=device)
+    kn = 1.0 + 0.02 * torch.randn((D,), generator=gen, device=device)
+    cos, sin = _rope_tables(pos, device)
+    part = torch.empty((2 * n, S, D), dtype=torch.bfloat16, device=device)
+    tokens = torch.empty((S, HQ, D), dtype=torch.bfloat16, device=device)
+    cache = lib.kv_cache_alloc_ex(S + decode_steps + 8, pkg.ATTN_KV_BF16)
+    if not cache:
+        raise RuntimeError(pkg.last_error(lib))
+    cs = pkg.cache_struct(cache)
+    scale, eps = ctypes.c_float(pkg.SCALE), ctypes.c_float(pkg.RMS_EPS)
+    stream = torch.cuda.current_stream(device)
+    lib.attn_set_stream(ctypes.c_void_p(stream.cuda_stream))
+    vp = lambda t: ctypes.c_void_p(t.data_ptr())
+
+    def prefill():
+        cs.seq_len = 0
+        for layer in range(LAYERS):
+            if lib.attention_prefill_fused_gqa_heads(vp(q), vp(k), vp(v), pkg.ATTN_DT_BF16, vp(qn), vp(kn), vp(cos),
+                                                     vp(sin), cache, layer, vp(part), pkg.ATTN_DT_BF16, S, scale,
+                                                     eps, h0, n):
+                raise RuntimeError(pkg.last_error(lib))
+            full = shard.gather_heads(part) if world > 1 else part
+            if lib.attn_heads_to_tokens(vp(full), vp(tokens), S, pkg.ATTN_DT_BF16):
+                raise RuntimeError(pkg.last_error(lib))
+
+    dq = torch.randn((LAYERS, HQ, D), generator=gen, device=device)
+    dk = torch.randn((LAYERS, HKV, D), generator=gen, device=device)
+    dv = torch.randn((LAYERS, HKV, D), generator=gen, device=device)
+    dpart = torch.empty((2 * n, D), device=device)
+    dout = torch.empty((HQ, D), device=device)
+
+    def decode(steps):
+        for i in range(steps):
+            cs.seq_len = S + i
+            for layer in range(LAYERS):
+                if lib.attention_decode_append_gqa_heads(vp(dq[layer]), vp(dk[layer]), vp(dv[layer]), cache,
+                                                         vp(dpart), layer, scale, h0, n):
+                    raise RuntimeError(pkg.last_error(lib))
+                if world > 1:
+                    dout.copy_(shard.gather_heads(dpart))
+                else:
+                    dout.copy_(dpart)
+
+    def timed(fn):
+        dctx.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        dctx.barrier()
+        return dctx.max(e0.elapsed_time(e1))
+
+    prefill()  # warm-up
+    pf_ms = timed(prefill)
+    decode(2)  # warm-up
+    dec_ms = timed(lambda: decode(decode_steps))
+    if lib.attn_sync():
+        raise RuntimeError(pkg.last_error(lib))
+    lib.attn_set_stream(None)
+    lib.kv_cache_free(cache)
+    flops = LAYERS * 4.0 * D * HQ * S * (S + 1) / 2
+    return {
+        "workload": "config5: 32,768 tokens (30,000 vision 150x200 + 2,768 text), 28 layers, bf16, QK-RMSNorm + "
+                    "M-RoPE fused; KV heads sharded over the GPUs, NCCL all-gather of the head outputs per layer",
+        "kv_heads_per_gpu": n,
+        "prefill_ms": pf_ms, "prefill_tok_per_s": S / (pf_ms * 1e-3), "prefill_tflops": flops / (pf_ms * 1e-3) / 1e12,
+        "decode_us_per_step": dec_ms * 1e3 / decode_steps, "decode_steps": decode_steps,
+        "decode_kv_len": f"{S + 1}..{S + decode_steps}",
+        "allgather_bytes_per_layer": {"prefill": S * HQ * D * 2 if world > 1 else 0,
+                                      "decode": HQ * D * 4 if world > 1 else 0},
+        "path": "attention_prefill_fused_gqa_heads / attention_decode_append_gqa_heads + all_gather_into_tensor "
+                "+ attn_heads_to_tokens",
+    }
+
+
 def time_e2e(pkg, lib, cache, steps, device):
     """attention_decode_append_gqa with pinned HOST q, k_new, v_new and output: each call
     copies its inputs in, the output back, and returns when done (the reference's
@@ -519,6 +626,7 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=200)
     ap.add_argument("--cpu-budget", type=float, default=12.0)
     ap.add_argument("--prefill-pages", type=int, default=20)
+    ap.add_argument("--long-context", type=int, default=1, help="run the config-5 section (1) or not (0)")
     ap.add_argument("--case", choices=["decode-small", "prefill-small"],
                     help="run a small fixed invocation of one kernel (for profiler captures) and exit")
     args = ap.parse_args()
@@ -566,6 +674,7 @@ def main():
 
     pf_ms, pf_flops, pf_launches = time_prefill(pkg, lib, f"cuda:{local_rank}", pages=args.prefill_pages, warmup=2)
     pf_ms_max = dctx.max(pf_ms)
+    long_ctx = time_long_context(pkg, lib, dctx, f"cuda:{local_rank}") if args.long_context else None
     tc_sustained = tc_peak
     pk = ROOT / "MEASURED_PEAKS.json"
     if pk.exists():
@@ -629,6 +738,7 @@ def main():
                     "path": "attention_prefill_fused_gqa x28 (kv_prep + prefill_tc_kernel per layer)",
                     "flops_definition": "4*128*16*S*(S+1)/2 per layer (causal pairs)",
                     "peak_note": "bf16 cuBLAS sustained, measured"},
+        "long_context": long_ctx,
         "cpu_baseline": cpu,
         "clocks": clocks,
         "gpu_launches": launches,

@@ -72,6 +72,35 @@ int attention_prefill_fused_gqa(const void *q_raw, const void *k_raw, const void
 int attention_decode_append_gqa(const float *q, const float *k_new, const float *v_new,
                                 KVCache *cache, float *output, int layer_idx, float scale);
 
+/* ---- KV-head sharding (one long sequence over N GPUs) ---------------------------------
+ * The GQA heads are independent: KV head h and query heads 2h, 2h+1 need no other head.  A
+ * long sequence is split over N GPUs by KV head (8/N each); every GPU holds its heads'
+ * rows of the cache and computes its query heads' outputs as one contiguous shard, the
+ * shards are all-gathered (ncclAllGather in rank order, by the caller) into head-major
+ * [16][S][128], and attn_heads_to_tokens turns that into the token-major layout decoder.c
+ * uses.  The reference has no multi-GPU path; these extend attention_prefill_fused_gqa and
+ * attention_decode_append_gqa (SURVEY extension "shard by KV head").  kv_head0, kv_heads:
+ * the KV heads [kv_head0, kv_head0 + kv_heads) computed here, 1 <= kv_heads <= 8.
+ *
+ * attention_prefill_fused_gqa for the given KV heads only (their K/V rows appended, their
+ * query heads' attention); inputs as there (the full q_raw/k_raw/v_raw; the other heads are
+ * not read); output the shard [2 kv_heads][seq_len][128] in out_dtype.  0 on success. */
+int attention_prefill_fused_gqa_heads(const void *q_raw, const void *k_raw, const void *v_raw, int in_dtype,
+                                      const float *q_norm, const float *k_norm, const float *token_cos,
+                                      const float *token_sin, KVCache *cache, int layer_idx, void *output,
+                                      int out_dtype, int seq_len, float scale, float eps, int kv_head0,
+                                      int kv_heads);
+
+/* attention_decode_append_gqa for the given KV heads only: output the shard [2 kv_heads][128]
+ * (query heads 2 kv_head0 ..), host or device.  0 on success. */
+int attention_decode_append_gqa_heads(const float *q, const float *k_new, const float *v_new,
+                                      KVCache *cache, float *output, int layer_idx, float scale,
+                                      int kv_head0, int kv_heads);
+
+/* Gathered head-major [16][seq_len][128] -> token-major [seq_len][16][128], in dtype
+ * (ATTN_DT_F32 or ATTN_DT_BF16); device memory, queued on the library stream.  0 on success. */
+int attn_heads_to_tokens(const void *gathered, void *output, int seq_len, int dtype);
+
 /* No counterpart in the reference.  Decode attention for one sequence and one layer that
  * allocates no memory, for callers that cannot call cudaMalloc: a serving engine whose
  * device memory is all reserved up front by its own caching allocator (an allocation behind

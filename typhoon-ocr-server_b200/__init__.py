@@ -105,6 +105,12 @@ _SIGNATURES = {
     "attention_decode_append_gqa": (ctypes.c_int, [_VP, _VP, _VP, _VP, _VP, ctypes.c_int, ctypes.c_float]),
     "attention_decode_gqa_noalloc": (ctypes.c_int, [_VP, _VP, _VP, ctypes.c_int, ctypes.c_int, _VP,
                                                     ctypes.c_int, ctypes.c_float, _VP]),
+    "attention_prefill_fused_gqa_heads": (ctypes.c_int, [_VP, _VP, _VP, ctypes.c_int, _VP, _VP, _VP, _VP, _VP,
+                                                         ctypes.c_int, _VP, ctypes.c_int, ctypes.c_int, ctypes.c_float,
+                                                         ctypes.c_float, ctypes.c_int, ctypes.c_int]),
+    "attention_decode_append_gqa_heads": (ctypes.c_int, [_VP, _VP, _VP, _VP, _VP, ctypes.c_int, ctypes.c_float,
+                                                         ctypes.c_int, ctypes.c_int]),
+    "attn_heads_to_tokens": (ctypes.c_int, [_VP, _VP, ctypes.c_int, ctypes.c_int]),
 }
 
 

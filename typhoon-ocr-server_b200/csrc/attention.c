@@ -286,10 +286,9 @@ int attention_decode_gqa_batched(const float *q, const KVCache *const *caches, c
     return 0;
 }
 
-int attention_decode_append_gqa(const float *q, const float *k_new, const float *v_new, KVCache *cache,
-                                float *output, int layer_idx, float scale)
+static int decode_append_impl(const float *q, const float *k_new, const float *v_new, KVCache *cache, float *output,
+                              int layer_idx, float scale, int kvh0, int nkvh, const char *what)
 {
-    const char *what = "attention_decode_append_gqa";
     tyb_cache *t = tyb_cache_from(cache);
     if (!t || !check_layer(layer_idx, what)) return 1;
     if (!q || !k_new || !v_new || !output) {
@@ -309,6 +308,7 @@ int attention_decode_append_gqa(const float *q, const float *k_new, const float 
     const float *dv = dk ? small_view(v_new, t->d_kv_stage + TYB_ROW_FLOATS, row, &vk, st, what) : NULL;
     if (!dq || !dk || !dv) return 1;
     float *dout = small_view(output, NULL, 0, &ok, st, what);
+    const size_t out_floats = (size_t)2 * nkvh * KV_HEAD_DIM;  /* rows of the query heads computed */
     if (ok < 0 || (ok != TYB_MEM_HOST && !dout)) return 1;
     if (ok == TYB_MEM_HOST) dout = t->d_out;
     tyb_seq_kv one;
@@ -317,12 +317,12 @@ int attention_decode_append_gqa(const float *q, const float *k_new, const float 
     one.kv_len = pos + 1;
     one.row_capacity = cache->max_seq_len;
     const int early = tyb_prefetch_rows(cache, layer_idx, pos);
-    if (!tyb_cuda_ok(decode_launch(t, dq, dout, NULL, one, 1, pos + 1, t->dtype, scale, dk, dv, early, t->d_partials,
-                                   t->d_counters, st),
+    if (!tyb_cuda_ok(tyb_decode_launch_heads(dq, dout, NULL, one, 1, pos + 1, t->dtype, scale, t->d_partials,
+                                             t->d_counters, dk, dv, early, kvh0, nkvh, st),
                      what))
         return 1;
     tyb_note_write(cache, layer_idx, pos, st);
-    if (ok == TYB_MEM_HOST && !tyb_cuda_ok(cudaMemcpyAsync(output, dout, TYB_Q_FLOATS * sizeof(float),
+    if (ok == TYB_MEM_HOST && !tyb_cuda_ok(cudaMemcpyAsync(output, dout, out_floats * sizeof(float),
                                                            cudaMemcpyDeviceToHost, (cudaStream_t)st),
                                            what))
         return 1;
@@ -332,12 +332,35 @@ int attention_decode_append_gqa(const float *q, const float *k_new, const float 
     return 0;
 }
 
-int attention_prefill_fused_gqa(const void *q_raw, const void *k_raw, const void *v_raw, int in_dtype,
-                                const float *q_norm, const float *k_norm, const float *token_cos,
-                                const float *token_sin, KVCache *cache, int layer_idx, void *output, int out_dtype,
-                                int seq_len, float scale, float eps)
+int attention_decode_append_gqa(const float *q, const float *k_new, const float *v_new, KVCache *cache,
+                                float *output, int layer_idx, float scale)
 {
-    const char *what = "attention_prefill_fused_gqa";
+    return decode_append_impl(q, k_new, v_new, cache, output, layer_idx, scale, 0, KV_NUM_KV_HEADS,
+                              "attention_decode_append_gqa");
+}
+
+static int check_heads(int kv_head0, int kv_heads, const char *what)
+{
+    if (kv_heads < 1 || kv_head0 < 0 || kv_head0 + kv_heads > KV_NUM_KV_HEADS) {
+        tyb_set_error("%s: KV heads [%d, %d) outside [0, %d)", what, kv_head0, kv_head0 + kv_heads, KV_NUM_KV_HEADS);
+        return 0;
+    }
+    return 1;
+}
+
+int attention_decode_append_gqa_heads(const float *q, const float *k_new, const float *v_new, KVCache *cache,
+                                      float *output, int layer_idx, float scale, int kv_head0, int kv_heads)
+{
+    const char *what = "attention_decode_append_gqa_heads";
+    if (!check_heads(kv_head0, kv_heads, what)) return 1;
+    return decode_append_impl(q, k_new, v_new, cache, output, layer_idx, scale, kv_head0, kv_heads, what);
+}
+
+static int prefill_fused_impl(const void *q_raw, const void *k_raw, const void *v_raw, int in_dtype,
+                              const float *q_norm, const float *k_norm, const float *token_cos, const float *token_sin,
+                              KVCache *cache, int layer_idx, void *output, int out_dtype, int seq_len, float scale,
+                              float eps, int kvh0, int nkvh, int head_major, const char *what)
+{
     tyb_cache *t = tyb_cache_from(cache);
     if (!t || !check_layer(layer_idx, what)) return 1;
     if (t->dtype != TYB_BF16) {
@@ -366,15 +389,60 @@ int attention_prefill_fused_gqa(const void *q_raw, const void *k_raw, const void
     void *st = tyb_stream();
     void *kl = tyb_slab_head(t, t->k_slab, layer_idx, 0), *vl = tyb_slab_head(t, t->v_slab, layer_idx, 0);
     if (!tyb_cuda_ok(tyb_kv_prep_launch(k_raw, v_raw, in_dtype == ATTN_DT_BF16, k_norm, token_cos, token_sin, kl, vl,
-                                        cache->max_seq_len, pos0, seq_len, eps, st),
+                                        cache->max_seq_len, pos0, seq_len, eps, kvh0, nkvh, st),
                      what))
         return 1;
     tyb_note_write(cache, layer_idx, pos0, st);
     if (!tyb_cuda_ok(tyb_prefill_tc_launch(q_raw, in_dtype == ATTN_DT_BF16, q_norm, token_cos, token_sin, kl, vl,
                                            cache->max_seq_len, output, out_dtype == ATTN_DT_BF16, seq_len, pos0, scale,
-                                           eps, st),
+                                           eps, kvh0, nkvh, head_major, st),
                      what))
         return 1;
     tyb_note_nowrite(st);
     return 0;
+}
+
+int attention_prefill_fused_gqa(const void *q_raw, const void *k_raw, const void *v_raw, int in_dtype,
+                                const float *q_norm, const float *k_norm, const float *token_cos,
+                                const float *token_sin, KVCache *cache, int layer_idx, void *output, int out_dtype,
+                                int seq_len, float scale, float eps)
+{
+    return prefill_fused_impl(q_raw, k_raw, v_raw, in_dtype, q_norm, k_norm, token_cos, token_sin, cache, layer_idx,
+                              output, out_dtype, seq_len, scale, eps, 0, KV_NUM_KV_HEADS, 0,
+                              "attention_prefill_fused_gqa");
+}
+
+int attention_prefill_fused_gqa_heads(const void *q_raw, const void *k_raw, const void *v_raw, int in_dtype,
+                                      const float *q_norm, const float *k_norm, const float *token_cos,
+                                      const float *token_sin, KVCache *cache, int layer_idx, void *output,
+                                      int out_dtype, int seq_len, float scale, float eps, int kv_head0, int kv_heads)
+{
+    const char *what = "attention_prefill_fused_gqa_heads";
+    if (!check_heads(kv_head0, kv_heads, what)) return 1;
+    return prefill_fused_impl(q_raw, k_raw, v_raw, in_dtype, q_norm, k_norm, token_cos, token_sin, cache, layer_idx,
+                              output, out_dtype, seq_len, scale, eps, kv_head0, kv_heads, 1, what);
+}
+
+int attn_heads_to_tokens(const void *gathered, void *output, int seq_len, int dtype)
+{
+    const char *what = "attn_heads_to_tokens";
+    if (dtype != ATTN_DT_F32 && dtype != ATTN_DT_BF16) {
+        tyb_set_error("%s: unknown element type", what);
+        return 1;
+    }
+    if (seq_len < 0 || !gathered || !output) {
+        tyb_set_error("%s: bad arguments", what);
+        return 1;
+    }
+    if (seq_len == 0) return 0;
+    const int a = tyb_is_device_ptr(gathered), b = tyb_is_device_ptr(output);
+    if (a < 0 || b < 0) return 1;
+    if (!a || !b) {
+        tyb_set_error("%s: gathered and output must be device memory", what);
+        return 1;
+    }
+    return tyb_cuda_ok(tyb_heads_to_tokens_launch(gathered, output, seq_len, dtype == ATTN_DT_BF16 ? 2 : 4, tyb_stream()),
+                       what)
+               ? 0
+               : 1;
 }

@@ -59,6 +59,15 @@ int tyb_decode_launch_ex(const float *q, float *out, const tyb_seq_kv *seqs_dev,
                          int batch, int max_kv_len, int kv_dtype, float scale, float *partials,
                          unsigned int *counters, const float *k_new, const float *v_new, int prefetch_rows,
                          void *stream);
+/* tyb_decode_launch_ex for KV heads [kvh0, kvh0 + nkvh) only; `out` points at the row of query
+ * head 2 kvh0 (the shard's rows [2 nkvh][128] are contiguous). */
+int tyb_decode_launch_heads(const float *q, float *out, const tyb_seq_kv *seqs_dev, tyb_seq_kv one, int batch,
+                            int max_kv_len, int kv_dtype, float scale, float *partials, unsigned int *counters,
+                            const float *k_new, const float *v_new, int prefetch_rows, int kvh0, int nkvh,
+                            void *stream);
+/* Relayout of a gathered head-major tensor [16][S][128] into token-major [S][16][128]
+ * (elem_bytes 2 or 4). */
+int tyb_heads_to_tokens_launch(const void *src, void *dst, int S, int elem_bytes, void *stream);
 
 /* ---- FP32 flash prefill on CUDA cores (prefill_simt.cu) --------------------------- */
 
@@ -73,17 +82,19 @@ int tyb_prefill_simt_launch(const float *q, float *out, const void *k, const voi
 
 /* Raw K/V rows [S][8][128] (fp32, or bf16 when in_bf16) -> BF16 cache rows [pos0, pos0+S) of
  * one layer (layout of tyb_seq_kv): K through RMSNorm(k_norm) and rotate_half M-RoPE with the
- * per-token cos/sin [S][64]; V as is. */
+ * per-token cos/sin [S][64]; V as is.  KV heads [kvh0, kvh0 + nkvh) only. */
 int tyb_kv_prep_launch(const void *k_raw, const void *v_raw, int in_bf16, const float *k_norm, const float *cos,
                        const float *sin, void *k_dst, void *v_dst, int row_capacity, int pos0, int S, float eps,
-                       void *stream);
+                       int kvh0, int nkvh, void *stream);
 
 /* Causal attention of Sq raw queries [Sq][16][128] (fp32 or bf16; RMSNorm(q_norm) + M-RoPE
  * applied on load) over BF16 cache rows [0, pos_offset + Sq) of one layer; query i sits at
- * position pos_offset + i.  Output [Sq][16][128], fp32 or bf16. */
+ * position pos_offset + i.  KV heads [kvh0, kvh0 + nkvh) and their query heads only.
+ * Output [Sq][16][128], or with out_head_major the shard [2 nkvh][Sq][128]; fp32 or bf16. */
 int tyb_prefill_tc_launch(const void *q, int q_bf16, const float *q_norm, const float *cos, const float *sin,
                           const void *k_cache, const void *v_cache, int row_capacity, void *out, int out_bf16,
-                          int Sq, int pos_offset, float scale, float eps, void *stream);
+                          int Sq, int pos_offset, float scale, float eps, int kvh0, int nkvh, int out_head_major,
+                          void *stream);
 
 /* ---- KV-cache row writes (kv_write.cu) -------------------------------------------- */
 

@@ -51,6 +51,7 @@ struct DecodeArgs {
     int prefetch_rows;  // rows [0, prefetch_rows) may be requested before the dependency wait
     float* partials;
     unsigned int* counters;
+    int kvh0;  // KV heads [kvh0, kvh0 + gridDim.y); out points at query head 2 kvh0's row
 };
 
 __device__ __forceinline__ float fast_exp2(float x)
@@ -89,7 +90,7 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_split_kernel(const Deco
 {
     extern __shared__ __align__(128) unsigned char smem[];
     const int s = blockIdx.x;
-    const int kvh = blockIdx.y;
+    const int kvh = a.kvh0 + blockIdx.y;
     const int b = blockIdx.z;
     const int tid = threadIdx.x;
     const int lane = tid & 31;
@@ -318,7 +319,7 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_split_kernel(const Deco
 #pragma unroll
     for (int g = 0; g < kRowGroups; g++) acc += red[((size_t)g * 2 + h) * kD + d];
     __syncthreads();  // stat[2..3] (the sums) are written
-    const size_t out_head = (size_t)b * kHq * kD + (size_t)(kGroup * kvh) * kD;
+    const size_t out_head = (size_t)b * kHq * kD + (size_t)(kGroup * (kvh - a.kvh0)) * kD;
 
     if (nsplit == 1) {
         a.out[out_head + (size_t)h * kD + d] = acc / stat[2 + h];
@@ -464,13 +465,13 @@ static bool set_smem_attr()
 // dependent launch) finds room to start streaming its own rows meanwhile.  The largest
 // chunk when none fits (then the grid runs in several waves, e.g. for large batches).
 template <typename T>
-static void plan(int batch, int max_kv_len, int* chunk_rows, int* nsplit)
+static void plan(int batch, int max_kv_len, int* chunk_rows, int* nsplit, int nkvh = kHkv)
 {
     set_smem_attr<T>();
     const long long slots_sms = num_sms();
     int chosen = DecodeTile<T>::kMaxChunk;
     for (int c = 16; c <= DecodeTile<T>::kMaxChunk; c += 16) {
-        const long long ctas = (long long)((max_kv_len + c - 1) / c) * kHkv * batch;
+        const long long ctas = (long long)((max_kv_len + c - 1) / c) * nkvh * batch;
         const int half_slots = blocks_per_sm<T>(c) / 2 > 0 ? blocks_per_sm<T>(c) / 2 : 1;
         if (ctas <= slots_sms * half_slots) {
             chosen = c;
@@ -482,11 +483,11 @@ static void plan(int batch, int max_kv_len, int* chunk_rows, int* nsplit)
 }
 
 template <typename T>
-static int launch_decode(const DecodeArgs& a, int batch, void* stream)
+static int launch_decode(const DecodeArgs& a, int batch, int nkvh, void* stream)
 {
     if (!set_smem_attr<T>()) return (int)cudaGetLastError();
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(a.nsplit_max, kHkv, batch);
+    cfg.gridDim = dim3(a.nsplit_max, nkvh, batch);
     cfg.blockDim = dim3(kDecThreads);
     cfg.dynamicSmemBytes = decode_smem_bytes<T>(a.chunk);
     cfg.stream = (cudaStream_t)stream;
@@ -515,13 +516,14 @@ extern "C" size_t tyb_decode_partial_floats(int batch, int nsplit)
     return (size_t)batch * kHkv * (size_t)nsplit * kRec;
 }
 
-extern "C" int tyb_decode_launch_ex(const float* q, float* out, const tyb_seq_kv* seqs_dev, tyb_seq_kv one,
-                                    int batch, int max_kv_len, int kv_dtype, float scale, float* partials,
-                                    unsigned int* counters, const float* k_new, const float* v_new,
-                                    int prefetch_rows, void* stream)
+extern "C" int tyb_decode_launch_heads(const float* q, float* out, const tyb_seq_kv* seqs_dev, tyb_seq_kv one,
+                                       int batch, int max_kv_len, int kv_dtype, float scale, float* partials,
+                                       unsigned int* counters, const float* k_new, const float* v_new,
+                                       int prefetch_rows, int kvh0, int nkvh, void* stream)
 {
-    if (batch <= 0 || max_kv_len <= 0) return 0;
+    if (batch <= 0 || max_kv_len <= 0 || nkvh <= 0) return 0;
     DecodeArgs a;
+    a.kvh0 = kvh0;
     a.q = q;
     a.out = out;
     a.seqs = seqs_dev;
@@ -530,14 +532,26 @@ extern "C" int tyb_decode_launch_ex(const float* q, float* out, const tyb_seq_kv
     a.v_new = v_new;
     a.scale_log2 = scale * kLog2e;
     int chunk, nsplit;
-    tyb_decode_plan(batch, max_kv_len, kv_dtype, &chunk, &nsplit);
+    if (kv_dtype == TYB_BF16)
+        plan<__nv_bfloat16>(batch, max_kv_len, &chunk, &nsplit, nkvh);
+    else
+        plan<float>(batch, max_kv_len, &chunk, &nsplit, nkvh);
     a.chunk = chunk;
     a.nsplit_max = nsplit;
     a.prefetch_rows = seqs_dev ? 0 : prefetch_rows;
     a.partials = partials;
     a.counters = counters;
-    if (kv_dtype == TYB_BF16) return launch_decode<__nv_bfloat16>(a, batch, stream);
-    return launch_decode<float>(a, batch, stream);
+    if (kv_dtype == TYB_BF16) return launch_decode<__nv_bfloat16>(a, batch, nkvh, stream);
+    return launch_decode<float>(a, batch, nkvh, stream);
+}
+
+extern "C" int tyb_decode_launch_ex(const float* q, float* out, const tyb_seq_kv* seqs_dev, tyb_seq_kv one,
+                                    int batch, int max_kv_len, int kv_dtype, float scale, float* partials,
+                                    unsigned int* counters, const float* k_new, const float* v_new,
+                                    int prefetch_rows, void* stream)
+{
+    return tyb_decode_launch_heads(q, out, seqs_dev, one, batch, max_kv_len, kv_dtype, scale, partials, counters,
+                                   k_new, v_new, prefetch_rows, 0, kHkv, stream);
 }
 
 extern "C" int tyb_decode_launch(const float* q, float* out, const tyb_seq_kv* seqs_dev, tyb_seq_kv one,

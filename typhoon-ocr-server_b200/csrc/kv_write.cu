@@ -106,6 +106,30 @@ extern "C" unsigned int* tyb_status_mirror_device(void)
     return g_mirror_dev[dev];
 }
 
+// Head-major [16][S][128] -> token-major [S][16][128]: one 16-byte vector per thread step.
+__global__ void heads_to_tokens_kernel(const uint4* __restrict__ src, uint4* __restrict__ dst, int S, int vec_per_row)
+{
+    const long long total = (long long)kHq * S * vec_per_row;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+        const int v = (int)(i % vec_per_row);
+        const long long hr = i / vec_per_row;  // h * S + t
+        const int t = (int)(hr % S), h = (int)(hr / S);
+        dst[((long long)t * kHq + h) * vec_per_row + v] = src[i];
+    }
+}
+
+extern "C" int tyb_heads_to_tokens_launch(const void* src, void* dst, int S, int elem_bytes, void* stream)
+{
+    if (S <= 0) return 0;
+    const int vec_per_row = kD * elem_bytes / 16;
+    const long long total = (long long)kHq * S * vec_per_row;
+    long long blocks = (total + 255) / 256;
+    if (blocks > 148LL * 32) blocks = 148LL * 32;
+    heads_to_tokens_kernel<<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(static_cast<const uint4*>(src),
+                                                                               static_cast<uint4*>(dst), S, vec_per_row);
+    return (int)cudaGetLastError();
+}
+
 extern "C" unsigned int* tyb_status_word(void)
 {
     // Device address of the status word on the current device (looked up once per device).

@@ -63,6 +63,9 @@ struct PrefillTcArgs {
     int n_qtiles;
     float scale_log2;
     float eps;
+    int kvh0;              // KV heads [kvh0, kvh0 + nkvh) (and their query heads) are computed
+    int nkvh;
+    int out_head_major;    // output [2 nkvh][Sq][128] (a contiguous head shard) instead of [Sq][16][128]
     unsigned int* status;  // the library's status word (tyb_status_word)
     unsigned int* mirror;  // its page-locked host mirror flag (tyb_status_mirror_device), or NULL
 };
@@ -418,8 +421,8 @@ __global__ void __launch_bounds__(kPtThreads, 1)
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     // Longest items first: q-tile index descends with blockIdx.
     const int item = blockIdx.x;
-    const int qt = a.n_qtiles - 1 - item / kHkv;
-    const int kvh = item % kHkv;
+    const int qt = a.n_qtiles - 1 - item / a.nkvh;
+    const int kvh = a.kvh0 + item % a.nkvh;
     const int t0 = qt * kPtRows;
     const int ntok = min(kPtRows, a.Sq - t0);
     const int last_pos = a.pos_offset + t0 + ntok - 1;
@@ -635,7 +638,9 @@ __global__ void __launch_bounds__(kPtThreads, 1)
             tc_fence_after();
             const int tok = t0 + r;
             const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-            const size_t ooff = ((size_t)tok * kHq + kGroup * kvh + h) * kD;
+            const size_t ooff = a.out_head_major
+                                    ? ((size_t)(kGroup * (kvh - a.kvh0) + h) * a.Sq + tok) * kD
+                                    : ((size_t)tok * kHq + kGroup * kvh + h) * kD;
 #pragma unroll
             for (int c = 0; c < 4; c++) {
                 float v[32];
@@ -676,16 +681,17 @@ __global__ void __launch_bounds__(kPtThreads, 1)
 __global__ void kv_prep_kernel(const void* __restrict__ k_raw, const void* __restrict__ v_raw, int in_bf16,
                                const float* __restrict__ k_norm, const float* __restrict__ cosv,
                                const float* __restrict__ sinv, __nv_bfloat16* __restrict__ k_dst,
-                               __nv_bfloat16* __restrict__ v_dst, int row_capacity, int pos0, int S, float eps)
+                               __nv_bfloat16* __restrict__ v_dst, int row_capacity, int pos0, int S, float eps,
+                               int kvh0, int nkvh)
 {
     const int lane = threadIdx.x & 31;
     const long long nwarps = (long long)gridDim.x * (blockDim.x >> 5);
     const float4 w = *reinterpret_cast<const float4*>(k_norm + 4 * lane);
     const float w4[4] = {w.x, w.y, w.z, w.w};
     const int jr = 4 * (lane & 15);
-    for (long long wi = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); wi < (long long)S * kHkv;
+    for (long long wi = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); wi < (long long)S * nkvh;
          wi += nwarps) {
-        const int t = (int)(wi / kHkv), hh = (int)(wi % kHkv);
+        const int t = (int)(wi / nkvh), hh = kvh0 + (int)(wi % nkvh);
         const size_t off = ((size_t)t * kHkv + hh) * kD + 4 * lane;
         float x[4], v4[4];
         if (in_bf16) {
@@ -767,24 +773,24 @@ using namespace tyb;
 
 extern "C" int tyb_kv_prep_launch(const void* k_raw, const void* v_raw, int in_bf16, const float* k_norm,
                                   const float* cos, const float* sin, void* k_dst, void* v_dst, int row_capacity,
-                                  int pos0, int S, float eps, void* stream)
+                                  int pos0, int S, float eps, int kvh0, int nkvh, void* stream)
 {
-    if (S <= 0) return 0;
+    if (S <= 0 || nkvh <= 0) return 0;
     const int threads = 256;
-    long long blocks = ((long long)S * kHkv + threads / 32 - 1) / (threads / 32);
+    long long blocks = ((long long)S * nkvh + threads / 32 - 1) / (threads / 32);
     if (blocks > 148LL * 16) blocks = 148LL * 16;
     kv_prep_kernel<<<(unsigned)blocks, threads, 0, (cudaStream_t)stream>>>(
         k_raw, v_raw, in_bf16, k_norm, cos, sin, static_cast<__nv_bfloat16*>(k_dst), static_cast<__nv_bfloat16*>(v_dst),
-        row_capacity, pos0, S, eps);
+        row_capacity, pos0, S, eps, kvh0, nkvh);
     return (int)cudaGetLastError();
 }
 
 extern "C" int tyb_prefill_tc_launch(const void* q, int q_bf16, const float* q_norm, const float* cos,
                                      const float* sin, const void* k_cache, const void* v_cache, int row_capacity,
                                      void* out, int out_bf16, int Sq, int pos_offset, float scale, float eps,
-                                     void* stream)
+                                     int kvh0, int nkvh, int out_head_major, void* stream)
 {
-    if (Sq <= 0) return 0;
+    if (Sq <= 0 || nkvh <= 0) return 0;
     // Once per device: the shared-memory opt-in, and a check that the kernel was compiled
     // for the launch register count its setmaxnreg split is sized against (a split above
     // the launch's registers would never be granted).
@@ -816,12 +822,15 @@ extern "C" int tyb_prefill_tc_launch(const void* q, int q_bf16, const float* q_n
     a.n_qtiles = (Sq + kPtRows - 1) / kPtRows;
     a.scale_log2 = scale * kLog2e;
     a.eps = eps;
+    a.kvh0 = kvh0;
+    a.nkvh = nkvh;
+    a.out_head_major = out_head_major;
     a.status = tyb_status_word();
     if (!a.status) return (int)cudaErrorInvalidSymbol;
     a.mirror = tyb_status_mirror_device();
     CUtensorMap mk, mv;
     if (!make_kv_map(&mk, k_cache, a.total_kv, row_capacity) || !make_kv_map(&mv, v_cache, a.total_kv, row_capacity))
         return (int)cudaErrorInvalidValue;
-    prefill_tc_kernel<<<a.n_qtiles * kHkv, kPtThreads, kPtSmemBytes, (cudaStream_t)stream>>>(mk, mv, a);
+    prefill_tc_kernel<<<a.n_qtiles * nkvh, kPtThreads, kPtSmemBytes, (cudaStream_t)stream>>>(mk, mv, a);
     return (int)cudaGetLastError();
 }
