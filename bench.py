@@ -441,12 +441,15 @@ class DistCtx:
         if n > 1:
             import datetime
             import torch.distributed as dist
-            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+            import torch
+            dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
             self.dist = dist
+        self._rank = self.dist.get_rank() if self.dist else 0
 
     @property
     def rank(self):
-        return self.dist.get_rank() if self.dist else 0
+        return self._rank
 
     def barrier(self):
         if self.dist:
