@@ -400,6 +400,73 @@ def time_long_context(pkg, lib, dctx, device, decode_steps=16):
     }
 
 
+def time_batched(pkg, lib, dctx, device, per_gpu=64, steps=8):
+    """batched multi-page decode, 64 sequences per GPU (64/128/256/512 on
+    1/2/4/8 GPUs, weak scaling, no collective), ragged KV lengths ~ U[1024, 8192] from the
+    seeded list (rank r takes sequences [64r, 64r + 64)), BF16 per-sequence caches filled with
+    N(0, 0.5) rows; per step 28 layers of attention_decode_gqa_batched (one launch per layer
+    for all sequences), kv_len + 1 each step.  CUDA events, max over ranks."""
+    import torch
+    wl = importlib.import_module(pkg.__name__ + ".workloads")
+    lens = wl.config4_kv_lens(512)[dctx.rank * per_gpu:(dctx.rank + 1) * per_gpu].astype(np.int64)
+    gen = torch.Generator(device=device)
+    gen.manual_seed(4)
+    rows = (0.5 * torch.randn((int(lens.max()), HKV, D), generator=gen, device=device)).float()
+    stream = torch.cuda.current_stream(device)
+    lib.attn_set_stream(ctypes.c_void_p(stream.cuda_stream))
+    caches = []
+    for kv in lens:
+        c = lib.kv_cache_alloc_ex(int(kv) + steps + 4, pkg.ATTN_KV_BF16)
+        if not c:
+            raise RuntimeError(pkg.last_error(lib))
+        cs = pkg.cache_struct(c)
+        for layer in range(LAYERS):
+            cs.seq_len = 0
+            lib.kv_cache_append_prefill(c, layer, ctypes.c_void_p(rows.data_ptr()), ctypes.c_void_p(rows.data_ptr()),
+                                        int(kv))
+        caches.append(c)
+    arr = (ctypes.c_void_p * per_gpu)(*caches)
+    q = torch.randn((LAYERS, per_gpu, HQ, D), generator=gen, device=device)
+    out = torch.empty((per_gpu, HQ, D), device=device)
+    scale = ctypes.c_float(pkg.SCALE)
+    kvb = [np.ascontiguousarray(lens + i, dtype=np.int32) for i in range(steps + 1)]
+
+    def run(step_list):
+        for i in step_list:
+            for layer in range(LAYERS):
+                if lib.attention_decode_gqa_batched(ctypes.c_void_p(q[layer].data_ptr()), arr,
+                                                    kvb[i].ctypes.data_as(ctypes.c_void_p),
+                                                    ctypes.c_void_p(out.data_ptr()), per_gpu, layer, scale):
+                    raise RuntimeError(pkg.last_error(lib))
+
+    run([0])
+    torch.cuda.synchronize()
+    dctx.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    run(range(1, steps + 1))
+    e1.record(stream)
+    torch.cuda.synchronize()
+    dctx.barrier()
+    ms = dctx.max(e0.elapsed_time(e1))
+    if lib.attn_sync():
+        raise RuntimeError(pkg.last_error(lib))
+    lib.attn_set_stream(None)
+    for c in caches:
+        lib.kv_cache_free(c)
+    # K/V bytes per step, averaged over the timed steps (kv_len + 1 .. kv_len + steps)
+    bytes_step = sum(float(LAYERS * 2 * (int(kv) + (steps + 1) / 2) * HKV * D * 2) for kv in lens)
+    us = ms * 1e3 / steps
+    return {
+        "workload": f"config4: {per_gpu} sequences per GPU ({per_gpu * dctx.n} in all), kv_len ~ U[1024, 8192] "
+                    "seeded, BF16 per-sequence caches, 28 layers per step",
+        "us_per_step": us, "steps": steps,
+        "achieved_gbs_per_gpu": bytes_step / (us * 1e-6) / 1e9,
+        "sequences_per_s": per_gpu * dctx.n / (us * 1e-6),
+        "path": "attention_decode_gqa_batched x28 per step (one launch per layer for all sequences)",
+    }
+
+
 def time_e2e(pkg, lib, cache, steps, device):
     """attention_decode_append_gqa with pinned HOST q, k_new, v_new and output: each call
     copies its inputs in, the output back, and returns when done (the reference's
@@ -630,6 +697,7 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=12.0)
     ap.add_argument("--prefill-pages", type=int, default=20)
     ap.add_argument("--long-context", type=int, default=1, help="run the config-5 section (1) or not (0)")
+    ap.add_argument("--batched", type=int, default=1, help="run the config-4 section (1) or not (0)")
     ap.add_argument("--case", choices=["decode-small", "prefill-small"],
                     help="run a small fixed invocation of one kernel (for profiler captures) and exit")
     args = ap.parse_args()
@@ -678,6 +746,7 @@ def main():
     pf_ms, pf_flops, pf_launches = time_prefill(pkg, lib, f"cuda:{local_rank}", pages=args.prefill_pages, warmup=2)
     pf_ms_max = dctx.max(pf_ms)
     long_ctx = time_long_context(pkg, lib, dctx, f"cuda:{local_rank}") if args.long_context else None
+    batched = time_batched(pkg, lib, dctx, f"cuda:{local_rank}") if args.batched else None
     tc_sustained = tc_peak
     pk = ROOT / "MEASURED_PEAKS.json"
     if pk.exists():
@@ -742,6 +811,7 @@ def main():
                     "flops_definition": "4*128*16*S*(S+1)/2 per layer (causal pairs)",
                     "peak_note": "bf16 cuBLAS sustained, measured"},
         "long_context": long_ctx,
+        "batched": batched,
         "cpu_baseline": cpu,
         "clocks": clocks,
         "gpu_launches": launches,
