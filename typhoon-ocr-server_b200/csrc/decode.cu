@@ -85,6 +85,40 @@ __host__ __device__ constexpr size_t decode_smem_bytes(int chunk)
            16;
 }
 
+// The 16 dims of a 128-dim row that lane part p (0..7) of an 8-lane row group takes in the
+// score pass, chosen so that the 8 lanes of a row read 8 different 16-byte units of a
+// 128-byte line at every load (no bank conflicts across the 4 rows of a warp pass): BF16 rows
+// (256 B) in two 8-dim chunks [8p, 8p+8) and [64+8p, 64+8p+8); FP32 rows (512 B) in four
+// 4-dim chunks [32c+4p, 32c+4p+4).  The query uses the same dims.
+__device__ __forceinline__ void load_lane16(const __nv_bfloat16* row, int p, float (&x)[16])
+{
+    load8(row + 8 * p, *reinterpret_cast<float(*)[8]>(&x[0]));
+    load8(row + 64 + 8 * p, *reinterpret_cast<float(*)[8]>(&x[8]));
+}
+
+__device__ __forceinline__ void load_lane16(const float* row, int p, float (&x)[16])
+{
+#pragma unroll
+    for (int c = 0; c < 4; c++) {
+        const float4 v = *reinterpret_cast<const float4*>(row + 32 * c + 4 * p);
+        x[4 * c] = v.x;
+        x[4 * c + 1] = v.y;
+        x[4 * c + 2] = v.z;
+        x[4 * c + 3] = v.w;
+    }
+}
+
+template <typename T>
+__device__ __forceinline__ void load_query16(const float* q, int p, float (&x)[16])
+{
+    if (sizeof(T) == 2) {
+        load8(q + 8 * p, *reinterpret_cast<float(*)[8]>(&x[0]));
+        load8(q + 64 + 8 * p, *reinterpret_cast<float(*)[8]>(&x[8]));
+    } else {
+        load_lane16(q, p, x);
+    }
+}
+
 template <typename T>
 __global__ void __launch_bounds__(kDecThreads, 2) decode_split_kernel(const DecodeArgs a)
 {
@@ -157,16 +191,14 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_split_kernel(const Deco
     if (tid == 0 && !issued) issue();
 
     // Query vectors of the two heads sharing this KV head, for the scores: 8 lanes per row,
-    // lane part p holds dims [8p, 8p+8) and [64+8p, 64+8p+8).
+    // lane part p holds the 16 dims of load_lane16.
     const int g16 = lane & 15;
     const int part = lane & 7;
     float q0[16], q1[16];
     {
-        const float* qb = a.q + (size_t)b * kHq * kD + (size_t)(kGroup * kvh) * kD + part * 8;
-        load8(qb, *reinterpret_cast<float(*)[8]>(&q0[0]));
-        load8(qb + 64, *reinterpret_cast<float(*)[8]>(&q0[8]));
-        load8(qb + kD, *reinterpret_cast<float(*)[8]>(&q1[0]));
-        load8(qb + kD + 64, *reinterpret_cast<float(*)[8]>(&q1[8]));
+        const float* qb = a.q + (size_t)b * kHq * kD + (size_t)(kGroup * kvh) * kD;
+        load_query16<T>(qb, part, q0);
+        load_query16<T>(qb + kD, part, q1);
     }
 
     // The new token's row (fused append): threads 0..15 write it to the cache and into its
@@ -196,10 +228,8 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_split_kernel(const Deco
             const int ra = base + rsub, rb = base + 32 + rsub;
             const int ra_c = min(ra, nrows - 1), rb_c = min(rb, nrows - 1);
             float ka[16], kb[16];
-            load8(Ks + (size_t)ra_c * kD + part * 8, *reinterpret_cast<float(*)[8]>(&ka[0]));
-            load8(Ks + (size_t)ra_c * kD + 64 + part * 8, *reinterpret_cast<float(*)[8]>(&ka[8]));
-            load8(Ks + (size_t)rb_c * kD + part * 8, *reinterpret_cast<float(*)[8]>(&kb[0]));
-            load8(Ks + (size_t)rb_c * kD + 64 + part * 8, *reinterpret_cast<float(*)[8]>(&kb[8]));
+            load_lane16(Ks + (size_t)ra_c * kD, part, ka);
+            load_lane16(Ks + (size_t)rb_c * kD, part, kb);
             float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f, a2 = 0.f, a3 = 0.f, b2 = 0.f, b3 = 0.f;
 #pragma unroll
             for (int j = 0; j < 8; j++) {
@@ -333,17 +363,18 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_split_kernel(const Deco
         mine[4 + h * kD + d] = acc;
     }
     // Publish the record, then take a ticket; the CTA that takes the last one merges.  One
-    // thread fences on behalf of the CTA (the barrier orders the other threads' writes
-    // before its fence).
+    // thread takes the ticket with an acquire-release atomic on behalf of the CTA: the barrier
+    // orders the other threads' record writes before its release, and its acquire makes the
+    // other CTAs' records visible to the last CTA.
     __syncthreads();
     if (tid == 0) {
-        __threadfence();
-        const unsigned int ticket = atomicAdd(&a.counters[b * kHkv + kvh], 1u);
+        unsigned int ticket;
+        asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;"
+                     : "=r"(ticket)
+                     : "l"(&a.counters[b * kHkv + kvh])
+                     : "memory");
         const int last = ticket == (unsigned int)(nsplit - 1);
-        if (last) {
-            __threadfence();
-            asm volatile("fence.proxy.async.global;" ::: "memory");  // records are read by TMA below
-        }
+        if (last) asm volatile("fence.proxy.async.global;" ::: "memory");  // records are read by TMA below
         *last_flag = last;
     }
     __syncthreads();
