@@ -328,3 +328,59 @@ def test_decode_append_pinned_host_buffers(pkg, lib, oracle, dtype, pos):
     want = oracle.decode(q, head_first(kk), head_first(vv), rows)
     assert max_abs(out, want) <= TOL_MAX and rel_l2(out, want) <= TOL_REL
     assert np.array_equal(out, again)
+
+
+def _plan(lib, kv_len, dtype):
+    chunk, nsplit = ctypes.c_int(), ctypes.c_int()
+    lib.tyb_decode_plan(1, kv_len, dtype, ctypes.byref(chunk), ctypes.byref(nsplit))
+    return chunk.value, nsplit.value
+
+
+def _edge_lengths(pkg, lib):
+    """kv lengths around 16-row steps and split edges of the BF16 single-sequence kernel,
+    including ones whose last split holds only the appended row."""
+    lens = {1, 2, 15, 16, 17, 100, 191, 192, 193, 2000, 4097, 4608, 8192}
+    for target in (300, 2000, 4097):
+        chunk, _ = _plan(lib, target, pkg.ATTN_KV_BF16)
+        n = (target // chunk) * chunk + 1
+        if _plan(lib, n, pkg.ATTN_KV_BF16)[0] == chunk:
+            lens.add(n)
+    return sorted(lens)
+
+
+@pytest.mark.parametrize("append", [False, True])
+def test_decode_bf16_split_edges(pkg, lib, oracle, append):
+    """BF16 cache, one sequence (the tensor-core form): every split/step edge against the
+    oracle on the same bf16-rounded rows, FP32 bar; NaN in the slab past the attended rows."""
+    lib.tyb_decode_plan.restype = None
+    for kv_len in _edge_lengths(pkg, lib):
+        rng = np.random.default_rng(5000 + kv_len)
+        q = rng.standard_normal((16, 128), dtype=np.float32)
+        k = rng.standard_normal((kv_len, 8, 128), dtype=np.float32)
+        v = rng.standard_normal((kv_len, 8, 128), dtype=np.float32)
+        h = new_cache(pkg, lib, kv_len + 40, pkg.ATTN_KV_BF16)
+        try:
+            qd = dev(q)
+            od = torch.full((16, 128), float("nan"), dtype=torch.float32, device="cuda")
+            # Rows past the attended ones (the appended row's slot included) hold NaN: the
+            # kernel reads whole tiles and must not let them in.
+            n_old = kv_len - 1 if append else kv_len
+            pad = np.full((kv_len + 40, 8, 128), np.nan, dtype=np.float32)
+            kf, vf = pad.copy(), pad.copy()
+            kf[:n_old], vf[:n_old] = k[:n_old], v[:n_old]
+            fill_layer(pkg, lib, h, 4, kf, vf)
+            if append:
+                pkg.cache_struct(h).seq_len = kv_len - 1
+                kn, vn = dev(k[kv_len - 1]), dev(v[kv_len - 1])
+                rc = lib.attention_decode_append_gqa(vp(qd), vp(kn), vp(vn), h, vp(od), 4, SCALE)
+                assert rc == 0, pkg.last_error(lib)
+            else:
+                lib.attention_decode_gqa(vp(qd), h, vp(od), 4, kv_len, SCALE)
+            assert lib.attn_sync() == 0, pkg.last_error(lib)
+            check(pkg, lib, "decode")
+            out = od.cpu().numpy()
+        finally:
+            lib.kv_cache_free(h)
+        want = oracle.decode(q, head_first(bf16_round(k)), head_first(bf16_round(v)), kv_len)
+        assert np.isfinite(out).all(), kv_len
+        assert max_abs(out, want) <= TOL_MAX and rel_l2(out, want) <= TOL_REL, kv_len

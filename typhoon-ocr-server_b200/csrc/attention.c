@@ -22,13 +22,13 @@
 #include "attn_ext.h"
 #include "host_internal.h"
 
-static int decode_launch(tyb_cache *t, const float *q, float *out, const tyb_seq_kv *seqs_dev, tyb_seq_kv one,
-                         int batch, int max_kv, int dtype, float scale, const float *k_new, const float *v_new,
-                         int prefetch_rows, float *partials, unsigned int *counters, void *st)
+/* flags: TYB_DEC_DEVICE_SMALL when q is device memory (not a mapped page-locked host buffer). */
+static int decode_launch(const float *q, float *out, const tyb_seq_kv *seqs_dev, tyb_seq_kv one, int batch,
+                         int max_kv, int dtype, float scale, int prefetch_rows, float *partials,
+                         unsigned int *counters, int flags, void *st)
 {
-    (void)t;
-    return tyb_decode_launch_ex(q, out, seqs_dev, one, batch, max_kv, dtype, scale, partials, counters, k_new, v_new,
-                                prefetch_rows, st);
+    return tyb_decode_launch_heads(q, out, seqs_dev, one, batch, max_kv, dtype, scale, partials, counters, NULL, NULL,
+                                   prefetch_rows, 0, KV_NUM_KV_HEADS, flags, st);
 }
 
 static int check_layer(int layer, const char *what)
@@ -107,8 +107,8 @@ void attention_decode_gqa(const float *q, const KVCache *cache, float *output, i
         one.kv_len = kv_len;
         one.row_capacity = cache->max_seq_len;
         const int early = tyb_prefetch_rows(cache, layer_idx, kv_len);
-        if (!tyb_cuda_ok(decode_launch(t, dq, dout, NULL, one, 1, kv_len, t->dtype, scale, NULL, NULL, early,
-                                       t->d_partials, t->d_counters, st),
+        if (!tyb_cuda_ok(decode_launch(dq, dout, NULL, one, 1, kv_len, t->dtype, scale, early, t->d_partials,
+                                       t->d_counters, qk != TYB_MEM_PINNED ? TYB_DEC_DEVICE_SMALL : 0, st),
                          what))
             return;
         tyb_note_nowrite(st);
@@ -275,8 +275,8 @@ int attention_decode_gqa_batched(const float *q, const KVCache *const *caches, c
     unsigned int *cnt =
         (unsigned int *)tyb_workspace(TYB_WS_COUNTERS, sizeof(unsigned int) * (size_t)batch * KV_NUM_KV_HEADS);
     if (!part || !cnt) return 1;
-    if (!tyb_cuda_ok(decode_launch(NULL, dq, dout, ddesc, none, batch, max_kv, dtype, scale, NULL, NULL, 0, part, cnt,
-                                   st),
+    if (!tyb_cuda_ok(decode_launch(dq, dout, ddesc, none, batch, max_kv, dtype, scale, 0, part, cnt,
+                                   TYB_DEC_DEVICE_SMALL, st),
                      what))
         return 1;
     tyb_note_nowrite(st);
@@ -318,7 +318,11 @@ static int decode_append_impl(const float *q, const float *k_new, const float *v
     one.row_capacity = cache->max_seq_len;
     const int early = tyb_prefetch_rows(cache, layer_idx, pos);
     if (!tyb_cuda_ok(tyb_decode_launch_heads(dq, dout, NULL, one, 1, pos + 1, t->dtype, scale, t->d_partials,
-                                             t->d_counters, dk, dv, early, kvh0, nkvh, st),
+                                             t->d_counters, dk, dv, early, kvh0, nkvh,
+                                             (qk != TYB_MEM_PINNED && kk != TYB_MEM_PINNED && vk != TYB_MEM_PINNED)
+                                                 ? TYB_DEC_DEVICE_SMALL
+                                                 : 0,
+                                             st),
                      what))
         return 1;
     tyb_note_write(cache, layer_idx, pos, st);

@@ -64,7 +64,15 @@ int tyb_decode_launch_ex(const float *q, float *out, const tyb_seq_kv *seqs_dev,
 int tyb_decode_launch_heads(const float *q, float *out, const tyb_seq_kv *seqs_dev, tyb_seq_kv one, int batch,
                             int max_kv_len, int kv_dtype, float scale, float *partials, unsigned int *counters,
                             const float *k_new, const float *v_new, int prefetch_rows, int kvh0, int nkvh,
-                            void *stream);
+                            int flags, void *stream);
+/* Encodes into `map` (a CUtensorMap: 128 bytes, 64-byte aligned) rows [0, rows) of the 8
+ * heads of one layer's BF16 cache slab (head stride row_capacity rows) as a 3-D tensor
+ * {128 dims, rows, 8 heads}, copied in 128-byte-swizzled boxes of {64, box_rows, 1}; rows
+ * past `rows` read as zeros.  0 on success. */
+int tyb_encode_rows_map(void *map, const void *base, int rows, int row_capacity, int box_rows);
+/* flags of tyb_decode_launch_heads: q, k_new and v_new are device memory (not page-locked host
+ * memory mapped into the device), so their L2 lines may be requested before the dependency wait. */
+#define TYB_DEC_DEVICE_SMALL 1
 /* Relayout of a gathered head-major tensor [16][S][128] into token-major [S][16][128]
  * (elem_bytes 2 or 4). */
 int tyb_heads_to_tokens_launch(const void *src, void *dst, int S, int elem_bytes, void *stream);

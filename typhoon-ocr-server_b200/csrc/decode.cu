@@ -5,20 +5,25 @@
 // KV head and its two query heads, scores = q.K*scale over kv_len rows, max, exp, sum,
 // normalise, out = sum p*V) and, fused, kernel/kv_cache.c:53-65 (the new row written at
 // row seq_len first).  One CTA owns one (sequence, KV head, split of rows):
-//   1. one thread starts two bulk async copies (TMA, 1-D) of the split's K and V rows --
-//      contiguous in the head-first cache -- into shared memory on two mbarriers.  The
-//      kernel is launched with programmatic dependent launch and the grid is planned to
+//   1. the split's K and V rows are requested into shared memory by TMA on two mbarriers.
+//      Kernels are launched with programmatic dependent launch and the grid is planned to
 //      fill only half of the SM slots, so the next kernel's CTAs are resident early and
 //      request their rows BEFORE griddepcontrol.wait (only rows the host knows the
-//      previous launch did not write); the stream of K/V bytes continues across kernels;
+//      previous launch did not write).  On B200 such copies were measured to complete only
+//      once the previous grid has finished (they land right after the wait returns), so
+//      what this saves is the request latency, not the transfer;
 //   2. after the wait: the query (and the new row, written to the cache and into its
-//      slot), scores of both query heads (16-byte vectors, 16 lanes per row, shuffle-xor
-//      reduction), max and exp2 per head;
+//      slot), scores of both query heads, max and exp2 per head;
 //   3. p.V for both heads from the same V bytes (GQA pair read once);
 //   4. the split's (max, sum, unnormalised o) goes to a workspace record; the CTA that
 //      takes the last ticket merges all records, pulled into shared memory by bulk
 //      copies, and writes the output.  No second launch.
+// Two kernels implement it: decode_mma_kernel (one sequence, BF16 cache: the contractions on
+// the tensor cores through mma.sync, tiles by TMA tensor copies) and decode_split_kernel<T>
+// (FP32 caches and request batches: CUDA-core dot products, tiles by 1-D bulk copies).
 // Bandwidth-bound: 2 * kv_len * 128 * sizeof(T) bytes per (sequence, KV head).
+#include <cuda.h>
+
 #include <mutex>
 
 #include "common.cuh"
@@ -52,6 +57,7 @@ struct DecodeArgs {
     float* partials;
     unsigned int* counters;
     int kvh0;  // KV heads [kvh0, kvh0 + gridDim.y); out points at query head 2 kvh0's row
+    int prefetch_small;  // q, k_new, v_new are device memory: ask L2 for their lines early
 };
 
 __device__ __forceinline__ float fast_exp2(float x)
@@ -71,7 +77,7 @@ __host__ __device__ constexpr size_t dec_kv_bytes(int chunk)
 }
 
 // Shared memory: [K (>= kRedBytes, reused for the p.V reduction and merge headers)]
-// [V (reused for merge weights)] [scores 2 x chunk] [stat 24] [2 mbarriers] [flag].
+// [V (reused for merge weights)] [scores 2 x chunk] [stat 24] [3 mbarriers] [flag].
 template <typename T>
 __host__ __device__ constexpr size_t dec_k_region(int chunk)
 {
@@ -81,7 +87,7 @@ __host__ __device__ constexpr size_t dec_k_region(int chunk)
 template <typename T>
 __host__ __device__ constexpr size_t decode_smem_bytes(int chunk)
 {
-    return dec_k_region<T>(chunk) + dec_kv_bytes<T>(chunk) + sizeof(float) * (2 * chunk + 24) + 2 * sizeof(uint64_t) +
+    return dec_k_region<T>(chunk) + dec_kv_bytes<T>(chunk) + sizeof(float) * (2 * chunk + 24) + 3 * sizeof(uint64_t) +
            16;
 }
 
@@ -119,6 +125,81 @@ __device__ __forceinline__ void load_query16(const float* q, int p, float (&x)[1
     }
 }
 
+// Merge of the `nsplit` split records of one (sequence, KV head) by the CTA that took the last
+// ticket; every thread of the CTA calls it.  Records arrive in shared memory (`region`, the
+// CTA's free K/V space) in batches by one bulk copy each on `bar` (phase 0 first); every
+// thread then merges one output element (h, d) = (tid / 128, tid % 128), with an online
+// maximum across batches, and writes out[h * 128 + d].  red32: 32 floats of scratch.
+// False when a wait ran out (the status word is raised).
+__device__ __forceinline__ bool merge_records(const float* recs, int nsplit, float* region, size_t region_bytes, uint64_t* bar,
+                              float* red32, float* out)
+{
+    const int tid = threadIdx.x;
+    const int lane = tid & 31;
+    const int warp = tid >> 5;
+    const int h = tid >> 7;
+    const int d = tid & 127;
+    const int cap = (int)(region_bytes / (sizeof(float) * (kRec + 2)));
+    float* wts = region + (size_t)cap * kRec;  // [cap][2]
+    float run0 = -INFINITY, run1 = -INFINITY;  // running max of each head (uniform)
+    float L = 0.f, O = 0.f;                     // this thread's head h, element d
+    uint32_t phase = 0;
+    for (int j0 = 0; j0 < nsplit; j0 += cap) {
+        const int nb = min(cap, nsplit - j0);
+        __syncthreads();  // the previous batch is consumed
+        if (tid == 0) {
+            const uint32_t bytes = (uint32_t)nb * kRec * sizeof(float);
+            mbar_arrive_expect_tx(bar, bytes);
+            bulk_g2s(region, recs + (size_t)j0 * kRec, bytes, bar);
+        }
+        if (__syncthreads_or(!mbar_wait_bounded(bar, phase, kWaitLimitNs, TYB_STATUS_WAIT_TIMEOUT))) return false;
+        phase ^= 1u;
+        // Batch maximum of each head: a block reduction over the records' headers.
+        float x0 = -INFINITY, x1 = -INFINITY;
+        for (int j = tid; j < nb; j += kDecThreads) {
+            x0 = fmaxf(x0, region[(size_t)j * kRec + 0]);
+            x1 = fmaxf(x1, region[(size_t)j * kRec + 2]);
+        }
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) {
+            x0 = fmaxf(x0, __shfl_xor_sync(0xffffffffu, x0, off));
+            x1 = fmaxf(x1, __shfl_xor_sync(0xffffffffu, x1, off));
+        }
+        if (lane == 0) {
+            red32[warp] = x0;
+            red32[16 + warp] = x1;
+        }
+        __syncthreads();
+        float n0 = run0, n1 = run1;
+#pragma unroll
+        for (int w = 0; w < kDecThreads / 32; w++) {
+            n0 = fmaxf(n0, red32[w]);
+            n1 = fmaxf(n1, red32[16 + w]);
+        }
+        // Weights of this batch's records against the new maxima.
+        for (int j = tid; j < nb; j += kDecThreads) {
+            wts[2 * j] = fast_exp2(region[(size_t)j * kRec + 0] - n0);
+            wts[2 * j + 1] = fast_exp2(region[(size_t)j * kRec + 2] - n1);
+        }
+        __syncthreads();
+        const float alpha = fast_exp2((h ? run1 : run0) - (h ? n1 : n0));  // 0 on the first batch
+        L *= alpha;
+        O *= alpha;
+        const float* lp = region + 1 + 2 * h;
+        const float* op = region + 4 + (size_t)h * kD + d;
+#pragma unroll 4
+        for (int j = 0; j < nb; j++) {
+            const float w = wts[2 * j + h];
+            L = fmaf(lp[(size_t)j * kRec], w, L);
+            O = fmaf(op[(size_t)j * kRec], w, O);
+        }
+        run0 = n0;
+        run1 = n1;
+    }
+    out[(size_t)h * kD + d] = O / L;
+    return true;
+}
+
 template <typename T>
 __global__ void __launch_bounds__(kDecThreads, 2) decode_split_kernel(const DecodeArgs a)
 {
@@ -136,17 +217,9 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_split_kernel(const Deco
     T* Vs = reinterpret_cast<T*>(vreg);
     float* sc = reinterpret_cast<float*>(vreg + dec_kv_bytes<T>(a.chunk));  // [2][chunk]
     float* stat = sc + 2 * a.chunk;  // m0 m1 l0 l1, then [8 warps][2] score maxima
-    uint64_t* bars = reinterpret_cast<uint64_t*>(stat + 24);
-    int* last_flag = reinterpret_cast<int*>(bars + 2);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(stat + 24);  // K rows, V rows, merge records
+    int* last_flag = reinterpret_cast<int*>(bars + 3);
     float* red = reinterpret_cast<float*>(kreg);  // [16][2][128], after the scores
-
-    if (tid == 0) {
-        mbar_init(&bars[0], 1);
-        mbar_init(&bars[1], 1);
-        fence_barrier_init();
-        fence_proxy_async_smem();
-    }
-    __syncthreads();
 
     // Split geometry.  The new token's row (fused append) never comes from the cache.
     int kv_len = 0, nsplit = 0, r0 = 0, nrows = 0, tma_rows = 0;
@@ -174,21 +247,42 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_split_kernel(const Deco
         }
     };
     // Single-sequence form: the geometry is in the parameters, so the split's rows are
-    // requested before waiting for the previous kernel when that kernel did not write them.
-    bool issued = false;
+    // copied before waiting for the previous kernel when that kernel did not write them.
+    bool early = false;
     if (!a.seqs) {
         geometry(a.one);
-        if (tid == 0 && s < nsplit && r0 + tma_rows <= a.prefetch_rows) {
-            issue();
-            issued = true;
-        }
+        early = s < nsplit && r0 + tma_rows <= a.prefetch_rows;
     }
+    if (tid == 0) {
+        mbar_init(&bars[0], 1);
+        mbar_init(&bars[1], 1);
+        mbar_init(&bars[2], 1);
+        fence_barrier_init();
+        fence_proxy_async_smem();
+    }
+    __syncthreads();
+    // The query and the appended row may be written by the previous kernel, so they are read
+    // only after the wait; asking L2 for their lines first is still safe (device writes land in
+    // L2, which the later loads read) and takes the DRAM latency off the path after the wait.
+    // Plain prefetch instructions, one 128-byte line per lane: q of the two heads (8 lines),
+    // then the new K and V rows (4 lines each) in the CTA that appends them.
+    if (a.prefetch_small && warp == 1) {
+        const float* line = nullptr;
+        if (lane < 8) {
+            line = a.q + ((size_t)b * kHq + kGroup * kvh) * kD + lane * 32;
+        } else if (lane < 16 && !a.seqs && a.k_new && kv_len - 1 >= r0 && kv_len - 1 < r0 + nrows) {
+            const size_t off = ((size_t)b * kHkv + kvh) * kD + (lane & 3) * 32;
+            line = (lane < 12 ? a.k_new : a.v_new) + off;
+        }
+        if (line) asm volatile("prefetch.global.L2 [%0];" ::"l"(line));
+    }
+    if (tid == 0 && early) issue();
     // Everything below reads data earlier kernels wrote (descriptors, cache rows, q).
     pdl_wait();
     pdl_trigger();
     if (a.seqs) geometry(a.seqs[b]);
     if (s >= nsplit) return;
-    if (tid == 0 && !issued) issue();
+    if (tid == 0 && !early) issue();
 
     // Query vectors of the two heads sharing this KV head, for the scores: 8 lanes per row,
     // lane part p holds the 16 dims of load_lane16.
@@ -381,69 +475,357 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_split_kernel(const Deco
     if (!*last_flag) return;
 
     // ---- merge (last CTA of this sequence/KV head) -----------------------------------
-    // Records arrive in shared memory in batches by one bulk copy each; every thread then
-    // merges one output element (h, d) from shared memory, with an online max across batches.
-    float* region = reinterpret_cast<float*>(kreg);  // K and V regions are free now
-    const size_t region_bytes = dec_k_region<T>(a.chunk) + dec_kv_bytes<T>(a.chunk);
-    const int cap = (int)(region_bytes / (sizeof(float) * (kRec + 2)));
-    float* wts = region + (size_t)cap * kRec;  // [cap][2]
-    float run0 = -INFINITY, run1 = -INFINITY;  // running max of each head (uniform)
-    float L = 0.f, O = 0.f;                     // this thread's head h, element d
-    uint32_t phase = 1;                         // bars[0] completed phase 0 with the K rows
-    for (int j0 = 0; j0 < nsplit; j0 += cap) {
-        const int nb = min(cap, nsplit - j0);
-        __syncthreads();  // the previous batch is consumed
-        if (tid == 0) {
-            const uint32_t bytes = (uint32_t)nb * kRec * sizeof(float);
-            mbar_arrive_expect_tx(&bars[0], bytes);
-            bulk_g2s(region, recs + (size_t)j0 * kRec, bytes, &bars[0]);
-        }
-        if (__syncthreads_or(!mbar_wait_bounded(&bars[0], phase, kWaitLimitNs, TYB_STATUS_WAIT_TIMEOUT))) return;
-        phase ^= 1u;
-        // Batch maximum of each head: a block reduction over the records' headers.
-        float x0 = -INFINITY, x1 = -INFINITY;
-        for (int j = tid; j < nb; j += kDecThreads) {
-            x0 = fmaxf(x0, region[(size_t)j * kRec + 0]);
-            x1 = fmaxf(x1, region[(size_t)j * kRec + 2]);
-        }
-#pragma unroll
-        for (int off = 16; off >= 1; off >>= 1) {
-            x0 = fmaxf(x0, __shfl_xor_sync(0xffffffffu, x0, off));
-            x1 = fmaxf(x1, __shfl_xor_sync(0xffffffffu, x1, off));
-        }
-        if (lane == 0) {
-            sc[warp] = x0;
-            sc[16 + warp] = x1;
-        }
-        __syncthreads();
-        float n0 = run0, n1 = run1;
-#pragma unroll
-        for (int w = 0; w < kDecThreads / 32; w++) {
-            n0 = fmaxf(n0, sc[w]);
-            n1 = fmaxf(n1, sc[16 + w]);
-        }
-        // Weights of this batch's records against the new maxima.
-        for (int j = tid; j < nb; j += kDecThreads) {
-            wts[2 * j] = fast_exp2(region[(size_t)j * kRec + 0] - n0);
-            wts[2 * j + 1] = fast_exp2(region[(size_t)j * kRec + 2] - n1);
-        }
-        __syncthreads();
-        const float alpha = fast_exp2((h ? run1 : run0) - (h ? n1 : n0));  // 0 on the first batch
-        L *= alpha;
-        O *= alpha;
-        const float* lp = region + 1 + 2 * h;
-        const float* op = region + 4 + (size_t)h * kD + d;
-#pragma unroll 4
-        for (int j = 0; j < nb; j++) {
-            const float w = wts[2 * j + h];
-            L = fmaf(lp[(size_t)j * kRec], w, L);
-            O = fmaf(op[(size_t)j * kRec], w, O);
-        }
-        run0 = n0;
-        run1 = n1;
-    }
-    a.out[out_head + (size_t)h * kD + d] = O / L;
+    if (!merge_records(recs, nsplit, reinterpret_cast<float*>(kreg),
+                       dec_k_region<T>(a.chunk) + dec_kv_bytes<T>(a.chunk), &bars[2], sc, a.out + out_head))
+        return;
     if (tid == 0) a.counters[b * kHkv + kvh] = 0u;
+}
+
+// ---- BF16 single-sequence decode on the tensor cores ---------------------------------------
+//
+// Same split-KV scheme as decode_split_kernel, for one sequence with a BF16 cache, with the two
+// contractions of a split on the tensor cores through warp-level mma.sync (m16n8k16, BF16 in,
+// FP32 accumulate).  The contraction per split is tiny (2 query heads), so it is latency, not
+// throughput, that matters: one mma.sync instruction replaces 128 scalar FMAs, a shuffle tree and
+// the BF16 unpacking of the CUDA-core form.  The FP32 query and the FP32 softmax weights enter as
+// hi + lo BF16 pairs (x = hi + lo to 2^-16 relative), each pair two rows of the 16-row A operand:
+//   scores   S[4][n] = [q0_hi; q0_lo; q1_hi; q1_lo] . K^T      (rows 4..15 of A are zero)
+//            s_h = S[2h] + S[2h+1]
+//   output   O[4][d] = [p0_hi; p0_lo; p1_hi; p1_lo] . V,  o_h = O[2h] + O[2h+1]
+// K and V tiles come by TMA tensor copies ({64 dims, chunk rows} boxes, 128-byte swizzle), so the
+// fragments load with ldmatrix free of bank conflicts.  The tensor maps span the whole slab (so
+// they depend on the cache alone and are encoded once): tile rows past the attended rows hold
+// whatever the slab has there -- masked out of the scores, and zeroed in the V tile.
+// Warps split the score rows by 8-row tiles and the output by 16-dim slices, so no cross-warp
+// reduction of partial outputs is needed.  Split records and the merge are those of
+// decode_split_kernel.
+
+constexpr int kMmaMaxChunk = 192;
+constexpr int kQaPitch = 272;  // bytes per A row of the query (256 + 16: conflict-free A loads)
+
+struct DecodeMmaArgs {
+    const float* q;  // [16][128]
+    float* out;      // query head 2 kvh0's row
+    __nv_bfloat16* k;  // layer slab, head 0 (the new row is written through these)
+    __nv_bfloat16* v;
+    int row_capacity;
+    int kv_len;
+    const float* k_new;  // [8][128] fp32 row appended at kv_len - 1, or NULL
+    const float* v_new;
+    float scale_log2;
+    int chunk;
+    int nsplit;
+    int prefetch_rows;
+    float* partials;
+    unsigned int* counters;
+    int kvh0;
+    int prefetch_small;
+};
+
+__host__ __device__ constexpr size_t mma_pa_pitch(int chunk) { return (size_t)(chunk + 8) * 2; }
+
+// [K tile chunk x 256 B][V tile][P A rows 4 x pitch][q A rows 4 x 272][stat 80 floats]
+// [3 mbarriers][flag], after rounding the base up to 1024 bytes (the swizzle repeats per 1 KB).
+__host__ __device__ constexpr size_t decode_mma_smem_bytes(int chunk)
+{
+    return 1024 + (size_t)chunk * 512 + 4 * mma_pa_pitch(chunk) + 4 * kQaPitch + 80 * sizeof(float) +
+           3 * sizeof(uint64_t) + 16;
+}
+
+__device__ __forceinline__ void mma_16816(float (&c)[4], uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1)
+{
+    // A rows 8..15 (registers a1, a3) are zero.
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], uint32_t addr)
+{
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t (&r)[4], uint32_t addr)
+{
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+
+// TMA tensor copy of the box at {c0 dims, c1 rows, c2 heads} into shared memory, on `bar`.
+__device__ __forceinline__ void tma_box_3d(uint32_t smem_dst, const CUtensorMap* map, int c0, int c1, int c2,
+                                           uint64_t* bar)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::
+            "r"(smem_dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// Byte offset of dims [8 c16, 8 c16 + 8) of row r in a tile of `chunk` rows stored as two
+// 64-dim halves with the 128-byte swizzle of the TMA copy (16-byte unit c ^ (r & 7)).
+__device__ __forceinline__ uint32_t swz(int chunk, int r, int c16)
+{
+    return (uint32_t)((c16 >> 3) * chunk * 128 + r * 128 + (((c16 & 7) ^ (r & 7)) << 4));
+}
+
+__device__ __forceinline__ uint32_t pack_bf16_pair(float lo_elem, float hi_elem)
+{
+    __nv_bfloat162 h = __floats2bfloat162_rn(lo_elem, hi_elem);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// x ~ hi + lo in BF16 (hi = bf16(x), lo = bf16(x - hi)), for a pair of consecutive elements.
+__device__ __forceinline__ void split_pair(float x0, float x1, uint32_t& hi, uint32_t& lo)
+{
+    const __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
+    const float2 hf = __bfloat1622float2(h);
+    hi = *reinterpret_cast<const uint32_t*>(&h);
+    lo = pack_bf16_pair(x0 - hf.x, x1 - hf.y);
+}
+
+__global__ void __launch_bounds__(kDecThreads, 2)
+    decode_mma_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
+                      const DecodeMmaArgs a)
+{
+    extern __shared__ unsigned char smem_raw[];
+    unsigned char* smem =
+        reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const int s = blockIdx.x;
+    const int kvh = a.kvh0 + blockIdx.y;
+    const int tid = threadIdx.x;
+    const int lane = tid & 31;
+    const int warp = tid >> 5;
+    const int g = lane >> 2;  // fragment row group
+    const int t = lane & 3;   // thread in group
+    const int chunk = a.chunk;
+
+    unsigned char* Kt = smem;
+    unsigned char* Vt = smem + (size_t)chunk * 256;
+    unsigned char* Pa = Vt + (size_t)chunk * 256;
+    const int ppitch = (int)mma_pa_pitch(chunk);
+    unsigned char* Qa = Pa + 4 * ppitch;
+    float* stat = reinterpret_cast<float*>(Qa + 4 * kQaPitch);  // wmax[8][2] lw[8][2] | red32 at +48
+    uint64_t* bars = reinterpret_cast<uint64_t*>(stat + 80);    // K, V, merge records
+    int* last_flag = reinterpret_cast<int*>(bars + 3);
+    const uint32_t kt_u32 = smem_u32(Kt), vt_u32 = smem_u32(Vt);
+
+    const int kv_len = a.kv_len;
+    const int nsplit = a.nsplit;
+    const int r0 = s * chunk;
+    const int nrows = min(chunk, kv_len - r0);       // >= 1: the grid has nsplit splits
+    const int cache_rows = a.k_new ? kv_len - 1 : kv_len;  // rows read from the cache
+    const int trows = max(0, min(nrows, cache_rows - r0));
+    const bool early = r0 + trows <= a.prefetch_rows;
+
+    if (tid == 0) {
+        mbar_init(&bars[0], 1);
+        mbar_init(&bars[1], 1);
+        mbar_init(&bars[2], 1);
+        fence_barrier_init();
+        fence_proxy_async_smem();
+    }
+    __syncthreads();
+    auto issue = [&]() {  // full boxes (rows past the slab arrive as zeros and count)
+        const uint32_t half = (uint32_t)chunk * 128;
+        mbar_arrive_expect_tx(&bars[0], 2 * half);
+        tma_box_3d(kt_u32, &tmk, 0, r0, kvh, &bars[0]);
+        tma_box_3d(kt_u32 + half, &tmk, 64, r0, kvh, &bars[0]);
+        mbar_arrive_expect_tx(&bars[1], 2 * half);
+        tma_box_3d(vt_u32, &tmv, 0, r0, kvh, &bars[1]);
+        tma_box_3d(vt_u32 + half, &tmv, 64, r0, kvh, &bars[1]);
+    };
+    if (tid == 0 && early) issue();
+    const bool has_new = a.k_new && kv_len - 1 >= r0 && kv_len - 1 < r0 + nrows;
+    // q and the appended row may be written by the previous kernel: read after the wait, but
+    // their L2 lines requested now (plain prefetches, one 128-byte line per lane).
+    if (a.prefetch_small && warp == 1) {
+        const float* line = nullptr;
+        if (lane < 8)
+            line = a.q + (size_t)(kGroup * kvh) * kD + lane * 32;
+        else if (lane < 16 && has_new)
+            line = (lane < 12 ? a.k_new : a.v_new) + (size_t)kvh * kD + (lane & 3) * 32;
+        if (line) asm volatile("prefetch.global.L2 [%0];" ::"l"(line));
+    }
+    pdl_wait();
+    pdl_trigger();
+    if (tid == 0 && !early) issue();
+
+    // The query of both heads as A rows q0_hi, q0_lo, q1_hi, q1_lo (BF16).
+    if (tid < 64) {
+        const int h = tid >> 5, d0 = (tid & 31) * 4;
+        const float4 x = *reinterpret_cast<const float4*>(a.q + (size_t)(kGroup * kvh + h) * kD + d0);
+        uint32_t hi0, lo0, hi1, lo1;
+        split_pair(x.x, x.y, hi0, lo0);
+        split_pair(x.z, x.w, hi1, lo1);
+        *reinterpret_cast<uint2*>(Qa + (2 * h) * kQaPitch + d0 * 2) = make_uint2(hi0, hi1);
+        *reinterpret_cast<uint2*>(Qa + (2 * h + 1) * kQaPitch + d0 * 2) = make_uint2(lo0, lo1);
+    }
+    // The appended row: threads 64..79 write it to the cache and, once the tiles have landed,
+    // into its tile row (the copy may have read the slab's old contents there).
+    const int rn = kv_len - 1 - r0;
+    const bool new_thread = has_new && tid >= 64 && tid < 80;
+    float nk[8], nv[8];
+    if (new_thread) {
+        const int i = tid - 64;
+        const size_t off = (size_t)kvh * kD + i * 8;
+        load8(a.k_new + off, nk);
+        load8(a.v_new + off, nv);
+        const size_t row = ((size_t)kvh * a.row_capacity + (kv_len - 1)) * kD + i * 8;
+        store8(a.k + row, nk);
+        store8(a.v + row, nv);
+    }
+    const bool kok = mbar_wait_bounded(&bars[0], 0, kWaitLimitNs, TYB_STATUS_WAIT_TIMEOUT);
+    if (new_thread) store8(reinterpret_cast<__nv_bfloat16*>(Kt + swz(chunk, rn, tid - 64)), nk);
+    if (__syncthreads_or(!kok)) return;
+
+    // Scores.  Warp w takes the 8-row tiles w, w + 8, ... of the first ceil16(nrows) rows (a
+    // whole 16-row step, so that the weights of the last step are all written).
+    const int ntiles = ((nrows + 15) >> 4) * 2;
+    uint32_t qa0[8], qa2[8];
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        qa0[j] = 0u;
+        qa2[j] = 0u;
+        if (lane < 16) {
+            qa0[j] = *reinterpret_cast<const uint32_t*>(Qa + g * kQaPitch + (16 * j + 2 * t) * 2);
+            qa2[j] = *reinterpret_cast<const uint32_t*>(Qa + g * kQaPitch + (16 * j + 8 + 2 * t) * 2);
+        }
+    }
+    // Lanes 0..3 hold head 0, lanes 8..11 head 1: rows 8 nt + 2t, +1 of each of their tiles.
+    const bool holder = (lane & 4) == 0 && lane < 16;
+    const int hh = lane >> 3;  // head of a holder lane
+    float sv[3][2];
+    float m = -INFINITY;
+#pragma unroll
+    for (int k = 0; k < 3; k++) {
+        sv[k][0] = sv[k][1] = -INFINITY;
+        const int nt = warp + 8 * k;
+        if (nt >= ntiles) break;
+        float c[4] = {0.f, 0.f, 0.f, 0.f};
+        const int rr = nt * 8 + (lane & 7);
+#pragma unroll
+        for (int jj = 0; jj < 4; jj++) {
+            uint32_t b[4];
+            ldsm_x4(b, kt_u32 + swz(chunk, rr, 4 * jj + (lane >> 3)));
+            mma_16816(c, qa0[2 * jj], qa2[2 * jj], b[0], b[1]);
+            mma_16816(c, qa0[2 * jj + 1], qa2[2 * jj + 1], b[2], b[3]);
+        }
+        const float s0 = c[0] + __shfl_down_sync(0xffffffffu, c[0], 4);
+        const float s1 = c[1] + __shfl_down_sync(0xffffffffu, c[1], 4);
+        const int ra = nt * 8 + 2 * t;
+        sv[k][0] = ra < nrows ? s0 * a.scale_log2 : -INFINITY;
+        sv[k][1] = ra + 1 < nrows ? s1 * a.scale_log2 : -INFINITY;
+        m = fmaxf(m, fmaxf(sv[k][0], sv[k][1]));
+    }
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+    float* wmax = stat;       // [8 warps][2]
+    float* lw = stat + 16;    // [8 warps][2]
+    if (lane == 0 || lane == 8) wmax[2 * warp + hh] = m;
+    __syncthreads();
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kDecThreads / 32; w++) M = fmaxf(M, wmax[2 * w + (hh & 1)]);
+
+    // Weights: p = 2^(s - M), written as A rows p0_hi, p0_lo, p1_hi, p1_lo; sums per warp.
+    float l = 0.f;
+#pragma unroll
+    for (int k = 0; k < 3; k++) {
+        const int nt = warp + 8 * k;
+        if (nt >= ntiles) break;
+        if (holder) {
+            const float p0 = fast_exp2(sv[k][0] - M), p1 = fast_exp2(sv[k][1] - M);
+            l += p0 + p1;
+            uint32_t hi, lo;
+            split_pair(p0, p1, hi, lo);
+            *reinterpret_cast<uint32_t*>(Pa + (2 * hh) * ppitch + (nt * 8 + 2 * t) * 2) = hi;
+            *reinterpret_cast<uint32_t*>(Pa + (2 * hh + 1) * ppitch + (nt * 8 + 2 * t) * 2) = lo;
+        }
+    }
+    l += __shfl_xor_sync(0xffffffffu, l, 1);
+    l += __shfl_xor_sync(0xffffffffu, l, 2);
+    if (lane == 0 || lane == 8) lw[2 * warp + hh] = l;
+
+    const bool vok = mbar_wait_bounded(&bars[1], 0, kWaitLimitNs, TYB_STATUS_WAIT_TIMEOUT);
+    // V rows the weights do not cover but the last 16-row step reads: zeros (0 * stale NaN is NaN).
+    {
+        const int z0 = trows + (has_new ? 1 : 0), z1 = ntiles * 8;
+        for (int i = tid; i < (z1 - z0) * 16; i += kDecThreads)
+            *reinterpret_cast<uint4*>(Vt + swz(chunk, z0 + (i >> 4), i & 15)) = make_uint4(0u, 0u, 0u, 0u);
+    }
+    if (new_thread) store8(reinterpret_cast<__nv_bfloat16*>(Vt + swz(chunk, rn, tid - 64)), nv);
+    if (__syncthreads_or(!vok)) return;
+
+    // Output slice: warp w owns dims [16 w, 16 w + 16), two 8-dim tiles, over all rows.
+    float o0[4] = {0.f, 0.f, 0.f, 0.f}, o1[4] = {0.f, 0.f, 0.f, 0.f};
+    const int ksteps = ntiles >> 1;
+    const int vrow_in = (lane & 7) + 8 * ((lane >> 3) & 1);
+    const int vc16 = 2 * warp + (lane >> 4);
+    for (int j = 0; j < ksteps; j++) {
+        uint32_t pa0 = 0u, pa2 = 0u;
+        if (lane < 16) {
+            pa0 = *reinterpret_cast<const uint32_t*>(Pa + g * ppitch + (16 * j + 2 * t) * 2);
+            pa2 = *reinterpret_cast<const uint32_t*>(Pa + g * ppitch + (16 * j + 8 + 2 * t) * 2);
+        }
+        uint32_t b[4];
+        ldsm_x4_trans(b, vt_u32 + swz(chunk, 16 * j + vrow_in, vc16));
+        mma_16816(o0, pa0, pa2, b[0], b[1]);
+        mma_16816(o1, pa0, pa2, b[2], b[3]);
+    }
+    // o_h = O[2h] + O[2h+1]: holder lanes, dims 16 w + 8 tile + 2t, +1.
+    const float y00 = o0[0] + __shfl_down_sync(0xffffffffu, o0[0], 4);
+    const float y01 = o0[1] + __shfl_down_sync(0xffffffffu, o0[1], 4);
+    const float y10 = o1[0] + __shfl_down_sync(0xffffffffu, o1[0], 4);
+    const float y11 = o1[1] + __shfl_down_sync(0xffffffffu, o1[1], 4);
+    float L = 0.f;
+#pragma unroll
+    for (int w = 0; w < kDecThreads / 32; w++) L += lw[2 * w + (hh & 1)];
+    const int dim = 16 * warp + 2 * t;
+    float* out_pair = a.out + (size_t)(kGroup * (kvh - a.kvh0)) * kD;  // rows of query heads 2 kvh, 2 kvh + 1
+
+    if (nsplit == 1) {
+        if (holder) {
+            float* o = out_pair + (size_t)hh * kD + dim;
+            const float inv = 1.f / L;
+            *reinterpret_cast<float2*>(o) = make_float2(y00 * inv, y01 * inv);
+            *reinterpret_cast<float2*>(o + 8) = make_float2(y10 * inv, y11 * inv);
+        }
+        return;
+    }
+
+    float* recs = a.partials + (size_t)kvh * a.nsplit * kRec;
+    {
+        float* mine = recs + (size_t)s * kRec;
+        if (holder) {
+            float* o = mine + 4 + (size_t)hh * kD + dim;
+            *reinterpret_cast<float2*>(o) = make_float2(y00, y01);
+            *reinterpret_cast<float2*>(o + 8) = make_float2(y10, y11);
+            if (t == 0 && warp == 0) {
+                mine[2 * hh] = M;
+                mine[2 * hh + 1] = L;
+            }
+        }
+    }
+    __syncthreads();
+    if (tid == 0) {
+        unsigned int ticket;
+        asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(ticket) : "l"(&a.counters[kvh]) : "memory");
+        const int last = ticket == (unsigned int)(nsplit - 1);
+        if (last) asm volatile("fence.proxy.async.global;" ::: "memory");  // records are read by TMA below
+        *last_flag = last;
+    }
+    __syncthreads();
+    if (!*last_flag) return;
+    if (!merge_records(recs, nsplit, reinterpret_cast<float*>(Kt), (size_t)chunk * 512, &bars[2], stat + 48,
+                       out_pair))
+        return;
+    if (tid == 0) a.counters[kvh] = 0u;
 }
 
 // ---- host-side planning ----------------------------------------------------------------
@@ -530,6 +912,67 @@ static int launch_decode(const DecodeArgs& a, int batch, int nkvh, void* stream)
     return (int)cudaLaunchKernelEx(&cfg, decode_split_kernel<T>, a);
 }
 
+// Tensor maps of a layer's K and V slabs (all row_capacity rows, boxes of `chunk` rows), kept in
+// a small direct-mapped table: they depend only on the slab, so a decode step reuses the maps of
+// the previous one instead of encoding two per launch (a few microseconds of host time each).
+struct SlabMaps {
+    CUtensorMap mk, mv;
+    const void* k;
+    const void* v;
+    int row_capacity;
+    int chunk;
+};
+static std::mutex g_maps_mu;
+static SlabMaps g_maps[128];
+
+static bool slab_maps(const tyb_seq_kv& one, int chunk, CUtensorMap* mk, CUtensorMap* mv)
+{
+    const uintptr_t key = reinterpret_cast<uintptr_t>(one.k);
+    const size_t i = (size_t)(((key >> 8) ^ (key >> 20) ^ (uintptr_t)chunk * 0x9e37u) % 128);
+    std::lock_guard<std::mutex> lock(g_maps_mu);
+    SlabMaps& e = g_maps[i];
+    if (e.k != one.k || e.v != one.v || e.row_capacity != one.row_capacity || e.chunk != chunk) {
+        if (tyb_encode_rows_map(&e.mk, one.k, one.row_capacity, one.row_capacity, chunk) != 0 ||
+            tyb_encode_rows_map(&e.mv, one.v, one.row_capacity, one.row_capacity, chunk) != 0) {
+            e.k = e.v = nullptr;
+            return false;
+        }
+        e.k = one.k;
+        e.v = one.v;
+        e.row_capacity = one.row_capacity;
+        e.chunk = chunk;
+    }
+    *mk = e.mk;
+    *mv = e.mv;
+    return true;
+}
+
+// The tensor-core form for one sequence with a BF16 cache.  Splits as planned for
+// decode_split_kernel<bf16> (same record count, so the callers' workspaces fit).
+static int launch_decode_mma(DecodeMmaArgs a, const tyb_seq_kv& one, int nkvh, void* stream)
+{
+    static bool attr_done = false;
+    if (!attr_done) {
+        cudaError_t e = cudaFuncSetAttribute(decode_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)decode_mma_smem_bytes(kMmaMaxChunk));
+        if (e != cudaSuccess) return (int)e;
+        attr_done = true;
+    }
+    CUtensorMap mk, mv;
+    if (!slab_maps(one, a.chunk, &mk, &mv)) return (int)cudaErrorInvalidValue;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(a.nsplit, nkvh, 1);
+    cfg.blockDim = dim3(kDecThreads);
+    cfg.dynamicSmemBytes = decode_mma_smem_bytes(a.chunk);
+    cfg.stream = (cudaStream_t)stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return (int)cudaLaunchKernelEx(&cfg, decode_mma_kernel, mk, mv, a);
+}
+
 }  // namespace tyb
 
 using namespace tyb;
@@ -550,11 +993,12 @@ extern "C" size_t tyb_decode_partial_floats(int batch, int nsplit)
 extern "C" int tyb_decode_launch_heads(const float* q, float* out, const tyb_seq_kv* seqs_dev, tyb_seq_kv one,
                                        int batch, int max_kv_len, int kv_dtype, float scale, float* partials,
                                        unsigned int* counters, const float* k_new, const float* v_new,
-                                       int prefetch_rows, int kvh0, int nkvh, void* stream)
+                                       int prefetch_rows, int kvh0, int nkvh, int flags, void* stream)
 {
     if (batch <= 0 || max_kv_len <= 0 || nkvh <= 0) return 0;
     DecodeArgs a;
     a.kvh0 = kvh0;
+    a.prefetch_small = (flags & TYB_DEC_DEVICE_SMALL) != 0;
     a.q = q;
     a.out = out;
     a.seqs = seqs_dev;
@@ -572,6 +1016,26 @@ extern "C" int tyb_decode_launch_heads(const float* q, float* out, const tyb_seq
     a.prefetch_rows = seqs_dev ? 0 : prefetch_rows;
     a.partials = partials;
     a.counters = counters;
+    if (kv_dtype == TYB_BF16 && !seqs_dev && batch == 1 && chunk <= kMmaMaxChunk) {
+        DecodeMmaArgs m;
+        m.q = q;
+        m.out = out;
+        m.k = static_cast<__nv_bfloat16*>(const_cast<void*>(one.k));
+        m.v = static_cast<__nv_bfloat16*>(const_cast<void*>(one.v));
+        m.row_capacity = one.row_capacity;
+        m.kv_len = one.kv_len;
+        m.k_new = k_new;
+        m.v_new = v_new;
+        m.scale_log2 = a.scale_log2;
+        m.chunk = chunk;
+        m.nsplit = (one.kv_len + chunk - 1) / chunk;
+        m.prefetch_rows = prefetch_rows;
+        m.partials = partials;
+        m.counters = counters;
+        m.kvh0 = kvh0;
+        m.prefetch_small = a.prefetch_small;
+        return launch_decode_mma(m, one, nkvh, stream);
+    }
     if (kv_dtype == TYB_BF16) return launch_decode<__nv_bfloat16>(a, batch, nkvh, stream);
     return launch_decode<float>(a, batch, nkvh, stream);
 }
@@ -582,7 +1046,7 @@ extern "C" int tyb_decode_launch_ex(const float* q, float* out, const tyb_seq_kv
                                     int prefetch_rows, void* stream)
 {
     return tyb_decode_launch_heads(q, out, seqs_dev, one, batch, max_kv_len, kv_dtype, scale, partials, counters,
-                                   k_new, v_new, prefetch_rows, 0, kHkv, stream);
+                                   k_new, v_new, prefetch_rows, 0, kHkv, 0, stream);
 }
 
 extern "C" int tyb_decode_launch(const float* q, float* out, const tyb_seq_kv* seqs_dev, tyb_seq_kv one,

@@ -750,19 +750,25 @@ static EncodeTiledFn encode_fn()
     return fn;
 }
 
-// Rows [0, rows) of the 8 heads of one layer's BF16 cache as a 3-D tensor {128, rows, 8};
-// rows past `rows` read as zeros.
-static bool make_kv_map(CUtensorMap* map, const void* base, int rows, int row_capacity)
+// Rows [0, rows) of the 8 heads of one layer's BF16 cache as a 3-D tensor {128, rows, 8},
+// copied in boxes of {64 dims, box_rows rows, 1 head} with the 128-byte swizzle; rows past
+// `rows` read as zeros.
+static bool make_rows_map(CUtensorMap* map, const void* base, int rows, int row_capacity, int box_rows)
 {
     EncodeTiledFn fn = encode_fn();
-    if (!fn) return false;
+    if (!fn || rows <= 0 || box_rows <= 0 || box_rows > 256) return false;
     const cuuint64_t dims[3] = {(cuuint64_t)kD, (cuuint64_t)rows, (cuuint64_t)kHkv};
     const cuuint64_t strides[2] = {(cuuint64_t)kD * 2, (cuuint64_t)row_capacity * kD * 2};
-    const cuuint32_t box[3] = {64, (cuuint32_t)kPtKeys, 1};
+    const cuuint32_t box[3] = {64, (cuuint32_t)box_rows, 1};
     const cuuint32_t estr[3] = {1, 1, 1};
     return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+static bool make_kv_map(CUtensorMap* map, const void* base, int rows, int row_capacity)
+{
+    return make_rows_map(map, base, rows, row_capacity, kPtKeys);
 }
 
 constexpr size_t kPtSmemBytes = 6 * (size_t)kPtTile + 256 + 1024;  // tiles + barriers + alignment slack
@@ -770,6 +776,11 @@ constexpr size_t kPtSmemBytes = 6 * (size_t)kPtTile + 256 + 1024;  // tiles + ba
 }  // namespace tyb
 
 using namespace tyb;
+
+extern "C" int tyb_encode_rows_map(void* map, const void* base, int rows, int row_capacity, int box_rows)
+{
+    return make_rows_map(static_cast<CUtensorMap*>(map), base, rows, row_capacity, box_rows) ? 0 : 1;
+}
 
 extern "C" int tyb_kv_prep_launch(const void* k_raw, const void* v_raw, int in_bf16, const float* k_norm,
                                   const float* cos, const float* sin, void* k_dst, void* v_dst, int row_capacity,
