@@ -485,20 +485,19 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_split_kernel(const Deco
 //
 // Same split-KV scheme as decode_split_kernel, for one sequence with a BF16 cache, with the two
 // contractions of a split on the tensor cores through warp-level mma.sync (m16n8k16, BF16 in,
-// FP32 accumulate).  The contraction per split is tiny (2 query heads), so it is latency, not
-// throughput, that matters: one mma.sync instruction replaces 128 scalar FMAs, a shuffle tree and
-// the BF16 unpacking of the CUDA-core form.  The FP32 query and the FP32 softmax weights enter as
-// hi + lo BF16 pairs (x = hi + lo to 2^-16 relative), each pair two rows of the 16-row A operand:
-//   scores   S[4][n] = [q0_hi; q0_lo; q1_hi; q1_lo] . K^T      (rows 4..15 of A are zero)
-//            s_h = S[2h] + S[2h+1]
-//   output   O[4][d] = [p0_hi; p0_lo; p1_hi; p1_lo] . V,  o_h = O[2h] + O[2h+1]
-// K and V tiles come by TMA tensor copies ({64 dims, chunk rows} boxes, 128-byte swizzle), so the
-// fragments load with ldmatrix free of bank conflicts.  The tensor maps span the whole slab (so
-// they depend on the cache alone and are encoded once): tile rows past the attended rows hold
-// whatever the slab has there -- masked out of the scores, and zeroed in the V tile.
-// Warps split the score rows by 8-row tiles and the output by 16-dim slices, so no cross-warp
-// reduction of partial outputs is needed.  Split records and the merge are those of
-// decode_split_kernel.
+// FP32 accumulate).  The contraction per split is tiny (2 query heads), so latency, not
+// throughput, is what matters: one mma.sync replaces 256 scalar FMAs, a shuffle tree and the BF16
+// unpacking of the CUDA-core form.  The FP32 query and the FP32 softmax weights enter as hi + lo
+// BF16 pairs (x = hi + lo to 2^-16 relative), each pair two of the 8 columns of the B operand:
+//   scores   S^T[rows][4] = K[rows][128] . [q0_hi q0_lo q1_hi q1_lo]^T,  s_h = S_h,hi + S_h,lo
+//   output   O^T[128][4]  = V^T[128][rows] . [p0_hi p0_lo p1_hi p1_lo]^T, o_h = O_h,hi + O_h,lo
+// (columns 4..7 are zero).  K and V tiles come by TMA tensor copies ({64 dims, chunk rows} boxes,
+// 128-byte swizzle), so the A fragments load with ldmatrix free of bank conflicts.  The tensor
+// maps span the whole slab (so they depend on the cache alone and are encoded once): tile rows
+// past the attended rows hold whatever the slab has there -- masked out of the scores, and
+// zeroed in the V tile.  Warps split the score rows by 16-row tiles and the output by 16-dim
+// slices, so no cross-warp reduction of partial outputs is needed.  Split records and tickets
+// are those of decode_split_kernel; the last CTA merges with plain loads from L2.
 
 constexpr int kMmaMaxChunk = 192;
 constexpr int kQaPitch = 272;  // bytes per A row of the query (256 + 16: conflict-free A loads)
@@ -532,14 +531,13 @@ __host__ __device__ constexpr size_t decode_mma_smem_bytes(int chunk)
            3 * sizeof(uint64_t) + 16;
 }
 
-__device__ __forceinline__ void mma_16816(float (&c)[4], uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1)
+__device__ __forceinline__ void mma_16816_full(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1)
 {
-    // A rows 8..15 (registers a1, a3) are zero.
     asm volatile(
         "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
         "{%0,%1,%2,%3};"
         : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-        : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
 __device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], uint32_t addr)
@@ -587,6 +585,66 @@ __device__ __forceinline__ void split_pair(float x0, float x1, uint32_t& hi, uin
     const float2 hf = __bfloat1622float2(h);
     hi = *reinterpret_cast<const uint32_t*>(&h);
     lo = pack_bf16_pair(x0 - hf.x, x1 - hf.y);
+}
+
+// Merge of the `nsplit` split records of one KV head by the CTA that took the last ticket, with
+// plain loads from L2 (no copy into shared memory; one load round trip per 32 records).  Per batch
+// of 32: warp h (h = 0, 1) fetches the records' headers, one per lane, and computes head h's
+// batch maximum, the rescale of what came before, each record's weight 2^(m_j - max) into `wts`
+// and the running sum; meanwhile every thread fetches its element (h, d) = (tid / 128, tid % 128)
+// of each record, then accumulates it against the weights with four independent chains.  Loads
+// bypass L1 (.cg): the records were written by other CTAs, and the workspace by earlier launches.
+// wts: 2 * 32 + 4 floats of shared memory.  Every thread of the CTA calls it; writes
+// out[h * 128 + d].
+__device__ __forceinline__ void merge_records_direct(const float* recs, int nsplit, float* wts, float* out)
+{
+    const int tid = threadIdx.x;
+    const int lane = tid & 31;
+    const int warp = tid >> 5;
+    const int h = tid >> 7;
+    const int d = tid & 127;
+    float* alpha_s = wts + 64;  // [2] rescale of the running sums, [2] running weight sums
+    float run = -INFINITY, Lrun = 0.f;  // warps 0, 1: head `warp`'s running maximum and sum
+    float O = 0.f;
+    for (int j0 = 0; j0 < nsplit; j0 += 32) {
+        const int nb = min(32, nsplit - j0);
+        const float* r = recs + (size_t)j0 * kRec;
+        if (j0) __syncthreads();  // the previous batch's weights are consumed
+        float ov[32];
+#pragma unroll
+        for (int j = 0; j < 32; j++) ov[j] = j < nb ? __ldcg(r + (size_t)j * kRec + 4 + h * kD + d) : 0.f;
+        if (warp < 2) {
+            float mj = -INFINITY, lj = 0.f;
+            if (lane < nb) {
+                const float2 e = __ldcg(reinterpret_cast<const float2*>(r + (size_t)lane * kRec + 2 * warp));
+                mj = e.x;
+                lj = e.y;
+            }
+            float mb = mj;
+#pragma unroll
+            for (int off = 16; off >= 1; off >>= 1) mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, off));
+            const float nr = fmaxf(run, mb);
+            const float alpha = fast_exp2(run - nr);  // 0 on the first batch
+            const float w = lane < nb ? fast_exp2(mj - nr) : 0.f;
+            float lw = w * lj;
+#pragma unroll
+            for (int off = 16; off >= 1; off >>= 1) lw += __shfl_xor_sync(0xffffffffu, lw, off);
+            Lrun = Lrun * alpha + lw;
+            run = nr;
+            wts[32 * warp + lane] = w;
+            if (lane == 0) {
+                alpha_s[warp] = alpha;
+                alpha_s[2 + warp] = Lrun;
+            }
+        }
+        __syncthreads();
+        const float* wh = wts + 32 * h;
+        float o4[4] = {O * alpha_s[h], 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int j = 0; j < 32; j++) o4[j & 3] = fmaf(wh[j], ov[j], o4[j & 3]);  // w = 0 past nb
+        O = (o4[0] + o4[1]) + (o4[2] + o4[3]);
+    }
+    out[(size_t)h * kD + d] = O / alpha_s[2 + h];
 }
 
 __global__ void __launch_bounds__(kDecThreads, 2)
@@ -684,117 +742,138 @@ __global__ void __launch_bounds__(kDecThreads, 2)
     if (new_thread) store8(reinterpret_cast<__nv_bfloat16*>(Kt + swz(chunk, rn, tid - 64)), nk);
     if (__syncthreads_or(!kok)) return;
 
-    // Scores.  Warp w takes the 8-row tiles w, w + 8, ... of the first ceil16(nrows) rows (a
-    // whole 16-row step, so that the weights of the last step are all written).
-    const int ntiles = ((nrows + 15) >> 4) * 2;
-    uint32_t qa0[8], qa2[8];
+    // Scores: S^T[16 rows][8] = K[16 rows][128] . [q0_hi q0_lo q1_hi q1_lo 0 0 0 0]^T per 16-row
+    // tile (K rows as the A operand, ldmatrix from the swizzled tile; the query as the 8 B
+    // columns, 4 of them zero).  Warp w takes tiles w and w + 8 of the first ceil16(nrows) rows.
+    // In the accumulator, lane (g, t) holds rows g and g + 8 of columns 2t, 2t + 1: lanes with
+    // t = h < 2 get s_h = column hi + column lo of both rows, with no data exchange.
+    const int ntiles = (nrows + 15) >> 4;  // 16-row tiles
+    uint32_t qb0[8], qb1[8];
 #pragma unroll
     for (int j = 0; j < 8; j++) {
-        qa0[j] = 0u;
-        qa2[j] = 0u;
+        qb0[j] = 0u;
+        qb1[j] = 0u;
         if (lane < 16) {
-            qa0[j] = *reinterpret_cast<const uint32_t*>(Qa + g * kQaPitch + (16 * j + 2 * t) * 2);
-            qa2[j] = *reinterpret_cast<const uint32_t*>(Qa + g * kQaPitch + (16 * j + 8 + 2 * t) * 2);
+            qb0[j] = *reinterpret_cast<const uint32_t*>(Qa + g * kQaPitch + (16 * j + 2 * t) * 2);
+            qb1[j] = *reinterpret_cast<const uint32_t*>(Qa + g * kQaPitch + (16 * j + 8 + 2 * t) * 2);
         }
     }
-    // Lanes 0..3 hold head 0, lanes 8..11 head 1: rows 8 nt + 2t, +1 of each of their tiles.
-    const bool holder = (lane & 4) == 0 && lane < 16;
-    const int hh = lane >> 3;  // head of a holder lane
-    float sv[3][2];
+    const bool holder = t < 2;  // head t
+    const int nmine = ntiles > warp ? (ntiles - warp + 7) >> 3 : 0;  // warp-uniform, <= 2
+    const int arow = (lane & 7) + 8 * ((lane >> 3) & 1);
+    const int acol = lane >> 4;
+    // All A fragments of the warp's tiles are loaded before the first mma (ldmatrix takes ~50
+    // cycles; loading each just before its mma would serialise the two).
+    float c[2][2][4];  // [tile][even / odd 16-dim step]
+#pragma unroll
+    for (int e = 0; e < 4; e++) c[0][0][e] = c[0][1][e] = c[1][0][e] = c[1][1][e] = 0.f;
+    uint32_t af[2][8][4];
+#pragma unroll
+    for (int k = 0; k < 2; k++)
+        if (k < nmine)
+#pragma unroll
+            for (int j = 0; j < 8; j++) ldsm_x4(af[k][j], kt_u32 + swz(chunk, (warp + 8 * k) * 16 + arow, 2 * j + acol));
+#pragma unroll
+    for (int k = 0; k < 2; k++)
+        if (k < nmine)
+#pragma unroll
+            for (int j = 0; j < 8; j++) mma_16816_full(c[k][j & 1], af[k][j], qb0[j], qb1[j]);
+    float sv[2][2];  // [tile][row g, row g + 8]
     float m = -INFINITY;
 #pragma unroll
-    for (int k = 0; k < 3; k++) {
-        sv[k][0] = sv[k][1] = -INFINITY;
-        const int nt = warp + 8 * k;
-        if (nt >= ntiles) break;
-        float c[4] = {0.f, 0.f, 0.f, 0.f};
-        const int rr = nt * 8 + (lane & 7);
-#pragma unroll
-        for (int jj = 0; jj < 4; jj++) {
-            uint32_t b[4];
-            ldsm_x4(b, kt_u32 + swz(chunk, rr, 4 * jj + (lane >> 3)));
-            mma_16816(c, qa0[2 * jj], qa2[2 * jj], b[0], b[1]);
-            mma_16816(c, qa0[2 * jj + 1], qa2[2 * jj + 1], b[2], b[3]);
-        }
-        const float s0 = c[0] + __shfl_down_sync(0xffffffffu, c[0], 4);
-        const float s1 = c[1] + __shfl_down_sync(0xffffffffu, c[1], 4);
-        const int ra = nt * 8 + 2 * t;
-        sv[k][0] = ra < nrows ? s0 * a.scale_log2 : -INFINITY;
-        sv[k][1] = ra + 1 < nrows ? s1 * a.scale_log2 : -INFINITY;
+    for (int k = 0; k < 2; k++) {
+        const int rb = (warp + 8 * k) * 16 + g;
+        const float s0 = c[k][0][0] + c[k][1][0] + c[k][0][1] + c[k][1][1];
+        const float s1 = c[k][0][2] + c[k][1][2] + c[k][0][3] + c[k][1][3];
+        sv[k][0] = k < nmine && rb < nrows ? s0 * a.scale_log2 : -INFINITY;
+        sv[k][1] = k < nmine && rb + 8 < nrows ? s1 * a.scale_log2 : -INFINITY;
         m = fmaxf(m, fmaxf(sv[k][0], sv[k][1]));
     }
-    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
-    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
-    float* wmax = stat;       // [8 warps][2]
-    float* lw = stat + 16;    // [8 warps][2]
-    if (lane == 0 || lane == 8) wmax[2 * warp + hh] = m;
+    // Maximum over the warp's rows: lanes of equal t.
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 8));
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 16));
+    float* wmax = stat;     // [8 warps][2]
+    float* lw = stat + 16;  // [8 warps][2]
+    if (lane < 2) wmax[2 * warp + lane] = m;
     __syncthreads();
+    const int hh = t & 1;
     float M = -INFINITY;
 #pragma unroll
-    for (int w = 0; w < kDecThreads / 32; w++) M = fmaxf(M, wmax[2 * w + (hh & 1)]);
+    for (int w = 0; w < kDecThreads / 32; w++) M = fmaxf(M, wmax[2 * w + hh]);
 
-    // Weights: p = 2^(s - M), written as A rows p0_hi, p0_lo, p1_hi, p1_lo; sums per warp.
+    // Weights: p = 2^(s - M), written as P rows p0_hi, p0_lo, p1_hi, p1_lo; sums per warp.
     float l = 0.f;
 #pragma unroll
-    for (int k = 0; k < 3; k++) {
-        const int nt = warp + 8 * k;
-        if (nt >= ntiles) break;
+    for (int k = 0; k < 2; k++) {
+        if (k >= nmine) break;
         if (holder) {
-            const float p0 = fast_exp2(sv[k][0] - M), p1 = fast_exp2(sv[k][1] - M);
-            l += p0 + p1;
-            uint32_t hi, lo;
-            split_pair(p0, p1, hi, lo);
-            *reinterpret_cast<uint32_t*>(Pa + (2 * hh) * ppitch + (nt * 8 + 2 * t) * 2) = hi;
-            *reinterpret_cast<uint32_t*>(Pa + (2 * hh + 1) * ppitch + (nt * 8 + 2 * t) * 2) = lo;
+            const int rb = (warp + 8 * k) * 16 + g;
+#pragma unroll
+            for (int u = 0; u < 2; u++) {
+                const float p = fast_exp2(sv[k][u] - M);
+                l += p;
+                const __nv_bfloat16 hi = __float2bfloat16_rn(p);
+                const __nv_bfloat16 lo = __float2bfloat16_rn(p - __bfloat162float(hi));
+                *reinterpret_cast<__nv_bfloat16*>(Pa + (2 * hh) * ppitch + (rb + 8 * u) * 2) = hi;
+                *reinterpret_cast<__nv_bfloat16*>(Pa + (2 * hh + 1) * ppitch + (rb + 8 * u) * 2) = lo;
+            }
         }
     }
-    l += __shfl_xor_sync(0xffffffffu, l, 1);
-    l += __shfl_xor_sync(0xffffffffu, l, 2);
-    if (lane == 0 || lane == 8) lw[2 * warp + hh] = l;
+    l += __shfl_xor_sync(0xffffffffu, l, 4);
+    l += __shfl_xor_sync(0xffffffffu, l, 8);
+    l += __shfl_xor_sync(0xffffffffu, l, 16);
+    if (lane < 2) lw[2 * warp + lane] = l;
 
     const bool vok = mbar_wait_bounded(&bars[1], 0, kWaitLimitNs, TYB_STATUS_WAIT_TIMEOUT);
     // V rows the weights do not cover but the last 16-row step reads: zeros (0 * stale NaN is NaN).
     {
-        const int z0 = trows + (has_new ? 1 : 0), z1 = ntiles * 8;
+        const int z0 = trows + (has_new ? 1 : 0), z1 = ntiles * 16;
         for (int i = tid; i < (z1 - z0) * 16; i += kDecThreads)
             *reinterpret_cast<uint4*>(Vt + swz(chunk, z0 + (i >> 4), i & 15)) = make_uint4(0u, 0u, 0u, 0u);
     }
     if (new_thread) store8(reinterpret_cast<__nv_bfloat16*>(Vt + swz(chunk, rn, tid - 64)), nv);
     if (__syncthreads_or(!vok)) return;
 
-    // Output slice: warp w owns dims [16 w, 16 w + 16), two 8-dim tiles, over all rows.
-    float o0[4] = {0.f, 0.f, 0.f, 0.f}, o1[4] = {0.f, 0.f, 0.f, 0.f};
-    const int ksteps = ntiles >> 1;
-    const int vrow_in = (lane & 7) + 8 * ((lane >> 3) & 1);
-    const int vc16 = 2 * warp + (lane >> 4);
-    for (int j = 0; j < ksteps; j++) {
-        uint32_t pa0 = 0u, pa2 = 0u;
-        if (lane < 16) {
-            pa0 = *reinterpret_cast<const uint32_t*>(Pa + g * ppitch + (16 * j + 2 * t) * 2);
-            pa2 = *reinterpret_cast<const uint32_t*>(Pa + g * ppitch + (16 * j + 8 + 2 * t) * 2);
+    // Output: O^T[16 dims][8] = V^T[16 dims][rows] . [p0_hi p0_lo p1_hi p1_lo 0 0 0 0]^T; warp w
+    // owns dims [16 w, 16 w + 16) (V^T fragments by transposing ldmatrix), two accumulators
+    // (even and odd 16-row steps).  Lane (g, t < 2) ends with head t's dims 16 w + g, + 8.
+    float o[2][4];
+#pragma unroll
+    for (int e = 0; e < 4; e++) o[0][e] = o[1][e] = 0.f;
+    const int vrow = (lane & 7) + 8 * (lane >> 4);
+    const int vcol = 2 * warp + ((lane >> 3) & 1);
+    // Fragments of all (<= 12) row steps first, then the mma chain.
+    uint32_t va[kMmaMaxChunk / 16][4], pb[kMmaMaxChunk / 16][2];
+#pragma unroll
+    for (int j = 0; j < kMmaMaxChunk / 16; j++) {
+        if (j < ntiles) {
+            pb[j][0] = pb[j][1] = 0u;
+            if (lane < 16) {
+                const unsigned char* row = Pa + g * ppitch + (16 * j + 2 * t) * 2;
+                pb[j][0] = *reinterpret_cast<const uint32_t*>(row);
+                pb[j][1] = *reinterpret_cast<const uint32_t*>(row + 16);
+            }
+            ldsm_x4_trans(va[j], vt_u32 + swz(chunk, 16 * j + vrow, vcol));
         }
-        uint32_t b[4];
-        ldsm_x4_trans(b, vt_u32 + swz(chunk, 16 * j + vrow_in, vc16));
-        mma_16816(o0, pa0, pa2, b[0], b[1]);
-        mma_16816(o1, pa0, pa2, b[2], b[3]);
     }
-    // o_h = O[2h] + O[2h+1]: holder lanes, dims 16 w + 8 tile + 2t, +1.
-    const float y00 = o0[0] + __shfl_down_sync(0xffffffffu, o0[0], 4);
-    const float y01 = o0[1] + __shfl_down_sync(0xffffffffu, o0[1], 4);
-    const float y10 = o1[0] + __shfl_down_sync(0xffffffffu, o1[0], 4);
-    const float y11 = o1[1] + __shfl_down_sync(0xffffffffu, o1[1], 4);
+#pragma unroll
+    for (int j = 0; j < kMmaMaxChunk / 16; j++)
+        if (j < ntiles) mma_16816_full(o[j & 1], va[j], pb[j][0], pb[j][1]);
+    const float y0 = o[0][0] + o[1][0] + o[0][1] + o[1][1];  // dim 16 w + g
+    const float y1 = o[0][2] + o[1][2] + o[0][3] + o[1][3];  // dim 16 w + g + 8
     float L = 0.f;
 #pragma unroll
-    for (int w = 0; w < kDecThreads / 32; w++) L += lw[2 * w + (hh & 1)];
-    const int dim = 16 * warp + 2 * t;
+    for (int w = 0; w < kDecThreads / 32; w++) L += lw[2 * w + hh];
+    const int dim = 16 * warp + g;
     float* out_pair = a.out + (size_t)(kGroup * (kvh - a.kvh0)) * kD;  // rows of query heads 2 kvh, 2 kvh + 1
 
     if (nsplit == 1) {
         if (holder) {
-            float* o = out_pair + (size_t)hh * kD + dim;
+            float* o_ = out_pair + (size_t)hh * kD + dim;
             const float inv = 1.f / L;
-            *reinterpret_cast<float2*>(o) = make_float2(y00 * inv, y01 * inv);
-            *reinterpret_cast<float2*>(o + 8) = make_float2(y10 * inv, y11 * inv);
+            o_[0] = y0 * inv;
+            o_[8] = y1 * inv;
         }
         return;
     }
@@ -803,10 +882,10 @@ __global__ void __launch_bounds__(kDecThreads, 2)
     {
         float* mine = recs + (size_t)s * kRec;
         if (holder) {
-            float* o = mine + 4 + (size_t)hh * kD + dim;
-            *reinterpret_cast<float2*>(o) = make_float2(y00, y01);
-            *reinterpret_cast<float2*>(o + 8) = make_float2(y10, y11);
-            if (t == 0 && warp == 0) {
+            float* o_ = mine + 4 + (size_t)hh * kD + dim;
+            o_[0] = y0;
+            o_[8] = y1;
+            if (g == 0 && warp == 0) {
                 mine[2 * hh] = M;
                 mine[2 * hh + 1] = L;
             }
@@ -816,15 +895,11 @@ __global__ void __launch_bounds__(kDecThreads, 2)
     if (tid == 0) {
         unsigned int ticket;
         asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(ticket) : "l"(&a.counters[kvh]) : "memory");
-        const int last = ticket == (unsigned int)(nsplit - 1);
-        if (last) asm volatile("fence.proxy.async.global;" ::: "memory");  // records are read by TMA below
-        *last_flag = last;
+        *last_flag = ticket == (unsigned int)(nsplit - 1);
     }
     __syncthreads();
     if (!*last_flag) return;
-    if (!merge_records(recs, nsplit, reinterpret_cast<float*>(Kt), (size_t)chunk * 512, &bars[2], stat + 48,
-                       out_pair))
-        return;
+    merge_records_direct(recs, nsplit, reinterpret_cast<float*>(Kt), out_pair);
     if (tid == 0) a.counters[kvh] = 0u;
 }
 
