@@ -384,3 +384,44 @@ def test_decode_bf16_split_edges(pkg, lib, oracle, append):
         want = oracle.decode(q, head_first(bf16_round(k)), head_first(bf16_round(v)), kv_len)
         assert np.isfinite(out).all(), kv_len
         assert max_abs(out, want) <= TOL_MAX and rel_l2(out, want) <= TOL_REL, kv_len
+
+
+def test_decode_batched_bf16_edges_nan_tail(pkg, lib, oracle):
+    """Request batch over BF16 caches (the tensor-core form with per-sequence tensor maps):
+    lengths at 16-row and split edges, NaN rows past every sequence's length, device buffers,
+    two calls in a row (tickets reset), one cache used by two sequences."""
+    rng = np.random.default_rng(23)
+    lens = [1, 15, 16, 17, 191, 192, 193, 385, 1000, 4097, 8191]
+    caches, rows = [], []
+    try:
+        for L in lens:
+            h = new_cache(pkg, lib, L + 40, pkg.ATTN_KV_BF16)
+            caches.append(h)
+            k = np.full((L + 40, 8, 128), np.nan, dtype=np.float32)
+            v = np.full((L + 40, 8, 128), np.nan, dtype=np.float32)
+            k[:L] = rng.standard_normal((L, 8, 128), dtype=np.float32)
+            v[:L] = rng.standard_normal((L, 8, 128), dtype=np.float32)
+            fill_layer(pkg, lib, h, 9, k, v)
+            rows.append((k[:L], v[:L]))
+        # the last sequence reads the first cache again, shorter
+        lens_all = lens + [1]
+        cache_all = caches + [caches[0]]
+        rows_all = rows + [rows[0]]
+        n = len(lens_all)
+        arr = (ctypes.c_void_p * n)(*cache_all)
+        kvl = (ctypes.c_int * n)(*lens_all)
+        for call in range(2):
+            q = rng.standard_normal((n, 16, 128), dtype=np.float32)
+            qd = dev(q)
+            od = torch.full((n, 16, 128), float("nan"), dtype=torch.float32, device="cuda")
+            rc = lib.attention_decode_gqa_batched(vp(qd), arr, kvl, vp(od), n, 9, SCALE)
+            assert rc == 0, pkg.last_error(lib)
+            assert lib.attn_sync() == 0, pkg.last_error(lib)
+            out = od.cpu().numpy()
+            for b, (L, (k, v)) in enumerate(zip(lens_all, rows_all)):
+                want = oracle.decode(q[b], head_first(bf16_round(k)), head_first(bf16_round(v)), L)
+                assert np.isfinite(out[b]).all(), (call, b, L)
+                assert max_abs(out[b], want) <= TOL_MAX and rel_l2(out[b], want) <= TOL_REL, (call, b, L)
+    finally:
+        for h in caches:
+            lib.kv_cache_free(h)

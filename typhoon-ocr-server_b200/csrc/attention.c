@@ -249,7 +249,11 @@ int attention_decode_gqa_batched(const float *q, const KVCache *const *caches, c
     }
     void *st = tyb_stream();
     const size_t qb = (size_t)batch * TYB_Q_FLOATS * sizeof(float);
-    tyb_seq_kv *ddesc = (tyb_seq_kv *)tyb_workspace(TYB_WS_DESC, sizeof(tyb_seq_kv) * (size_t)batch);
+    /* Descriptors (and, for BF16 caches, two tensor maps per sequence ahead of them). */
+    const size_t desc_bytes = sizeof(tyb_seq_kv) * (size_t)batch;
+    const size_t upload_bytes = (dtype == TYB_BF16 ? tyb_decode_maps_bytes(batch) : 0) + desc_bytes;
+    unsigned char *upload = (unsigned char *)tyb_workspace(TYB_WS_DESC, upload_bytes);
+    tyb_seq_kv *ddesc = upload ? (tyb_seq_kv *)(upload + (upload_bytes - desc_bytes)) : NULL;
     int qd = tyb_is_device_ptr(q), od = tyb_is_device_ptr(output);
     float *sq = (qd == 0) ? (float *)tyb_workspace(TYB_WS_Q, qb) : NULL;
     float *so = (od == 0) ? (float *)tyb_workspace(TYB_WS_OUT, qb) : NULL;
@@ -257,28 +261,35 @@ int attention_decode_gqa_batched(const float *q, const KVCache *const *caches, c
         free(descs);
         return 1;
     }
-    /* The descriptor upload reads host memory: pageable copies are staged by the driver
-     * before cudaMemcpyAsync returns, so `descs` can be freed right after. */
-    ok = tyb_cuda_ok(cudaMemcpyAsync(ddesc, descs, sizeof(tyb_seq_kv) * (size_t)batch, cudaMemcpyHostToDevice,
-                                     (cudaStream_t)st),
-                     what);
-    free(descs);
-    if (!ok) return 1;
-    const float *dq = to_device(q, sq, qb, &qd, st, what);
-    if (!dq) return 1;
-    float *dout = od ? output : so;
-    tyb_seq_kv none;
-    memset(&none, 0, sizeof none);
     int chunk, nsplit;
     tyb_decode_plan(batch, max_kv, dtype, &chunk, &nsplit);
     float *part = (float *)tyb_workspace(TYB_WS_PARTIALS, tyb_decode_partial_floats(batch, nsplit) * sizeof(float));
     unsigned int *cnt =
         (unsigned int *)tyb_workspace(TYB_WS_COUNTERS, sizeof(unsigned int) * (size_t)batch * KV_NUM_KV_HEADS);
-    if (!part || !cnt) return 1;
-    if (!tyb_cuda_ok(decode_launch(dq, dout, ddesc, none, batch, max_kv, dtype, scale, 0, part, cnt,
-                                   TYB_DEC_DEVICE_SMALL, st),
-                     what))
+    const float *dq = (part && cnt) ? to_device(q, sq, qb, &qd, st, what) : NULL;
+    if (!dq) {
+        free(descs);
         return 1;
+    }
+    float *dout = od ? output : so;
+    if (dtype == TYB_BF16) {
+        /* Uploads the tensor maps and the descriptors in one copy, then launches. */
+        ok = tyb_cuda_ok(tyb_decode_launch_batched(dq, dout, descs, upload, batch, max_kv, scale, part, cnt, st), what);
+        free(descs);
+        if (!ok) return 1;
+    } else {
+        /* The descriptor upload reads host memory: pageable copies are staged by the driver
+         * before cudaMemcpyAsync returns, so `descs` can be freed right after. */
+        ok = tyb_cuda_ok(cudaMemcpyAsync(ddesc, descs, desc_bytes, cudaMemcpyHostToDevice, (cudaStream_t)st), what);
+        free(descs);
+        if (!ok) return 1;
+        tyb_seq_kv none;
+        memset(&none, 0, sizeof none);
+        if (!tyb_cuda_ok(decode_launch(dq, dout, ddesc, none, batch, max_kv, dtype, scale, 0, part, cnt,
+                                       TYB_DEC_DEVICE_SMALL, st),
+                         what))
+            return 1;
+    }
     tyb_note_nowrite(st);
     if (!od && !tyb_cuda_ok(cudaMemcpyAsync(output, dout, qb, cudaMemcpyDeviceToHost, (cudaStream_t)st), what))
         return 1;

@@ -70,6 +70,14 @@ int tyb_decode_launch_heads(const float *q, float *out, const tyb_seq_kv *seqs_d
  * {128 dims, rows, 8 heads}, copied in 128-byte-swizzled boxes of {64, box_rows, 1}; rows
  * past `rows` read as zeros.  0 on success. */
 int tyb_encode_rows_map(void *map, const void *base, int rows, int row_capacity, int box_rows);
+/* Bytes of the tensor maps tyb_decode_launch_batched uploads for `batch` sequences. */
+size_t tyb_decode_maps_bytes(int batch);
+/* Decode for a request batch over BF16 caches on the tensor-core kernel: uploads, in one copy
+ * into `upload` (device, 64-byte aligned, tyb_decode_maps_bytes(batch) + batch descriptors),
+ * two tensor maps per sequence followed by the descriptors `seqs_host`, then launches.  q and
+ * out are device [batch][16][128]; partials/counters as for tyb_decode_launch. */
+int tyb_decode_launch_batched(const float *q, float *out, const tyb_seq_kv *seqs_host, void *upload, int batch,
+                              int max_kv_len, float scale, float *partials, unsigned int *counters, void *stream);
 /* flags of tyb_decode_launch_heads: q, k_new and v_new are device memory (not page-locked host
  * memory mapped into the device), so their L2 lines may be requested before the dependency wait. */
 #define TYB_DEC_DEVICE_SMALL 1

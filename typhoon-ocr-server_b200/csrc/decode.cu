@@ -24,6 +24,8 @@
 // Bandwidth-bound: 2 * kv_len * 128 * sizeof(T) bytes per (sequence, KV head).
 #include <cuda.h>
 
+#include <cstdlib>
+#include <cstring>
 #include <mutex>
 
 #include "common.cuh"
@@ -499,12 +501,18 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_split_kernel(const Deco
 // slices, so no cross-warp reduction of partial outputs is needed.  Split records and tickets
 // are those of decode_split_kernel; the last CTA merges with plain loads from L2.
 
-constexpr int kMmaMaxChunk = 192;
+constexpr int kMmaMaxChunk = 256;    // rows per split (TMA boxes are at most 256 rows)
+constexpr int kMmaBatchChunk = 192;  // rows per split for request batches
 constexpr int kQaPitch = 272;  // bytes per A row of the query (256 + 16: conflict-free A loads)
 
 struct DecodeMmaArgs {
-    const float* q;  // [16][128]
-    float* out;      // query head 2 kvh0's row
+    const float* q;  // [batch][16][128]
+    float* out;      // query head 2 kvh0's row of sequence 0 (row stride 16 x 128 per sequence)
+    // Request batch: per-sequence descriptors and tensor maps (K, V of sequence b at 2b, 2b + 1),
+    // read after the dependency wait; NULL for one sequence (the fields below and the maps in
+    // the parameters are used).
+    const tyb_seq_kv* seqs;
+    const CUtensorMap* maps;
     __nv_bfloat16* k;  // layer slab, head 0 (the new row is written through these)
     __nv_bfloat16* v;
     int row_capacity;
@@ -673,13 +681,24 @@ __global__ void __launch_bounds__(kDecThreads, 2)
     int* last_flag = reinterpret_cast<int*>(bars + 3);
     const uint32_t kt_u32 = smem_u32(Kt), vt_u32 = smem_u32(Vt);
 
-    const int kv_len = a.kv_len;
-    const int nsplit = a.nsplit;
+    const int b = blockIdx.z;
+    const float* qb = a.q + (size_t)b * kHq * kD;
+    int kv_len = a.kv_len;
+    int nsplit = a.nsplit;
+    const CUtensorMap* mk = &tmk;
+    const CUtensorMap* mv = &tmv;
     const int r0 = s * chunk;
-    const int nrows = min(chunk, kv_len - r0);       // >= 1: the grid has nsplit splits
-    const int cache_rows = a.k_new ? kv_len - 1 : kv_len;  // rows read from the cache
-    const int trows = max(0, min(nrows, cache_rows - r0));
-    const bool early = r0 + trows <= a.prefetch_rows;
+    int nrows = 0, trows = 0;
+    auto geometry = [&]() {
+        nrows = min(chunk, kv_len - r0);                       // >= 1 for a split that runs
+        const int cache_rows = a.k_new ? kv_len - 1 : kv_len;  // rows read from the cache
+        trows = max(0, min(nrows, cache_rows - r0));
+    };
+    bool early = false;
+    if (!a.seqs) {
+        geometry();
+        early = r0 + trows <= a.prefetch_rows;
+    }
 
     if (tid == 0) {
         mbar_init(&bars[0], 1);
@@ -692,32 +711,46 @@ __global__ void __launch_bounds__(kDecThreads, 2)
     auto issue = [&]() {  // full boxes (rows past the slab arrive as zeros and count)
         const uint32_t half = (uint32_t)chunk * 128;
         mbar_arrive_expect_tx(&bars[0], 2 * half);
-        tma_box_3d(kt_u32, &tmk, 0, r0, kvh, &bars[0]);
-        tma_box_3d(kt_u32 + half, &tmk, 64, r0, kvh, &bars[0]);
+        tma_box_3d(kt_u32, mk, 0, r0, kvh, &bars[0]);
+        tma_box_3d(kt_u32 + half, mk, 64, r0, kvh, &bars[0]);
         mbar_arrive_expect_tx(&bars[1], 2 * half);
-        tma_box_3d(vt_u32, &tmv, 0, r0, kvh, &bars[1]);
-        tma_box_3d(vt_u32 + half, &tmv, 64, r0, kvh, &bars[1]);
+        tma_box_3d(vt_u32, mv, 0, r0, kvh, &bars[1]);
+        tma_box_3d(vt_u32 + half, mv, 64, r0, kvh, &bars[1]);
     };
     if (tid == 0 && early) issue();
-    const bool has_new = a.k_new && kv_len - 1 >= r0 && kv_len - 1 < r0 + nrows;
+    const bool has_new = !a.seqs && a.k_new && kv_len - 1 >= r0 && kv_len - 1 < r0 + nrows;
     // q and the appended row may be written by the previous kernel: read after the wait, but
     // their L2 lines requested now (plain prefetches, one 128-byte line per lane).
     if (a.prefetch_small && warp == 1) {
         const float* line = nullptr;
         if (lane < 8)
-            line = a.q + (size_t)(kGroup * kvh) * kD + lane * 32;
+            line = qb + (size_t)(kGroup * kvh) * kD + lane * 32;
         else if (lane < 16 && has_new)
             line = (lane < 12 ? a.k_new : a.v_new) + (size_t)kvh * kD + (lane & 3) * 32;
         if (line) asm volatile("prefetch.global.L2 [%0];" ::"l"(line));
     }
     pdl_wait();
     pdl_trigger();
+    if (a.seqs) {
+        // Request batch: this sequence's geometry and tensor maps (written before the launch).
+        const tyb_seq_kv d = a.seqs[b];
+        kv_len = d.kv_len;
+        nsplit = (kv_len + chunk - 1) / chunk;
+        if (s >= nsplit) return;
+        geometry();
+        mk = a.maps + 2 * b;
+        mv = mk + 1;
+        if (tid == 0) {
+            asm volatile("fence.proxy.tensormap::generic.acquire.gpu [%0], 128;" ::"l"(mk) : "memory");
+            asm volatile("fence.proxy.tensormap::generic.acquire.gpu [%0], 128;" ::"l"(mv) : "memory");
+        }
+    }
     if (tid == 0 && !early) issue();
 
     // The query of both heads as A rows q0_hi, q0_lo, q1_hi, q1_lo (BF16).
     if (tid < 64) {
         const int h = tid >> 5, d0 = (tid & 31) * 4;
-        const float4 x = *reinterpret_cast<const float4*>(a.q + (size_t)(kGroup * kvh + h) * kD + d0);
+        const float4 x = *reinterpret_cast<const float4*>(qb + (size_t)(kGroup * kvh + h) * kD + d0);
         uint32_t hi0, lo0, hi1, lo1;
         split_pair(x.x, x.y, hi0, lo0);
         split_pair(x.z, x.w, hi1, lo1);
@@ -866,7 +899,8 @@ __global__ void __launch_bounds__(kDecThreads, 2)
 #pragma unroll
     for (int w = 0; w < kDecThreads / 32; w++) L += lw[2 * w + hh];
     const int dim = 16 * warp + g;
-    float* out_pair = a.out + (size_t)(kGroup * (kvh - a.kvh0)) * kD;  // rows of query heads 2 kvh, 2 kvh + 1
+    // rows of query heads 2 kvh, 2 kvh + 1 of sequence b
+    float* out_pair = a.out + (size_t)b * kHq * kD + (size_t)(kGroup * (kvh - a.kvh0)) * kD;
 
     if (nsplit == 1) {
         if (holder) {
@@ -878,7 +912,7 @@ __global__ void __launch_bounds__(kDecThreads, 2)
         return;
     }
 
-    float* recs = a.partials + (size_t)kvh * a.nsplit * kRec;
+    float* recs = a.partials + ((size_t)b * kHkv + kvh) * a.nsplit * kRec;  // a.nsplit: the record stride
     {
         float* mine = recs + (size_t)s * kRec;
         if (holder) {
@@ -894,13 +928,16 @@ __global__ void __launch_bounds__(kDecThreads, 2)
     __syncthreads();
     if (tid == 0) {
         unsigned int ticket;
-        asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(ticket) : "l"(&a.counters[kvh]) : "memory");
+        asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;"
+                     : "=r"(ticket)
+                     : "l"(&a.counters[b * kHkv + kvh])
+                     : "memory");
         *last_flag = ticket == (unsigned int)(nsplit - 1);
     }
     __syncthreads();
     if (!*last_flag) return;
     merge_records_direct(recs, nsplit, reinterpret_cast<float*>(Kt), out_pair);
-    if (tid == 0) a.counters[kvh] = 0u;
+    if (tid == 0) a.counters[b * kHkv + kvh] = 0u;
 }
 
 // ---- host-side planning ----------------------------------------------------------------
@@ -997,13 +1034,14 @@ struct SlabMaps {
     int row_capacity;
     int chunk;
 };
+constexpr int kSlabMapSlots = 1024;
 static std::mutex g_maps_mu;
-static SlabMaps g_maps[128];
+static SlabMaps g_maps[kSlabMapSlots];
 
 static bool slab_maps(const tyb_seq_kv& one, int chunk, CUtensorMap* mk, CUtensorMap* mv)
 {
     const uintptr_t key = reinterpret_cast<uintptr_t>(one.k);
-    const size_t i = (size_t)(((key >> 8) ^ (key >> 20) ^ (uintptr_t)chunk * 0x9e37u) % 128);
+    const size_t i = (size_t)(((key >> 8) ^ (key >> 20) ^ (uintptr_t)chunk * 0x9e37u) % kSlabMapSlots);
     std::lock_guard<std::mutex> lock(g_maps_mu);
     SlabMaps& e = g_maps[i];
     if (e.k != one.k || e.v != one.v || e.row_capacity != one.row_capacity || e.chunk != chunk) {
@@ -1022,19 +1060,55 @@ static bool slab_maps(const tyb_seq_kv& one, int chunk, CUtensorMap* mk, CUtenso
     return true;
 }
 
+// Splits of the tensor-core form.  One sequence that fits in one CTA per SM (at most 256 rows per
+// split): the split size (a multiple of 16 rows) that minimises the rows one SM must stream --
+// ceil(CTAs / SMs) x rows per split, since the tile reads from shared memory bound a split and
+// CTAs that share an SM share that bandwidth -- plus a fixed cost, in row equivalents, for the
+// ticket and merge when there is more than one split.  At 4K context this gives 18 splits per KV
+// head (144 CTAs, one per SM).  Longer sequences and request batches run in many waves: 192 rows,
+// two CTAs per SM (one streams while the other computes; larger splits amortise fixed costs).
+static void plan_mma(int batch, int max_kv_len, int nkvh, int* chunk_rows, int* nsplit)
+{
+    int best = kMmaBatchChunk;
+    const long long sms = num_sms();
+    if (batch == 1 && (long long)((max_kv_len + kMmaMaxChunk - 1) / kMmaMaxChunk) * nkvh <= sms) {
+        long long best_cost = -1;
+        for (int c = 16; c <= kMmaMaxChunk; c += 16) {
+            const long long splits = (max_kv_len + c - 1) / c;
+            const long long rounds = (splits * nkvh + sms - 1) / sms;
+            const long long cost = rounds * c + (splits > 1 ? 300 + 4 * splits : 0);
+            if (best_cost < 0 || cost <= best_cost) {
+                best_cost = cost;
+                best = c;
+            }
+        }
+    }
+    *chunk_rows = best;
+    *nsplit = max_kv_len > 0 ? (max_kv_len + best - 1) / best : 0;
+}
+
+static int set_mma_smem_attr()
+{
+    static bool done = false;
+    if (!done) {
+        cudaError_t e = cudaFuncSetAttribute(decode_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)decode_mma_smem_bytes(kMmaMaxChunk));
+        if (e != cudaSuccess) return (int)e;
+        done = true;
+    }
+    return 0;
+}
+
 // The tensor-core form for one sequence with a BF16 cache.  Splits as planned for
 // decode_split_kernel<bf16> (same record count, so the callers' workspaces fit).
 static int launch_decode_mma(DecodeMmaArgs a, const tyb_seq_kv& one, int nkvh, void* stream)
 {
-    static bool attr_done = false;
-    if (!attr_done) {
-        cudaError_t e = cudaFuncSetAttribute(decode_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)decode_mma_smem_bytes(kMmaMaxChunk));
-        if (e != cudaSuccess) return (int)e;
-        attr_done = true;
-    }
+    const int e = set_mma_smem_attr();
+    if (e) return e;
     CUtensorMap mk, mv;
     if (!slab_maps(one, a.chunk, &mk, &mv)) return (int)cudaErrorInvalidValue;
+    a.seqs = nullptr;
+    a.maps = nullptr;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.nsplit, nkvh, 1);
     cfg.blockDim = dim3(kDecThreads);
@@ -1052,10 +1126,62 @@ static int launch_decode_mma(DecodeMmaArgs a, const tyb_seq_kv& one, int nkvh, v
 
 using namespace tyb;
 
+extern "C" size_t tyb_decode_maps_bytes(int batch) { return (size_t)batch * 2 * sizeof(CUtensorMap); }
+
+extern "C" int tyb_decode_launch_batched(const float* q, float* out, const tyb_seq_kv* seqs_host, void* upload,
+                                         int batch, int max_kv_len, float scale, float* partials,
+                                         unsigned int* counters, void* stream)
+{
+    if (batch <= 0 || max_kv_len <= 0) return 0;
+    int e = set_mma_smem_attr();
+    if (e) return e;
+    int chunk, nsplit;
+    plan_mma(batch, max_kv_len, kHkv, &chunk, &nsplit);
+    // Host staging: [maps 2 x batch][descriptors batch], one pageable copy (staged by the driver
+    // before cudaMemcpyAsync returns, so the buffer may be freed right after).
+    const size_t maps_bytes = tyb_decode_maps_bytes(batch);
+    const size_t bytes = maps_bytes + sizeof(tyb_seq_kv) * (size_t)batch;
+    CUtensorMap* host = static_cast<CUtensorMap*>(aligned_alloc(64, (bytes + 63) & ~size_t(63)));
+    if (!host) return (int)cudaErrorMemoryAllocation;
+    for (int b = 0; b < batch; b++) {
+        if (!slab_maps(seqs_host[b], chunk, &host[2 * b], &host[2 * b + 1])) {
+            free(host);
+            return (int)cudaErrorInvalidValue;
+        }
+    }
+    memcpy(reinterpret_cast<unsigned char*>(host) + maps_bytes, seqs_host, sizeof(tyb_seq_kv) * (size_t)batch);
+    cudaError_t ce = cudaMemcpyAsync(upload, host, bytes, cudaMemcpyHostToDevice, (cudaStream_t)stream);
+    const CUtensorMap m0 = host[0], m1 = host[1];
+    free(host);
+    if (ce != cudaSuccess) return (int)ce;
+    DecodeMmaArgs a = {};
+    a.q = q;
+    a.out = out;
+    a.seqs = reinterpret_cast<const tyb_seq_kv*>(static_cast<unsigned char*>(upload) + maps_bytes);
+    a.maps = static_cast<const CUtensorMap*>(upload);
+    a.scale_log2 = scale * kLog2e;
+    a.chunk = chunk;
+    a.nsplit = nsplit;  // the record stride; each sequence's own split count comes from its length
+    a.partials = partials;
+    a.counters = counters;
+    a.prefetch_small = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(nsplit, kHkv, batch);
+    cfg.blockDim = dim3(kDecThreads);
+    cfg.dynamicSmemBytes = decode_mma_smem_bytes(chunk);
+    cfg.stream = (cudaStream_t)stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return (int)cudaLaunchKernelEx(&cfg, decode_mma_kernel, m0, m1, a);
+}
+
 extern "C" void tyb_decode_plan(int batch, int max_kv_len, int kv_dtype, int* chunk_rows, int* nsplit)
 {
     if (kv_dtype == TYB_BF16)
-        plan<__nv_bfloat16>(batch, max_kv_len, chunk_rows, nsplit);
+        plan_mma(batch, max_kv_len, kHkv, chunk_rows, nsplit);
     else
         plan<float>(batch, max_kv_len, chunk_rows, nsplit);
 }
@@ -1082,7 +1208,9 @@ extern "C" int tyb_decode_launch_heads(const float* q, float* out, const tyb_seq
     a.v_new = v_new;
     a.scale_log2 = scale * kLog2e;
     int chunk, nsplit;
-    if (kv_dtype == TYB_BF16)
+    if (kv_dtype == TYB_BF16 && !seqs_dev && batch == 1)
+        plan_mma(1, max_kv_len, nkvh, &chunk, &nsplit);
+    else if (kv_dtype == TYB_BF16)
         plan<__nv_bfloat16>(batch, max_kv_len, &chunk, &nsplit, nkvh);
     else
         plan<float>(batch, max_kv_len, &chunk, &nsplit, nkvh);
@@ -1091,7 +1219,7 @@ extern "C" int tyb_decode_launch_heads(const float* q, float* out, const tyb_seq
     a.prefetch_rows = seqs_dev ? 0 : prefetch_rows;
     a.partials = partials;
     a.counters = counters;
-    if (kv_dtype == TYB_BF16 && !seqs_dev && batch == 1 && chunk <= kMmaMaxChunk) {
+    if (kv_dtype == TYB_BF16 && !seqs_dev && batch == 1) {
         DecodeMmaArgs m;
         m.q = q;
         m.out = out;
@@ -1195,8 +1323,7 @@ extern "C" int attention_decode_gqa_noalloc(const float* q, const void* k_rows, 
     int chunk = 0, nsplit = 0;
     tyb_decode_plan(1, kv_len, kv_dtype, &chunk, &nsplit);
     if (nsplit > kNoAllocMaxSplits) {
-        const int max_chunk =
-            kv_dtype == TYB_BF16 ? DecodeTile<__nv_bfloat16>::kMaxChunk : DecodeTile<float>::kMaxChunk;
+        const int max_chunk = kv_dtype == TYB_BF16 ? kMmaMaxChunk : DecodeTile<float>::kMaxChunk;
         tyb_set_error("%s: kv_len %d needs %d splits; the fixed scratch holds %d (kv_len <= %d for this "
                       "element type)",
                       what, kv_len, nsplit, kNoAllocMaxSplits, kNoAllocMaxSplits * max_chunk);
