@@ -82,7 +82,7 @@ def peaks():
 
 def profile_traffic(kind):
     """DRAM bytes per decode launch from the committed ncu summary, if present."""
-    f = ROOT / "profiles" / "decode_split_kernel_config2.md"
+    f = ROOT / "profiles" / "decode_mma_kernel_config2.md"
     if not f.exists():
         return None
     m = re.search(rf"traffic_bytes_per_launch_{kind}:\s*([0-9.eE+]+)", f.read_text())
@@ -788,7 +788,7 @@ def main():
         "roofline": {
             "bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
             "frac": achieved / hbm_peak, "traffic": profile_traffic("bf16"),
-            "kernel": "decode_split_kernel<bf16>",
+            "kernel": "decode_mma_kernel",
             "note": f"algorithmic bytes (K+V rows + q/out) / mean launch time incl. gaps; peak {peak_src}",
         },
         "e2e": {"value": e2e_max * 1e3 / args.e2e_steps, "unit": "us/step", "h2d_bytes_per_step": h2d,

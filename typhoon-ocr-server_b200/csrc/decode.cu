@@ -657,6 +657,7 @@ __device__ __forceinline__ void merge_records_direct(const float* recs, int nspl
 
 __global__ void __launch_bounds__(kDecThreads, 2)
     decode_mma_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
+                      const __grid_constant__ CUtensorMap tmk16, const __grid_constant__ CUtensorMap tmv16,
                       const DecodeMmaArgs a)
 {
     extern __shared__ unsigned char smem_raw[];
@@ -710,6 +711,22 @@ __global__ void __launch_bounds__(kDecThreads, 2)
     __syncthreads();
     auto issue = [&]() {  // full boxes (rows past the slab arrive as zeros and count)
         const uint32_t half = (uint32_t)chunk * 128;
+        if (!a.seqs && s == nsplit - 1 && nrows < chunk) {
+            // Last split of one sequence: only the 16-row groups it attends, with the 16-row
+            // maps (the same swizzle, since each group starts at a multiple of 16 rows).
+            const int groups = (nrows + 15) >> 4;
+            mbar_arrive_expect_tx(&bars[0], (uint32_t)groups * 4096u);
+            for (int i = 0; i < groups; i++) {
+                tma_box_3d(kt_u32 + i * 2048, &tmk16, 0, r0 + 16 * i, kvh, &bars[0]);
+                tma_box_3d(kt_u32 + half + i * 2048, &tmk16, 64, r0 + 16 * i, kvh, &bars[0]);
+            }
+            mbar_arrive_expect_tx(&bars[1], (uint32_t)groups * 4096u);
+            for (int i = 0; i < groups; i++) {
+                tma_box_3d(vt_u32 + i * 2048, &tmv16, 0, r0 + 16 * i, kvh, &bars[1]);
+                tma_box_3d(vt_u32 + half + i * 2048, &tmv16, 64, r0 + 16 * i, kvh, &bars[1]);
+            }
+            return;
+        }
         mbar_arrive_expect_tx(&bars[0], 2 * half);
         tma_box_3d(kt_u32, mk, 0, r0, kvh, &bars[0]);
         tma_box_3d(kt_u32 + half, mk, 64, r0, kvh, &bars[0]);
@@ -1028,7 +1045,8 @@ static int launch_decode(const DecodeArgs& a, int batch, int nkvh, void* stream)
 // a small direct-mapped table: they depend only on the slab, so a decode step reuses the maps of
 // the previous one instead of encoding two per launch (a few microseconds of host time each).
 struct SlabMaps {
-    CUtensorMap mk, mv;
+    CUtensorMap mk, mv;      // boxes of `chunk` rows
+    CUtensorMap mk16, mv16;  // boxes of 16 rows (the last split of a sequence)
     const void* k;
     const void* v;
     int row_capacity;
@@ -1038,7 +1056,8 @@ constexpr int kSlabMapSlots = 1024;
 static std::mutex g_maps_mu;
 static SlabMaps g_maps[kSlabMapSlots];
 
-static bool slab_maps(const tyb_seq_kv& one, int chunk, CUtensorMap* mk, CUtensorMap* mv)
+static bool slab_maps(const tyb_seq_kv& one, int chunk, CUtensorMap* mk, CUtensorMap* mv,
+                      CUtensorMap* mk16 = nullptr, CUtensorMap* mv16 = nullptr)
 {
     const uintptr_t key = reinterpret_cast<uintptr_t>(one.k);
     const size_t i = (size_t)(((key >> 8) ^ (key >> 20) ^ (uintptr_t)chunk * 0x9e37u) % kSlabMapSlots);
@@ -1046,7 +1065,9 @@ static bool slab_maps(const tyb_seq_kv& one, int chunk, CUtensorMap* mk, CUtenso
     SlabMaps& e = g_maps[i];
     if (e.k != one.k || e.v != one.v || e.row_capacity != one.row_capacity || e.chunk != chunk) {
         if (tyb_encode_rows_map(&e.mk, one.k, one.row_capacity, one.row_capacity, chunk) != 0 ||
-            tyb_encode_rows_map(&e.mv, one.v, one.row_capacity, one.row_capacity, chunk) != 0) {
+            tyb_encode_rows_map(&e.mv, one.v, one.row_capacity, one.row_capacity, chunk) != 0 ||
+            tyb_encode_rows_map(&e.mk16, one.k, one.row_capacity, one.row_capacity, 16) != 0 ||
+            tyb_encode_rows_map(&e.mv16, one.v, one.row_capacity, one.row_capacity, 16) != 0) {
             e.k = e.v = nullptr;
             return false;
         }
@@ -1057,6 +1078,8 @@ static bool slab_maps(const tyb_seq_kv& one, int chunk, CUtensorMap* mk, CUtenso
     }
     *mk = e.mk;
     *mv = e.mv;
+    if (mk16) *mk16 = e.mk16;
+    if (mv16) *mv16 = e.mv16;
     return true;
 }
 
@@ -1105,8 +1128,8 @@ static int launch_decode_mma(DecodeMmaArgs a, const tyb_seq_kv& one, int nkvh, v
 {
     const int e = set_mma_smem_attr();
     if (e) return e;
-    CUtensorMap mk, mv;
-    if (!slab_maps(one, a.chunk, &mk, &mv)) return (int)cudaErrorInvalidValue;
+    CUtensorMap mk, mv, mk16, mv16;
+    if (!slab_maps(one, a.chunk, &mk, &mv, &mk16, &mv16)) return (int)cudaErrorInvalidValue;
     a.seqs = nullptr;
     a.maps = nullptr;
     cudaLaunchConfig_t cfg = {};
@@ -1119,7 +1142,7 @@ static int launch_decode_mma(DecodeMmaArgs a, const tyb_seq_kv& one, int nkvh, v
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return (int)cudaLaunchKernelEx(&cfg, decode_mma_kernel, mk, mv, a);
+    return (int)cudaLaunchKernelEx(&cfg, decode_mma_kernel, mk, mv, mk16, mv16, a);
 }
 
 }  // namespace tyb
@@ -1175,7 +1198,7 @@ extern "C" int tyb_decode_launch_batched(const float* q, float* out, const tyb_s
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return (int)cudaLaunchKernelEx(&cfg, decode_mma_kernel, m0, m1, a);
+    return (int)cudaLaunchKernelEx(&cfg, decode_mma_kernel, m0, m1, m0, m1, a);
 }
 
 extern "C" void tyb_decode_plan(int batch, int max_kv_len, int kv_dtype, int* chunk_rows, int* nsplit)
