@@ -504,6 +504,10 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_split_kernel(const Deco
 constexpr int kMmaMaxChunk = 256;    // rows per split (TMA boxes are at most 256 rows)
 constexpr int kMmaBatchChunk = 192;  // rows per split for request batches
 constexpr int kQaPitch = 272;  // bytes per A row of the query (256 + 16: conflict-free A loads)
+// Warps per CTA (NW): the kernel is written for 8 or 16; 8 is the one launched (16 warps -- a score
+// tile per warp, P.V in two row halves -- measured 4-7 % slower at 4K: more barrier and exchange
+// cost than latency hidden).
+constexpr int kMmaStat = 64 + 256;  // floats: block maxima and sums [16][2] x 2, P.V half exchange [8][2][16]
 
 struct DecodeMmaArgs {
     const float* q;  // [batch][16][128]
@@ -531,11 +535,11 @@ struct DecodeMmaArgs {
 
 __host__ __device__ constexpr size_t mma_pa_pitch(int chunk) { return (size_t)(chunk + 8) * 2; }
 
-// [K tile chunk x 256 B][V tile][P A rows 4 x pitch][q A rows 4 x 272][stat 80 floats]
+// [K tile chunk x 256 B][V tile][P rows 4 x pitch][q rows 4 x 272][stat kMmaStat floats]
 // [3 mbarriers][flag], after rounding the base up to 1024 bytes (the swizzle repeats per 1 KB).
 __host__ __device__ constexpr size_t decode_mma_smem_bytes(int chunk)
 {
-    return 1024 + (size_t)chunk * 512 + 4 * mma_pa_pitch(chunk) + 4 * kQaPitch + 80 * sizeof(float) +
+    return 1024 + (size_t)chunk * 512 + 4 * mma_pa_pitch(chunk) + 4 * kQaPitch + kMmaStat * sizeof(float) +
            3 * sizeof(uint64_t) + 16;
 }
 
@@ -609,7 +613,8 @@ __device__ __forceinline__ void merge_records_direct(const float* recs, int nspl
     const int tid = threadIdx.x;
     const int lane = tid & 31;
     const int warp = tid >> 5;
-    const int h = tid >> 7;
+    const bool active = tid < 2 * kD;  // threads past 256 only take part in the barriers
+    const int h = (tid >> 7) & 1;
     const int d = tid & 127;
     float* alpha_s = wts + 64;  // [2] rescale of the running sums, [2] running weight sums
     float run = -INFINITY, Lrun = 0.f;  // warps 0, 1: head `warp`'s running maximum and sum
@@ -618,16 +623,17 @@ __device__ __forceinline__ void merge_records_direct(const float* recs, int nspl
         const int nb = min(32, nsplit - j0);
         const float* r = recs + (size_t)j0 * kRec;
         if (j0) __syncthreads();  // the previous batch's weights are consumed
+        // Headers first: the weights (on the path to the output) need them.
+        float mj = -INFINITY, lj = 0.f;
+        if (warp < 2 && lane < nb) {
+            const float2 e = __ldcg(reinterpret_cast<const float2*>(r + (size_t)lane * kRec + 2 * warp));
+            mj = e.x;
+            lj = e.y;
+        }
         float ov[32];
 #pragma unroll
-        for (int j = 0; j < 32; j++) ov[j] = j < nb ? __ldcg(r + (size_t)j * kRec + 4 + h * kD + d) : 0.f;
+        for (int j = 0; j < 32; j++) ov[j] = active && j < nb ? __ldcg(r + (size_t)j * kRec + 4 + h * kD + d) : 0.f;
         if (warp < 2) {
-            float mj = -INFINITY, lj = 0.f;
-            if (lane < nb) {
-                const float2 e = __ldcg(reinterpret_cast<const float2*>(r + (size_t)lane * kRec + 2 * warp));
-                mj = e.x;
-                lj = e.y;
-            }
             float mb = mj;
 #pragma unroll
             for (int off = 16; off >= 1; off >>= 1) mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, off));
@@ -646,16 +652,19 @@ __device__ __forceinline__ void merge_records_direct(const float* recs, int nspl
             }
         }
         __syncthreads();
-        const float* wh = wts + 32 * h;
-        float o4[4] = {O * alpha_s[h], 0.f, 0.f, 0.f};
+        if (active) {
+            const float* wh = wts + 32 * h;
+            float o4[4] = {O * alpha_s[h], 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int j = 0; j < 32; j++) o4[j & 3] = fmaf(wh[j], ov[j], o4[j & 3]);  // w = 0 past nb
-        O = (o4[0] + o4[1]) + (o4[2] + o4[3]);
+            for (int j = 0; j < 32; j++) o4[j & 3] = fmaf(wh[j], ov[j], o4[j & 3]);  // w = 0 past nb
+            O = (o4[0] + o4[1]) + (o4[2] + o4[3]);
+        }
     }
-    out[(size_t)h * kD + d] = O / alpha_s[2 + h];
+    if (active) out[(size_t)h * kD + d] = O / alpha_s[2 + h];
 }
 
-__global__ void __launch_bounds__(kDecThreads, 2)
+template <int NW>
+__global__ void __launch_bounds__(NW * 32, 16 / NW)
     decode_mma_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
                       const __grid_constant__ CUtensorMap tmk16, const __grid_constant__ CUtensorMap tmv16,
                       const DecodeMmaArgs a)
@@ -677,8 +686,8 @@ __global__ void __launch_bounds__(kDecThreads, 2)
     unsigned char* Pa = Vt + (size_t)chunk * 256;
     const int ppitch = (int)mma_pa_pitch(chunk);
     unsigned char* Qa = Pa + 4 * ppitch;
-    float* stat = reinterpret_cast<float*>(Qa + 4 * kQaPitch);  // wmax[8][2] lw[8][2] | red32 at +48
-    uint64_t* bars = reinterpret_cast<uint64_t*>(stat + 80);    // K, V, merge records
+    float* stat = reinterpret_cast<float*>(Qa + 4 * kQaPitch);  // wmax[16][2] lw[16][2] xo[8][2][16]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(stat + kMmaStat);  // K, V, merge records
     int* last_flag = reinterpret_cast<int*>(bars + 3);
     const uint32_t kt_u32 = smem_u32(Kt), vt_u32 = smem_u32(Vt);
 
@@ -711,9 +720,10 @@ __global__ void __launch_bounds__(kDecThreads, 2)
     __syncthreads();
     auto issue = [&]() {  // full boxes (rows past the slab arrive as zeros and count)
         const uint32_t half = (uint32_t)chunk * 128;
-        if (!a.seqs && s == nsplit - 1 && nrows < chunk) {
-            // Last split of one sequence: only the 16-row groups it attends, with the 16-row
-            // maps (the same swizzle, since each group starts at a multiple of 16 rows).
+        if (!a.seqs && s == nsplit - 1 && nrows <= 64 && nrows < chunk) {
+            // Short last split of one sequence: only the (at most 4) 16-row groups it attends,
+            // with the 16-row maps (the same swizzle, since each group starts at a multiple of 16
+            // rows); longer last splits take the full box (fewer copies to issue).
             const int groups = (nrows + 15) >> 4;
             mbar_arrive_expect_tx(&bars[0], (uint32_t)groups * 4096u);
             for (int i = 0; i < groups; i++) {
@@ -808,57 +818,65 @@ __global__ void __launch_bounds__(kDecThreads, 2)
             qb1[j] = *reinterpret_cast<const uint32_t*>(Qa + g * kQaPitch + (16 * j + 8 + 2 * t) * 2);
         }
     }
+    constexpr int KT = 16 / NW;      // score tiles per warp
+    constexpr int HALVES = NW / 8;   // row parts of P.V
+    constexpr int STEPS = 16 / HALVES;  // 16-row steps per part
     const bool holder = t < 2;  // head t
-    const int nmine = ntiles > warp ? (ntiles - warp + 7) >> 3 : 0;  // warp-uniform, <= 2
     const int arow = (lane & 7) + 8 * ((lane >> 3) & 1);
     const int acol = lane >> 4;
-    // All A fragments of the warp's tiles are loaded before the first mma (ldmatrix takes ~50
-    // cycles; loading each just before its mma would serialise the two).
-    float c[2][2][4];  // [tile][even / odd 16-dim step]
+    // Warp w scores tiles w, w + NW, ...  All A fragments of a warp's tiles are loaded before the
+    // first mma (ldmatrix takes ~50 cycles; loading each just before its mma would serialise them).
+    float c[KT][2][4];  // [tile][even / odd 16-dim step]
 #pragma unroll
-    for (int e = 0; e < 4; e++) c[0][0][e] = c[0][1][e] = c[1][0][e] = c[1][1][e] = 0.f;
-    uint32_t af[2][8][4];
+    for (int k = 0; k < KT; k++)
 #pragma unroll
-    for (int k = 0; k < 2; k++)
-        if (k < nmine)
+        for (int e = 0; e < 4; e++) c[k][0][e] = c[k][1][e] = 0.f;
+    {
+        uint32_t af[KT][8][4];
 #pragma unroll
-            for (int j = 0; j < 8; j++) ldsm_x4(af[k][j], kt_u32 + swz(chunk, (warp + 8 * k) * 16 + arow, 2 * j + acol));
+        for (int k = 0; k < KT; k++)
+            if (warp + NW * k < ntiles)
 #pragma unroll
-    for (int k = 0; k < 2; k++)
-        if (k < nmine)
+                for (int j = 0; j < 8; j++)
+                    ldsm_x4(af[k][j], kt_u32 + swz(chunk, (warp + NW * k) * 16 + arow, 2 * j + acol));
 #pragma unroll
-            for (int j = 0; j < 8; j++) mma_16816_full(c[k][j & 1], af[k][j], qb0[j], qb1[j]);
-    float sv[2][2];  // [tile][row g, row g + 8]
+        for (int k = 0; k < KT; k++)
+            if (warp + NW * k < ntiles)
+#pragma unroll
+                for (int j = 0; j < 8; j++) mma_16816_full(c[k][j & 1], af[k][j], qb0[j], qb1[j]);
+    }
+    float sv[KT][2];  // [tile][row g, row g + 8]
     float m = -INFINITY;
 #pragma unroll
-    for (int k = 0; k < 2; k++) {
-        const int rb = (warp + 8 * k) * 16 + g;
+    for (int k = 0; k < KT; k++) {
+        const int rb = (warp + NW * k) * 16 + g;
+        const bool live = warp + NW * k < ntiles;
         const float s0 = c[k][0][0] + c[k][1][0] + c[k][0][1] + c[k][1][1];
         const float s1 = c[k][0][2] + c[k][1][2] + c[k][0][3] + c[k][1][3];
-        sv[k][0] = k < nmine && rb < nrows ? s0 * a.scale_log2 : -INFINITY;
-        sv[k][1] = k < nmine && rb + 8 < nrows ? s1 * a.scale_log2 : -INFINITY;
+        sv[k][0] = live && rb < nrows ? s0 * a.scale_log2 : -INFINITY;
+        sv[k][1] = live && rb + 8 < nrows ? s1 * a.scale_log2 : -INFINITY;
         m = fmaxf(m, fmaxf(sv[k][0], sv[k][1]));
     }
     // Maximum over the warp's rows: lanes of equal t.
     m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
     m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 8));
     m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 16));
-    float* wmax = stat;     // [8 warps][2]
-    float* lw = stat + 16;  // [8 warps][2]
+    float* wmax = stat;     // [NW warps][2]
+    float* lw = stat + 32;  // [NW warps][2]
+    float* xo = stat + 64;  // [8 dim slices][2 heads][16 dims]
     if (lane < 2) wmax[2 * warp + lane] = m;
     __syncthreads();
     const int hh = t & 1;
     float M = -INFINITY;
 #pragma unroll
-    for (int w = 0; w < kDecThreads / 32; w++) M = fmaxf(M, wmax[2 * w + hh]);
+    for (int w = 0; w < NW; w++) M = fmaxf(M, wmax[2 * w + hh]);
 
     // Weights: p = 2^(s - M), written as P rows p0_hi, p0_lo, p1_hi, p1_lo; sums per warp.
     float l = 0.f;
 #pragma unroll
-    for (int k = 0; k < 2; k++) {
-        if (k >= nmine) break;
-        if (holder) {
-            const int rb = (warp + 8 * k) * 16 + g;
+    for (int k = 0; k < KT; k++) {
+        if (holder && warp + NW * k < ntiles) {
+            const int rb = (warp + NW * k) * 16 + g;
 #pragma unroll
             for (int u = 0; u < 2; u++) {
                 const float p = fast_exp2(sv[k][u] - M);
@@ -879,48 +897,66 @@ __global__ void __launch_bounds__(kDecThreads, 2)
     // V rows the weights do not cover but the last 16-row step reads: zeros (0 * stale NaN is NaN).
     {
         const int z0 = trows + (has_new ? 1 : 0), z1 = ntiles * 16;
-        for (int i = tid; i < (z1 - z0) * 16; i += kDecThreads)
+        for (int i = tid; i < (z1 - z0) * 16; i += NW * 32)
             *reinterpret_cast<uint4*>(Vt + swz(chunk, z0 + (i >> 4), i & 15)) = make_uint4(0u, 0u, 0u, 0u);
     }
     if (new_thread) store8(reinterpret_cast<__nv_bfloat16*>(Vt + swz(chunk, rn, tid - 64)), nv);
     if (__syncthreads_or(!vok)) return;
 
-    // Output: O^T[16 dims][8] = V^T[16 dims][rows] . [p0_hi p0_lo p1_hi p1_lo 0 0 0 0]^T; warp w
-    // owns dims [16 w, 16 w + 16) (V^T fragments by transposing ldmatrix), two accumulators
-    // (even and odd 16-row steps).  Lane (g, t < 2) ends with head t's dims 16 w + g, + 8.
+    // Output: O^T[16 dims][8] = V^T[16 dims][rows] . [p0_hi p0_lo p1_hi p1_lo 0 0 0 0]^T.  Warp w
+    // owns dims [16 (w % 8), + 16) of row part w / 8 (steps STEPS part .. + STEPS - 1; V^T
+    // fragments by transposing ldmatrix), two accumulators (even and odd steps); with two parts
+    // the second part's partial outputs go through shared memory to the first.  Lane (g, t < 2)
+    // ends with head t's dims 16 (w % 8) + g, + 8.
+    const int slice = warp & 7;
+    const int half = warp >> 3;
     float o[2][4];
 #pragma unroll
     for (int e = 0; e < 4; e++) o[0][e] = o[1][e] = 0.f;
-    const int vrow = (lane & 7) + 8 * (lane >> 4);
-    const int vcol = 2 * warp + ((lane >> 3) & 1);
-    // Fragments of all (<= 12) row steps first, then the mma chain.
-    uint32_t va[kMmaMaxChunk / 16][4], pb[kMmaMaxChunk / 16][2];
+    {
+        const int vrow = (lane & 7) + 8 * (lane >> 4);
+        const int vcol = 2 * slice + ((lane >> 3) & 1);
+        uint32_t va[STEPS][4], pb[STEPS][2];
 #pragma unroll
-    for (int j = 0; j < kMmaMaxChunk / 16; j++) {
-        if (j < ntiles) {
-            pb[j][0] = pb[j][1] = 0u;
-            if (lane < 16) {
-                const unsigned char* row = Pa + g * ppitch + (16 * j + 2 * t) * 2;
-                pb[j][0] = *reinterpret_cast<const uint32_t*>(row);
-                pb[j][1] = *reinterpret_cast<const uint32_t*>(row + 16);
+        for (int i = 0; i < STEPS; i++) {
+            const int j = STEPS * half + i;
+            if (j < ntiles) {
+                pb[i][0] = pb[i][1] = 0u;
+                if (lane < 16) {
+                    const unsigned char* row = Pa + g * ppitch + (16 * j + 2 * t) * 2;
+                    pb[i][0] = *reinterpret_cast<const uint32_t*>(row);
+                    pb[i][1] = *reinterpret_cast<const uint32_t*>(row + 16);
+                }
+                ldsm_x4_trans(va[i], vt_u32 + swz(chunk, 16 * j + vrow, vcol));
             }
-            ldsm_x4_trans(va[j], vt_u32 + swz(chunk, 16 * j + vrow, vcol));
+        }
+#pragma unroll
+        for (int i = 0; i < STEPS; i++)
+            if (STEPS * half + i < ntiles) mma_16816_full(o[i & 1], va[i], pb[i][0], pb[i][1]);
+    }
+    float y0 = o[0][0] + o[1][0] + o[0][1] + o[1][1];  // dim 16 slice + g
+    float y1 = o[0][2] + o[1][2] + o[0][3] + o[1][3];  // dim 16 slice + g + 8
+    const bool writer = half == 0 && holder;  // the first part's warps write the result
+    if (HALVES > 1) {
+        if (half && holder) {
+            xo[(slice * 2 + hh) * 16 + g] = y0;
+            xo[(slice * 2 + hh) * 16 + g + 8] = y1;
+        }
+        __syncthreads();
+        if (writer) {
+            y0 += xo[(slice * 2 + hh) * 16 + g];
+            y1 += xo[(slice * 2 + hh) * 16 + g + 8];
         }
     }
-#pragma unroll
-    for (int j = 0; j < kMmaMaxChunk / 16; j++)
-        if (j < ntiles) mma_16816_full(o[j & 1], va[j], pb[j][0], pb[j][1]);
-    const float y0 = o[0][0] + o[1][0] + o[0][1] + o[1][1];  // dim 16 w + g
-    const float y1 = o[0][2] + o[1][2] + o[0][3] + o[1][3];  // dim 16 w + g + 8
     float L = 0.f;
 #pragma unroll
-    for (int w = 0; w < kDecThreads / 32; w++) L += lw[2 * w + hh];
-    const int dim = 16 * warp + g;
+    for (int w = 0; w < NW; w++) L += lw[2 * w + hh];
+    const int dim = 16 * slice + g;
     // rows of query heads 2 kvh, 2 kvh + 1 of sequence b
     float* out_pair = a.out + (size_t)b * kHq * kD + (size_t)(kGroup * (kvh - a.kvh0)) * kD;
 
     if (nsplit == 1) {
-        if (holder) {
+        if (writer) {
             float* o_ = out_pair + (size_t)hh * kD + dim;
             const float inv = 1.f / L;
             o_[0] = y0 * inv;
@@ -932,7 +968,7 @@ __global__ void __launch_bounds__(kDecThreads, 2)
     float* recs = a.partials + ((size_t)b * kHkv + kvh) * a.nsplit * kRec;  // a.nsplit: the record stride
     {
         float* mine = recs + (size_t)s * kRec;
-        if (holder) {
+        if (writer) {
             float* o_ = mine + 4 + (size_t)hh * kD + dim;
             o_[0] = y0;
             o_[8] = y1;
@@ -1114,7 +1150,7 @@ static int set_mma_smem_attr()
 {
     static bool done = false;
     if (!done) {
-        cudaError_t e = cudaFuncSetAttribute(decode_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        cudaError_t e = cudaFuncSetAttribute(decode_mma_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)decode_mma_smem_bytes(kMmaMaxChunk));
         if (e != cudaSuccess) return (int)e;
         done = true;
@@ -1134,7 +1170,7 @@ static int launch_decode_mma(DecodeMmaArgs a, const tyb_seq_kv& one, int nkvh, v
     a.maps = nullptr;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.nsplit, nkvh, 1);
-    cfg.blockDim = dim3(kDecThreads);
+    cfg.blockDim = dim3(256);
     cfg.dynamicSmemBytes = decode_mma_smem_bytes(a.chunk);
     cfg.stream = (cudaStream_t)stream;
     cudaLaunchAttribute attr[1];
@@ -1142,7 +1178,7 @@ static int launch_decode_mma(DecodeMmaArgs a, const tyb_seq_kv& one, int nkvh, v
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return (int)cudaLaunchKernelEx(&cfg, decode_mma_kernel, mk, mv, mk16, mv16, a);
+    return (int)cudaLaunchKernelEx(&cfg, decode_mma_kernel<8>, mk, mv, mk16, mv16, a);
 }
 
 }  // namespace tyb
@@ -1190,7 +1226,7 @@ extern "C" int tyb_decode_launch_batched(const float* q, float* out, const tyb_s
     a.prefetch_small = 1;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(nsplit, kHkv, batch);
-    cfg.blockDim = dim3(kDecThreads);
+    cfg.blockDim = dim3(256);
     cfg.dynamicSmemBytes = decode_mma_smem_bytes(chunk);
     cfg.stream = (cudaStream_t)stream;
     cudaLaunchAttribute attr[1];
@@ -1198,7 +1234,7 @@ extern "C" int tyb_decode_launch_batched(const float* q, float* out, const tyb_s
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return (int)cudaLaunchKernelEx(&cfg, decode_mma_kernel, m0, m1, m0, m1, a);
+    return (int)cudaLaunchKernelEx(&cfg, decode_mma_kernel<8>, m0, m1, m0, m1, a);
 }
 
 extern "C" void tyb_decode_plan(int batch, int max_kv_len, int kv_dtype, int* chunk_rows, int* nsplit)
