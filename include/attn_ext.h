@@ -110,8 +110,9 @@ int attn_heads_to_tokens(const void *gathered, void *output, int seq_len, int dt
  *   q, output       device [16][128] fp32
  *   k_rows, v_rows  device, head-first [8][row_capacity][128] of kv_dtype (ATTN_KV_F32 or
  *                   ATTN_KV_BF16), 16-byte aligned -- e.g. kv_cache_k(cache, layer, 0)
- *   kv_len          rows attended, 1 <= kv_len <= row_capacity; at most 24,576 (F32) or
- *                   65,536 (BF16) rows (256 splits); longer requests are rejected
+ *   kv_len          rows attended, 1 <= kv_len <= row_capacity; for ATTN_KV_F32 at most 24,576
+ *                   rows (256 splits of 96; longer requests are rejected); ATTN_KV_BF16 has no
+ *                   such limit (long sequences are streamed in at most 2 x SMs / 8 spans)
  *   stream          cudaStream_t (NULL = legacy default stream); the call only queues work
  * The first call on each device looks up the array's device address (cudaGetSymbolAddress);
  * make that first call before any stream capture.  All calls share the one array and it

@@ -337,9 +337,11 @@ def _plan(lib, kv_len, dtype):
 
 
 def _edge_lengths(pkg, lib):
-    """kv lengths around 16-row steps and split edges of the BF16 single-sequence kernel,
-    including ones whose last split holds only the appended row."""
-    lens = {1, 2, 15, 16, 17, 100, 191, 192, 193, 2000, 4097, 4608, 8192}
+    """kv lengths around 16-row steps and split edges of the BF16 single-sequence kernels
+    (one wave of splits up to 4,608 rows, streamed spans past it), including ones whose last
+    split holds only the appended row."""
+    lens = {1, 2, 15, 16, 17, 100, 191, 192, 193, 2000, 4097, 4608, 8192,
+            4609, 12289, 20001}  # past one wave: the streaming form (64-row stages, spans)
     for target in (300, 2000, 4097):
         chunk, _ = _plan(lib, target, pkg.ATTN_KV_BF16)
         n = (target // chunk) * chunk + 1

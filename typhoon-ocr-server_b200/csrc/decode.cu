@@ -993,6 +993,302 @@ __global__ void __launch_bounds__(NW * 32, 16 / NW)
     if (tid == 0) a.counters[b * kHkv + kvh] = 0u;
 }
 
+// ---- streaming form: many waves (request batches, long sequences) ----------------------------
+//
+// When the splits of a launch cannot all be resident at once, each CTA instead walks a span of
+// rows of one (sequence, KV head) in 96-row stages: the K and V tiles of stage s + 2 are requested
+// (TMA tensor copies, 128-byte swizzle) while stage s is computed from the other buffer, with an
+// online softmax across stages (running maximum per head, the output accumulators rescaled in
+// registers).  The contractions are those of decode_mma_kernel (mma.sync, hi/lo BF16 query and
+// weights); one record per span, merged by the span that takes the last ticket.  Two CTAs per SM
+// (100 KB of shared memory each).  Measured alternatives: 64-row stages at three CTAs per SM and
+// 128-row stages at one: 18-22 % slower on the 64-sequence batch (config 4).
+
+constexpr int kStRows = 96;                         // rows per stage
+constexpr size_t kStTile = (size_t)kStRows * 256;   // bytes of a K (or V) stage tile
+constexpr int kStPitch = (kStRows + 8) * 2;         // bytes per P row (conflict-free B loads)
+
+__host__ __device__ constexpr size_t decode_stream_smem_bytes()
+{
+    return 1024 + 4 * kStTile + 4 * kStPitch + 4 * kQaPitch + 32 * sizeof(float) + 5 * sizeof(uint64_t) + 16;
+}
+
+__global__ void __launch_bounds__(256, 2)
+    decode_stream_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
+                         const DecodeMmaArgs a)
+{
+    extern __shared__ unsigned char smem_raw[];
+    unsigned char* smem =
+        reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const int span = blockIdx.x;
+    const int kvh = a.kvh0 + blockIdx.y;
+    const int b = blockIdx.z;
+    const int tid = threadIdx.x;
+    const int lane = tid & 31;
+    const int warp = tid >> 5;
+    const int g = lane >> 2;
+    const int t = lane & 3;
+
+    unsigned char* Pa = smem + 4 * kStTile;
+    unsigned char* Qa = Pa + 4 * kStPitch;
+    float* stat = reinterpret_cast<float*>(Qa + 4 * kQaPitch);  // wmax[8][2] lw[8][2]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(stat + 32);    // K0 K1 V0 V1 merge
+    int* last_flag = reinterpret_cast<int*>(bars + 5);
+    const uint32_t base_u32 = smem_u32(smem);  // K0 K1 V0 V1 tiles, kStTile apart
+
+    const float* qb = a.q + (size_t)b * kHq * kD;
+    int kv_len = a.kv_len;
+    const CUtensorMap* mk = &tmk;
+    const CUtensorMap* mv = &tmv;
+
+    if (tid == 0) {
+#pragma unroll
+        for (int i = 0; i < 5; i++) mbar_init(&bars[i], 1);
+        fence_barrier_init();
+        fence_proxy_async_smem();
+    }
+    __syncthreads();
+    if (a.prefetch_small && warp == 1 && lane < 8)
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(qb + (size_t)(kGroup * kvh) * kD + lane * 32));
+    pdl_wait();
+    pdl_trigger();
+    if (a.seqs) {
+        const tyb_seq_kv d = a.seqs[b];
+        kv_len = d.kv_len;
+        mk = a.maps + 2 * b;
+        mv = mk + 1;
+        if (tid == 0) {
+            asm volatile("fence.proxy.tensormap::generic.acquire.gpu [%0], 128;" ::"l"(mk) : "memory");
+            asm volatile("fence.proxy.tensormap::generic.acquire.gpu [%0], 128;" ::"l"(mv) : "memory");
+        }
+    }
+    const int r_begin = span * a.chunk;  // a.chunk: rows per span (a multiple of kStRows)
+    if (r_begin >= kv_len) return;
+    const int r_end = min(kv_len, r_begin + a.chunk);
+    const int nst = (r_end - r_begin + kStRows - 1) / kStRows;
+    const int nspan = (kv_len + a.chunk - 1) / a.chunk;
+    const bool append = !a.seqs && a.k_new;
+    const int cache_rows = append ? kv_len - 1 : kv_len;
+
+    auto issue_k = [&](int st) {
+        const int buf = st & 1;
+        const uint32_t dst = base_u32 + (uint32_t)(buf * kStTile);
+        mbar_arrive_expect_tx(&bars[buf], (uint32_t)kStTile);
+        tma_box_3d(dst, mk, 0, r_begin + st * kStRows, kvh, &bars[buf]);
+        tma_box_3d(dst + (uint32_t)(kStTile / 2), mk, 64, r_begin + st * kStRows, kvh, &bars[buf]);
+    };
+    auto issue_v = [&](int st) {
+        const int buf = st & 1;
+        const uint32_t dst = base_u32 + (uint32_t)((2 + buf) * kStTile);
+        mbar_arrive_expect_tx(&bars[2 + buf], (uint32_t)kStTile);
+        tma_box_3d(dst, mv, 0, r_begin + st * kStRows, kvh, &bars[2 + buf]);
+        tma_box_3d(dst + (uint32_t)(kStTile / 2), mv, 64, r_begin + st * kStRows, kvh, &bars[2 + buf]);
+    };
+    if (tid == 0) {
+        issue_k(0);
+        issue_v(0);
+        if (nst > 1) {
+            issue_k(1);
+            issue_v(1);
+        }
+    }
+
+    // The query as B columns q0_hi, q0_lo, q1_hi, q1_lo; the appended row to the cache.
+    if (tid < 64) {
+        const int h = tid >> 5, d0 = (tid & 31) * 4;
+        const float4 x = *reinterpret_cast<const float4*>(qb + (size_t)(kGroup * kvh + h) * kD + d0);
+        uint32_t hi0, lo0, hi1, lo1;
+        split_pair(x.x, x.y, hi0, lo0);
+        split_pair(x.z, x.w, hi1, lo1);
+        *reinterpret_cast<uint2*>(Qa + (2 * h) * kQaPitch + d0 * 2) = make_uint2(hi0, hi1);
+        *reinterpret_cast<uint2*>(Qa + (2 * h + 1) * kQaPitch + d0 * 2) = make_uint2(lo0, lo1);
+    }
+    const bool new_here_span = append && kv_len - 1 >= r_begin && kv_len - 1 < r_end;
+    const bool new_thread = new_here_span && tid >= 64 && tid < 80;
+    float nk[8], nv[8];
+    if (new_thread) {
+        const int i = tid - 64;
+        const size_t off = (size_t)kvh * kD + i * 8;
+        load8(a.k_new + off, nk);
+        load8(a.v_new + off, nv);
+        const size_t row = ((size_t)kvh * a.row_capacity + (kv_len - 1)) * kD + i * 8;
+        store8(a.k + row, nk);
+        store8(a.v + row, nv);
+    }
+    __syncthreads();
+    uint32_t qb0[8], qb1[8];
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        qb0[j] = 0u;
+        qb1[j] = 0u;
+        if (lane < 16) {
+            qb0[j] = *reinterpret_cast<const uint32_t*>(Qa + g * kQaPitch + (16 * j + 2 * t) * 2);
+            qb1[j] = *reinterpret_cast<const uint32_t*>(Qa + g * kQaPitch + (16 * j + 8 + 2 * t) * 2);
+        }
+    }
+
+    const bool holder = t < 2;
+    const int hh = t & 1;  // head of this lane's accumulator columns (holders)
+    const int arow = (lane & 7) + 8 * ((lane >> 3) & 1);
+    const int acol = lane >> 4;
+    const int vrow = (lane & 7) + 8 * (lane >> 4);
+    const int vcol = 2 * warp + ((lane >> 3) & 1);
+    float* wmax = stat;
+    float* lw = stat + 16;
+    float Mrun = -INFINITY, Lrun = 0.f;  // head hh
+    float o[2][4];
+#pragma unroll
+    for (int e = 0; e < 4; e++) o[0][e] = o[1][e] = 0.f;
+
+    for (int st = 0; st < nst; st++) {
+        const int buf = st & 1;
+        const uint32_t par = (uint32_t)((st >> 1) & 1);
+        const uint32_t kt_u32 = base_u32 + (uint32_t)(buf * kStTile);
+        const uint32_t vt_u32 = base_u32 + (uint32_t)((2 + buf) * kStTile);
+        const int r0 = r_begin + st * kStRows;
+        const int nrows = min(kStRows, r_end - r0);
+        const int ntiles = (nrows + 15) >> 4;
+        const int trows = max(0, min(nrows, cache_rows - r0));
+        const bool new_here = append && kv_len - 1 >= r0 && kv_len - 1 < r0 + nrows;
+        const int rn = kv_len - 1 - r0;
+
+        const bool kok = mbar_wait_bounded(&bars[buf], par, kWaitLimitNs, TYB_STATUS_WAIT_TIMEOUT);
+        if (new_here && new_thread)
+            store8(reinterpret_cast<__nv_bfloat16*>(smem + buf * kStTile + swz(kStRows, rn, tid - 64)), nk);
+        if (__syncthreads_or(!kok)) return;
+
+        // Scores of tile w (warp w < ntiles), rows g and g + 8.
+        float c[2][4];
+#pragma unroll
+        for (int e = 0; e < 4; e++) c[0][e] = c[1][e] = 0.f;
+        if (warp < ntiles) {
+            uint32_t af[8][4];
+#pragma unroll
+            for (int j = 0; j < 8; j++) ldsm_x4(af[j], kt_u32 + swz(kStRows, warp * 16 + arow, 2 * j + acol));
+#pragma unroll
+            for (int j = 0; j < 8; j++) mma_16816_full(c[j & 1], af[j], qb0[j], qb1[j]);
+        }
+        const int rb = warp * 16 + g;
+        const float sv0 = warp < ntiles && rb < nrows ? (c[0][0] + c[1][0] + c[0][1] + c[1][1]) * a.scale_log2
+                                                      : -INFINITY;
+        const float sv1 = warp < ntiles && rb + 8 < nrows ? (c[0][2] + c[1][2] + c[0][3] + c[1][3]) * a.scale_log2
+                                                          : -INFINITY;
+        float m = fmaxf(sv0, sv1);
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 8));
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 16));
+        if (lane < 2) wmax[2 * warp + lane] = m;
+        __syncthreads();
+        if (tid == 0 && st + 2 < nst) issue_k(st + 2);  // this K buffer is read no more
+        float mst = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < 8; w++) mst = fmaxf(mst, wmax[2 * w + hh]);
+        const float Mnew = fmaxf(Mrun, mst);
+        const float alpha = fast_exp2(Mrun - Mnew);  // 0 on the first stage
+
+        float l = 0.f;
+        if (holder && warp < ntiles) {
+#pragma unroll
+            for (int u = 0; u < 2; u++) {
+                const float p = fast_exp2((u ? sv1 : sv0) - Mnew);
+                l += p;
+                const __nv_bfloat16 hi = __float2bfloat16_rn(p);
+                const __nv_bfloat16 lo = __float2bfloat16_rn(p - __bfloat162float(hi));
+                *reinterpret_cast<__nv_bfloat16*>(Pa + (2 * hh) * kStPitch + (rb + 8 * u) * 2) = hi;
+                *reinterpret_cast<__nv_bfloat16*>(Pa + (2 * hh + 1) * kStPitch + (rb + 8 * u) * 2) = lo;
+            }
+        }
+        l += __shfl_xor_sync(0xffffffffu, l, 4);
+        l += __shfl_xor_sync(0xffffffffu, l, 8);
+        l += __shfl_xor_sync(0xffffffffu, l, 16);
+        if (lane < 2) lw[2 * warp + lane] = l;
+
+        const bool vok = mbar_wait_bounded(&bars[2 + buf], par, kWaitLimitNs, TYB_STATUS_WAIT_TIMEOUT);
+        {
+            // Tile rows past the attended ones that the last 16-row step reads: zeros.
+            const int z0 = trows + (new_here ? 1 : 0), z1 = ntiles * 16;
+            for (int i = tid; i < (z1 - z0) * 16; i += 256)
+                *reinterpret_cast<uint4*>(smem + (2 + buf) * kStTile + swz(kStRows, z0 + (i >> 4), i & 15)) =
+                    make_uint4(0u, 0u, 0u, 0u);
+        }
+        if (new_here && new_thread)
+            store8(reinterpret_cast<__nv_bfloat16*>(smem + (2 + buf) * kStTile + swz(kStRows, rn, tid - 64)), nv);
+        if (__syncthreads_or(!vok)) return;
+
+        // O^T for the warp's 16 dims, rescaled to the new maximum first.
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            o[0][e] *= alpha;
+            o[1][e] *= alpha;
+        }
+        {
+            uint32_t va[kStRows / 16][4], pb[kStRows / 16][2];
+#pragma unroll
+            for (int i = 0; i < kStRows / 16; i++) {
+                if (i < ntiles) {
+                    pb[i][0] = pb[i][1] = 0u;
+                    if (lane < 16) {
+                        const unsigned char* row = Pa + g * kStPitch + (16 * i + 2 * t) * 2;
+                        pb[i][0] = *reinterpret_cast<const uint32_t*>(row);
+                        pb[i][1] = *reinterpret_cast<const uint32_t*>(row + 16);
+                    }
+                    ldsm_x4_trans(va[i], vt_u32 + swz(kStRows, 16 * i + vrow, vcol));
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < kStRows / 16; i++)
+                if (i < ntiles) mma_16816_full(o[i & 1], va[i], pb[i][0], pb[i][1]);
+        }
+        float lsum = 0.f;
+#pragma unroll
+        for (int w = 0; w < 8; w++) lsum += lw[2 * w + hh];
+        Lrun = Lrun * alpha + lsum;
+        Mrun = Mnew;
+        __syncthreads();  // this V buffer, P, and the per-warp maxima and sums are read no more
+        if (tid == 0 && st + 2 < nst) issue_v(st + 2);
+    }
+
+    const float y0 = o[0][0] + o[1][0] + o[0][1] + o[1][1];  // dim 16 warp + g, head hh (holders)
+    const float y1 = o[0][2] + o[1][2] + o[0][3] + o[1][3];  // dim 16 warp + g + 8
+    const int dim = 16 * warp + g;
+    float* out_pair = a.out + (size_t)b * kHq * kD + (size_t)(kGroup * (kvh - a.kvh0)) * kD;
+    if (nspan == 1) {
+        if (holder) {
+            float* o_ = out_pair + (size_t)hh * kD + dim;
+            const float inv = 1.f / Lrun;
+            o_[0] = y0 * inv;
+            o_[8] = y1 * inv;
+        }
+        return;
+    }
+    float* recs = a.partials + ((size_t)b * kHkv + kvh) * a.nsplit * kRec;  // a.nsplit: the record stride
+    {
+        float* mine = recs + (size_t)span * kRec;
+        if (holder) {
+            float* o_ = mine + 4 + (size_t)hh * kD + dim;
+            o_[0] = y0;
+            o_[8] = y1;
+            if (g == 0 && warp == 0) {
+                mine[2 * hh] = Mrun;
+                mine[2 * hh + 1] = Lrun;
+            }
+        }
+    }
+    __syncthreads();
+    if (tid == 0) {
+        unsigned int ticket;
+        asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;"
+                     : "=r"(ticket)
+                     : "l"(&a.counters[b * kHkv + kvh])
+                     : "memory");
+        *last_flag = ticket == (unsigned int)(nspan - 1);
+    }
+    __syncthreads();
+    if (!*last_flag) return;
+    merge_records_direct(recs, nspan, reinterpret_cast<float*>(smem), out_pair);
+    if (tid == 0) a.counters[b * kHkv + kvh] = 0u;
+}
+
 // ---- host-side planning ----------------------------------------------------------------
 
 static int g_num_sms = 0;
@@ -1146,12 +1442,37 @@ static void plan_mma(int batch, int max_kv_len, int nkvh, int* chunk_rows, int* 
     *nsplit = max_kv_len > 0 ? (max_kv_len + best - 1) / best : 0;
 }
 
+// Spans of the streaming form: one sequence -- as many spans as fill two CTAs per SM once;
+// request batches -- 768 rows (8 stages).
+static void plan_stream(int batch, int max_kv_len, int nkvh, int* span_rows, int* nspan)
+{
+    int rows = 8 * kStRows;
+    if (batch == 1) {
+        long long per_head = 2LL * num_sms() / nkvh;
+        if (per_head < 1) per_head = 1;
+        rows = (int)(((max_kv_len + per_head - 1) / per_head + kStRows - 1) / kStRows * kStRows);
+        if (rows < kStRows) rows = kStRows;
+    }
+    *span_rows = rows;
+    *nspan = max_kv_len > 0 ? (max_kv_len + rows - 1) / rows : 0;
+}
+
+// One sequence whose splits fit in one wave at one CTA per SM takes decode_mma_kernel; longer ones
+// and request batches take decode_stream_kernel.
+static bool one_wave(int batch, int max_kv_len, int nkvh)
+{
+    return batch == 1 && (long long)((max_kv_len + kMmaMaxChunk - 1) / kMmaMaxChunk) * nkvh <= num_sms();
+}
+
 static int set_mma_smem_attr()
 {
     static bool done = false;
     if (!done) {
         cudaError_t e = cudaFuncSetAttribute(decode_mma_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)decode_mma_smem_bytes(kMmaMaxChunk));
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(decode_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)decode_stream_smem_bytes());
         if (e != cudaSuccess) return (int)e;
         done = true;
     }
@@ -1181,6 +1502,22 @@ static int launch_decode_mma(DecodeMmaArgs a, const tyb_seq_kv& one, int nkvh, v
     return (int)cudaLaunchKernelEx(&cfg, decode_mma_kernel<8>, mk, mv, mk16, mv16, a);
 }
 
+static int launch_stream(const DecodeMmaArgs& a, const CUtensorMap& mk, const CUtensorMap& mv, int nkvh, int batch,
+                         void* stream)
+{
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(a.nsplit, nkvh, batch);
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = decode_stream_smem_bytes();
+    cfg.stream = (cudaStream_t)stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return (int)cudaLaunchKernelEx(&cfg, decode_stream_kernel, mk, mv, a);
+}
+
 }  // namespace tyb
 
 using namespace tyb;
@@ -1195,7 +1532,7 @@ extern "C" int tyb_decode_launch_batched(const float* q, float* out, const tyb_s
     int e = set_mma_smem_attr();
     if (e) return e;
     int chunk, nsplit;
-    plan_mma(batch, max_kv_len, kHkv, &chunk, &nsplit);
+    plan_stream(batch, max_kv_len, kHkv, &chunk, &nsplit);
     // Host staging: [maps 2 x batch][descriptors batch], one pageable copy (staged by the driver
     // before cudaMemcpyAsync returns, so the buffer may be freed right after).
     const size_t maps_bytes = tyb_decode_maps_bytes(batch);
@@ -1203,7 +1540,7 @@ extern "C" int tyb_decode_launch_batched(const float* q, float* out, const tyb_s
     CUtensorMap* host = static_cast<CUtensorMap*>(aligned_alloc(64, (bytes + 63) & ~size_t(63)));
     if (!host) return (int)cudaErrorMemoryAllocation;
     for (int b = 0; b < batch; b++) {
-        if (!slab_maps(seqs_host[b], chunk, &host[2 * b], &host[2 * b + 1])) {
+        if (!slab_maps(seqs_host[b], kStRows, &host[2 * b], &host[2 * b + 1])) {
             free(host);
             return (int)cudaErrorInvalidValue;
         }
@@ -1219,28 +1556,20 @@ extern "C" int tyb_decode_launch_batched(const float* q, float* out, const tyb_s
     a.seqs = reinterpret_cast<const tyb_seq_kv*>(static_cast<unsigned char*>(upload) + maps_bytes);
     a.maps = static_cast<const CUtensorMap*>(upload);
     a.scale_log2 = scale * kLog2e;
-    a.chunk = chunk;
-    a.nsplit = nsplit;  // the record stride; each sequence's own split count comes from its length
+    a.chunk = chunk;    // rows per span
+    a.nsplit = nsplit;  // the record stride; each sequence's own span count comes from its length
     a.partials = partials;
     a.counters = counters;
     a.prefetch_small = 1;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(nsplit, kHkv, batch);
-    cfg.blockDim = dim3(256);
-    cfg.dynamicSmemBytes = decode_mma_smem_bytes(chunk);
-    cfg.stream = (cudaStream_t)stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    return (int)cudaLaunchKernelEx(&cfg, decode_mma_kernel<8>, m0, m1, m0, m1, a);
+    return launch_stream(a, m0, m1, kHkv, batch, stream);
 }
 
 extern "C" void tyb_decode_plan(int batch, int max_kv_len, int kv_dtype, int* chunk_rows, int* nsplit)
 {
-    if (kv_dtype == TYB_BF16)
+    if (kv_dtype == TYB_BF16 && one_wave(batch, max_kv_len, kHkv))
         plan_mma(batch, max_kv_len, kHkv, chunk_rows, nsplit);
+    else if (kv_dtype == TYB_BF16)
+        plan_stream(batch, max_kv_len, kHkv, chunk_rows, nsplit);  // spans
     else
         plan<float>(batch, max_kv_len, chunk_rows, nsplit);
 }
@@ -1267,8 +1596,11 @@ extern "C" int tyb_decode_launch_heads(const float* q, float* out, const tyb_seq
     a.v_new = v_new;
     a.scale_log2 = scale * kLog2e;
     int chunk, nsplit;
-    if (kv_dtype == TYB_BF16 && !seqs_dev && batch == 1)
+    const bool bf16_one = kv_dtype == TYB_BF16 && !seqs_dev && batch == 1;
+    if (bf16_one && one_wave(1, max_kv_len, nkvh))
         plan_mma(1, max_kv_len, nkvh, &chunk, &nsplit);
+    else if (bf16_one)
+        plan_stream(1, max_kv_len, nkvh, &chunk, &nsplit);
     else if (kv_dtype == TYB_BF16)
         plan<__nv_bfloat16>(batch, max_kv_len, &chunk, &nsplit, nkvh);
     else
@@ -1278,7 +1610,7 @@ extern "C" int tyb_decode_launch_heads(const float* q, float* out, const tyb_seq
     a.prefetch_rows = seqs_dev ? 0 : prefetch_rows;
     a.partials = partials;
     a.counters = counters;
-    if (kv_dtype == TYB_BF16 && !seqs_dev && batch == 1) {
+    if (bf16_one) {
         DecodeMmaArgs m;
         m.q = q;
         m.out = out;
@@ -1296,7 +1628,14 @@ extern "C" int tyb_decode_launch_heads(const float* q, float* out, const tyb_seq
         m.counters = counters;
         m.kvh0 = kvh0;
         m.prefetch_small = a.prefetch_small;
-        return launch_decode_mma(m, one, nkvh, stream);
+        if (one_wave(1, max_kv_len, nkvh)) return launch_decode_mma(m, one, nkvh, stream);
+        const int e = set_mma_smem_attr();
+        if (e) return e;
+        CUtensorMap mk, mv;
+        if (!slab_maps(one, kStRows, &mk, &mv)) return (int)cudaErrorInvalidValue;
+        m.seqs = nullptr;
+        m.maps = nullptr;
+        return launch_stream(m, mk, mv, nkvh, 1, stream);
     }
     if (kv_dtype == TYB_BF16) return launch_decode<__nv_bfloat16>(a, batch, nkvh, stream);
     return launch_decode<float>(a, batch, nkvh, stream);
@@ -1382,7 +1721,7 @@ extern "C" int attention_decode_gqa_noalloc(const float* q, const void* k_rows, 
     int chunk = 0, nsplit = 0;
     tyb_decode_plan(1, kv_len, kv_dtype, &chunk, &nsplit);
     if (nsplit > kNoAllocMaxSplits) {
-        const int max_chunk = kv_dtype == TYB_BF16 ? kMmaMaxChunk : DecodeTile<float>::kMaxChunk;
+        const int max_chunk = DecodeTile<float>::kMaxChunk;  // BF16 never gets here (at most 2 x SMs / 8 spans)
         tyb_set_error("%s: kv_len %d needs %d splits; the fixed scratch holds %d (kv_len <= %d for this "
                       "element type)",
                       what, kv_len, nsplit, kNoAllocMaxSplits, kNoAllocMaxSplits * max_chunk);
