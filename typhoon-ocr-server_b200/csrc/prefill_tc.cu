@@ -709,6 +709,9 @@ __global__ void kv_prep_kernel(const void* __restrict__ k_raw, const void* __res
             x[0] = fk.x; x[1] = fk.y; x[2] = fk.z; x[3] = fk.w;
             v4[0] = fv.x; v4[1] = fv.y; v4[2] = fv.z; v4[3] = fv.w;
         }
+        // cos/sin do not depend on the norm: requested with the row, before the reductions.
+        const float4 c = *reinterpret_cast<const float4*>(cosv + (size_t)t * 64 + jr);
+        const float4 s = *reinterpret_cast<const float4*>(sinv + (size_t)t * 64 + jr);
         float ss = x[0] * x[0] + x[1] * x[1] + x[2] * x[2] + x[3] * x[3];
 #pragma unroll
         for (int o = 16; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
@@ -718,8 +721,6 @@ __global__ void kv_prep_kernel(const void* __restrict__ k_raw, const void* __res
         for (int e = 0; e < 4; e++) y[e] = x[e] * rs * w4[e];
 #pragma unroll
         for (int e = 0; e < 4; e++) partner[e] = __shfl_xor_sync(0xffffffffu, y[e], 16);
-        const float4 c = *reinterpret_cast<const float4*>(cosv + (size_t)t * 64 + jr);
-        const float4 s = *reinterpret_cast<const float4*>(sinv + (size_t)t * 64 + jr);
         const float c4[4] = {c.x, c.y, c.z, c.w}, s4[4] = {s.x, s.y, s.z, s.w};
         float z[4];
 #pragma unroll
