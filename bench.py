@@ -309,8 +309,11 @@ def time_long_context(pkg, lib, dctx, device, decode_steps=16):
     grid + 2,768 text tokens), 28 layers, BF16, sharded by KV head over the ranks (8/N heads
     each): per layer attention_prefill_fused_gqa_heads -> NCCL all-gather of the head-major
     shards -> attn_heads_to_tokens; then decode steps at 32K context the same way
-    (attention_decode_append_gqa_heads + all-gather of the [2n][128] shard).  CUDA events on
-    the compute stream, max over ranks; one warm-up pass first."""
+    (attention_decode_append_gqa_heads + all-gather of the [2n][128] shard straight into the
+    [16][128] output -- for one token the head-major and token-major layouts coincide), each
+    decode step replayed from a CUDA graph of its 28 (attention + NCCL all-gather) pairs, as a
+    serving loop would.  CUDA events on the compute stream, max over ranks; one warm-up pass
+    first.  The graphs are released before returning (before the process group goes away)."""
     import torch
     shard = importlib.import_module(pkg.__name__ + ".shard")
     wl = importlib.import_module(pkg.__name__ + ".workloads")
@@ -354,17 +357,15 @@ def time_long_context(pkg, lib, dctx, device, decode_steps=16):
     dpart = torch.empty((2 * n, D), device=device)
     dout = torch.empty((HQ, D), device=device)
 
-    def decode(steps):
-        for i in range(steps):
-            cs.seq_len = S + i
-            for layer in range(LAYERS):
-                if lib.attention_decode_append_gqa_heads(vp(dq[layer]), vp(dk[layer]), vp(dv[layer]), cache,
-                                                         vp(dpart), layer, scale, h0, n):
-                    raise RuntimeError(pkg.last_error(lib))
-                if world > 1:
-                    dout.copy_(shard.gather_heads(dpart))
-                else:
-                    dout.copy_(dpart)
+    def decode_step(i):
+        cs.seq_len = S + i
+        for layer in range(LAYERS):
+            # one GPU: the shard is the whole [16][128] output
+            if lib.attention_decode_append_gqa_heads(vp(dq[layer]), vp(dk[layer]), vp(dv[layer]), cache,
+                                                     vp(dpart if world > 1 else dout), layer, scale, h0, n):
+                raise RuntimeError(pkg.last_error(lib))
+            if world > 1:
+                dctx.dist.all_gather_into_tensor(dout, dpart)
 
     def timed(fn):
         dctx.barrier()
@@ -379,8 +380,42 @@ def time_long_context(pkg, lib, dctx, device, decode_steps=16):
 
     prefill()  # warm-up
     pf_ms = timed(prefill)
-    decode(2)  # warm-up
-    dec_ms = timed(lambda: decode(decode_steps))
+    # Decode: one graph per step (the step's kv_len is in the captured launch arguments),
+    # captured on a side stream after an eager warm-up step (NCCL communicator set up).
+    gstream = torch.cuda.Stream(device)
+    gstream.wait_stream(stream)
+    lib.attn_set_stream(ctypes.c_void_p(gstream.cuda_stream))
+    with torch.cuda.stream(gstream):
+        decode_step(0)
+    gstream.synchronize()
+    graphs = []
+    for i in range(decode_steps):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=gstream):
+            decode_step(i)
+        graphs.append(g)
+    if lib.attn_sync():
+        raise RuntimeError(pkg.last_error(lib))
+    for g in graphs[:2]:  # warm-up replays
+        g.replay()
+    gstream.synchronize()
+
+    def replay_all():
+        with torch.cuda.stream(gstream):
+            for g in graphs:
+                g.replay()
+
+    dctx.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(gstream)
+    replay_all()
+    e1.record(gstream)
+    torch.cuda.synchronize()
+    dctx.barrier()
+    dec_ms = dctx.max(e0.elapsed_time(e1))
+    del graphs, g
+    torch.cuda.synchronize()
     if lib.attn_sync():
         raise RuntimeError(pkg.last_error(lib))
     lib.attn_set_stream(None)
