@@ -308,11 +308,12 @@ def time_long_context(pkg, lib, dctx, device, decode_steps=16):
     """one 32,768-token sequence (30,000 vision tokens on a 150x200 M-RoPE
     grid + 2,768 text tokens), 28 layers, BF16, sharded by KV head over the ranks (8/N heads
     each): per layer attention_prefill_fused_gqa_heads -> NCCL all-gather of the head-major
-    shards -> attn_heads_to_tokens; then decode steps at 32K context the same way
-    (attention_decode_append_gqa_heads + all-gather of the [2n][128] shard straight into the
-    [16][128] output -- for one token the head-major and token-major layouts coincide), each
-    decode step replayed from a CUDA graph of its 28 (attention + NCCL all-gather) pairs, as a
-    serving loop would.  CUDA events on the compute stream, max over ranks; one warm-up pass
+    shards -> attn_heads_to_tokens; then decode steps at 32K context, every rank ending each
+    layer with the whole [16][128] output: attention_decode_append_gqa_gathered (the shards
+    stored straight into every rank's buffer by the decode kernels over NVLink, no collective
+    call), and for comparison attention_decode_append_gqa_heads + NCCL all-gather of the
+    [2n][128] shard (for one token the head-major and token-major layouts coincide).  Each decode
+    step is replayed from a CUDA graph of its 28 layers, as a serving loop would.  CUDA events on the compute stream, max over ranks; one warm-up pass
     first.  The graphs are released before returning (before the process group goes away)."""
     import torch
     shard = importlib.import_module(pkg.__name__ + ".shard")
@@ -357,14 +358,18 @@ def time_long_context(pkg, lib, dctx, device, decode_steps=16):
     dpart = torch.empty((2 * n, D), device=device)
     dout = torch.empty((HQ, D), device=device)
 
-    def decode_step(i):
+    def decode_step(i, fused):
         cs.seq_len = S + i
         for layer in range(LAYERS):
-            # one GPU: the shard is the whole [16][128] output
-            if lib.attention_decode_append_gqa_heads(vp(dq[layer]), vp(dk[layer]), vp(dv[layer]), cache,
-                                                     vp(dpart if world > 1 else dout), layer, scale, h0, n):
+            if fused:  # the library's peer-store gather: the whole [16][128] output on every rank
+                rc = lib.attention_decode_append_gqa_gathered(vp(dq[layer]), vp(dk[layer]), vp(dv[layer]), cache,
+                                                              vp(dout), layer, scale, h0, n)
+            else:      # one GPU: the shard is the whole output; else NCCL all-gather of the shards
+                rc = lib.attention_decode_append_gqa_heads(vp(dq[layer]), vp(dk[layer]), vp(dv[layer]), cache,
+                                                           vp(dpart if world > 1 else dout), layer, scale, h0, n)
+            if rc:
                 raise RuntimeError(pkg.last_error(lib))
-            if world > 1:
+            if world > 1 and not fused:
                 dctx.dist.all_gather_into_tensor(dout, dpart)
 
     def timed(fn):
@@ -381,43 +386,53 @@ def time_long_context(pkg, lib, dctx, device, decode_steps=16):
     prefill()  # warm-up
     pf_ms = timed(prefill)
     # Decode: one graph per step (the step's kv_len is in the captured launch arguments),
-    # captured on a side stream after an eager warm-up step (NCCL communicator set up).
+    # captured on a side stream after an eager warm-up step (communicators set up).
     gstream = torch.cuda.Stream(device)
     gstream.wait_stream(stream)
     lib.attn_set_stream(ctypes.c_void_p(gstream.cuda_stream))
-    with torch.cuda.stream(gstream):
-        decode_step(0)
-    gstream.synchronize()
-    graphs = []
-    for i in range(decode_steps):
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g, stream=gstream):
-            decode_step(i)
-        graphs.append(g)
-    if lib.attn_sync():
-        raise RuntimeError(pkg.last_error(lib))
-    for g in graphs[:2]:  # warm-up replays
-        g.replay()
-    gstream.synchronize()
+    peers = shard.PeerGather(lib) if world > 1 else None
 
-    def replay_all():
+    def time_decode(fused):
+        with torch.cuda.stream(gstream):
+            decode_step(0, fused)
+        gstream.synchronize()
+        graphs = []
+        for i in range(decode_steps):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=gstream):
+                decode_step(i, fused)
+            graphs.append(g)
+        if lib.attn_sync():
+            raise RuntimeError(pkg.last_error(lib))
+        with torch.cuda.stream(gstream):
+            for g in graphs[:2]:  # warm-up replays
+                g.replay()
+        gstream.synchronize()
+        dctx.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(gstream)
         with torch.cuda.stream(gstream):
             for g in graphs:
                 g.replay()
+        e1.record(gstream)
+        torch.cuda.synchronize()
+        dctx.barrier()
+        ms = dctx.max(e0.elapsed_time(e1))
+        del graphs, g  # released before the process group (and the peer mapping) go away
+        torch.cuda.synchronize()
+        if lib.attn_sync():
+            raise RuntimeError(pkg.last_error(lib))
+        return ms
 
-    dctx.barrier()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(gstream)
-    replay_all()
-    e1.record(gstream)
-    torch.cuda.synchronize()
-    dctx.barrier()
-    dec_ms = dctx.max(e0.elapsed_time(e1))
-    del graphs, g
-    torch.cuda.synchronize()
-    if lib.attn_sync():
-        raise RuntimeError(pkg.last_error(lib))
+    try:
+        dec_ms = time_decode(fused=world > 1)
+        dec_nccl_ms = time_decode(fused=False) if world > 1 else None
+    finally:
+        torch.cuda.synchronize()
+        dctx.barrier()
+        if peers is not None:
+            peers.close()
     lib.attn_set_stream(None)
     lib.kv_cache_free(cache)
     flops = LAYERS * 4.0 * D * HQ * S * (S + 1) / 2
@@ -427,11 +442,14 @@ def time_long_context(pkg, lib, dctx, device, decode_steps=16):
         "kv_heads_per_gpu": n,
         "prefill_ms": pf_ms, "prefill_tok_per_s": S / (pf_ms * 1e-3), "prefill_tflops": flops / (pf_ms * 1e-3) / 1e12,
         "decode_us_per_step": dec_ms * 1e3 / decode_steps, "decode_steps": decode_steps,
+        "decode_gather": "peer stores over NVLink fused into the decode kernel (attention_decode_append_gqa_gathered)"
+                         if world > 1 else "none (one GPU)",
+        "decode_us_per_step_nccl_allgather": dec_nccl_ms * 1e3 / decode_steps if dec_nccl_ms else None,
         "decode_kv_len": f"{S + 1}..{S + decode_steps}",
         "allgather_bytes_per_layer": {"prefill": S * HQ * D * 2 if world > 1 else 0,
                                       "decode": HQ * D * 4 if world > 1 else 0},
-        "path": "attention_prefill_fused_gqa_heads / attention_decode_append_gqa_heads + all_gather_into_tensor "
-                "+ attn_heads_to_tokens",
+        "path": "prefill: attention_prefill_fused_gqa_heads + NCCL all_gather_into_tensor + attn_heads_to_tokens; "
+                "decode: attention_decode_append_gqa_gathered (N > 1) / attention_decode_append_gqa_heads",
     }
 
 

@@ -97,6 +97,27 @@ int attention_decode_append_gqa_heads(const float *q, const float *k_new, const 
                                       KVCache *cache, float *output, int layer_idx, float scale,
                                       int kv_head0, int kv_heads);
 
+/* Decode output gather over NVLink, without a collective library: attention_decode_append_gqa_heads
+ * whose output is the whole [16][128] on every rank.  The CTA that finishes a head pair stores it
+ * into every rank's exchange buffer (peer stores into memory mapped by CUDA IPC), the rank's last
+ * one raises its flag there, and a one-block kernel waits (bounded; attn_last_error on timeout)
+ * for all ranks' flags of the call and copies the result to `output`.  One rank per GPU on one
+ * node, up to 8 ranks; every rank calls with the same layers in the same order.
+ *   attn_gather_init(rank, world)   allocates this rank's exchange buffer on the current device
+ *   attn_gather_handle(h)           writes its 64-byte CUDA IPC handle to h
+ *   attn_gather_connect(handles)    handles: world x 64 bytes in rank order (exchanged by the
+ *                                   caller, e.g. with torch.distributed); maps the peers' buffers
+ *   attn_gather_close()             unmaps and frees (after all calls have completed)
+ * attention_decode_append_gqa_gathered: as attention_decode_append_gqa_heads for the KV heads
+ * [kv_head0, kv_head0 + kv_heads) of this rank (BF16 cache), output [16][128] fp32 (host or
+ * device).  0 on success. */
+int  attn_gather_init(int rank, int world);
+int  attn_gather_handle(void *handle_out);
+int  attn_gather_connect(const void *handles);
+void attn_gather_close(void);
+int  attention_decode_append_gqa_gathered(const float *q, const float *k_new, const float *v_new, KVCache *cache,
+                                          float *output, int layer_idx, float scale, int kv_head0, int kv_heads);
+
 /* Gathered head-major [16][seq_len][128] -> token-major [seq_len][16][128], in dtype
  * (ATTN_DT_F32 or ATTN_DT_BF16); device memory, queued on the library stream.  0 on success. */
 int attn_heads_to_tokens(const void *gathered, void *output, int seq_len, int dtype);

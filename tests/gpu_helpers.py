@@ -76,3 +76,11 @@ def bf16_round(a):
 def head_first(rows):
     """token-major [n,8,128] -> head-first [8,n,128]."""
     return np.ascontiguousarray(rows.transpose(1, 0, 2))
+
+
+def load_pkg_and_lib():
+    """The package (from the repository) and its loaded library, for child processes that run
+    outside the pytest fixtures."""
+    import conftest
+    pkg = conftest.load_pkg()
+    return pkg, pkg.load_attention_lib()

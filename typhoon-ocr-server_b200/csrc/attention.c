@@ -28,7 +28,7 @@ static int decode_launch(const float *q, float *out, const tyb_seq_kv *seqs_dev,
                          unsigned int *counters, int flags, void *st)
 {
     return tyb_decode_launch_heads(q, out, seqs_dev, one, batch, max_kv, dtype, scale, partials, counters, NULL, NULL,
-                                   prefetch_rows, 0, KV_NUM_KV_HEADS, flags, st);
+                                   prefetch_rows, 0, KV_NUM_KV_HEADS, flags, NULL, st);
 }
 
 static int check_layer(int layer, const char *what)
@@ -297,8 +297,10 @@ int attention_decode_gqa_batched(const float *q, const KVCache *const *caches, c
     return 0;
 }
 
+/* gather: NULL, or the connected output gather (the output is then the whole [16][128],
+ * assembled from every rank's shard; see attn_gather_init). */
 static int decode_append_impl(const float *q, const float *k_new, const float *v_new, KVCache *cache, float *output,
-                              int layer_idx, float scale, int kvh0, int nkvh, const char *what)
+                              int layer_idx, float scale, int kvh0, int nkvh, const void *gather, const char *what)
 {
     tyb_cache *t = tyb_cache_from(cache);
     if (!t || !check_layer(layer_idx, what)) return 1;
@@ -319,7 +321,8 @@ static int decode_append_impl(const float *q, const float *k_new, const float *v
     const float *dv = dk ? small_view(v_new, t->d_kv_stage + TYB_ROW_FLOATS, row, &vk, st, what) : NULL;
     if (!dq || !dk || !dv) return 1;
     float *dout = small_view(output, NULL, 0, &ok, st, what);
-    const size_t out_floats = (size_t)2 * nkvh * KV_HEAD_DIM;  /* rows of the query heads computed */
+    /* rows of the query heads computed (all 16 when gathered from every rank) */
+    const size_t out_floats = (size_t)2 * (gather ? KV_NUM_KV_HEADS : nkvh) * KV_HEAD_DIM;
     if (ok < 0 || (ok != TYB_MEM_HOST && !dout)) return 1;
     if (ok == TYB_MEM_HOST) dout = t->d_out;
     tyb_seq_kv one;
@@ -333,9 +336,10 @@ static int decode_append_impl(const float *q, const float *k_new, const float *v
                                              (qk != TYB_MEM_PINNED && kk != TYB_MEM_PINNED && vk != TYB_MEM_PINNED)
                                                  ? TYB_DEC_DEVICE_SMALL
                                                  : 0,
-                                             st),
+                                             gather, st),
                      what))
         return 1;
+    if (gather && !tyb_cuda_ok(tyb_gather_wait_launch(dout, st), what)) return 1;
     tyb_note_write(cache, layer_idx, pos, st);
     if (ok == TYB_MEM_HOST && !tyb_cuda_ok(cudaMemcpyAsync(output, dout, out_floats * sizeof(float),
                                                            cudaMemcpyDeviceToHost, (cudaStream_t)st),
@@ -350,7 +354,7 @@ static int decode_append_impl(const float *q, const float *k_new, const float *v
 int attention_decode_append_gqa(const float *q, const float *k_new, const float *v_new, KVCache *cache,
                                 float *output, int layer_idx, float scale)
 {
-    return decode_append_impl(q, k_new, v_new, cache, output, layer_idx, scale, 0, KV_NUM_KV_HEADS,
+    return decode_append_impl(q, k_new, v_new, cache, output, layer_idx, scale, 0, KV_NUM_KV_HEADS, NULL,
                               "attention_decode_append_gqa");
 }
 
@@ -368,7 +372,47 @@ int attention_decode_append_gqa_heads(const float *q, const float *k_new, const 
 {
     const char *what = "attention_decode_append_gqa_heads";
     if (!check_heads(kv_head0, kv_heads, what)) return 1;
-    return decode_append_impl(q, k_new, v_new, cache, output, layer_idx, scale, kv_head0, kv_heads, what);
+    return decode_append_impl(q, k_new, v_new, cache, output, layer_idx, scale, kv_head0, kv_heads, NULL, what);
+}
+
+int attn_gather_init(int rank, int world)
+{
+    if (world < 1 || world > 8 || rank < 0 || rank >= world) {
+        tyb_set_error("attn_gather_init: need 0 <= rank (%d) < world (%d) <= 8", rank, world);
+        return 1;
+    }
+    return tyb_cuda_ok(tyb_gather_init(rank, world), "attn_gather_init") ? 0 : 1;
+}
+
+int attn_gather_handle(void *handle_out)
+{
+    return tyb_cuda_ok(tyb_gather_handle(handle_out), "attn_gather_handle") ? 0 : 1;
+}
+
+int attn_gather_connect(const void *handles)
+{
+    return tyb_cuda_ok(tyb_gather_connect(handles), "attn_gather_connect") ? 0 : 1;
+}
+
+void attn_gather_close(void) { tyb_gather_close(); }
+
+int attention_decode_append_gqa_gathered(const float *q, const float *k_new, const float *v_new, KVCache *cache,
+                                         float *output, int layer_idx, float scale, int kv_head0, int kv_heads)
+{
+    const char *what = "attention_decode_append_gqa_gathered";
+    if (!check_heads(kv_head0, kv_heads, what)) return 1;
+    int world = 0, rank = 0;
+    const void *g = tyb_gather_dev(&world, &rank);
+    if (!g) {
+        tyb_set_error("%s: no connected output gather (attn_gather_init / attn_gather_connect)", what);
+        return 1;
+    }
+    tyb_cache *t = tyb_cache_from(cache);
+    if (t && t->dtype != TYB_BF16) {
+        tyb_set_error("%s: the cache must hold BF16 rows", what);
+        return 1;
+    }
+    return decode_append_impl(q, k_new, v_new, cache, output, layer_idx, scale, kv_head0, kv_heads, g, what);
 }
 
 static int prefill_fused_impl(const void *q_raw, const void *k_raw, const void *v_raw, int in_dtype,

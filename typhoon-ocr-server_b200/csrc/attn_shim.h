@@ -64,7 +64,14 @@ int tyb_decode_launch_ex(const float *q, float *out, const tyb_seq_kv *seqs_dev,
 int tyb_decode_launch_heads(const float *q, float *out, const tyb_seq_kv *seqs_dev, tyb_seq_kv one, int batch,
                             int max_kv_len, int kv_dtype, float scale, float *partials, unsigned int *counters,
                             const float *k_new, const float *v_new, int prefetch_rows, int kvh0, int nkvh,
-                            int flags, void *stream);
+                            int flags, const void *gather, void *stream);
+/* Decode output gather over NVLink (decode.cu): this rank's exchange buffer and peers'. */
+int tyb_gather_init(int rank, int world);
+int tyb_gather_handle(void *handle_out);            /* 64-byte cudaIpcMemHandle_t */
+int tyb_gather_connect(const void *handles);         /* world x 64 bytes, rank order */
+const void *tyb_gather_dev(int *world, int *rank);   /* NULL until connected */
+int tyb_gather_wait_launch(float *out, void *stream);
+void tyb_gather_close(void);
 /* Encodes into `map` (a CUtensorMap: 128 bytes, 64-byte aligned) rows [0, rows) of the 8
  * heads of one layer's BF16 cache slab (head stride row_capacity rows) as a 3-D tensor
  * {128 dims, rows, 8 heads}, copied in 128-byte-swizzled boxes of {64, box_rows, 1}; rows

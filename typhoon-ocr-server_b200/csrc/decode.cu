@@ -509,6 +509,75 @@ constexpr int kQaPitch = 272;  // bytes per A row of the query (256 + 16: confli
 // cost than latency hidden).
 constexpr int kMmaStat = 64 + 256;  // floats: block maxima and sums [16][2] x 2, P.V half exchange [8][2][16]
 
+// ---- decode output gather over NVLink (KV-head sharding, one rank per GPU) -------------------
+//
+// With the KV heads of one sequence split over N ranks, every rank needs the whole [16][128]
+// output of each decode call.  Instead of a separate collective per layer, the CTA that writes a
+// head pair's final output also stores it into every rank's exchange buffer (peer stores over
+// NVLink into memory mapped by CUDA IPC), and the last such CTA of the rank then raises the rank's
+// flag in every exchange buffer; a one-block wait kernel per rank waits for all ranks' flags
+// (bounded) and copies the assembled output to the caller.  Epochs (one per call, counted on
+// each rank) make the flags monotone, and the exchange buffer is double-buffered by epoch parity:
+// a rank can run at most one call ahead of another (its next wait needs the other's next
+// publication, which follows the other's current wait).
+
+constexpr int kGatherMaxRanks = 8;
+
+struct GatherBuf {                          // one per rank, in that rank's device memory
+    float data[2][kHq][kD];                 // assembled outputs, by epoch parity
+    unsigned int flags[kGatherMaxRanks];    // flags[r]: last epoch rank r has published here
+    unsigned int epoch;                     // calls this rank has completed (local)
+    unsigned int done;                      // this rank's head pairs published in the current call
+};
+
+struct GatherDev {                          // device table, in this rank's memory
+    GatherBuf* buf[kGatherMaxRanks];        // every rank's exchange buffer (peers through IPC)
+    int rank;
+    int world;
+};
+
+__device__ __forceinline__ unsigned int ld_acquire_sys(const unsigned int* p)
+{
+    unsigned int v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void st_release_sys(unsigned int* p, unsigned int v)
+{
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Called by every thread of the CTA that has just written rows row0, row0 + 1 of this rank's
+// exchange slot data[epoch & 1]: copies them to the other ranks' slots and, for the rank's last
+// head pair of the call, raises the rank's flag everywhere (a system-scope acquire-release count
+// orders the peer stores of all the rank's CTAs before the flags).
+__device__ __forceinline__ void gather_publish(const GatherDev* g, int row0, int nkvh_local, unsigned int epoch)
+{
+    const int par = (int)(epoch & 1u);
+    __syncthreads();
+    const float* src = &g->buf[g->rank]->data[par][row0][0];
+    for (int i = threadIdx.x; i < 2 * kD; i += blockDim.x) {
+        const float v = src[i];
+        for (int p = 0; p < g->world; p++)
+            if (p != g->rank) (&g->buf[p]->data[par][row0][0])[i] = v;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        // Acquire-release at system scope: releases this CTA's peer stores (ordered by the barrier)
+        // and, for the last CTA, acquires the other CTAs' before the flags go out.
+        unsigned int old;
+        asm volatile("atom.acq_rel.sys.global.add.u32 %0, [%1], 1;"
+                     : "=r"(old)
+                     : "l"(&g->buf[g->rank]->done)
+                     : "memory");
+        if (old == (unsigned int)(nkvh_local - 1)) {
+            atomicExch(&g->buf[g->rank]->done, 0u);
+            for (int p = 0; p < g->world; p++) st_release_sys(&g->buf[p]->flags[g->rank], epoch);
+        }
+    }
+}
+
 struct DecodeMmaArgs {
     const float* q;  // [batch][16][128]
     float* out;      // query head 2 kvh0's row of sequence 0 (row stride 16 x 128 per sequence)
@@ -531,6 +600,7 @@ struct DecodeMmaArgs {
     unsigned int* counters;
     int kvh0;
     int prefetch_small;
+    const GatherDev* gather;  // non-NULL: outputs go to the exchange buffer and to every rank
 };
 
 __host__ __device__ constexpr size_t mma_pa_pitch(int chunk) { return (size_t)(chunk + 8) * 2; }
@@ -952,8 +1022,13 @@ __global__ void __launch_bounds__(NW * 32, 16 / NW)
 #pragma unroll
     for (int w = 0; w < NW; w++) L += lw[2 * w + hh];
     const int dim = 16 * slice + g;
-    // rows of query heads 2 kvh, 2 kvh + 1 of sequence b
+    // rows of query heads 2 kvh, 2 kvh + 1 of sequence b (or of this rank's exchange slot)
+    unsigned int epoch = 0;
     float* out_pair = a.out + (size_t)b * kHq * kD + (size_t)(kGroup * (kvh - a.kvh0)) * kD;
+    if (a.gather) {
+        epoch = __ldcg(&a.gather->buf[a.gather->rank]->epoch) + 1u;
+        out_pair = &a.gather->buf[a.gather->rank]->data[epoch & 1u][kGroup * kvh][0];
+    }
 
     if (nsplit == 1) {
         if (writer) {
@@ -962,6 +1037,7 @@ __global__ void __launch_bounds__(NW * 32, 16 / NW)
             o_[0] = y0 * inv;
             o_[8] = y1 * inv;
         }
+        if (a.gather) gather_publish(a.gather, kGroup * kvh, gridDim.y, epoch);
         return;
     }
 
@@ -991,6 +1067,7 @@ __global__ void __launch_bounds__(NW * 32, 16 / NW)
     if (!*last_flag) return;
     merge_records_direct(recs, nsplit, reinterpret_cast<float*>(Kt), out_pair);
     if (tid == 0) a.counters[b * kHkv + kvh] = 0u;
+    if (a.gather) gather_publish(a.gather, kGroup * kvh, gridDim.y, epoch);
 }
 
 // ---- streaming form: many waves (request batches, long sequences) ----------------------------
@@ -1251,7 +1328,12 @@ __global__ void __launch_bounds__(256, 2)
     const float y0 = o[0][0] + o[1][0] + o[0][1] + o[1][1];  // dim 16 warp + g, head hh (holders)
     const float y1 = o[0][2] + o[1][2] + o[0][3] + o[1][3];  // dim 16 warp + g + 8
     const int dim = 16 * warp + g;
+    unsigned int epoch = 0;
     float* out_pair = a.out + (size_t)b * kHq * kD + (size_t)(kGroup * (kvh - a.kvh0)) * kD;
+    if (a.gather) {
+        epoch = __ldcg(&a.gather->buf[a.gather->rank]->epoch) + 1u;
+        out_pair = &a.gather->buf[a.gather->rank]->data[epoch & 1u][kGroup * kvh][0];
+    }
     if (nspan == 1) {
         if (holder) {
             float* o_ = out_pair + (size_t)hh * kD + dim;
@@ -1259,6 +1341,7 @@ __global__ void __launch_bounds__(256, 2)
             o_[0] = y0 * inv;
             o_[8] = y1 * inv;
         }
+        if (a.gather) gather_publish(a.gather, kGroup * kvh, gridDim.y, epoch);
         return;
     }
     float* recs = a.partials + ((size_t)b * kHkv + kvh) * a.nsplit * kRec;  // a.nsplit: the record stride
@@ -1287,6 +1370,41 @@ __global__ void __launch_bounds__(256, 2)
     if (!*last_flag) return;
     merge_records_direct(recs, nspan, reinterpret_cast<float*>(smem), out_pair);
     if (tid == 0) a.counters[b * kHkv + kvh] = 0u;
+    if (a.gather) gather_publish(a.gather, kGroup * kvh, gridDim.y, epoch);
+}
+
+// Waits (bounded) until every rank has published this call's epoch into this rank's exchange
+// buffer, copies the assembled [16][128] output to `out`, and counts the call.  One block,
+// launched as a programmatic dependent of the decode kernel: it needs nothing of that kernel but
+// the flags (system-scope acquire), so it starts waiting at once, and it lets the next kernel's
+// CTAs launch at once (they wait for its completion in their own dependency wait).  The epoch it
+// reads was written by the previous call's wait kernel, complete before the decode kernel passed
+// its own dependency wait.
+__global__ void __launch_bounds__(256) gather_wait_kernel(const GatherDev* g, float* out)
+{
+    __shared__ int fail;
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    GatherBuf* mine = g->buf[g->rank];
+    const unsigned int epoch = __ldcg(&mine->epoch) + 1u;
+    if (threadIdx.x == 0) fail = 0;
+    __syncthreads();
+    if (threadIdx.x < g->world) {
+        const uint64_t t0 = globaltimer_ns();
+        while ((int)(ld_acquire_sys(&mine->flags[threadIdx.x]) - epoch) < 0) {
+            if (globaltimer_ns() - t0 > kWaitLimitNs) {
+                raise_status(TYB_STATUS_WAIT_TIMEOUT);
+                fail = 1;
+                break;
+            }
+            __nanosleep(64);
+        }
+    }
+    __syncthreads();
+    if (fail) return;
+    const float* src = &mine->data[epoch & 1u][0][0];
+    for (int i = threadIdx.x; i < kHq * kD; i += blockDim.x) out[i] = __ldcg(src + i);
+    __syncthreads();
+    if (threadIdx.x == 0) mine->epoch = epoch;
 }
 
 // ---- host-side planning ----------------------------------------------------------------
@@ -1561,6 +1679,7 @@ extern "C" int tyb_decode_launch_batched(const float* q, float* out, const tyb_s
     a.partials = partials;
     a.counters = counters;
     a.prefetch_small = 1;
+    a.gather = nullptr;
     return launch_stream(a, m0, m1, kHkv, batch, stream);
 }
 
@@ -1582,8 +1701,10 @@ extern "C" size_t tyb_decode_partial_floats(int batch, int nsplit)
 extern "C" int tyb_decode_launch_heads(const float* q, float* out, const tyb_seq_kv* seqs_dev, tyb_seq_kv one,
                                        int batch, int max_kv_len, int kv_dtype, float scale, float* partials,
                                        unsigned int* counters, const float* k_new, const float* v_new,
-                                       int prefetch_rows, int kvh0, int nkvh, int flags, void* stream)
+                                       int prefetch_rows, int kvh0, int nkvh, int flags, const void* gather,
+                                       void* stream)
 {
+    if (gather && (kv_dtype != TYB_BF16 || seqs_dev || batch != 1)) return (int)cudaErrorInvalidValue;
     if (batch <= 0 || max_kv_len <= 0 || nkvh <= 0) return 0;
     DecodeArgs a;
     a.kvh0 = kvh0;
@@ -1628,6 +1749,7 @@ extern "C" int tyb_decode_launch_heads(const float* q, float* out, const tyb_seq
         m.counters = counters;
         m.kvh0 = kvh0;
         m.prefetch_small = a.prefetch_small;
+        m.gather = static_cast<const GatherDev*>(gather);
         if (one_wave(1, max_kv_len, nkvh)) return launch_decode_mma(m, one, nkvh, stream);
         const int e = set_mma_smem_attr();
         if (e) return e;
@@ -1647,7 +1769,7 @@ extern "C" int tyb_decode_launch_ex(const float* q, float* out, const tyb_seq_kv
                                     int prefetch_rows, void* stream)
 {
     return tyb_decode_launch_heads(q, out, seqs_dev, one, batch, max_kv_len, kv_dtype, scale, partials, counters,
-                                   k_new, v_new, prefetch_rows, 0, kHkv, 0, stream);
+                                   k_new, v_new, prefetch_rows, 0, kHkv, 0, nullptr, stream);
 }
 
 extern "C" int tyb_decode_launch(const float* q, float* out, const tyb_seq_kv* seqs_dev, tyb_seq_kv one,
@@ -1769,4 +1891,115 @@ extern "C" int attention_decode_gqa_noalloc(const float* q, const void* k_rows, 
         return 1;
     }
     return 0;
+}
+
+// ---- decode output gather: host side ----------------------------------------------------------
+
+namespace tyb {
+
+struct GatherHost {
+    GatherBuf* local = nullptr;  // this rank's exchange buffer
+    GatherDev* dev = nullptr;    // device table
+    GatherBuf* peer[kGatherMaxRanks] = {};
+    int rank = -1;
+    int world = 0;
+    bool connected = false;
+};
+static GatherHost g_gather;
+static std::mutex g_gather_mu;
+
+}  // namespace tyb
+
+extern "C" int tyb_gather_init(int rank, int world)
+{
+    std::lock_guard<std::mutex> lock(g_gather_mu);
+    if (world < 1 || world > kGatherMaxRanks || rank < 0 || rank >= world) return (int)cudaErrorInvalidValue;
+    if (g_gather.local) return (int)cudaErrorInvalidValue;  // already set up: close first
+    cudaError_t e = cudaMalloc(&g_gather.local, sizeof(GatherBuf));
+    if (e == cudaSuccess) e = cudaMemset(g_gather.local, 0, sizeof(GatherBuf));
+    if (e == cudaSuccess) e = cudaMalloc(&g_gather.dev, sizeof(GatherDev));
+    if (e != cudaSuccess) {
+        cudaFree(g_gather.local);
+        g_gather.local = nullptr;
+        return (int)e;
+    }
+    g_gather.rank = rank;
+    g_gather.world = world;
+    return 0;
+}
+
+extern "C" int tyb_gather_handle(void* handle_out)
+{
+    if (!g_gather.local || !handle_out) return (int)cudaErrorInvalidValue;
+    cudaIpcMemHandle_t h;
+    const cudaError_t e = cudaIpcGetMemHandle(&h, g_gather.local);
+    if (e != cudaSuccess) return (int)e;
+    memcpy(handle_out, &h, sizeof h);
+    return 0;
+}
+
+extern "C" int tyb_gather_connect(const void* handles)
+{
+    std::lock_guard<std::mutex> lock(g_gather_mu);
+    if (!g_gather.local || !handles || g_gather.connected) return (int)cudaErrorInvalidValue;
+    GatherDev d = {};
+    d.rank = g_gather.rank;
+    d.world = g_gather.world;
+    for (int p = 0; p < g_gather.world; p++) {
+        if (p == g_gather.rank) {
+            d.buf[p] = g_gather.local;
+            continue;
+        }
+        cudaIpcMemHandle_t h;
+        memcpy(&h, static_cast<const unsigned char*>(handles) + (size_t)p * sizeof h, sizeof h);
+        void* ptr = nullptr;
+        const cudaError_t e = cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) {
+            for (int q = 0; q < p; q++)
+                if (g_gather.peer[q]) cudaIpcCloseMemHandle(g_gather.peer[q]);
+            return (int)e;
+        }
+        g_gather.peer[p] = static_cast<GatherBuf*>(ptr);
+        d.buf[p] = g_gather.peer[p];
+    }
+    const cudaError_t e = cudaMemcpy(g_gather.dev, &d, sizeof d, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) return (int)e;
+    g_gather.connected = true;
+    return 0;
+}
+
+extern "C" const void* tyb_gather_dev(int* world, int* rank)
+{
+    if (!g_gather.connected) return nullptr;
+    if (world) *world = g_gather.world;
+    if (rank) *rank = g_gather.rank;
+    return g_gather.dev;
+}
+
+extern "C" int tyb_gather_wait_launch(float* out, void* stream)
+{
+    if (!g_gather.connected) return (int)cudaErrorInvalidValue;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1);
+    cfg.blockDim = dim3(256);
+    cfg.stream = (cudaStream_t)stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return (int)cudaLaunchKernelEx(&cfg, gather_wait_kernel, (const GatherDev*)g_gather.dev, out);
+}
+
+extern "C" void tyb_gather_close(void)
+{
+    std::lock_guard<std::mutex> lock(g_gather_mu);
+    cudaDeviceSynchronize();
+    for (int p = 0; p < kGatherMaxRanks; p++) {
+        if (g_gather.peer[p]) cudaIpcCloseMemHandle(g_gather.peer[p]);
+        g_gather.peer[p] = nullptr;
+    }
+    cudaFree(g_gather.dev);
+    cudaFree(g_gather.local);
+    g_gather = GatherHost();
 }

@@ -54,3 +54,38 @@ def tokens_from_heads(gathered):
     """Head-major [16][S][128] -> token-major [S][16][128] (host-side twin of
     attn_heads_to_tokens, for tensors or arrays)."""
     return gathered.swapaxes(0, 1)
+
+
+class PeerGather:
+    """The library's decode output gather over NVLink (attn_gather_*), set up for the ranks of
+    `group`: each rank allocates its exchange buffer, the 64-byte CUDA IPC handles are
+    exchanged with torch.distributed (any backend) and the peers' buffers mapped.  Then
+    attention_decode_append_gqa_gathered returns the whole [16][128] output on every rank.
+    close() after the last call (all of them completed)."""
+
+    def __init__(self, lib, group=None):
+        import ctypes
+        import torch.distributed as dist
+
+        self.lib = lib
+        rank, world = dist.get_rank(group), dist.get_world_size(group)
+        if lib.attn_gather_init(rank, world):
+            raise RuntimeError((lib.attn_last_error() or b"").decode())
+        try:
+            h = (ctypes.c_char * 64)()
+            if lib.attn_gather_handle(h):
+                raise RuntimeError((lib.attn_last_error() or b"").decode())
+            handles = [None] * world
+            dist.all_gather_object(handles, bytes(h), group=group)
+            blob = b"".join(handles)
+            buf = (ctypes.c_char * len(blob)).from_buffer_copy(blob)
+            if lib.attn_gather_connect(buf):
+                raise RuntimeError((lib.attn_last_error() or b"").decode())
+        except BaseException:
+            lib.attn_gather_close()
+            raise
+
+    def close(self):
+        if self.lib is not None:
+            self.lib.attn_gather_close()
+            self.lib = None
