@@ -438,7 +438,8 @@ def time_long_context(pkg, lib, dctx, device, decode_steps=16):
     flops = LAYERS * 4.0 * D * HQ * S * (S + 1) / 2
     return {
         "workload": "config5: 32,768 tokens (30,000 vision 150x200 + 2,768 text), 28 layers, bf16, QK-RMSNorm + "
-                    "M-RoPE fused; KV heads sharded over the GPUs, NCCL all-gather of the head outputs per layer",
+                    "M-RoPE fused; KV heads sharded over the GPUs; per layer the head outputs gathered on every "
+                    "rank (prefill: NCCL all-gather; decode: peer stores fused into the decode kernels)",
         "kv_heads_per_gpu": n,
         "prefill_ms": pf_ms, "prefill_tok_per_s": S / (pf_ms * 1e-3), "prefill_tflops": flops / (pf_ms * 1e-3) / 1e12,
         "decode_us_per_step": dec_ms * 1e3 / decode_steps, "decode_steps": decode_steps,
@@ -692,6 +693,8 @@ def run_case(case):
       decode-small   4 decode steps of config 2 (28 layers, BF16 cache filled to 4,096 rows, 470 MB
                      of K/V: larger than L2) through attention_decode_append_gqa, device buffers
       prefill-small  4 passes of one config-3 layer (4,096 tokens) through attention_prefill_fused_gqa
+      batched-small  4 request-batch launches (the streaming form) over 6 sequences of config 4's
+                     seeded ragged list, alternating two layers (~230 MB of K/V: larger than L2)
     """
     import torch
     pkg = _pkg()
@@ -715,6 +718,34 @@ def run_case(case):
             for layer in range(LAYERS):
                 if lib.attention_decode_append_gqa(vp(q), vp(kn), vp(vn), h, vp(out), layer, ctypes.c_float(pkg.SCALE)):
                     raise RuntimeError(pkg.last_error(lib))
+    elif case == "batched-small":
+        wl = importlib.import_module(pkg.__name__ + ".workloads")
+        lens = wl.config4_kv_lens(512)[:6].astype(np.int64)
+        rows = (0.5 * torch.randn((int(lens.max()), HKV, D), generator=gen, device="cuda")).float()
+        caches = []
+        for kv in lens:
+            c = lib.kv_cache_alloc_ex(int(kv), pkg.ATTN_KV_BF16)
+            if not c:
+                raise RuntimeError(pkg.last_error(lib))
+            cs = pkg.cache_struct(c)
+            for layer in (0, 1):
+                cs.seq_len = 0
+                lib.kv_cache_append_prefill(c, layer, vp(rows), vp(rows), int(kv))
+            caches.append(c)
+        arr = (ctypes.c_void_p * len(caches))(*caches)
+        kvl = (ctypes.c_int * len(caches))(*[int(x) for x in lens])
+        q = torch.randn((len(caches), HQ, D), generator=gen, device="cuda")
+        out = torch.empty((len(caches), HQ, D), device="cuda")
+        for i in range(4):
+            if lib.attention_decode_gqa_batched(vp(q), arr, kvl, vp(out), len(caches), i % 2,
+                                                ctypes.c_float(pkg.SCALE)):
+                raise RuntimeError(pkg.last_error(lib))
+        if lib.attn_sync():
+            raise RuntimeError(pkg.last_error(lib))
+        for c in caches:
+            lib.kv_cache_free(c)
+        print(json.dumps({"case": case, "status": "ok"}))
+        return
     elif case == "prefill-small":
         S = 4096
         q = (0.5 * torch.randn((S, HQ, D), generator=gen, device="cuda")).bfloat16()
@@ -751,7 +782,7 @@ def main():
     ap.add_argument("--prefill-pages", type=int, default=20)
     ap.add_argument("--long-context", type=int, default=1, help="run the config-5 section (1) or not (0)")
     ap.add_argument("--batched", type=int, default=1, help="run the config-4 section (1) or not (0)")
-    ap.add_argument("--case", choices=["decode-small", "prefill-small"],
+    ap.add_argument("--case", choices=["decode-small", "prefill-small", "batched-small"],
                     help="run a small fixed invocation of one kernel (for profiler captures) and exit")
     args = ap.parse_args()
     if args.case:
