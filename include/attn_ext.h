@@ -79,7 +79,7 @@ int attention_decode_append_gqa(const float *q, const float *k_new, const float 
  * shards are all-gathered (ncclAllGather in rank order, by the caller) into head-major
  * [16][S][128], and attn_heads_to_tokens turns that into the token-major layout decoder.c
  * uses.  The reference has no multi-GPU path; these extend attention_prefill_fused_gqa and
- * attention_decode_append_gqa (SURVEY extension "shard by KV head").  kv_head0, kv_heads:
+ * attention_decode_append_gqa.  kv_head0, kv_heads:
  * the KV heads [kv_head0, kv_head0 + kv_heads) computed here, 1 <= kv_heads <= 8.
  *
  * attention_prefill_fused_gqa for the given KV heads only (their K/V rows appended, their

@@ -15,7 +15,7 @@
  *                      mantissa cut to 8 bits (the estimate's precision), so
  *                      the two Newton steps the caller applies converge the
  *                      same way.  Bit-exactness with Apple silicon is not a
- *                      goal: parity is judged by tolerance.
+ *                      goal: parity is checked by tolerance.
  *   vrsqrtsq_f32(a,b) = (3 - a*b) / 2                     vrecpsq_f32(a,b) = 2 - a*b
  *
  * Nothing here is product code; only the oracle build includes it.
