@@ -595,7 +595,8 @@ def cpu_reference_sample(budget_s=12.0, layers_cycle=LAYERS):
     for config 2's schedule.  Returns (us per 28-layer step, cores, kind, sample text)."""
     sys.path.insert(0, str(ROOT / "oracle"))
     import oracle as orc
-    threads = os.cpu_count() or 1
+    threads = orc.host_threads()
+    orc.set_host_threads(threads)  # all of them, whatever OMP_NUM_THREADS the launcher exported
     rng = np.random.default_rng(3)
     q = rng.standard_normal((HQ, D), dtype=np.float32)
     out = np.zeros((HQ, D), dtype=np.float32)
@@ -641,12 +642,15 @@ def run_reference_arm(args):
         return
     sys.path.insert(0, str(ROOT / "oracle"))
     import oracle as orc
-    threads = os.cpu_count() or 1
+    threads = orc.host_threads()
     if not orc.RefLib.available():
         kind = "port"
     else:
         kind = "reference"
     ref = orc.RefLib() if kind == "reference" else None
+    # torchrun exports OMP_NUM_THREADS=1 to every worker when it starts more than one; rank 0
+    # runs the reference alone here, on all the cores this process may use.
+    orc.set_host_threads(threads)
     rng = np.random.default_rng(3)
     q = rng.standard_normal((HQ, D), dtype=np.float32)
     out = np.zeros((HQ, D), dtype=np.float32)

@@ -29,6 +29,29 @@ EPS = 1e-6
 _VP = ctypes.c_void_p
 
 
+def host_threads():
+    """Cores this process may run on (its CPU affinity), at least 1."""
+    import os
+    try:
+        return max(1, len(os.sched_getaffinity(0)))
+    except (AttributeError, OSError):
+        return os.cpu_count() or 1
+
+
+def set_host_threads(n):
+    """Thread count of later OpenMP parallel regions in the libraries here (both link the
+    system libgomp).  Launchers such as torchrun export OMP_NUM_THREADS=1 to their workers;
+    this overrides it for the calling thread.  Returns the count set, or 0 if libgomp is
+    not loadable."""
+    try:
+        gomp = ctypes.CDLL("libgomp.so.1")
+    except OSError:
+        return 0
+    gomp.omp_set_num_threads.argtypes = [ctypes.c_int]
+    gomp.omp_set_num_threads(int(n))
+    return int(n)
+
+
 def _p(a):
     assert a.flags["C_CONTIGUOUS"], "arrays passed to the oracle must be C-contiguous"
     return a.ctypes.data_as(_VP)
