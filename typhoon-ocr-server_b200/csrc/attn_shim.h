@@ -113,7 +113,10 @@ int tyb_kv_prep_launch(const void *k_raw, const void *v_raw, int in_bf16, const 
 /* Causal attention of Sq raw queries [Sq][16][128] (fp32 or bf16; RMSNorm(q_norm) + M-RoPE
  * applied on load) over BF16 cache rows [0, pos_offset + Sq) of one layer; query i sits at
  * position pos_offset + i.  KV heads [kvh0, kvh0 + nkvh) and their query heads only.
- * Output [Sq][16][128], or with out_head_major the shard [2 nkvh][Sq][128]; fp32 or bf16. */
+ * Output [Sq][16][128], or with out_head_major the shard [2 nkvh][Sq][128]; fp32 or bf16.
+ * Launched as a programmatic dependent of the previous kernel in the stream, which must be the
+ * tyb_kv_prep_launch of the same rows (it starts before that kernel completes; its TMA producer
+ * waits for it before reading the cache). */
 int tyb_prefill_tc_launch(const void *q, int q_bf16, const float *q_norm, const float *cos, const float *sin,
                           const void *k_cache, const void *v_cache, int row_capacity, void *out, int out_bf16,
                           int Sq, int pos_offset, float scale, float eps, int kvh0, int nkvh, int out_head_major,

@@ -463,8 +463,11 @@ __global__ void __launch_bounds__(kPtThreads, 1)
         asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kPtIssueRegs));
         if (warp == 9) {
             // ---- TMA producer (one thread): K and V double-buffered, each stage refilled as soon
-            // as the MMAs of the tile two back have read it.
+            // as the MMAs of the tile two back have read it.  The kernel may start while the
+            // previous kernel in the stream (kv_prep, which writes the rows read here) still runs:
+            // this thread, the only reader of those rows, waits for it first.
             if (lane == 0) {
+                asm volatile("griddepcontrol.wait;" ::: "memory");
                 for (int j = 0; j < ntiles; j++) {
                     const int st = j & 1;
                     const uint32_t fpar = (uint32_t)((j - 2) >> 1) & 1u;
@@ -685,6 +688,9 @@ __global__ void kv_prep_kernel(const void* __restrict__ k_raw, const void* __res
                                int kvh0, int nkvh)
 {
     const int lane = threadIdx.x & 31;
+    // The attention kernel that follows may launch now; it waits for this grid before reading
+    // the rows written here.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const long long nwarps = (long long)gridDim.x * (blockDim.x >> 5);
     const float4 w = *reinterpret_cast<const float4*>(k_norm + 4 * lane);
     const float w4[4] = {w.x, w.y, w.z, w.w};
@@ -843,6 +849,21 @@ extern "C" int tyb_prefill_tc_launch(const void* q, int q_bf16, const float* q_n
     CUtensorMap mk, mv;
     if (!make_kv_map(&mk, k_cache, a.total_kv, row_capacity) || !make_kv_map(&mv, v_cache, a.total_kv, row_capacity))
         return (int)cudaErrorInvalidValue;
-    prefill_tc_kernel<<<a.n_qtiles * nkvh, kPtThreads, kPtSmemBytes, (cudaStream_t)stream>>>(mk, mv, a);
-    return (int)cudaGetLastError();
+    // Programmatic dependent launch: the CTAs may start (TMEM, barriers, the query prologue) while
+    // kv_prep finishes; the TMA producer waits for it before reading the cache rows.  This needs
+    // kv_prep to be the previous kernel in the stream, launched without the attribute (so that
+    // everything before it, e.g. whatever produced q, q_norm, cos and sin, has completed): the
+    // only caller launches the two back to back.  The outputs are written after the wait (the
+    // epilogue follows the P.V of every tile, which follows the K/V loads).
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(a.n_qtiles * nkvh));
+    cfg.blockDim = dim3(kPtThreads);
+    cfg.dynamicSmemBytes = kPtSmemBytes;
+    cfg.stream = (cudaStream_t)stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return (int)cudaLaunchKernelEx(&cfg, prefill_tc_kernel, mk, mv, a);
 }
