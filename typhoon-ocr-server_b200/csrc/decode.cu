@@ -1133,6 +1133,29 @@ __global__ void __launch_bounds__(256, 2)
     __syncthreads();
     if (a.prefetch_small && warp == 1 && lane < 8)
         asm volatile("prefetch.global.L2 [%0];" ::"l"(qb + (size_t)(kGroup * kvh) * kD + lane * 32));
+    // One sequence: the tiles of the first two stages are requested before the dependency wait
+    // when the previous kernel wrote none of their cache rows (rows of a box past them are masked
+    // out, zeroed, or -- the appended row -- replaced in shared memory).
+    int early_st = 0;
+    if (!a.seqs && tid == 0) {
+        const int rb = span * a.chunk;
+        if (rb < a.kv_len) {
+            const int re = min(a.kv_len, rb + a.chunk);
+            const int ns = (re - rb + kStRows - 1) / kStRows;
+            const int crows = a.k_new ? a.kv_len - 1 : a.kv_len;
+            for (int st = 0; st < min(2, ns); st++) {
+                if (min(crows, min(re, rb + (st + 1) * kStRows)) > a.prefetch_rows) break;
+                const uint32_t dk = base_u32 + (uint32_t)(st * kStTile), dv = base_u32 + (uint32_t)((2 + st) * kStTile);
+                mbar_arrive_expect_tx(&bars[st], (uint32_t)kStTile);
+                tma_box_3d(dk, &tmk, 0, rb + st * kStRows, kvh, &bars[st]);
+                tma_box_3d(dk + (uint32_t)(kStTile / 2), &tmk, 64, rb + st * kStRows, kvh, &bars[st]);
+                mbar_arrive_expect_tx(&bars[2 + st], (uint32_t)kStTile);
+                tma_box_3d(dv, &tmv, 0, rb + st * kStRows, kvh, &bars[2 + st]);
+                tma_box_3d(dv + (uint32_t)(kStTile / 2), &tmv, 64, rb + st * kStRows, kvh, &bars[2 + st]);
+                early_st = st + 1;
+            }
+        }
+    }
     pdl_wait();
     pdl_trigger();
     if (a.seqs) {
@@ -1168,11 +1191,9 @@ __global__ void __launch_bounds__(256, 2)
         tma_box_3d(dst + (uint32_t)(kStTile / 2), mv, 64, r_begin + st * kStRows, kvh, &bars[2 + buf]);
     };
     if (tid == 0) {
-        issue_k(0);
-        issue_v(0);
-        if (nst > 1) {
-            issue_k(1);
-            issue_v(1);
+        for (int st = early_st; st < min(2, nst); st++) {
+            issue_k(st);
+            issue_v(st);
         }
     }
 
