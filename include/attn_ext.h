@@ -72,6 +72,22 @@ int attention_prefill_fused_gqa(const void *q_raw, const void *k_raw, const void
 int attention_decode_append_gqa(const float *q, const float *k_new, const float *v_new,
                                 KVCache *cache, float *output, int layer_idx, float scale);
 
+/* One decode step of one layer with the whole of kernel/decoder.c:73-105 on the GPU: RMSNorm of
+ * the raw query heads with q_norm and of the raw key heads with k_norm (eps), rotate_half M-RoPE
+ * of both with the token's token_cos / token_sin [64] (one row of the per-token tables; for text
+ * decode all three sections share the position rope_offset or seq_len, kernel/decoder.c:80-83),
+ * the normed, rotated key row and v_new appended at row cache->seq_len, then the attention of
+ * the query over rows [0, seq_len + 1).  The normalisation and rotation run inside the decode
+ * kernel as it loads q and the new row, so the host no longer runs rmsnorm_f32 /
+ * mrope_apply_token per step.  q_raw [16][128], k_raw and v_new [8][128], q_norm / k_norm [128],
+ * token_cos / token_sin [64], output [16][128]: fp32, all DEVICE memory (queued on the library
+ * stream; attn_sync waits).  The cache must be ATTN_KV_BF16.  seq_len is not advanced.  0 on
+ * success. */
+int attention_decode_append_fused_gqa(const float *q_raw, const float *k_raw, const float *v_new,
+                                      const float *q_norm, const float *k_norm, const float *token_cos,
+                                      const float *token_sin, KVCache *cache, float *output, int layer_idx,
+                                      float scale, float eps);
+
 /* ---- KV-head sharding (one long sequence over N GPUs) ---------------------------------
  * The GQA heads are independent: KV head h and query heads 2h, 2h+1 need no other head.  A
  * long sequence is split over N GPUs by KV head (8/N each); every GPU holds its heads'

@@ -111,6 +111,8 @@ _SIGNATURES = {
     "attention_decode_append_gqa_heads": (ctypes.c_int, [_VP, _VP, _VP, _VP, _VP, ctypes.c_int, ctypes.c_float,
                                                          ctypes.c_int, ctypes.c_int]),
     "attn_heads_to_tokens": (ctypes.c_int, [_VP, _VP, ctypes.c_int, ctypes.c_int]),
+    "attention_decode_append_fused_gqa": (ctypes.c_int, [_VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, ctypes.c_int,
+                                                         ctypes.c_float, ctypes.c_float]),
     "attn_gather_init": (ctypes.c_int, [ctypes.c_int, ctypes.c_int]),
     "attn_gather_handle": (ctypes.c_int, [_VP]),
     "attn_gather_connect": (ctypes.c_int, [_VP]),

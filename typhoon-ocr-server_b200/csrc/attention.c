@@ -415,6 +415,53 @@ int attention_decode_append_gqa_gathered(const float *q, const float *k_new, con
     return decode_append_impl(q, k_new, v_new, cache, output, layer_idx, scale, kv_head0, kv_heads, g, what);
 }
 
+int attention_decode_append_fused_gqa(const float *q_raw, const float *k_raw, const float *v_new,
+                                      const float *q_norm, const float *k_norm, const float *token_cos,
+                                      const float *token_sin, KVCache *cache, float *output, int layer_idx,
+                                      float scale, float eps)
+{
+    const char *what = "attention_decode_append_fused_gqa";
+    tyb_cache *t = tyb_cache_from(cache);
+    if (!t || !check_layer(layer_idx, what)) return 1;
+    if (t->dtype != TYB_BF16) {
+        tyb_set_error("%s: the cache must hold BF16 rows (kv_cache_alloc_ex(.., ATTN_KV_BF16))", what);
+        return 1;
+    }
+    const int pos = cache->seq_len;
+    if (pos < 0 || pos >= cache->max_seq_len) {
+        tyb_set_error("%s: row %d exceeds max_seq_len %d", what, pos, cache->max_seq_len);
+        return 1;
+    }
+    const void *ptrs[8] = {q_raw, k_raw, v_new, q_norm, k_norm, token_cos, token_sin, output};
+    for (int i = 0; i < 8; i++) {
+        const int d = ptrs[i] ? tyb_is_device_ptr(ptrs[i]) : 0;
+        if (d < 0) return 1;
+        if (!d) {
+            tyb_set_error("%s: argument %d must be device memory", what, i);
+            return 1;
+        }
+    }
+    void *st = tyb_stream();
+    tyb_seq_kv one;
+    one.k = tyb_slab_head(t, t->k_slab, layer_idx, 0);
+    one.v = tyb_slab_head(t, t->v_slab, layer_idx, 0);
+    one.kv_len = pos + 1;
+    one.row_capacity = cache->max_seq_len;
+    const int early = tyb_prefetch_rows(cache, layer_idx, pos);
+    tyb_qk_prep prep;
+    prep.q_norm = q_norm;
+    prep.k_norm = k_norm;
+    prep.cos = token_cos;
+    prep.sin = token_sin;
+    prep.eps = eps;
+    if (!tyb_cuda_ok(tyb_decode_launch_fused(q_raw, output, one, pos + 1, scale, t->d_partials, t->d_counters, k_raw,
+                                             v_new, early, &prep, st),
+                     what))
+        return 1;
+    tyb_note_write(cache, layer_idx, pos, st);
+    return 0;
+}
+
 static int prefill_fused_impl(const void *q_raw, const void *k_raw, const void *v_raw, int in_dtype,
                               const float *q_norm, const float *k_norm, const float *token_cos, const float *token_sin,
                               KVCache *cache, int layer_idx, void *output, int out_dtype, int seq_len, float scale,

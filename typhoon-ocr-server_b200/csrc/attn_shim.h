@@ -65,6 +65,18 @@ int tyb_decode_launch_heads(const float *q, float *out, const tyb_seq_kv *seqs_d
                             int max_kv_len, int kv_dtype, float scale, float *partials, unsigned int *counters,
                             const float *k_new, const float *v_new, int prefetch_rows, int kvh0, int nkvh,
                             int flags, const void *gather, void *stream);
+/* QK-RMSNorm (q_norm / k_norm, eps) and rotate_half M-RoPE with one token's cos / sin [64],
+ * applied by the decode kernels on load: all device memory. */
+typedef struct {
+    const float *q_norm, *k_norm, *cos, *sin;
+    float eps;
+} tyb_qk_prep;
+/* tyb_decode_launch_ex for one sequence with a BF16 cache, all 8 KV heads, device q/k/v, the raw
+ * query q_raw [16][128] and raw key row k_raw [8][128] normed and rotated by `prep` on load (the
+ * cache receives the normed, rotated K row and v_new as given). */
+int tyb_decode_launch_fused(const float *q_raw, float *out, tyb_seq_kv one, int kv_len, float scale, float *partials,
+                            unsigned int *counters, const float *k_raw, const float *v_new, int prefetch_rows,
+                            const tyb_qk_prep *prep, void *stream);
 /* Decode output gather over NVLink (decode.cu): this rank's exchange buffer and peers'. */
 int tyb_gather_init(int rank, int world);
 int tyb_gather_handle(void *handle_out);            /* 64-byte cudaIpcMemHandle_t */

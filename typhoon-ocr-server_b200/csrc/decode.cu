@@ -601,6 +601,13 @@ struct DecodeMmaArgs {
     int kvh0;
     int prefetch_small;
     const GatherDev* gather;  // non-NULL: outputs go to the exchange buffer and to every rank
+    // Non-NULL q_norm: q and k_new arrive raw; RMSNorm(q_norm / k_norm, eps) and rotate_half
+    // M-RoPE with the token's rope_cos / rope_sin [64] are applied on load (one sequence only).
+    const float* q_norm;
+    const float* k_norm;
+    const float* rope_cos;
+    const float* rope_sin;
+    float eps;
 };
 
 __host__ __device__ constexpr size_t mma_pa_pitch(int chunk) { return (size_t)(chunk + 8) * 2; }
@@ -611,6 +618,51 @@ __host__ __device__ constexpr size_t decode_mma_smem_bytes(int chunk)
 {
     return 1024 + (size_t)chunk * 512 + 4 * mma_pa_pitch(chunk) + 4 * kQaPitch + kMmaStat * sizeof(float) +
            3 * sizeof(uint64_t) + 16;
+}
+
+// QK-RMSNorm + rotate_half M-RoPE of one 128-dim row (kernel/ops.c:22-62 and :297-343, as
+// kernel/decoder.c:73-93 applies them to q and k before the append and the attention):
+// y = x * rsqrt(mean(x^2) + eps) * w, then z[j] = y[j] c[j] - y[j+64] s[j] and
+// z[j+64] = y[j+64] c[j] + y[j] s[j] for j < 64.
+// qk_prep_row4: the row as 4 consecutive values per lane over a full warp (lane l: dims 4l..4l+3).
+__device__ __forceinline__ void qk_prep_row4(float (&x)[4], int lane, const float* w, const float* c,
+                                             const float* sn, float eps)
+{
+    float ss = x[0] * x[0] + x[1] * x[1] + x[2] * x[2] + x[3] * x[3];
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float rs = rsqrtf(ss * (1.f / kD) + eps);
+    float y[4], partner[4];
+#pragma unroll
+    for (int e = 0; e < 4; e++) y[e] = x[e] * rs * w[4 * lane + e];
+#pragma unroll
+    for (int e = 0; e < 4; e++) partner[e] = __shfl_xor_sync(0xffffffffu, y[e], 16);
+    const int j = (4 * lane) & 63;
+#pragma unroll
+    for (int e = 0; e < 4; e++)
+        x[e] = lane < 16 ? y[e] * c[j + e] - partner[e] * sn[j + e] : y[e] * c[j + e] + partner[e] * sn[j + e];
+}
+
+// qk_prep_row8: the row as 8 consecutive values per lane over lanes 0-15 of a warp (lane i: dims
+// 8i..8i+7); only those 16 lanes call it.
+__device__ __forceinline__ void qk_prep_row8(float (&x)[8], int i, const float* w, const float* c,
+                                             const float* sn, float eps)
+{
+    float ss = 0.f;
+#pragma unroll
+    for (int e = 0; e < 8; e++) ss += x[e] * x[e];
+#pragma unroll
+    for (int o = 8; o >= 1; o >>= 1) ss += __shfl_xor_sync(0x0000ffffu, ss, o);
+    const float rs = rsqrtf(ss * (1.f / kD) + eps);
+    float y[8], partner[8];
+#pragma unroll
+    for (int e = 0; e < 8; e++) y[e] = x[e] * rs * w[8 * i + e];
+#pragma unroll
+    for (int e = 0; e < 8; e++) partner[e] = __shfl_xor_sync(0x0000ffffu, y[e], 8);
+    const int j = (8 * i) & 63;
+#pragma unroll
+    for (int e = 0; e < 8; e++)
+        x[e] = i < 8 ? y[e] * c[j + e] - partner[e] * sn[j + e] : y[e] * c[j + e] + partner[e] * sn[j + e];
 }
 
 __device__ __forceinline__ void mma_16816_full(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1)
@@ -733,7 +785,8 @@ __device__ __forceinline__ void merge_records_direct(const float* recs, int nspl
     if (active) out[(size_t)h * kD + d] = O / alpha_s[2 + h];
 }
 
-template <int NW>
+// kQk: q and the new key row arrive raw and are normalised and rotated on load (DecodeMmaArgs).
+template <int NW, bool kQk = false>
 __global__ void __launch_bounds__(NW * 32, 16 / NW)
     decode_mma_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
                       const __grid_constant__ CUtensorMap tmk16, const __grid_constant__ CUtensorMap tmv16,
@@ -847,7 +900,12 @@ __global__ void __launch_bounds__(NW * 32, 16 / NW)
     // The query of both heads as A rows q0_hi, q0_lo, q1_hi, q1_lo (BF16).
     if (tid < 64) {
         const int h = tid >> 5, d0 = (tid & 31) * 4;
-        const float4 x = *reinterpret_cast<const float4*>(qb + (size_t)(kGroup * kvh + h) * kD + d0);
+        float4 x = *reinterpret_cast<const float4*>(qb + (size_t)(kGroup * kvh + h) * kD + d0);
+        if (kQk) {  // raw query: RMSNorm + M-RoPE here (warp = one head, lane = 4 dims)
+            float v4[4] = {x.x, x.y, x.z, x.w};
+            qk_prep_row4(v4, tid & 31, a.q_norm, a.rope_cos, a.rope_sin, a.eps);
+            x = make_float4(v4[0], v4[1], v4[2], v4[3]);
+        }
         uint32_t hi0, lo0, hi1, lo1;
         split_pair(x.x, x.y, hi0, lo0);
         split_pair(x.z, x.w, hi1, lo1);
@@ -864,6 +922,7 @@ __global__ void __launch_bounds__(NW * 32, 16 / NW)
         const size_t off = (size_t)kvh * kD + i * 8;
         load8(a.k_new + off, nk);
         load8(a.v_new + off, nv);
+        if (kQk) qk_prep_row8(nk, i, a.k_norm, a.rope_cos, a.rope_sin, a.eps);  // raw k: normed, rotated
         const size_t row = ((size_t)kvh * a.row_capacity + (kv_len - 1)) * kD + i * 8;
         store8(a.k + row, nk);
         store8(a.v + row, nv);
@@ -1096,6 +1155,7 @@ __host__ __device__ constexpr size_t decode_stream_smem_bytes()
     return 1024 + 4 * kStTile + 4 * kStPitch + 4 * kQaPitch + 32 * sizeof(float) + 5 * sizeof(uint64_t) + 16;
 }
 
+template <bool kQk = false>  // as in decode_mma_kernel
 __global__ void __launch_bounds__(256, 2)
     decode_stream_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
                          const DecodeMmaArgs a)
@@ -1200,7 +1260,12 @@ __global__ void __launch_bounds__(256, 2)
     // The query as B columns q0_hi, q0_lo, q1_hi, q1_lo; the appended row to the cache.
     if (tid < 64) {
         const int h = tid >> 5, d0 = (tid & 31) * 4;
-        const float4 x = *reinterpret_cast<const float4*>(qb + (size_t)(kGroup * kvh + h) * kD + d0);
+        float4 x = *reinterpret_cast<const float4*>(qb + (size_t)(kGroup * kvh + h) * kD + d0);
+        if (kQk) {  // raw query: RMSNorm + M-RoPE here (warp = one head, lane = 4 dims)
+            float v4[4] = {x.x, x.y, x.z, x.w};
+            qk_prep_row4(v4, tid & 31, a.q_norm, a.rope_cos, a.rope_sin, a.eps);
+            x = make_float4(v4[0], v4[1], v4[2], v4[3]);
+        }
         uint32_t hi0, lo0, hi1, lo1;
         split_pair(x.x, x.y, hi0, lo0);
         split_pair(x.z, x.w, hi1, lo1);
@@ -1215,6 +1280,7 @@ __global__ void __launch_bounds__(256, 2)
         const size_t off = (size_t)kvh * kD + i * 8;
         load8(a.k_new + off, nk);
         load8(a.v_new + off, nv);
+        if (kQk) qk_prep_row8(nk, i, a.k_norm, a.rope_cos, a.rope_sin, a.eps);  // raw k: normed, rotated
         const size_t row = ((size_t)kvh * a.row_capacity + (kv_len - 1)) * kD + i * 8;
         store8(a.k + row, nk);
         store8(a.v + row, nv);
@@ -1615,11 +1681,17 @@ static int set_mma_smem_attr()
 {
     static bool done = false;
     if (!done) {
-        cudaError_t e = cudaFuncSetAttribute(decode_mma_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)decode_mma_smem_bytes(kMmaMaxChunk));
+        const int mma_smem = (int)decode_mma_smem_bytes(kMmaMaxChunk), st_smem = (int)decode_stream_smem_bytes();
+        cudaError_t e = cudaFuncSetAttribute(decode_mma_kernel<8, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             mma_smem);
         if (e == cudaSuccess)
-            e = cudaFuncSetAttribute(decode_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)decode_stream_smem_bytes());
+            e = cudaFuncSetAttribute(decode_mma_kernel<8, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, mma_smem);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(decode_stream_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     st_smem);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(decode_stream_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     st_smem);
         if (e != cudaSuccess) return (int)e;
         done = true;
     }
@@ -1646,7 +1718,8 @@ static int launch_decode_mma(DecodeMmaArgs a, const tyb_seq_kv& one, int nkvh, v
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return (int)cudaLaunchKernelEx(&cfg, decode_mma_kernel<8>, mk, mv, mk16, mv16, a);
+    if (a.q_norm) return (int)cudaLaunchKernelEx(&cfg, decode_mma_kernel<8, true>, mk, mv, mk16, mv16, a);
+    return (int)cudaLaunchKernelEx(&cfg, decode_mma_kernel<8, false>, mk, mv, mk16, mv16, a);
 }
 
 static int launch_stream(const DecodeMmaArgs& a, const CUtensorMap& mk, const CUtensorMap& mv, int nkvh, int batch,
@@ -1662,7 +1735,8 @@ static int launch_stream(const DecodeMmaArgs& a, const CUtensorMap& mk, const CU
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return (int)cudaLaunchKernelEx(&cfg, decode_stream_kernel, mk, mv, a);
+    if (a.q_norm) return (int)cudaLaunchKernelEx(&cfg, decode_stream_kernel<true>, mk, mv, a);
+    return (int)cudaLaunchKernelEx(&cfg, decode_stream_kernel<false>, mk, mv, a);
 }
 
 }  // namespace tyb
@@ -1727,13 +1801,16 @@ extern "C" size_t tyb_decode_partial_floats(int batch, int nsplit)
     return (size_t)batch * kHkv * (size_t)nsplit * kRec;
 }
 
-extern "C" int tyb_decode_launch_heads(const float* q, float* out, const tyb_seq_kv* seqs_dev, tyb_seq_kv one,
-                                       int batch, int max_kv_len, int kv_dtype, float scale, float* partials,
-                                       unsigned int* counters, const float* k_new, const float* v_new,
-                                       int prefetch_rows, int kvh0, int nkvh, int flags, const void* gather,
-                                       void* stream)
+static int launch_heads_impl(const float* q, float* out, const tyb_seq_kv* seqs_dev, tyb_seq_kv one, int batch,
+                             int max_kv_len, int kv_dtype, float scale, float* partials, unsigned int* counters,
+                             const float* k_new, const float* v_new, int prefetch_rows, int kvh0, int nkvh,
+                             int flags, const void* gather, const tyb_qk_prep* prep, void* stream)
 {
     if (gather && (kv_dtype != TYB_BF16 || seqs_dev || batch != 1)) return (int)cudaErrorInvalidValue;
+    // QK-RMSNorm + M-RoPE on load: the tensor-core forms for one sequence (BF16 cache) only
+    if (prep && (kv_dtype != TYB_BF16 || seqs_dev || batch != 1 || !prep->q_norm || !prep->k_norm ||
+                 !prep->cos || !prep->sin))
+        return (int)cudaErrorInvalidValue;
     if (batch <= 0 || max_kv_len <= 0 || nkvh <= 0) return 0;
     DecodeArgs a;
     a.kvh0 = kvh0;
@@ -1761,7 +1838,7 @@ extern "C" int tyb_decode_launch_heads(const float* q, float* out, const tyb_seq
     a.partials = partials;
     a.counters = counters;
     if (bf16_one) {
-        DecodeMmaArgs m;
+        DecodeMmaArgs m = {};
         m.q = q;
         m.out = out;
         m.k = static_cast<__nv_bfloat16*>(const_cast<void*>(one.k));
@@ -1779,6 +1856,13 @@ extern "C" int tyb_decode_launch_heads(const float* q, float* out, const tyb_seq
         m.kvh0 = kvh0;
         m.prefetch_small = a.prefetch_small;
         m.gather = static_cast<const GatherDev*>(gather);
+        if (prep) {
+            m.q_norm = prep->q_norm;
+            m.k_norm = prep->k_norm;
+            m.rope_cos = prep->cos;
+            m.rope_sin = prep->sin;
+            m.eps = prep->eps;
+        }
         if (one_wave(1, max_kv_len, nkvh)) return launch_decode_mma(m, one, nkvh, stream);
         const int e = set_mma_smem_attr();
         if (e) return e;
@@ -1790,6 +1874,25 @@ extern "C" int tyb_decode_launch_heads(const float* q, float* out, const tyb_seq
     }
     if (kv_dtype == TYB_BF16) return launch_decode<__nv_bfloat16>(a, batch, nkvh, stream);
     return launch_decode<float>(a, batch, nkvh, stream);
+}
+
+extern "C" int tyb_decode_launch_heads(const float* q, float* out, const tyb_seq_kv* seqs_dev, tyb_seq_kv one,
+                                       int batch, int max_kv_len, int kv_dtype, float scale, float* partials,
+                                       unsigned int* counters, const float* k_new, const float* v_new,
+                                       int prefetch_rows, int kvh0, int nkvh, int flags, const void* gather,
+                                       void* stream)
+{
+    return launch_heads_impl(q, out, seqs_dev, one, batch, max_kv_len, kv_dtype, scale, partials, counters, k_new,
+                             v_new, prefetch_rows, kvh0, nkvh, flags, gather, nullptr, stream);
+}
+
+extern "C" int tyb_decode_launch_fused(const float* q_raw, float* out, tyb_seq_kv one, int kv_len, float scale,
+                                       float* partials, unsigned int* counters, const float* k_raw,
+                                       const float* v_new, int prefetch_rows, const tyb_qk_prep* prep, void* stream)
+{
+    if (!prep) return (int)cudaErrorInvalidValue;
+    return launch_heads_impl(q_raw, out, nullptr, one, 1, kv_len, TYB_BF16, scale, partials, counters, k_raw, v_new,
+                             prefetch_rows, 0, kHkv, TYB_DEC_DEVICE_SMALL, nullptr, prep, stream);
 }
 
 extern "C" int tyb_decode_launch_ex(const float* q, float* out, const tyb_seq_kv* seqs_dev, tyb_seq_kv one,
