@@ -13,6 +13,7 @@ All arrays are numpy fp32 / int32, C-contiguous.
 """
 
 import ctypes
+import os
 from pathlib import Path
 
 import numpy as np
@@ -20,6 +21,16 @@ import numpy as np
 HERE = Path(__file__).resolve().parent
 ORACLE_LIB = HERE / "liboracle.so"
 REF_LIB = HERE / "_ref" / "libref_attn.so"
+# The reference source tree, read only to compile oracle/_ref and by the boundary test that
+# compiles its decoder.c: the TYB_REFERENCE_DIR environment variable, else the mount point
+# used when this repository was built.  Nothing on a GPU box reads it.
+REFERENCE_DIR = Path(os.environ.get("TYB_REFERENCE_DIR", "/root/reference"))
+
+
+def reference_present():
+    """True when the reference tree (its kernel/ sources) is readable here."""
+    return (REFERENCE_DIR / "kernel" / "attention.c").exists()
+
 
 HQ, HKV, D = 16, 8, 128
 NUM_LAYERS = 28
@@ -31,7 +42,6 @@ _VP = ctypes.c_void_p
 
 def host_threads():
     """Cores this process may run on (its CPU affinity), at least 1."""
-    import os
     try:
         return max(1, len(os.sched_getaffinity(0)))
     except (AttributeError, OSError):
@@ -58,9 +68,10 @@ def _p(a):
 
 
 def build():
+    """liboracle.so, and oracle/_ref where the reference tree is present."""
     import subprocess
-    r = subprocess.run(["make", "-C", str(HERE), "all" if Path("/root/reference").exists() else "oracle"],
-                       capture_output=True, text=True)
+    target = "all" if reference_present() else "oracle"
+    r = subprocess.run(["make", "-C", str(HERE), target, f"REF={REFERENCE_DIR}"], capture_output=True, text=True)
     if r.returncode != 0:
         raise RuntimeError("oracle build failed:\n" + r.stdout[-3000:] + r.stderr[-3000:])
 

@@ -20,7 +20,9 @@ import pytest
 
 ROOT = Path(__file__).resolve().parents[1]
 INCLUDE = ROOT / "include"
-REF_KERNEL = Path("/root/reference/kernel")
+import oracle  # noqa: E402  (conftest puts oracle/ on sys.path)
+
+REF_KERNEL = oracle.REFERENCE_DIR / "kernel"
 CC = shutil.which("gcc", path="/usr/bin") or "gcc"
 
 

@@ -44,6 +44,11 @@ def test_noalloc_rejects_bad_arguments(pl, buf):
     assert "kv_len" in _err(pkg, lib)
     assert f(p, p + 4, p, 64, pkg.ATTN_KV_BF16, p, 8, sc, None) != 0
     assert "aligned" in _err(pkg, lib)
+    # the query and output are read and written with 16-byte vectors: refused on the host
+    assert f(p + 4, p, p, 64, pkg.ATTN_KV_BF16, p, 8, sc, None) != 0
+    assert "aligned" in _err(pkg, lib)
+    assert f(p, p, p, 64, pkg.ATTN_KV_BF16, p + 8, 8, sc, None) != 0
+    assert "aligned" in _err(pkg, lib)
 
 
 def test_heads_to_tokens_rejects_bad_arguments(pl, buf):

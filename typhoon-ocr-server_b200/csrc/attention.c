@@ -48,7 +48,7 @@ static const float *to_device(const float *p, float *stage, size_t bytes, int *i
     int d = tyb_is_device_ptr(p);
     if (d < 0) return NULL;
     *is_dev = d;
-    if (d) return p;
+    if (d) return tyb_aligned16(p, what) ? p : NULL;
     if (bytes && !tyb_cuda_ok(cudaMemcpyAsync(stage, p, bytes, cudaMemcpyHostToDevice, (cudaStream_t)st), what))
         return NULL;
     return stage;
@@ -65,7 +65,7 @@ static float *small_view(const float *p, float *stage, size_t bytes, int *kind, 
     const int k = tyb_residency(p, &view);
     *kind = k;
     if (k < 0) return NULL;
-    if (k != TYB_MEM_HOST) return (float *)view;
+    if (k != TYB_MEM_HOST) return tyb_aligned16(view, what) ? (float *)view : NULL;
     if (stage && !tyb_cuda_ok(cudaMemcpyAsync(stage, p, bytes, cudaMemcpyHostToDevice, (cudaStream_t)st), what))
         return NULL;
     return stage;
@@ -101,11 +101,7 @@ void attention_decode_gqa(const float *q, const KVCache *cache, float *output, i
             return;
         }
     } else {
-        tyb_seq_kv one;
-        one.k = tyb_slab_head(t, t->k_slab, layer_idx, 0);
-        one.v = tyb_slab_head(t, t->v_slab, layer_idx, 0);
-        one.kv_len = kv_len;
-        one.row_capacity = cache->max_seq_len;
+        const tyb_seq_kv one = tyb_layer_rows(t, layer_idx, kv_len);
         const int early = tyb_prefetch_rows(cache, layer_idx, kv_len);
         if (!tyb_cuda_ok(decode_launch(dq, dout, NULL, one, 1, kv_len, t->dtype, scale, early, t->d_partials,
                                        t->d_counters, qk != TYB_MEM_PINNED ? TYB_DEC_DEVICE_SMALL : 0, st),
@@ -241,6 +237,7 @@ int attention_decode_gqa_batched(const float *q, const KVCache *const *caches, c
         descs[b].v = tyb_slab_head(t, t->v_slab, layer_idx, 0);
         descs[b].kv_len = kv_lens[b];
         descs[b].row_capacity = t->pub.max_seq_len;
+        descs[b].pf_k = descs[b].pf_v = NULL;
         if (kv_lens[b] > max_kv) max_kv = kv_lens[b];
     }
     if (!ok) {
@@ -325,11 +322,7 @@ static int decode_append_impl(const float *q, const float *k_new, const float *v
     const size_t out_floats = (size_t)2 * (gather ? KV_NUM_KV_HEADS : nkvh) * KV_HEAD_DIM;
     if (ok < 0 || (ok != TYB_MEM_HOST && !dout)) return 1;
     if (ok == TYB_MEM_HOST) dout = t->d_out;
-    tyb_seq_kv one;
-    one.k = tyb_slab_head(t, t->k_slab, layer_idx, 0);
-    one.v = tyb_slab_head(t, t->v_slab, layer_idx, 0);
-    one.kv_len = pos + 1;
-    one.row_capacity = cache->max_seq_len;
+    const tyb_seq_kv one = tyb_layer_rows(t, layer_idx, pos + 1);
     const int early = tyb_prefetch_rows(cache, layer_idx, pos);
     if (!tyb_cuda_ok(tyb_decode_launch_heads(dq, dout, NULL, one, 1, pos + 1, t->dtype, scale, t->d_partials,
                                              t->d_counters, dk, dv, early, kvh0, nkvh,
@@ -440,13 +433,10 @@ int attention_decode_append_fused_gqa(const float *q_raw, const float *k_raw, co
             tyb_set_error("%s: argument %d must be device memory", what, i);
             return 1;
         }
+        if (!tyb_aligned16(ptrs[i], what)) return 1;
     }
     void *st = tyb_stream();
-    tyb_seq_kv one;
-    one.k = tyb_slab_head(t, t->k_slab, layer_idx, 0);
-    one.v = tyb_slab_head(t, t->v_slab, layer_idx, 0);
-    one.kv_len = pos + 1;
-    one.row_capacity = cache->max_seq_len;
+    const tyb_seq_kv one = tyb_layer_rows(t, layer_idx, pos + 1);
     const int early = tyb_prefetch_rows(cache, layer_idx, pos);
     tyb_qk_prep prep;
     prep.q_norm = q_norm;
@@ -491,6 +481,7 @@ static int prefill_fused_impl(const void *q_raw, const void *k_raw, const void *
             tyb_set_error("%s: argument %d must be device memory", what, i);
             return 1;
         }
+        if (!tyb_aligned16(ptrs[i], what)) return 1;
     }
     void *st = tyb_stream();
     void *kl = tyb_slab_head(t, t->k_slab, layer_idx, 0), *vl = tyb_slab_head(t, t->v_slab, layer_idx, 0);
@@ -547,6 +538,7 @@ int attn_heads_to_tokens(const void *gathered, void *output, int seq_len, int dt
         tyb_set_error("%s: gathered and output must be device memory", what);
         return 1;
     }
+    if (!tyb_aligned16(gathered, what) || !tyb_aligned16(output, what)) return 1;
     return tyb_cuda_ok(tyb_heads_to_tokens_launch(gathered, output, seq_len, dtype == ATTN_DT_BF16 ? 2 : 4, tyb_stream()),
                        what)
                ? 0

@@ -31,6 +31,11 @@ typedef struct {
     const void *v;
     int kv_len;       /* rows attended: [0, kv_len) */
     int row_capacity; /* rows allocated per head (the cache's max_seq_len) */
+    /* Single-sequence launches only (NULL otherwise): the same-shaped rows of the layer the
+     * next call will read.  Each split asks L2 for its own row range there once its tiles are
+     * requested, so the next layer's launch finds its rows in L2 (a hint: no data dependence). */
+    const void *pf_k;
+    const void *pf_v;
 } tyb_seq_kv;
 
 /* ---- split-KV flash decoding (decode.cu) ------------------------------------------ */

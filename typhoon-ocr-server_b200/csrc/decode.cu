@@ -278,13 +278,28 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_split_kernel(const Deco
         }
         if (line) asm volatile("prefetch.global.L2 [%0];" ::"l"(line));
     }
-    if (tid == 0 && early) issue();
+    // The next call's rows (tyb_seq_kv.pf_k): asked of L2 right after this split's own copies.
+    auto prefetch_next = [&]() {
+        if (a.one.pf_k && tma_rows > 0) {
+            const size_t off = ((size_t)kvh * a.one.row_capacity + r0) * kD;
+            const uint32_t bytes = (uint32_t)tma_rows * kD * sizeof(T);
+            bulk_prefetch_l2(static_cast<const T*>(a.one.pf_k) + off, bytes);
+            bulk_prefetch_l2(static_cast<const T*>(a.one.pf_v) + off, bytes);
+        }
+    };
+    if (tid == 0 && early) {
+        issue();
+        prefetch_next();
+    }
     // Everything below reads data earlier kernels wrote (descriptors, cache rows, q).
     pdl_wait();
     pdl_trigger();
     if (a.seqs) geometry(a.seqs[b]);
     if (s >= nsplit) return;
-    if (tid == 0 && !early) issue();
+    if (tid == 0 && !early) {
+        issue();
+        if (!a.seqs) prefetch_next();
+    }
 
     // Query vectors of the two heads sharing this KV head, for the scores: 8 lanes per row,
     // lane part p holds the 16 dims of load_lane16.
@@ -608,6 +623,9 @@ struct DecodeMmaArgs {
     const float* rope_cos;
     const float* rope_sin;
     float eps;
+    // One sequence: the next call's rows (tyb_seq_kv.pf_k / pf_v), or NULL.
+    const __nv_bfloat16* pf_k;
+    const __nv_bfloat16* pf_v;
 };
 
 __host__ __device__ constexpr size_t mma_pa_pitch(int chunk) { return (size_t)(chunk + 8) * 2; }
@@ -867,7 +885,20 @@ __global__ void __launch_bounds__(NW * 32, 16 / NW)
         tma_box_3d(vt_u32, mv, 0, r0, kvh, &bars[1]);
         tma_box_3d(vt_u32 + half, mv, 64, r0, kvh, &bars[1]);
     };
-    if (tid == 0 && early) issue();
+    // The rows of this split in the layer the next call reads (pf_k / pf_v): asked of L2 right
+    // after this split's own copies, so that launch's copies hit L2 (at 4K one layer's K/V is
+    // 16.8 MB: this layer's and the next one's fit in L2 together).
+    auto prefetch_next = [&]() {
+        if (a.pf_k && trows > 0) {
+            const size_t off = ((size_t)kvh * a.row_capacity + r0) * kD;
+            bulk_prefetch_l2(a.pf_k + off, (uint32_t)trows * kD * 2);
+            bulk_prefetch_l2(a.pf_v + off, (uint32_t)trows * kD * 2);
+        }
+    };
+    if (tid == 0 && early) {
+        issue();
+        prefetch_next();
+    }
     const bool has_new = !a.seqs && a.k_new && kv_len - 1 >= r0 && kv_len - 1 < r0 + nrows;
     // q and the appended row may be written by the previous kernel: read after the wait, but
     // their L2 lines requested now (plain prefetches, one 128-byte line per lane).
@@ -895,7 +926,10 @@ __global__ void __launch_bounds__(NW * 32, 16 / NW)
             asm volatile("fence.proxy.tensormap::generic.acquire.gpu [%0], 128;" ::"l"(mv) : "memory");
         }
     }
-    if (tid == 0 && !early) issue();
+    if (tid == 0 && !early) {
+        issue();
+        if (!a.seqs) prefetch_next();
+    }
 
     // The query of both heads as A rows q0_hi, q0_lo, q1_hi, q1_lo (BF16).
     if (tid < 64) {
@@ -1856,6 +1890,8 @@ static int launch_heads_impl(const float* q, float* out, const tyb_seq_kv* seqs_
         m.kvh0 = kvh0;
         m.prefetch_small = a.prefetch_small;
         m.gather = static_cast<const GatherDev*>(gather);
+        m.pf_k = static_cast<const __nv_bfloat16*>(one.pf_k);
+        m.pf_v = static_cast<const __nv_bfloat16*>(one.pf_v);
         if (prep) {
             m.q_norm = prep->q_norm;
             m.k_norm = prep->k_norm;
@@ -1870,6 +1906,7 @@ static int launch_heads_impl(const float* q, float* out, const tyb_seq_kv* seqs_
         if (!slab_maps(one, kStRows, &mk, &mv)) return (int)cudaErrorInvalidValue;
         m.seqs = nullptr;
         m.maps = nullptr;
+        m.pf_k = m.pf_v = nullptr;  // a long sequence's layer does not fit in L2 beside the next
         return launch_stream(m, mk, mv, nkvh, 1, stream);
     }
     if (kv_dtype == TYB_BF16) return launch_decode<__nv_bfloat16>(a, batch, nkvh, stream);
@@ -1967,6 +2004,11 @@ extern "C" int attention_decode_gqa_noalloc(const float* q, const void* k_rows, 
         tyb_set_error("%s: k_rows and v_rows must be 16-byte aligned", what);
         return 1;
     }
+    // The kernels read the query and write the output with 16-byte vector accesses.
+    if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(output)) & 15u) {
+        tyb_set_error("%s: q and output must be 16-byte aligned", what);
+        return 1;
+    }
     if (!is_device_memory(q) || !is_device_memory(k_rows) || !is_device_memory(v_rows) ||
         !is_device_memory(output)) {
         tyb_set_error("%s: q, k_rows, v_rows and output must be device memory", what);
@@ -2017,6 +2059,7 @@ extern "C" int attention_decode_gqa_noalloc(const float* q, const void* k_rows, 
     one.v = v_rows;
     one.kv_len = kv_len;
     one.row_capacity = row_capacity;
+    one.pf_k = one.pf_v = nullptr;
     const int rc = tyb_decode_launch(q, output, nullptr, one, 1, kv_len, kv_dtype, scale, records, tickets, stream);
     if (rc != 0) {
         tyb_set_error("%s: launch: %s", what, cudaGetErrorString((cudaError_t)rc));

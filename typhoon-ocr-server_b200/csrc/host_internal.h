@@ -47,8 +47,35 @@ static inline void *tyb_slab_head(const tyb_cache *c, void *slab, int layer, int
     return (char *)slab + (((size_t)layer * KV_NUM_KV_HEADS + head) * rows) * KV_HEAD_DIM * c->elem_bytes;
 }
 
+/* K/V rows of (cache, layer) for a single-sequence decode launch attending kv_len rows.  pf_k /
+ * pf_v point at the rows the next decode call of kernel/decoder.c's layer loop reads: layer + 1,
+ * and layer 0 (the next step) after the last layer.  Rows below seq_len there are final before
+ * the step starts, so the launch asks L2 for them while it runs. */
+static inline tyb_seq_kv tyb_layer_rows(const tyb_cache *c, int layer, int kv_len)
+{
+    const int next = layer + 1 < KV_NUM_LAYERS ? layer + 1 : 0;
+    tyb_seq_kv s;
+    s.k = tyb_slab_head(c, c->k_slab, layer, 0);
+    s.v = tyb_slab_head(c, c->v_slab, layer, 0);
+    s.kv_len = kv_len;
+    s.row_capacity = c->pub.max_seq_len;
+    s.pf_k = tyb_slab_head(c, c->k_slab, next, 0);
+    s.pf_v = tyb_slab_head(c, c->v_slab, next, 0);
+    return s;
+}
+
 /* Errors: thread-local message, "" when none. */
 void tyb_set_error(const char *fmt, ...);
+
+/* 1 when p is 16-byte aligned (the kernels read and write rows with 16-byte vector accesses);
+ * otherwise 0 with the error set, so a misaligned buffer is refused before any launch. */
+static inline int tyb_aligned16(const void *p, const char *what)
+{
+    if (((uintptr_t)p & 15u) == 0) return 1;
+    tyb_set_error("%s: buffer %p is not 16-byte aligned", what, p);
+    return 0;
+}
+
 /* 1 when err == 0 (cudaSuccess); otherwise records "<what>: <cuda error string>", returns 0. */
 int tyb_cuda_ok(int err, const char *what);
 
