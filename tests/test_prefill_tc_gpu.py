@@ -137,6 +137,35 @@ def test_fused_prefill_config3(pkg, lib, oracle):
     assert max_abs(out, fp32) <= TOL_TC32_MAX and rel_l2(out, fp32) <= TOL_TC32_REL
 
 
+def test_fused_prefill_config5_sampled_rows(pkg, lib, oracle):
+    """BASELINE config 5's prefill: 32,768 tokens = 30,000 vision tokens on a 150x200 grid + 2,768
+    text tokens.  The whole page runs on the GPU; the oracle checks a sample of query rows -- the
+    first and last rows, both sides of every 128-row tile edge in four regions, and random rows --
+    each as causal attention over the cache rows [0, row] (the causal prefill row of
+    kernel/attention.c:252-362 is that decode, :158-192, over the rows it sees), on the BF16 rows
+    the kernel wrote to the cache and the BF16-rounded normalised, rotated query."""
+    S = 32768
+    q, k, v, qn, kn, pos = _inputs(pkg, S, 5, grid=(150, 200, 2768))
+    cos, sin = oracle.mrope_cos_sin_3d(pos)
+    h = new_cache(pkg, lib, S, pkg.ATTN_KV_BF16)
+    try:
+        out = _fused(pkg, lib, h, 13, q, k, v, qn, kn, cos, sin, False, False)
+        as_f32 = lambda u: (u.astype(np.uint32) << 16).view(np.float32)  # noqa: E731
+        kc = as_f32(d2h(lib.kv_cache_k(h, 13, 0), (8, S, 128), np.uint16))
+        vc = as_f32(d2h(lib.kv_cache_v(h, 13, 0), (8, S, 128), np.uint16))
+    finally:
+        lib.kv_cache_free(h)
+    qr, _ = oracle.qk_norm_rope(q, k, qn, kn, cos, sin)
+    qr = bf16_round(qr)
+    rng = np.random.default_rng(55)
+    edges = [b + d for b in (128, 4096, 16384, 29952) for d in (-1, 0)]
+    rows = sorted(set([0, 1, S - 1, 29999, 30000] + edges + list(rng.integers(0, S, 40))))
+    got = np.stack([out[i] for i in rows])
+    want = np.stack([oracle.decode(np.ascontiguousarray(qr[i]), kc, vc, i + 1) for i in rows])
+    print(f"config5 sampled rows ({len(rows)}): max {max_abs(got, want):.3e} rel {rel_l2(got, want):.3e}")
+    assert max_abs(got, want) <= TOL_TC_MAX and rel_l2(got, want) <= TOL_TC_REL
+
+
 def test_fused_prefill_rejects_bad_arguments(pkg, lib):
     h = new_cache(pkg, lib, 8, pkg.ATTN_KV_F32)
     x = torch.zeros((4, 16, 128), device="cuda")

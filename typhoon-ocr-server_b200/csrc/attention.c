@@ -3,8 +3,9 @@
  * as host C that stages memory and launches the sm_100a kernels.
  *
  *   attention_decode_gqa          kernel/attention.c:194-204  -> decode.cu
- *   attention_prefill_gqa         kernel/attention.c:364-381  -> prefill_simt.cu (FP32)
- *   attention_chunked_prefill_gqa kernel/attention.c:527-543  -> prefill_simt.cu, K/V
+ *   attention_prefill_gqa         kernel/attention.c:364-381  -> prefill_tc32.cu (tensor cores,
+ *                                                                 FP32-accurate hi/lo splits)
+ *   attention_chunked_prefill_gqa kernel/attention.c:527-543  -> prefill_tc32.cu, K/V
  *                                                                 from the device cache
  *   attention_decode_gqa_batched  (new)                       -> decode.cu, many caches
  *   attention_decode_append_gqa   (new) kernel/kv_cache.c:53-65 + attention.c:194-204
@@ -128,33 +129,58 @@ void attention_prefill_gqa(const float *q, const float *k, const float *v, float
         return;
     }
     if (Sq == 0) return;
-    if (!q || !k || !v || !output) {
-        tyb_set_error("%s: NULL q/k/v/output", what);
+    if (!q || !output) {
+        tyb_set_error("%s: NULL q/output", what);
+        return;
+    }
+    /* Keys visible to any query are rows < min(Sk, Sq) (mask k_pos > q_pos, :293). */
+    const int kv_rows = Sk < Sq ? Sk : Sq;
+    if (kv_rows > 0 && (!k || !v)) {
+        tyb_set_error("%s: NULL k/v", what);
         return;
     }
     void *st = tyb_stream();
-    /* Keys visible to any query are rows < min(Sk, Sq) (mask k_pos > q_pos, :293). */
-    const int kv_rows = Sk < Sq ? Sk : Sq;
     const size_t qb = (size_t)Sq * TYB_Q_FLOATS * sizeof(float);
-    const size_t kb = (size_t)kv_rows * TYB_ROW_FLOATS * sizeof(float);
+    const size_t kb = (size_t)kv_rows * TYB_ROW_FLOATS * sizeof(float); /* = bytes of its hi|lo BF16 pair */
 
-    int qd = tyb_is_device_ptr(q), kd = tyb_is_device_ptr(k), vd = tyb_is_device_ptr(v),
-        od = tyb_is_device_ptr(output);
+    int qd = tyb_is_device_ptr(q), od = tyb_is_device_ptr(output);
+    int kd = kv_rows ? tyb_is_device_ptr(k) : 1, vd = kv_rows ? tyb_is_device_ptr(v) : 1;
     if (qd < 0 || kd < 0 || vd < 0 || od < 0) return;
-    /* Staging: the scratch's device slots when large enough, else the workspace. */
-    float *sq = NULL, *sk = NULL, *sv = NULL, *so = NULL;
+    if (kv_rows == 0) {
+        /* No key at all: every row's sum is 0 and the reference writes zeros (:347-361). */
+        if (!od) {
+            memset(output, 0, qb);
+            return;
+        }
+        tyb_cuda_ok(cudaMemsetAsync(output, 0, qb, (cudaStream_t)st), what);
+        return;
+    }
+    /* The scratch's device slots (kernel/scratch.h q_hm..o_hm, sized by max_seq_len) hold all
+     * the staging when the caller passes them, as kernel/decoder.c:113-117 does: q_hm the queries
+     * of a host q; k_hm / v_hm the BF16 hi|lo pairs of K / V; o_hm the FP32 rows of a host K and V
+     * on their way to the split, then the output of a host `output` (the split has consumed the
+     * rows by then: the attention kernel waits for it).  Otherwise the library's workspace. */
+    const size_t kv_stage = (kd ? 0 : kb) + (vd ? 0 : kb);
+    const size_t o_stage = (!od && qb > kv_stage) ? qb : kv_stage;
+    float *sq = NULL, *so = NULL;
     if (!qd) sq = (q_hm && tyb_registry_size(q_hm) >= qb) ? q_hm : (float *)tyb_workspace(TYB_WS_Q, qb);
-    if (!kd) sk = (k_hm && tyb_registry_size(k_hm) >= kb) ? k_hm : (float *)tyb_workspace(TYB_WS_K, kb);
-    if (!vd) sv = (v_hm && tyb_registry_size(v_hm) >= kb) ? v_hm : (float *)tyb_workspace(TYB_WS_V, kb);
-    if (!od) so = (o_hm && tyb_registry_size(o_hm) >= qb) ? o_hm : (float *)tyb_workspace(TYB_WS_OUT, qb);
-    if ((!qd && !sq) || (!kd && !sk) || (!vd && !sv) || (!od && !so)) return;
+    unsigned char *ksp = (k_hm && tyb_registry_size(k_hm) >= kb) ? (unsigned char *)k_hm
+                                                               : (unsigned char *)tyb_workspace(TYB_WS_K, kb);
+    unsigned char *vsp = (v_hm && tyb_registry_size(v_hm) >= kb) ? (unsigned char *)v_hm
+                                                               : (unsigned char *)tyb_workspace(TYB_WS_V, kb);
+    if (o_stage) so = (o_hm && tyb_registry_size(o_hm) >= o_stage) ? o_hm : (float *)tyb_workspace(TYB_WS_OUT, o_stage);
+    if ((!qd && !sq) || !ksp || !vsp || (o_stage && !so)) return;
 
     const float *dq = to_device(q, sq, qb, &qd, st, what);
-    const float *dk = kv_rows ? to_device(k, sk, kb, &kd, st, what) : k;
-    const float *dv = kv_rows ? to_device(v, sv, kb, &vd, st, what) : v;
+    const float *dk = to_device(k, so, kb, &kd, st, what);
+    const float *dv = dk ? to_device(v, so + (kd ? 0 : kb / sizeof(float)), kb, &vd, st, what) : NULL;
     if (!dq || !dk || !dv) return;
     float *dout = od ? output : so;
-    if (!tyb_cuda_ok(tyb_prefill_simt_launch(dq, dout, dk, dv, TYB_ROW_FLOATS, KV_HEAD_DIM, TYB_F32, Sq, Sk, 0,
+    /* Token-major rows: row stride 8 x 128, head stride 128 (:27-30). */
+    if (!tyb_cuda_ok(tyb_kv_split_launch(dk, dv, TYB_ROW_FLOATS, KV_HEAD_DIM, kv_rows, ksp, ksp + kb / 2, vsp,
+                                         vsp + kb / 2, st),
+                     what) ||
+        !tyb_cuda_ok(tyb_prefill_tc32_launch(dq, dout, Sq, 0, kv_rows, ksp, ksp + kb / 2, vsp, vsp + kb / 2, kv_rows,
                                              scale, st),
                      what))
         return;
@@ -192,12 +218,26 @@ void attention_chunked_prefill_gqa(const float *q, const KVCache *cache, float *
     float *dout = od ? output : so;
     const void *kl = tyb_slab_head(t, t->k_slab, layer_idx, 0);
     const void *vl = tyb_slab_head(t, t->v_slab, layer_idx, 0);
-    /* Head-first cache rows: row stride 128, head stride max_seq*128 (:425-427, :461). */
-    if (!tyb_cuda_ok(tyb_prefill_simt_launch(dq, dout, kl, vl, KV_HEAD_DIM,
-                                             (long long)cache->max_seq_len * KV_HEAD_DIM, t->dtype, chunk_len,
-                                             pos_offset + chunk_len, pos_offset, scale, st),
-                     what))
-        return;
+    const int total = pos_offset + chunk_len; /* keys of query i: rows <= pos_offset + i (:443-459) */
+    int rc;
+    if (t->dtype == TYB_BF16) {
+        /* BF16 rows are exact as BF16 operands (lo = 0): the tiles come straight from the cache. */
+        rc = tyb_prefill_tc32_launch(dq, dout, chunk_len, pos_offset, total, kl, NULL, vl, NULL, cache->max_seq_len,
+                                     scale, st);
+    } else {
+        /* FP32 rows: split rows [0, total) of the layer (head-first: row stride 128, head stride
+         * max_seq x 128, :425-427) into hi|lo pairs in the cache's staging area, which holds
+         * 8 KB per row of max_seq_len (K hi, K lo, V hi, V lo at 2 KB per row each). */
+        unsigned char *sp = (unsigned char *)t->d_kv_stage;
+        const size_t part = (size_t)total * TYB_ROW_FLOATS * 2;
+        rc = tyb_kv_split_launch((const float *)kl, (const float *)vl, KV_HEAD_DIM,
+                                 (long long)cache->max_seq_len * KV_HEAD_DIM, total, sp, sp + part, sp + 2 * part,
+                                 sp + 3 * part, st);
+        if (rc == 0)
+            rc = tyb_prefill_tc32_launch(dq, dout, chunk_len, pos_offset, total, sp, sp + part, sp + 2 * part,
+                                         sp + 3 * part, total, scale, st);
+    }
+    if (!tyb_cuda_ok(rc, what)) return;
     tyb_note_nowrite(st);
     if (!od && !tyb_cuda_ok(cudaMemcpyAsync(output, dout, qb, cudaMemcpyDeviceToHost, (cudaStream_t)st), what))
         return;

@@ -32,8 +32,9 @@ typedef struct {
     int kv_len;       /* rows attended: [0, kv_len) */
     int row_capacity; /* rows allocated per head (the cache's max_seq_len) */
     /* Single-sequence launches only (NULL otherwise): the same-shaped rows of the layer the
-     * next call will read.  Each split asks L2 for its own row range there once its tiles are
-     * requested, so the next layer's launch finds its rows in L2 (a hint: no data dependence). */
+     * next call will read.  The FP32-cache kernel asks L2 for its split's row range there once
+     * its tiles are requested, so the next layer's launch finds its rows in L2 (a hint: no data
+     * dependence). */
     const void *pf_k;
     const void *pf_v;
 } tyb_seq_kv;
@@ -109,15 +110,6 @@ int tyb_decode_launch_batched(const float *q, float *out, const tyb_seq_kv *seqs
  * (elem_bytes 2 or 4). */
 int tyb_heads_to_tokens_launch(const void *src, void *dst, int S, int elem_bytes, void *stream);
 
-/* ---- FP32 flash prefill on CUDA cores (prefill_simt.cu) --------------------------- */
-
-/* q/out token-major [Sq][16][128] fp32.  K/V element (row r, kv head h, dim d) at
- * base + r*row_stride + h*head_stride + d (elements of kv_dtype).  Query i sits at
- * absolute position pos_offset + i and sees keys r <= pos_offset + i, r < Sk. */
-int tyb_prefill_simt_launch(const float *q, float *out, const void *k, const void *v,
-                            long long row_stride, long long head_stride, int kv_dtype, int Sq,
-                            int Sk, int pos_offset, float scale, void *stream);
-
 /* ---- tensor-core prefill (prefill_tc.cu) ---------------------------------------------- */
 
 /* Raw K/V rows [S][8][128] (fp32, or bf16 when in_bf16) -> BF16 cache rows [pos0, pos0+S) of
@@ -138,6 +130,24 @@ int tyb_prefill_tc_launch(const void *q, int q_bf16, const float *q_norm, const 
                           const void *k_cache, const void *v_cache, int row_capacity, void *out, int out_bf16,
                           int Sq, int pos_offset, float scale, float eps, int kvh0, int nkvh, int out_head_major,
                           void *stream);
+
+/* ---- tensor-core prefill at the FP32 bar (prefill_tc32.cu) ----------------------------- */
+
+/* FP32 K and V rows [0, n) of the 8 KV heads, element (row r, head h, dim d) at
+ * base + r*row_stride + h*head_stride + d, split into head-first [8][n][128] BF16 pairs:
+ * hi = bf16(x), lo = bf16(x - hi). */
+int tyb_kv_split_launch(const float *k, const float *v, long long row_stride, long long head_stride, int n,
+                        void *k_hi, void *k_lo, void *v_hi, void *v_lo, void *stream);
+
+/* Causal attention of Sq queries q [Sq][16][128] fp32 (already normalised and rotated) into
+ * out [Sq][16][128] fp32: query i sees keys k <= pos_offset + i with k < total_kv (>= 1).  K and
+ * V as head-first [8][head_rows][128] BF16: hi / lo pairs from tyb_kv_split_launch (FP32-accurate
+ * products, three BF16 MMAs each), or the rows of a BF16 cache with k_lo = v_lo = NULL.
+ * Launched as a programmatic dependent of the previous kernel in the stream (it waits for that
+ * kernel before reading anything). */
+int tyb_prefill_tc32_launch(const float *q, float *out, int Sq, int pos_offset, int total_kv, const void *k_hi,
+                            const void *k_lo, const void *v_hi, const void *v_lo, int head_rows, float scale,
+                            void *stream);
 
 /* ---- KV-cache row writes (kv_write.cu) -------------------------------------------- */
 

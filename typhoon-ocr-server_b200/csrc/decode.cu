@@ -278,7 +278,11 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_split_kernel(const Deco
         }
         if (line) asm volatile("prefetch.global.L2 [%0];" ::"l"(line));
     }
-    // The next call's rows (tyb_seq_kv.pf_k): asked of L2 right after this split's own copies.
+    // The next call's rows (tyb_seq_kv.pf_k): asked of L2 right after this split's own copies, so
+    // that the next layer's copies hit L2 (at 4K one FP32 layer's K/V is 33.6 MB: it fits in L2
+    // beside this one).  Measured at 4K, 28 layers: 362 against 386 us per step.  (The BF16
+    // tensor-core form gains nothing from it: its tiles land within ~0.6 us of the dependency
+    // release, and the prefetch, issued with the tiles or after the split's work, cost 4-9 %.)
     auto prefetch_next = [&]() {
         if (a.one.pf_k && tma_rows > 0) {
             const size_t off = ((size_t)kvh * a.one.row_capacity + r0) * kD;
@@ -623,9 +627,6 @@ struct DecodeMmaArgs {
     const float* rope_cos;
     const float* rope_sin;
     float eps;
-    // One sequence: the next call's rows (tyb_seq_kv.pf_k / pf_v), or NULL.
-    const __nv_bfloat16* pf_k;
-    const __nv_bfloat16* pf_v;
 };
 
 __host__ __device__ constexpr size_t mma_pa_pitch(int chunk) { return (size_t)(chunk + 8) * 2; }
@@ -885,20 +886,7 @@ __global__ void __launch_bounds__(NW * 32, 16 / NW)
         tma_box_3d(vt_u32, mv, 0, r0, kvh, &bars[1]);
         tma_box_3d(vt_u32 + half, mv, 64, r0, kvh, &bars[1]);
     };
-    // The rows of this split in the layer the next call reads (pf_k / pf_v): asked of L2 right
-    // after this split's own copies, so that launch's copies hit L2 (at 4K one layer's K/V is
-    // 16.8 MB: this layer's and the next one's fit in L2 together).
-    auto prefetch_next = [&]() {
-        if (a.pf_k && trows > 0) {
-            const size_t off = ((size_t)kvh * a.row_capacity + r0) * kD;
-            bulk_prefetch_l2(a.pf_k + off, (uint32_t)trows * kD * 2);
-            bulk_prefetch_l2(a.pf_v + off, (uint32_t)trows * kD * 2);
-        }
-    };
-    if (tid == 0 && early) {
-        issue();
-        prefetch_next();
-    }
+    if (tid == 0 && early) issue();
     const bool has_new = !a.seqs && a.k_new && kv_len - 1 >= r0 && kv_len - 1 < r0 + nrows;
     // q and the appended row may be written by the previous kernel: read after the wait, but
     // their L2 lines requested now (plain prefetches, one 128-byte line per lane).
@@ -926,10 +914,7 @@ __global__ void __launch_bounds__(NW * 32, 16 / NW)
             asm volatile("fence.proxy.tensormap::generic.acquire.gpu [%0], 128;" ::"l"(mv) : "memory");
         }
     }
-    if (tid == 0 && !early) {
-        issue();
-        if (!a.seqs) prefetch_next();
-    }
+    if (tid == 0 && !early) issue();
 
     // The query of both heads as A rows q0_hi, q0_lo, q1_hi, q1_lo (BF16).
     if (tid < 64) {
@@ -1890,8 +1875,6 @@ static int launch_heads_impl(const float* q, float* out, const tyb_seq_kv* seqs_
         m.kvh0 = kvh0;
         m.prefetch_small = a.prefetch_small;
         m.gather = static_cast<const GatherDev*>(gather);
-        m.pf_k = static_cast<const __nv_bfloat16*>(one.pf_k);
-        m.pf_v = static_cast<const __nv_bfloat16*>(one.pf_v);
         if (prep) {
             m.q_norm = prep->q_norm;
             m.k_norm = prep->k_norm;
@@ -1906,7 +1889,6 @@ static int launch_heads_impl(const float* q, float* out, const tyb_seq_kv* seqs_
         if (!slab_maps(one, kStRows, &mk, &mv)) return (int)cudaErrorInvalidValue;
         m.seqs = nullptr;
         m.maps = nullptr;
-        m.pf_k = m.pf_v = nullptr;  // a long sequence's layer does not fit in L2 beside the next
         return launch_stream(m, mk, mv, nkvh, 1, stream);
     }
     if (kv_dtype == TYB_BF16) return launch_decode<__nv_bfloat16>(a, batch, nkvh, stream);
