@@ -144,7 +144,13 @@ class ClockSampler:
 # ---------------------------------------------------------------------------------------
 
 class DecodeBench:
-    def __init__(self, pkg, lib, kv_dtype, device, fused=True):
+    """Config 2's decode step replayed from per-step CUDA graphs of 28 calls, device buffers.
+    mode: "append"   attention_decode_append_gqa (append + attention, as decoder.c:97,104 pairs them)
+          "attn"     attention_decode_gqa (rows already in the cache)
+          "fused_qk" attention_decode_append_fused_gqa (raw q/k: QK-RMSNorm + M-RoPE on the GPU too,
+                     the whole of decoder.c:73-105 per layer)"""
+
+    def __init__(self, pkg, lib, kv_dtype, device, mode="append"):
         import torch
         self.torch = torch
         self.pkg, self.lib = pkg, lib
@@ -167,12 +173,18 @@ class DecodeBench:
             pkg.check(lib, "fill cache")
         cs.seq_len = PREFILLED
         del buf_k, buf_v
-        self.fused = fused
+        self.mode = mode
+        self.fused = mode != "attn"
         self.q = torch.empty((LAYERS, HQ, D), dtype=torch.float32, device=device).normal_(generator=gen)
         self.k_new = torch.empty((LAYERS, HKV, D), dtype=torch.float32, device=device).normal_(0.0, 0.5, generator=gen)
         self.v_new = torch.empty((LAYERS, HKV, D), dtype=torch.float32, device=device).normal_(0.0, 0.5, generator=gen)
         self.out = torch.zeros((LAYERS, HQ, D), dtype=torch.float32, device=device)
         self.scale = ctypes.c_float(pkg.SCALE)
+        if mode == "fused_qk":  # per-layer norm weights; a text token's cos/sin row per step position
+            self.qn = 1.0 + 0.02 * torch.randn((LAYERS, D), generator=gen, device=device)
+            self.kn = 1.0 + 0.02 * torch.randn((LAYERS, D), generator=gen, device=device)
+            pos = np.repeat(np.arange(PREFILLED, PREFILLED + SCHEDULE, dtype=np.int32)[None, :], 3, axis=0)
+            self.cos, self.sin = _rope_tables(pos, device)
         self.graphs = {}
         self.stream = torch.cuda.Stream(device=device)
 
@@ -185,7 +197,16 @@ class DecodeBench:
         for layer in range(LAYERS):
             q_l = ctypes.c_void_p(qp + layer * HQ * D * 4)
             o_l = ctypes.c_void_p(op + layer * HQ * D * 4)
-            if self.fused:
+            if self.mode == "fused_qk":
+                r = step % SCHEDULE
+                rc = self.lib.attention_decode_append_fused_gqa(
+                    q_l, ctypes.c_void_p(kp + layer * HKV * D * 4), ctypes.c_void_p(vp + layer * HKV * D * 4),
+                    ctypes.c_void_p(self.qn[layer].data_ptr()), ctypes.c_void_p(self.kn[layer].data_ptr()),
+                    ctypes.c_void_p(self.cos[r].data_ptr()), ctypes.c_void_p(self.sin[r].data_ptr()), self.cache,
+                    o_l, layer, self.scale, ctypes.c_float(self.pkg.RMS_EPS))
+                if rc:
+                    raise RuntimeError(self.pkg.last_error(self.lib))
+            elif self.fused:
                 rc = self.lib.attention_decode_append_gqa(q_l, ctypes.c_void_p(kp + layer * HKV * D * 4),
                                                           ctypes.c_void_p(vp + layer * HKV * D * 4), self.cache,
                                                           o_l, layer, self.scale)
@@ -425,9 +446,14 @@ def time_long_context(pkg, lib, dctx, device, decode_steps=16):
             raise RuntimeError(pkg.last_error(lib))
         return ms
 
+    parity = None
     try:
         dec_ms = time_decode(fused=world > 1)
         dec_nccl_ms = time_decode(fused=False) if world > 1 else None
+        if world > 1:
+            parity = long_context_parity(pkg, lib, dctx, device, decode_step, dout, gstream, dict(
+                q=q, k=k, v=v, qn=qn, kn=kn, cos=cos, sin=sin, dq=dq, dk=dk, dv=dv, S=S, steps=decode_steps,
+                tokens=tokens))
     finally:
         torch.cuda.synchronize()
         dctx.barrier()
@@ -443,6 +469,7 @@ def time_long_context(pkg, lib, dctx, device, decode_steps=16):
         "kv_heads_per_gpu": n,
         "prefill_ms": pf_ms, "prefill_tok_per_s": S / (pf_ms * 1e-3), "prefill_tflops": flops / (pf_ms * 1e-3) / 1e12,
         "decode_us_per_step": dec_ms * 1e3 / decode_steps, "decode_steps": decode_steps,
+        "parity": parity,
         "decode_gather": "peer stores over NVLink fused into the decode kernel (attention_decode_append_gqa_gathered)"
                          if world > 1 else "none (one GPU)",
         "decode_us_per_step_nccl_allgather": dec_nccl_ms * 1e3 / decode_steps if dec_nccl_ms else None,
@@ -452,6 +479,60 @@ def time_long_context(pkg, lib, dctx, device, decode_steps=16):
         "path": "prefill: attention_prefill_fused_gqa_heads + NCCL all_gather_into_tensor + attn_heads_to_tokens; "
                 "decode: attention_decode_append_gqa_gathered (N > 1) / attention_decode_append_gqa_heads",
     }
+
+
+def long_context_parity(pkg, lib, dctx, device, decode_step, dout, stream, d):
+    """What the sharded config-5 decode computes, checked after it was timed (N > 1): the last
+    decode step once more through the fused peer-store gather and once through the NCCL
+    all-gather -- bitwise equal on every rank -- and, on rank 0, against attention_decode_append_gqa
+    over a full-head cache that went through the same prefill and decode steps on one GPU (the
+    same BF16 rows; the split-merge order differs, so within the FP32 bar).  Every rank takes the
+    same collective steps.  Returns a dict with the verdict and the errors."""
+    import torch
+    last = d["steps"] - 1
+    with torch.cuda.stream(stream):
+        decode_step(last, True)
+        out_fused = dout.clone()
+        decode_step(last, False)
+        out_nccl = dout.clone()
+    torch.cuda.synchronize()
+    if lib.attn_sync():
+        raise RuntimeError(pkg.last_error(lib))
+    bitwise = bool(torch.equal(out_fused, out_nccl))
+    e_max = e_rel = 0.0
+    if dctx.rank == 0:
+        S, vp = d["S"], (lambda t: ctypes.c_void_p(t.data_ptr()))
+        full = lib.kv_cache_alloc_ex(S + d["steps"] + 8, pkg.ATTN_KV_BF16)
+        if not full:
+            raise RuntimeError(pkg.last_error(lib))
+        cs = pkg.cache_struct(full)
+        scale, eps = ctypes.c_float(pkg.SCALE), ctypes.c_float(pkg.RMS_EPS)
+        ref = torch.empty((HQ, D), device=device)
+        with torch.cuda.stream(stream):
+            for layer in range(LAYERS):
+                cs.seq_len = 0
+                if lib.attention_prefill_fused_gqa(vp(d["q"]), vp(d["k"]), vp(d["v"]), pkg.ATTN_DT_BF16, vp(d["qn"]),
+                                                   vp(d["kn"]), vp(d["cos"]), vp(d["sin"]), full, layer,
+                                                   vp(d["tokens"]), pkg.ATTN_DT_BF16, S, scale, eps):
+                    raise RuntimeError(pkg.last_error(lib))
+            for i in range(d["steps"]):
+                cs.seq_len = S + i
+                for layer in range(LAYERS):
+                    if lib.attention_decode_append_gqa(vp(d["dq"][layer]), vp(d["dk"][layer]), vp(d["dv"][layer]),
+                                                       full, vp(ref), layer, scale):
+                        raise RuntimeError(pkg.last_error(lib))
+        torch.cuda.synchronize()
+        if lib.attn_sync():
+            raise RuntimeError(pkg.last_error(lib))
+        lib.kv_cache_free(full)
+        diff = (out_fused - ref).double()
+        e_max = float(diff.abs().max())
+        e_rel = float(diff.norm() / ref.double().norm())
+    ok_local = bitwise and e_max <= 2e-3 and e_rel <= 1e-3
+    ok_all = dctx.max(0.0 if ok_local else 1.0) == 0.0
+    return {"pass": ok_all, "fused_vs_nccl_bitwise_all_ranks": dctx.max(0.0 if bitwise else 1.0) == 0.0,
+            "rank0_vs_unsharded": {"max_abs": e_max, "rel_l2": e_rel, "tolerance": [2e-3, 1e-3]},
+            "what": "layer 27 output of decode step kv_len " + str(d["S"] + d["steps"])}
 
 
 def time_batched(pkg, lib, dctx, device, per_gpu=64, steps=8):
@@ -502,7 +583,8 @@ def time_batched(pkg, lib, dctx, device, per_gpu=64, steps=8):
     e1.record(stream)
     torch.cuda.synchronize()
     dctx.barrier()
-    ms = dctx.max(e0.elapsed_time(e1))
+    ms_own = e0.elapsed_time(e1)
+    ms = dctx.max(ms_own)
     if lib.attn_sync():
         raise RuntimeError(pkg.last_error(lib))
     lib.attn_set_stream(None)
@@ -511,11 +593,15 @@ def time_batched(pkg, lib, dctx, device, per_gpu=64, steps=8):
     # K/V bytes per step, averaged over the timed steps (kv_len + 1 .. kv_len + steps)
     bytes_step = sum(float(LAYERS * 2 * (int(kv) + (steps + 1) / 2) * HKV * D * 2) for kv in lens)
     us = ms * 1e3 / steps
+    # Each rank's own bytes over its own time (its sequences' lengths differ from the others').
+    own_gbs = dctx.gather(bytes_step / (ms_own * 1e-3 / steps) / 1e9)
+    own_us = dctx.gather(ms_own * 1e3 / steps)
     return {
         "workload": f"config4: {per_gpu} sequences per GPU ({per_gpu * dctx.n} in all), kv_len ~ U[1024, 8192] "
                     "seeded, BF16 per-sequence caches, 28 layers per step",
         "us_per_step": us, "steps": steps,
-        "achieved_gbs_per_gpu": bytes_step / (us * 1e-6) / 1e9,
+        "achieved_gbs_per_gpu": sum(own_gbs) / len(own_gbs),
+        "per_rank": {"us_per_step": own_us, "achieved_gbs": own_gbs},
         "sequences_per_s": per_gpu * dctx.n / (us * 1e-6),
         "path": "attention_decode_gqa_batched x28 per step (one launch per layer for all sequences)",
     }
@@ -555,6 +641,145 @@ def time_e2e(pkg, lib, cache, steps, device):
     return (t1 - t0) * 1e3, LAYERS * (HQ + 2 * HKV) * D * 4, LAYERS * HQ * D * 4
 
 
+def time_decode_dropin(pkg, lib, cache, steps):
+    """The decode step exactly as the unmodified kernel/decoder.c issues it (:96-105, :313): per
+    layer kv_cache_append(cache, layer, s->k, s->v) then attention_decode_gqa(s->q, cache,
+    s->attn, layer, seq_len + 1, scale), over the reference-layout FP32 cache, with the page-locked
+    DecoderScratch buffers decoder_scratch_alloc hands out; kv_cache_advance(cache, 1) after the 28
+    layers.  Every call blocks as the reference's do.  Wall clock per step."""
+    import torch
+    lib.attn_set_stream(None)
+    sh = lib.decoder_scratch_alloc(8)
+    if not sh:
+        raise RuntimeError(pkg.last_error(lib))
+    s = pkg.scratch_struct(sh)
+    rng = np.random.default_rng(11)
+    for name, n in (("q", HQ * D), ("k", HKV * D), ("v", HKV * D)):
+        src = rng.standard_normal(n, dtype=np.float32)  # kept alive across the copy
+        ctypes.memmove(getattr(s, name), src.ctypes.data, n * 4)
+    scale = ctypes.c_float(pkg.SCALE)
+    cs = pkg.cache_struct(cache)
+
+    def one(step):
+        cs.seq_len = kv_len_of(step) - 1
+        for layer in range(LAYERS):
+            lib.kv_cache_append(cache, layer, s.k, s.v)
+            lib.attention_decode_gqa(s.q, cache, s.attn, layer, cs.seq_len + 1, scale)
+        lib.kv_cache_advance(cache, 1)
+
+    try:
+        for i in range(5):
+            one(i)
+        pkg.check(lib, "drop-in decode warm-up")
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for i in range(steps):
+            one(i)
+        t1 = time.perf_counter()
+        pkg.check(lib, "drop-in decode")
+    finally:
+        lib.decoder_scratch_free(sh)
+    return {"value": (t1 - t0) * 1e6 / steps, "unit": "us/step", "steps": steps,
+            "h2d_bytes_per_step": LAYERS * (HQ + 2 * HKV) * D * 4, "d2h_bytes_per_step": LAYERS * HQ * D * 4,
+            "path": "kv_cache_append + attention_decode_gqa per layer (unmodified decoder.c), FP32 cache from "
+                    "kv_cache_alloc, page-locked DecoderScratch q/k/v/attn, blocking calls, wall clock"}
+
+
+def time_prefill_fp32(pkg, lib, device, pages=2, seq=4096):
+    """The drop-in prefill of kernel/decoder.c:106-117 at config 3's page size: per layer
+    attention_prefill_gqa over FP32 q [S][16][128], k/v [S][8][128] that the host's ops already
+    normalised and rotated, on the tensor cores at the FP32 bar (prefill_tc32_kernel + its K/V
+    split pass).  Device-resident: distinct FP32 inputs per layer (64 MB each, 1.8 GB per page),
+    CUDA events.  End to end: the page-locked DecoderScratch buffers with the scratch's device
+    slots passed as decoder.c passes them (q, k, v copied in and the output back inside every
+    call), wall clock.  Returns a dict."""
+    import torch
+    gen = torch.Generator(device=device)
+    gen.manual_seed(6)
+    q = torch.randn((LAYERS, seq, HQ, D), generator=gen, device=device)
+    k = torch.randn((LAYERS, seq, HKV, D), generator=gen, device=device)
+    v = torch.randn((LAYERS, seq, HKV, D), generator=gen, device=device)
+    out = torch.empty((seq, HQ, D), device=device)
+    scale = ctypes.c_float(pkg.SCALE)
+    lib.attn_set_stream(None)
+    vp = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+
+    def page():
+        for layer in range(LAYERS):
+            lib.attention_prefill_gqa(vp(q[layer]), vp(k[layer]), vp(v[layer]), vp(out), seq, seq, scale,
+                                      None, None, None, None)
+
+    page()
+    torch.cuda.synchronize()
+    pkg.check(lib, "fp32 prefill warm-up")
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(pages):
+        page()
+    e1.record()
+    torch.cuda.synchronize()
+    pkg.check(lib, "fp32 prefill")
+    ms = e0.elapsed_time(e1) / pages
+    del q, k, v, out
+    sh = lib.decoder_scratch_alloc(seq)
+    if not sh:
+        raise RuntimeError(pkg.last_error(lib))
+    s = pkg.scratch_struct(sh)
+    try:
+        rng = np.random.default_rng(6)
+        for name, n in (("q", seq * HQ * D), ("k", seq * HKV * D), ("v", seq * HKV * D)):
+            src = rng.standard_normal(n, dtype=np.float32)  # kept alive across the copy
+            ctypes.memmove(getattr(s, name), src.ctypes.data, n * 4)
+
+        def page_host():
+            for _ in range(LAYERS):
+                lib.attention_prefill_gqa(s.q, s.k, s.v, s.attn, seq, seq, scale, s.q_hm, s.k_hm, s.v_hm, s.o_hm)
+
+        page_host()
+        pkg.check(lib, "fp32 prefill e2e warm-up")
+        t0 = time.perf_counter()
+        page_host()
+        e2e_ms = (time.perf_counter() - t0) * 1e3
+        pkg.check(lib, "fp32 prefill e2e")
+    finally:
+        lib.decoder_scratch_free(sh)
+    flops = LAYERS * 4.0 * D * HQ * seq * (seq + 1) / 2
+    return {"ms_per_page": ms, "value": seq / (ms * 1e-3), "unit": "tok/s", "pages": pages,
+            "tflops": flops / (ms * 1e-3) / 1e12,
+            "e2e": {"ms_per_page": e2e_ms, "value": seq / (e2e_ms * 1e-3), "unit": "tok/s",
+                    "h2d_bytes_per_page": LAYERS * seq * (HQ + 2 * HKV) * D * 4,
+                    "d2h_bytes_per_page": LAYERS * seq * HQ * D * 4,
+                    "path": "attention_prefill_gqa x28 with page-locked DecoderScratch q/k/v/attn and its "
+                            "q_hm/k_hm/v_hm/o_hm slots (blocking, wall clock)"},
+            "workload": "config 3's page size (4,096 tokens, 28 layers) on the drop-in FP32 path: Q/K/V ~ N(0,1) "
+                        "FP32, already normalised and rotated (decoder.c's host ops)",
+            "path": "attention_prefill_gqa x28, device FP32 buffers: kv_split_kernel + prefill_tc32_kernel per layer",
+            "flops_definition": "4*128*16*S*(S+1)/2 per layer (causal pairs); each product takes 3 BF16 MMAs "
+                                "(2 where K/V are BF16 rows), so the tensor pipe executes ~3x these FLOPs"}
+
+
+def cpu_reference_prefill(seq=4096):
+    """The reference's attention_prefill_gqa (oracle/_ref; the C restatement when absent) on the
+    host cores: one layer at config 3's page size, the work of every layer being the same, x28."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import oracle as orc
+    threads = orc.host_threads()
+    orc.set_host_threads(threads)
+    rng = np.random.default_rng(7)
+    q = rng.standard_normal((seq, HQ, D), dtype=np.float32)
+    k = rng.standard_normal((seq, HKV, D), dtype=np.float32)
+    v = rng.standard_normal((seq, HKV, D), dtype=np.float32)
+    impl = orc.RefLib() if orc.RefLib.available() else orc.Oracle()
+    kind = "reference" if isinstance(impl, orc.RefLib) else "port"
+    t0 = time.perf_counter()
+    impl.prefill(q, k, v)
+    dt = time.perf_counter() - t0
+    return {"ms_per_page": dt * 1e3 * LAYERS, "value": seq / (dt * LAYERS), "unit": "tok/s", "cores": threads,
+            "kind": kind,
+            "sample": f"one layer's attention_prefill_gqa at S={seq} (FP32) on {threads} OpenMP threads, "
+                      f"{dt:.2f} s; per page = x28 layers (extrapolated by layer count)"}
+
+
 class DistCtx:
     def __init__(self, n):
         self.n = n
@@ -575,6 +800,16 @@ class DistCtx:
     def barrier(self):
         if self.dist:
             self.dist.barrier()
+
+    def gather(self, x):
+        """x from every rank, in rank order."""
+        if not self.dist:
+            return [x]
+        import torch
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        out = torch.empty(self.n, dtype=torch.float64, device="cuda")
+        self.dist.all_gather_into_tensor(out, t)
+        return [float(y) for y in out.tolist()]
 
     def max(self, x):
         if not self.dist:
@@ -817,22 +1052,33 @@ def main():
     e2e_max = dctx.max(e2e_ms)
     bf.close()
 
-    ao = DecodeBench(pkg, lib, pkg.ATTN_KV_BF16, f"cuda:{local_rank}", fused=False)
+    ao = DecodeBench(pkg, lib, pkg.ATTN_KV_BF16, f"cuda:{local_rank}", mode="attn")
     ao.capture()
     ao_steps = min(args.steps, 4096)
     ms_ao = dctx.max(time_device(ao, args.warmup, ao_steps, dctx))
     bytes_ao = sum(step_bytes(args.warmup + i, 2, fused=False) for i in range(ao_steps))
     ao.close()
 
+    fq = DecodeBench(pkg, lib, pkg.ATTN_KV_BF16, f"cuda:{local_rank}", mode="fused_qk")
+    fq.capture()
+    ms_fq = dctx.max(time_device(fq, args.warmup, ao_steps, dctx))
+    fq.close()
+
     f32 = DecodeBench(pkg, lib, pkg.ATTN_KV_F32, f"cuda:{local_rank}")
     f32.capture()
     f32_steps = min(args.steps, 4096)
     ms32 = dctx.max(time_device(f32, args.warmup, f32_steps, dctx))
     bytes32 = sum(step_bytes(args.warmup + i, 4) for i in range(f32_steps))
+    f32.graphs.clear()
+    dropin = time_decode_dropin(pkg, lib, f32.cache, args.e2e_steps)
+    dropin["value"] = dctx.max(dropin["value"])
     f32.close()
 
     pf_ms, pf_flops, pf_launches = time_prefill(pkg, lib, f"cuda:{local_rank}", pages=args.prefill_pages, warmup=2)
     pf_ms_max = dctx.max(pf_ms)
+    pf32 = time_prefill_fp32(pkg, lib, f"cuda:{local_rank}")
+    pf32["ms_per_page"] = dctx.max(pf32["ms_per_page"])
+    pf32["e2e"]["ms_per_page"] = dctx.max(pf32["e2e"]["ms_per_page"])
     long_ctx = time_long_context(pkg, lib, dctx, f"cuda:{local_rank}") if args.long_context else None
     batched = time_batched(pkg, lib, dctx, f"cuda:{local_rank}") if args.batched else None
     tc_sustained = tc_peak
@@ -843,7 +1089,8 @@ def main():
     cpu = None
     if dctx.rank == 0:
         us_cpu, cores, kind, sample = cpu_reference_sample(args.cpu_budget)
-        cpu = {"value": us_cpu, "unit": "us/step", "cores": cores, "kind": kind, "sample": sample}
+        cpu = {"value": us_cpu, "unit": "us/step", "cores": cores, "kind": kind, "sample": sample,
+               "prefill": cpu_reference_prefill()}
     dctx.close()
     if dctx.rank != 0:
         return
@@ -886,18 +1133,27 @@ def main():
                       "achieved_gbs": bytes_ao / (ms_ao * 1e-3) / 1e9,
                       "frac": bytes_ao / (ms_ao * 1e-3) / 1e9 / hbm_peak,
                       "path": "attention_decode_gqa x28 (no append)"},
+        "fused_qk": {"value": ms_fq * 1e3 / ao_steps, "unit": "us/step", "steps": ao_steps,
+                     "achieved_gbs": bytes_ao / (ms_fq * 1e-3) / 1e9,
+                     "path": "attention_decode_append_fused_gqa x28: raw q/k, QK-RMSNorm + M-RoPE + append + "
+                             "attention in the decode kernel (decoder.c:73-105 per layer on the GPU)"},
+        "e2e_dropin": dropin,
         "fp32_kv": {"value": ms32 * 1e3 / f32_steps, "unit": "us/step", "steps": f32_steps,
                     "achieved_gbs": bytes32 / (ms32 * 1e-3) / 1e9,
                     "frac": bytes32 / (ms32 * 1e-3) / 1e9 / hbm_peak},
         "prefill": {"value": 4096 * n / (pf_ms_max * 1e-3), "unit": "tok/s", "ms_per_page": pf_ms_max,
                     "pages": args.prefill_pages,
-                    "tflops": pf_flops / (pf_ms * 1e-3) / 1e12, "peak_tflops": tc_sustained,
-                    "frac": pf_flops / (pf_ms * 1e-3) / 1e12 / tc_sustained,
+                    "tflops": pf_flops / (pf_ms * 1e-3) / 1e12, "peak_tflops": tc_peak,
+                    "frac": pf_flops / (pf_ms * 1e-3) / 1e12 / tc_peak,
+                    "frac_of_sustained": pf_flops / (pf_ms * 1e-3) / 1e12 / tc_sustained,
                     "workload": "config3: 4096-token page (3600 vision 60x60 + 496 text), 28 layers, bf16, "
                                 "QK-RMSNorm + M-RoPE fused, K/V appended to the cache",
                     "path": "attention_prefill_fused_gqa x28 (kv_prep + prefill_tc_kernel per layer)",
                     "flops_definition": "4*128*16*S*(S+1)/2 per layer (causal pairs)",
-                    "peak_note": "bf16 cuBLAS sustained, measured"},
+                    "peak_note": f"bf16 cuBLAS burst ({peak_src}; the page is ~50 ms of back-to-back work, "
+                                 f"frac_of_sustained divides by the seconds-long figure)"},
+        "prefill_fp32": dict(pf32, frac=pf32["tflops"] / tc_peak,
+                             peak_note=f"algorithmic TFLOP/s over the bf16 cuBLAS burst peak ({peak_src})"),
         "long_context": long_ctx,
         "batched": batched,
         "cpu_baseline": cpu,

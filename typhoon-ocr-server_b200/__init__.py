@@ -52,6 +52,15 @@ class KVCache(ctypes.Structure):
     ]
 
 
+class DecoderScratch(ctypes.Structure):
+    """Byte-for-byte the reference struct (kernel/scratch.h:17-34): token-major activations
+    (page-locked host memory here), then the head-major slots, which are device memory here."""
+
+    _fields_ = [(name, ctypes.c_void_p) for name in (
+        "residual", "q", "k", "v", "attn", "gate", "up", "mlp", "q_hm", "k_hm", "v_hm", "o_hm", "qkv_fused",
+        "gate_up_fused")]
+
+
 _F32P = ctypes.POINTER(ctypes.c_float)
 _VP = ctypes.c_void_p
 
@@ -143,6 +152,11 @@ def load_attention_lib(path=None) -> ctypes.CDLL:
 def cache_struct(handle) -> KVCache:
     """The host-visible KVCache fields behind a handle (seq_len, rope_offset, pointers)."""
     return KVCache.from_address(handle)
+
+
+def scratch_struct(handle) -> DecoderScratch:
+    """The fields of a DecoderScratch handle from decoder_scratch_alloc."""
+    return DecoderScratch.from_address(handle)
 
 
 def last_error(lib) -> str:
