@@ -33,6 +33,22 @@ void attn_set_stream(void *stream);
  * 0 on success, else nonzero with attn_last_error() set. */
 int  attn_sync(void);
 
+/* Limit, in nanoseconds, of every bounded wait in this library's kernels on the current device
+ * (a tile copy that never lands, a peer rank that never raises its flag); 2 s until set.  A wait
+ * that runs out ends its kernel early with a device status bit, which the next blocking call or
+ * attn_sync() reports through attn_last_error() ("wait timed out"); the CUDA context stays
+ * usable.  Applies to kernels launched afterwards.  ns >= 1000.  0 on success. */
+int attn_set_wait_limit_ns(unsigned long long ns);
+
+/* Sizes the current device's workspace now, so that later calls within these sizes allocate
+ * nothing: the staging of host buffers and the K/V operand splits of attention_prefill_gqa
+ * without scratch slots and of attention_chunked_prefill_gqa (max_tokens query tokens), and the
+ * descriptors, staging and split records of attention_decode_gqa_batched (max_batch sequences of
+ * at most max_kv_len rows).  Without it the first call that needs more grows the workspace
+ * (after waiting for the device).  The workspace is per device; calls from several host threads
+ * on one device share it and must not overlap.  0 on success. */
+int attn_workspace_reserve(int max_tokens, int max_batch, int max_kv_len);
+
 /* Decode for `batch` independent sequences in one launch (request-level batching;
  * ragged kv lengths).  q, output: [batch][16][128] fp32 (host or device);
  * caches[b]: the cache of sequence b (all with the same element type);
@@ -152,7 +168,9 @@ int attn_heads_to_tokens(const void *gathered, void *output, int seq_len, int dt
  *                   such limit (long sequences are streamed in at most 2 x SMs / 8 spans)
  *   stream          cudaStream_t (NULL = legacy default stream); the call only queues work
  * The first call on each device looks up the array's device address (cudaGetSymbolAddress);
- * make that first call before any stream capture.  All calls share the one array and it
+ * make that first call before any stream capture.  The address is kept until the process exits,
+ * so this entry point must not be used on a device after cudaDeviceReset there (reload the
+ * library first).  All calls share the one array and it
  * keeps the last call's contents: calls that overlap on the GPU (other streams, other
  * threads) race, so serialise them, e.g. on one stream.  0 on success, else nonzero with
  * attn_last_error() set. */

@@ -93,3 +93,12 @@ def test_gather_requires_setup(pl):
     assert _err(pkg, lib)
     assert lib.attn_gather_init(0, 9) != 0  # more ranks than the exchange holds
     assert _err(pkg, lib)
+
+
+def test_wait_limit_and_reserve_reject_bad_arguments(pl):
+    pkg, lib = pl
+    lib.attn_clear_error()
+    assert lib.attn_set_wait_limit_ns(10) != 0  # below 1 us: refused before any CUDA call
+    assert "below" in _err(pkg, lib)
+    assert lib.attn_workspace_reserve(-1, 0, 0) != 0
+    assert "negative" in _err(pkg, lib)

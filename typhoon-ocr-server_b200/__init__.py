@@ -107,6 +107,8 @@ _SIGNATURES = {
     "attn_clear_error": (None, []),
     "attn_set_stream": (None, [_VP]),
     "attn_sync": (ctypes.c_int, []),
+    "attn_set_wait_limit_ns": (ctypes.c_int, [ctypes.c_ulonglong]),
+    "attn_workspace_reserve": (ctypes.c_int, [ctypes.c_int, ctypes.c_int, ctypes.c_int]),
     "attention_decode_gqa_batched": (ctypes.c_int, [_VP, _VP, _VP, _VP, ctypes.c_int, ctypes.c_int,
                                                     ctypes.c_float]),
     "attention_prefill_fused_gqa": (ctypes.c_int, [_VP, _VP, _VP, ctypes.c_int, _VP, _VP, _VP, _VP, _VP, ctypes.c_int,

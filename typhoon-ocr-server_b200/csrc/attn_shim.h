@@ -158,6 +158,11 @@ int tyb_kv_scatter_launch(const float *k_src, const float *v_src, void *k_dst, v
 
 /* ---- status word -------------------------------------------------------------------- */
 
+/* Limit of the kernels' bounded waits on the current device (default 2 s): kernels launched
+ * afterwards give up after `ns` nanoseconds and raise TYB_STATUS_WAIT_TIMEOUT. */
+int tyb_set_wait_limit(unsigned long long ns);
+unsigned long long tyb_wait_limit(void);
+
 /* Copy the status word to *bits after all work on `stream`, then clear it. */
 int tyb_status_fetch(unsigned int *bits, void *stream);
 /* Device address of the status word on the current device (NULL on failure). */

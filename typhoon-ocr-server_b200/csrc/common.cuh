@@ -210,6 +210,11 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
 {
     return mbar_wait_bounded_to(bar, parity, limit_ns, status_bit, &g_status, g_status_mirror);
 }
+
+// The current wait limit of this device (attn_set_wait_limit_ns; kWaitLimitNs until set).
+// Whole-program translation units receive it as a kernel argument instead.
+extern __device__ unsigned long long g_wait_limit_ns;
+__device__ __forceinline__ uint64_t wait_limit_ns() { return g_wait_limit_ns; }
 #endif
 
 // 1-D bulk copy global -> this CTA's shared memory, completing on `bar`.
@@ -231,6 +236,6 @@ __device__ __forceinline__ void bulk_prefetch_l2(const void* gmem, uint32_t byte
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(gmem), "r"(bytes) : "memory");
 }
 
-constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s: far beyond any legitimate wait
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // default limit, 2 s: far beyond any legitimate wait
 
 }  // namespace tyb

@@ -154,7 +154,7 @@ __device__ __forceinline__ bool merge_records(const float* recs, int nsplit, flo
             mbar_arrive_expect_tx(bar, bytes);
             bulk_g2s(region, recs + (size_t)j0 * kRec, bytes, bar);
         }
-        if (__syncthreads_or(!mbar_wait_bounded(bar, phase, kWaitLimitNs, TYB_STATUS_WAIT_TIMEOUT))) return false;
+        if (__syncthreads_or(!mbar_wait_bounded(bar, phase, wait_limit_ns(), TYB_STATUS_WAIT_TIMEOUT))) return false;
         phase ^= 1u;
         // Batch maximum of each head: a block reduction over the records' headers.
         float x0 = -INFINITY, x1 = -INFINITY;
@@ -330,7 +330,7 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_split_kernel(const Deco
     }
 
     // Every thread waits (bounded); the CTA leaves together if any wait ran out.
-    if (__syncthreads_or(!mbar_wait_bounded(&bars[0], 0, kWaitLimitNs, TYB_STATUS_WAIT_TIMEOUT))) return;
+    if (__syncthreads_or(!mbar_wait_bounded(&bars[0], 0, wait_limit_ns(), TYB_STATUS_WAIT_TIMEOUT))) return;
 
     // Scores: 8 lanes per row (each 16-byte chunk of a 128-byte line read by one lane: no
     // bank conflicts), 4 rows per warp pass, two passes 32 rows apart interleaved; a 3-level
@@ -418,7 +418,7 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_split_kernel(const Deco
     }
 
     if (has_new && tid < 16) store8(Vs + (size_t)(kv_len - 1 - r0) * kD + tid * 8, nv);
-    if (__syncthreads_or(!mbar_wait_bounded(&bars[1], 0, kWaitLimitNs, TYB_STATUS_WAIT_TIMEOUT))) return;
+    if (__syncthreads_or(!mbar_wait_bounded(&bars[1], 0, wait_limit_ns(), TYB_STATUS_WAIT_TIMEOUT))) return;
 
     // p.V: thread owns dims [8*g16, +8) of rows rg, rg+16, ...
     const int rg = tid >> 4;
@@ -946,7 +946,7 @@ __global__ void __launch_bounds__(NW * 32, 16 / NW)
         store8(a.k + row, nk);
         store8(a.v + row, nv);
     }
-    const bool kok = mbar_wait_bounded(&bars[0], 0, kWaitLimitNs, TYB_STATUS_WAIT_TIMEOUT);
+    const bool kok = mbar_wait_bounded(&bars[0], 0, wait_limit_ns(), TYB_STATUS_WAIT_TIMEOUT);
     if (new_thread) store8(reinterpret_cast<__nv_bfloat16*>(Kt + swz(chunk, rn, tid - 64)), nk);
     if (__syncthreads_or(!kok)) return;
 
@@ -1041,7 +1041,7 @@ __global__ void __launch_bounds__(NW * 32, 16 / NW)
     l += __shfl_xor_sync(0xffffffffu, l, 16);
     if (lane < 2) lw[2 * warp + lane] = l;
 
-    const bool vok = mbar_wait_bounded(&bars[1], 0, kWaitLimitNs, TYB_STATUS_WAIT_TIMEOUT);
+    const bool vok = mbar_wait_bounded(&bars[1], 0, wait_limit_ns(), TYB_STATUS_WAIT_TIMEOUT);
     // V rows the weights do not cover but the last 16-row step reads: zeros (0 * stale NaN is NaN).
     {
         const int z0 = trows + (has_new ? 1 : 0), z1 = ntiles * 16;
@@ -1341,7 +1341,7 @@ __global__ void __launch_bounds__(256, 2)
         const bool new_here = append && kv_len - 1 >= r0 && kv_len - 1 < r0 + nrows;
         const int rn = kv_len - 1 - r0;
 
-        const bool kok = mbar_wait_bounded(&bars[buf], par, kWaitLimitNs, TYB_STATUS_WAIT_TIMEOUT);
+        const bool kok = mbar_wait_bounded(&bars[buf], par, wait_limit_ns(), TYB_STATUS_WAIT_TIMEOUT);
         if (new_here && new_thread)
             store8(reinterpret_cast<__nv_bfloat16*>(smem + buf * kStTile + swz(kStRows, rn, tid - 64)), nk);
         if (__syncthreads_or(!kok)) return;
@@ -1392,7 +1392,7 @@ __global__ void __launch_bounds__(256, 2)
         l += __shfl_xor_sync(0xffffffffu, l, 16);
         if (lane < 2) lw[2 * warp + lane] = l;
 
-        const bool vok = mbar_wait_bounded(&bars[2 + buf], par, kWaitLimitNs, TYB_STATUS_WAIT_TIMEOUT);
+        const bool vok = mbar_wait_bounded(&bars[2 + buf], par, wait_limit_ns(), TYB_STATUS_WAIT_TIMEOUT);
         {
             // Tile rows past the attended ones that the last 16-row step reads: zeros.
             const int z0 = trows + (new_here ? 1 : 0), z1 = ntiles * 16;
@@ -1503,7 +1503,7 @@ __global__ void __launch_bounds__(256) gather_wait_kernel(const GatherDev* g, fl
     if (threadIdx.x < g->world) {
         const uint64_t t0 = globaltimer_ns();
         while ((int)(ld_acquire_sys(&mine->flags[threadIdx.x]) - epoch) < 0) {
-            if (globaltimer_ns() - t0 > kWaitLimitNs) {
+            if (globaltimer_ns() - t0 > wait_limit_ns()) {
                 raise_status(TYB_STATUS_WAIT_TIMEOUT);
                 fail = 1;
                 break;
@@ -1521,24 +1521,36 @@ __global__ void __launch_bounds__(256) gather_wait_kernel(const GatherDev* g, fl
 
 // ---- host-side planning ----------------------------------------------------------------
 
-static int g_num_sms = 0;
+// Everything cached below (SM counts, occupancies, kernel attributes) is per device: one process
+// may drive several GPUs, and function attributes belong to each device's context.
+constexpr int kMaxDevices = 64;
+
+static int cur_dev()
+{
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) dev = 0;
+    return dev;
+}
+
+static int g_num_sms[kMaxDevices];
 
 static int num_sms()
 {
-    if (!g_num_sms) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        if (cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || g_num_sms <= 0)
-            g_num_sms = 148;
+    const int dev = cur_dev();
+    if (!g_num_sms[dev]) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+        g_num_sms[dev] = n;
     }
-    return g_num_sms;
+    return g_num_sms[dev];
 }
 
 template <typename T>
 static int blocks_per_sm(int chunk)
 {
-    // Cached per chunk size (multiples of 16 up to kMaxChunk).
-    static int cache[DecodeTile<T>::kMaxChunk / 16 + 1];
+    // Cached per device and chunk size (multiples of 16 up to kMaxChunk).
+    static int cache_all[kMaxDevices][DecodeTile<T>::kMaxChunk / 16 + 1];
+    int* cache = cache_all[cur_dev()];
     const int i = chunk / 16;
     if (!cache[i]) {
         int n = 0;
@@ -1554,12 +1566,13 @@ static int blocks_per_sm(int chunk)
 template <typename T>
 static bool set_smem_attr()
 {
-    static bool done = false;
-    if (!done) {
+    static bool done[kMaxDevices];
+    const int dev = cur_dev();
+    if (!done[dev]) {
         if (cudaFuncSetAttribute(decode_split_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)decode_smem_bytes<T>(DecodeTile<T>::kMaxChunk)) != cudaSuccess)
             return false;
-        done = true;
+        done[dev] = true;
     }
     return true;
 }
@@ -1698,8 +1711,9 @@ static bool one_wave(int batch, int max_kv_len, int nkvh)
 
 static int set_mma_smem_attr()
 {
-    static bool done = false;
-    if (!done) {
+    static bool done[kMaxDevices];
+    const int dev = cur_dev();
+    if (!done[dev]) {
         const int mma_smem = (int)decode_mma_smem_bytes(kMmaMaxChunk), st_smem = (int)decode_stream_smem_bytes();
         cudaError_t e = cudaFuncSetAttribute(decode_mma_kernel<8, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              mma_smem);
@@ -1712,7 +1726,7 @@ static int set_mma_smem_attr()
             e = cudaFuncSetAttribute(decode_stream_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      st_smem);
         if (e != cudaSuccess) return (int)e;
-        done = true;
+        done[dev] = true;
     }
     return 0;
 }

@@ -95,7 +95,13 @@ int tyb_is_device_ptr(const void *p);
 enum { TYB_MEM_HOST = 0, TYB_MEM_DEVICE = 1, TYB_MEM_PINNED = 2 };
 int tyb_residency(const void *p, void **view);
 
-/* Process-wide device workspace slots, grown on demand; NULL on failure (error set). */
+/* cudaMalloc / cudaHostAlloc that honour the TYB_FAULT_ALLOC failure injection (runtime.c);
+ * 1 on success, else 0 with *p = NULL and the error set. */
+int tyb_dev_alloc(void **p, size_t bytes, const char *what);
+int tyb_host_alloc(void **p, size_t bytes, unsigned int flags, const char *what);
+
+/* The current device's workspace slots, grown on demand (attn_workspace_reserve sizes them
+ * ahead); NULL on failure (error set). */
 enum { TYB_WS_Q, TYB_WS_K, TYB_WS_V, TYB_WS_OUT, TYB_WS_PARTIALS, TYB_WS_COUNTERS, TYB_WS_DESC,
        TYB_WS_COUNT };
 void *tyb_workspace(int slot, size_t bytes);

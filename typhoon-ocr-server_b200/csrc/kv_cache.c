@@ -75,15 +75,16 @@ KVCache *kv_cache_alloc_ex(int max_seq_len, int kv_dtype)
     const int nsplit = (max_seq_len + 15) / 16 + 1;
     const size_t part = tyb_decode_partial_floats(1, nsplit) * sizeof(float);
 
-    int ok = tyb_cuda_ok(cudaMalloc(&t->k_slab, slab), "kv_cache_alloc: K slab") &&
-             tyb_cuda_ok(cudaMalloc(&t->v_slab, slab), "kv_cache_alloc: V slab") &&
-             tyb_cuda_ok(cudaMalloc((void **)&t->d_q, TYB_Q_FLOATS * sizeof(float)), "kv_cache_alloc: q") &&
-             tyb_cuda_ok(cudaMalloc((void **)&t->d_out, TYB_Q_FLOATS * sizeof(float)), "kv_cache_alloc: out") &&
-             tyb_cuda_ok(cudaMalloc((void **)&t->d_kv_stage, 2 * (size_t)max_seq_len * TYB_ROW_FLOATS * sizeof(float)),
-                         "kv_cache_alloc: staging") &&
-             tyb_cuda_ok(cudaMalloc((void **)&t->d_partials, part), "kv_cache_alloc: decode workspace") &&
-             tyb_cuda_ok(cudaMalloc((void **)&t->d_counters, KV_NUM_KV_HEADS * sizeof(unsigned int)),
-                         "kv_cache_alloc: counters") &&
+    /* Any failure frees what was allocated and returns NULL (kernel/kv_cache.c:17-30). */
+    int ok = tyb_dev_alloc(&t->k_slab, slab, "kv_cache_alloc: K slab") &&
+             tyb_dev_alloc(&t->v_slab, slab, "kv_cache_alloc: V slab") &&
+             tyb_dev_alloc((void **)&t->d_q, TYB_Q_FLOATS * sizeof(float), "kv_cache_alloc: q") &&
+             tyb_dev_alloc((void **)&t->d_out, TYB_Q_FLOATS * sizeof(float), "kv_cache_alloc: out") &&
+             tyb_dev_alloc((void **)&t->d_kv_stage, 2 * (size_t)max_seq_len * TYB_ROW_FLOATS * sizeof(float),
+                           "kv_cache_alloc: staging") &&
+             tyb_dev_alloc((void **)&t->d_partials, part, "kv_cache_alloc: decode workspace") &&
+             tyb_dev_alloc((void **)&t->d_counters, KV_NUM_KV_HEADS * sizeof(unsigned int),
+                           "kv_cache_alloc: counters") &&
              tyb_cuda_ok(cudaMemset(t->d_counters, 0, KV_NUM_KV_HEADS * sizeof(unsigned int)),
                          "kv_cache_alloc: counters memset");
     if (!ok) {

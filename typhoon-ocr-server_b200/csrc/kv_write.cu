@@ -11,6 +11,7 @@ namespace tyb {
 
 __device__ unsigned int g_status = 0u;
 __device__ unsigned int* g_status_mirror = nullptr;
+__device__ unsigned long long g_wait_limit_ns = kWaitLimitNs;
 
 template <typename TDst>
 __global__ void kv_scatter_kernel(const float* __restrict__ k_src, const float* __restrict__ v_src,
@@ -166,4 +167,27 @@ extern "C" int tyb_status_fetch(unsigned int* bits, void* stream)
         e = cudaMemcpyToSymbol(g_status, &zero, sizeof zero);
     }
     return (int)e;
+}
+
+// Wait limit of the bounded waits, per device: the device variable the relocatable kernels read,
+// and a host copy the launchers of the whole-program kernels pass as an argument.
+static unsigned long long g_wait_limit_host[64];
+
+extern "C" int tyb_set_wait_limit(unsigned long long ns)
+{
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return (int)e;
+    if (dev < 0 || dev >= 64) return (int)cudaErrorInvalidDevice;
+    e = cudaMemcpyToSymbol(g_wait_limit_ns, &ns, sizeof ns);
+    if (e != cudaSuccess) return (int)e;
+    g_wait_limit_host[dev] = ns;
+    return 0;
+}
+
+extern "C" unsigned long long tyb_wait_limit(void)
+{
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64 || !g_wait_limit_host[dev]) return kWaitLimitNs;
+    return g_wait_limit_host[dev];
 }

@@ -69,6 +69,7 @@ struct PrefillTcArgs {
     int out_head_major;    // output [2 nkvh][Sq][128] (a contiguous head shard) instead of [Sq][16][128]
     unsigned int* status;  // the library's status word (tyb_status_word)
     unsigned int* mirror;  // its page-locked host mirror flag (tyb_status_mirror_device), or NULL
+    unsigned long long wait_ns;  // limit of every bounded wait (tyb_wait_limit)
 };
 
 // Softmax weight split between the two exp2 units: of every four column pairs of an unmasked
@@ -304,11 +305,11 @@ __global__ void __launch_bounds__(kPtThreads, 1)
                 for (int j = 0; j < ntiles; j++) {
                     const int st = j & 1;
                     const uint32_t fpar = (uint32_t)((j - 2) >> 1) & 1u;
-                    if (j >= 2 && !mbar_wait_bounded_to(&k_free[st], fpar, kWaitLimitNs, TYB_STATUS_WAIT_TIMEOUT, a.status, a.mirror)) break;
+                    if (j >= 2 && !mbar_wait_bounded_to(&k_free[st], fpar, a.wait_ns, TYB_STATUS_WAIT_TIMEOUT, a.status, a.mirror)) break;
                     mbar_arrive_expect_tx(&k_full[st], kPtTile);
                     tma_load_3d(sK + st * kPtTile, &tmap_k, 0, j * kPtKeys, kvh, &k_full[st]);
                     tma_load_3d(sK + st * kPtTile + kPtBox, &tmap_k, 64, j * kPtKeys, kvh, &k_full[st]);
-                    if (j >= 2 && !mbar_wait_bounded_to(&v_free[st], fpar, kWaitLimitNs, TYB_STATUS_WAIT_TIMEOUT, a.status, a.mirror)) break;
+                    if (j >= 2 && !mbar_wait_bounded_to(&v_free[st], fpar, a.wait_ns, TYB_STATUS_WAIT_TIMEOUT, a.status, a.mirror)) break;
                     mbar_arrive_expect_tx(&v_full[st], kPtTile);
                     tma_load_3d(sV + st * kPtTile, &tmap_v, 0, j * kPtKeys, kvh, &v_full[st]);
                     tma_load_3d(sV + st * kPtTile + kPtBox, &tmap_v, 64, j * kPtKeys, kvh, &v_full[st]);
@@ -344,7 +345,7 @@ __global__ void __launch_bounds__(kPtThreads, 1)
                     tc_commit(&pv_done[h]);
                 };
                 auto wait = [&](uint64_t* bar, uint32_t parity) {
-                    const bool ok = mbar_wait_bounded_to(bar, parity, kWaitLimitNs, TYB_STATUS_WAIT_TIMEOUT, a.status, a.mirror);
+                    const bool ok = mbar_wait_bounded_to(bar, parity, a.wait_ns, TYB_STATUS_WAIT_TIMEOUT, a.status, a.mirror);
                     tc_fence_after();
                     return ok;
                 };
@@ -406,7 +407,7 @@ __global__ void __launch_bounds__(kPtThreads, 1)
         // warp-collective).
         auto warp_wait = [&](uint64_t* bar, uint32_t parity) {
             return !__any_sync(0xffffffffu,
-                               !mbar_wait_bounded_to(bar, parity, kWaitLimitNs, TYB_STATUS_WAIT_TIMEOUT, a.status, a.mirror));
+                               !mbar_wait_bounded_to(bar, parity, a.wait_ns, TYB_STATUS_WAIT_TIMEOUT, a.status, a.mirror));
         };
         for (int j = 0; j < ntiles; j++) {
             const uint32_t par = (uint32_t)j & 1u;
@@ -679,6 +680,7 @@ extern "C" int tyb_prefill_tc_launch(const void* q, int q_bf16, const float* q_n
     a.status = tyb_status_word();
     if (!a.status) return (int)cudaErrorInvalidSymbol;
     a.mirror = tyb_status_mirror_device();
+    a.wait_ns = tyb_wait_limit();
     CUtensorMap mk, mv;
     if (!make_kv_map(&mk, k_cache, a.total_kv, row_capacity) || !make_kv_map(&mv, v_cache, a.total_kv, row_capacity))
         return (int)cudaErrorInvalidValue;

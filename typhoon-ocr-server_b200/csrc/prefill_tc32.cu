@@ -47,6 +47,7 @@ struct PrefillTc32Args {
     float scale_log2;
     unsigned int* status;  // the library's status word
     unsigned int* mirror;  // its page-locked host mirror flag, or NULL
+    unsigned long long wait_ns;  // limit of every bounded wait (tyb_wait_limit)
 };
 
 // Largest visible score of a row: columns [0, lim).
@@ -188,7 +189,7 @@ __global__ void __launch_bounds__(kT32Threads, 1)
     asm volatile("griddepcontrol.wait;" ::: "memory");
 
     auto wait = [&](uint64_t* bar, uint32_t parity) {
-        return mbar_wait_bounded_to(bar, parity, kWaitLimitNs, TYB_STATUS_WAIT_TIMEOUT, a.status, a.mirror);
+        return mbar_wait_bounded_to(bar, parity, a.wait_ns, TYB_STATUS_WAIT_TIMEOUT, a.status, a.mirror);
     };
 
     if (warp == 5) {
@@ -423,6 +424,7 @@ extern "C" int tyb_prefill_tc32_launch(const float* q, float* out, int Sq, int p
     a.status = tyb_status_word();
     if (!a.status) return (int)cudaErrorInvalidSymbol;
     a.mirror = tyb_status_mirror_device();
+    a.wait_ns = tyb_wait_limit();
     // K/V: [8 heads][head_rows][128] BF16, rows [0, total_kv) visible to the copies (past it: zeros).
     CUtensorMap mkh, mkl, mvh, mvl;
     if (tyb_encode_rows_map(&mkh, k_hi, total_kv, head_rows, kT32Keys) ||

@@ -10,6 +10,7 @@
 #include <pthread.h>
 #include <stdarg.h>
 #include <stdio.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include "attn_ext.h"
@@ -75,41 +76,142 @@ int tyb_residency(const void *p, void **view)
     return TYB_MEM_HOST;
 }
 
-/* ---- workspace ------------------------------------------------------------------ */
+/* ---- device and page-locked allocations --------------------------------------------- */
 
+/* Host-side failure injection for tests of the allocation-failure paths: with
+ * TYB_FAULT_ALLOC=N in the environment (N > 0, optionally followed by non-digit text), the N-th
+ * allocation through tyb_dev_alloc / tyb_host_alloc after the variable takes that value fails as
+ * if the memory were exhausted.  A new value restarts the count; unset, nothing fails. */
+static pthread_mutex_t g_fault_lock = PTHREAD_MUTEX_INITIALIZER;
+static char g_fault_seen[64];
+static long g_fault_count;
+
+static int fault_now(void)
+{
+    const char *v = getenv("TYB_FAULT_ALLOC");
+    int fail = 0;
+    pthread_mutex_lock(&g_fault_lock);
+    if (!v || !*v) {
+        g_fault_seen[0] = '\0';
+        g_fault_count = 0;
+    } else {
+        if (strncmp(v, g_fault_seen, sizeof g_fault_seen) != 0) {
+            snprintf(g_fault_seen, sizeof g_fault_seen, "%s", v);
+            g_fault_count = 0;
+        }
+        const long n = strtol(v, NULL, 10);
+        fail = n > 0 && ++g_fault_count == n;
+    }
+    pthread_mutex_unlock(&g_fault_lock);
+    return fail;
+}
+
+int tyb_dev_alloc(void **p, size_t bytes, const char *what)
+{
+    *p = NULL;
+    if (fault_now()) {
+        tyb_set_error("%s: %s (injected by TYB_FAULT_ALLOC)", what, cudaGetErrorString(cudaErrorMemoryAllocation));
+        return 0;
+    }
+    if (!tyb_cuda_ok(cudaMalloc(p, bytes), what)) {
+        *p = NULL;
+        return 0;
+    }
+    return 1;
+}
+
+int tyb_host_alloc(void **p, size_t bytes, unsigned int flags, const char *what)
+{
+    *p = NULL;
+    if (fault_now()) {
+        tyb_set_error("%s: %s (injected by TYB_FAULT_ALLOC)", what, cudaGetErrorString(cudaErrorMemoryAllocation));
+        return 0;
+    }
+    if (!tyb_cuda_ok(cudaHostAlloc(p, bytes, flags), what)) {
+        *p = NULL;
+        return 0;
+    }
+    return 1;
+}
+
+/* ---- workspace: per device ---------------------------------------------------------- */
+
+#define TYB_MAX_DEVICES 64
 static pthread_mutex_t g_ws_lock = PTHREAD_MUTEX_INITIALIZER;
-static void *g_ws_ptr[TYB_WS_COUNT];
-static size_t g_ws_size[TYB_WS_COUNT];
+static void *g_ws_ptr[TYB_MAX_DEVICES][TYB_WS_COUNT];
+static size_t g_ws_size[TYB_MAX_DEVICES][TYB_WS_COUNT];
 
 void *tyb_workspace(int slot, size_t bytes)
 {
+    int dev = 0;
+    if (!tyb_cuda_ok(cudaGetDevice(&dev), "workspace")) return NULL;
+    if (dev < 0 || dev >= TYB_MAX_DEVICES) {
+        tyb_set_error("workspace: device %d beyond the %d this library tracks", dev, TYB_MAX_DEVICES);
+        return NULL;
+    }
     void *p = NULL;
     pthread_mutex_lock(&g_ws_lock);
-    if (g_ws_size[slot] >= bytes && g_ws_ptr[slot]) {
-        p = g_ws_ptr[slot];
+    if (g_ws_size[dev][slot] >= bytes && g_ws_ptr[dev][slot]) {
+        p = g_ws_ptr[dev][slot];
     } else {
-        if (g_ws_ptr[slot]) {
-            cudaDeviceSynchronize(); /* the old buffer may still be in use */
-            cudaFree(g_ws_ptr[slot]);
-            g_ws_ptr[slot] = NULL;
-            g_ws_size[slot] = 0;
+        if (g_ws_ptr[dev][slot]) {
+            cudaDeviceSynchronize(); /* the smaller buffer may still be in use on this device */
+            cudaFree(g_ws_ptr[dev][slot]);
+            g_ws_ptr[dev][slot] = NULL;
+            g_ws_size[dev][slot] = 0;
         }
         size_t want = bytes < 4096 ? 4096 : bytes;
-        if (tyb_cuda_ok(cudaMalloc(&p, want), "workspace cudaMalloc")) {
+        if (tyb_dev_alloc(&p, want, "workspace cudaMalloc")) {
             /* Counters and tickets must start at zero. */
             if (!tyb_cuda_ok(cudaMemset(p, 0, want), "workspace cudaMemset")) {
                 cudaFree(p);
                 p = NULL;
             } else {
-                g_ws_ptr[slot] = p;
-                g_ws_size[slot] = want;
+                g_ws_ptr[dev][slot] = p;
+                g_ws_size[dev][slot] = want;
             }
-        } else {
-            p = NULL;
         }
     }
     pthread_mutex_unlock(&g_ws_lock);
     return p;
+}
+
+int attn_workspace_reserve(int max_tokens, int max_batch, int max_kv_len)
+{
+    if (max_tokens < 0 || max_batch < 0 || max_kv_len < 0) {
+        tyb_set_error("attn_workspace_reserve: negative size");
+        return 1;
+    }
+    const size_t tok = (size_t)(max_tokens > max_batch ? max_tokens : max_batch);
+    const size_t q_bytes = tok * TYB_Q_FLOATS * sizeof(float);
+    const size_t kv_bytes = (size_t)max_tokens * TYB_ROW_FLOATS * sizeof(float);
+    /* the prefill output staging doubles as the staging of host K and V rows */
+    const size_t o_bytes = q_bytes > 2 * kv_bytes ? q_bytes : 2 * kv_bytes;
+    size_t part = 0, desc = 0, cnt = 0;
+    if (max_batch > 0 && max_kv_len > 0) {
+        int chunk = 0, nsplit = 0, nsplit32 = 0;
+        tyb_decode_plan(max_batch, max_kv_len, TYB_BF16, &chunk, &nsplit);
+        tyb_decode_plan(max_batch, max_kv_len, TYB_F32, &chunk, &nsplit32);
+        if (nsplit32 > nsplit) nsplit = nsplit32;
+        part = tyb_decode_partial_floats(max_batch, nsplit) * sizeof(float);
+        desc = tyb_decode_maps_bytes(max_batch) + sizeof(tyb_seq_kv) * (size_t)max_batch;
+        cnt = sizeof(unsigned int) * (size_t)max_batch * KV_NUM_KV_HEADS;
+    }
+    const size_t want[TYB_WS_COUNT] = {[TYB_WS_Q] = q_bytes, [TYB_WS_K] = kv_bytes, [TYB_WS_V] = kv_bytes,
+                                       [TYB_WS_OUT] = o_bytes, [TYB_WS_PARTIALS] = part, [TYB_WS_COUNTERS] = cnt,
+                                       [TYB_WS_DESC] = desc};
+    for (int s = 0; s < TYB_WS_COUNT; s++)
+        if (want[s] && !tyb_workspace(s, want[s])) return 1;
+    return 0;
+}
+
+int attn_set_wait_limit_ns(unsigned long long ns)
+{
+    if (ns < 1000ull) {
+        tyb_set_error("attn_set_wait_limit_ns: limit %llu ns is below 1000", ns);
+        return 1;
+    }
+    return tyb_cuda_ok(tyb_set_wait_limit(ns), "attn_set_wait_limit_ns") ? 0 : 1;
 }
 
 /* ---- registry of scratch device buffers ------------------------------------------- */

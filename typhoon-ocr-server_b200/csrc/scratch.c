@@ -18,8 +18,8 @@
 static void *host_buf(size_t floats, int *ok)
 {
     void *p = NULL;
-    if (*ok && !tyb_cuda_ok(cudaHostAlloc(&p, floats * sizeof(float), cudaHostAllocPortable),
-                            "decoder_scratch_alloc: pinned host buffer"))
+    if (*ok && !tyb_host_alloc(&p, floats * sizeof(float), cudaHostAllocPortable,
+                               "decoder_scratch_alloc: pinned host buffer"))
         *ok = 0;
     return p;
 }
@@ -27,7 +27,7 @@ static void *host_buf(size_t floats, int *ok)
 static float *dev_buf(size_t floats, int *ok)
 {
     void *p = NULL;
-    if (*ok && tyb_cuda_ok(cudaMalloc(&p, floats * sizeof(float)), "decoder_scratch_alloc: device buffer"))
+    if (*ok && tyb_dev_alloc(&p, floats * sizeof(float), "decoder_scratch_alloc: device buffer"))
         tyb_registry_add(p, floats * sizeof(float));
     else
         *ok = 0;
