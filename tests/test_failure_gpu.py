@@ -110,14 +110,14 @@ def test_cache_alloc_failure_frees_partial_state(pkg, lib, kv_dtype):
     lib.kv_cache_free(warm)
     base = _free_bytes()
     try:
-        for n in range(1, 8):  # each of its seven device allocations in turn
+        for n in range(1, 7):  # each of its six device allocations in turn
             os.environ["TYB_FAULT_ALLOC"] = f"{n}:cache{kv_dtype}"
             assert not lib.kv_cache_alloc_ex(4096, kv_dtype), n
             msg = pkg.last_error(lib)
             assert "injected" in msg and "kv_cache_alloc" in msg, msg
             lib.attn_clear_error()
             assert abs(_free_bytes() - base) < (8 << 20), f"allocation {n} failed but memory stayed allocated"
-        os.environ["TYB_FAULT_ALLOC"] = f"8:cache{kv_dtype}"  # past the last one: succeeds
+        os.environ["TYB_FAULT_ALLOC"] = f"7:cache{kv_dtype}"  # past the last one: succeeds
         h = lib.kv_cache_alloc_ex(4096, kv_dtype)
         assert h, pkg.last_error(lib)
         lib.kv_cache_free(h)

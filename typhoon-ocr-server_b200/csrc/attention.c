@@ -72,6 +72,47 @@ static float *small_view(const float *p, float *stage, size_t bytes, int *kind, 
     return stage;
 }
 
+static int decode_append_impl(const float *q, const float *k_new, const float *v_new, KVCache *cache, float *output,
+                              int layer_idx, float scale, int kvh0, int nkvh, const void *gather, int pos_at,
+                              const char *what);
+
+/* The single-token inputs of a decode call -- q [16][128] and, for an append, k_new / v_new
+ * [8][128] (NULL when absent) -- on the device.  Device buffers are used in place.  Host buffers
+ * (page-locked or not) are copied now into the layer's page-locked slot of the cache, so the
+ * caller may reuse them on return, and the slot reaches the device in ONE copy, into the cache's
+ * staging area, ahead of the kernel: the splits then read L2 instead of each fetching the query
+ * over the bus.  k_new / v_new may already be the slot's own rows (a deferred append).
+ * 1 on success, else 0 with the error set. */
+static int stage_inputs(tyb_cache *t, int layer, const float *q, const float *k_new, const float *v_new,
+                        const float **dq, const float **dk, const float **dv, void *st, const char *what)
+{
+    const int rq = tyb_is_device_ptr(q);
+    const int rk = k_new ? tyb_is_device_ptr(k_new) : 1, rv = v_new ? tyb_is_device_ptr(v_new) : 1;
+    if (rq < 0 || rk < 0 || rv < 0) return 0;
+    *dq = q;
+    *dk = k_new;
+    *dv = v_new;
+    if (rq && rk && rv) return 1;
+    if (!tyb_slots_ready(t, what)) return 0;
+    float *slot = tyb_row_slot(t, layer);
+    /* the slot's previous contents have been read (a deferred row is already in place) */
+    if (!tyb_cuda_ok(cudaEventSynchronize((cudaEvent_t)t->row_ev[layer]), what)) return 0;
+    if (!rk && k_new != slot) memcpy(slot, k_new, TYB_ROW_FLOATS * sizeof(float));
+    if (!rv && v_new != slot + TYB_ROW_FLOATS) memcpy(slot + TYB_ROW_FLOATS, v_new, TYB_ROW_FLOATS * sizeof(float));
+    if (!rq) memcpy(slot + 2 * TYB_ROW_FLOATS, q, TYB_Q_FLOATS * sizeof(float));
+    const size_t lo = (!rk || !rv) ? 0 : 2 * TYB_ROW_FLOATS, hi = !rq ? TYB_SLOT_FLOATS : 2 * TYB_ROW_FLOATS;
+    float *stage = t->d_kv_stage; /* >= 16 KB */
+    if (!tyb_cuda_ok(cudaMemcpyAsync(stage + lo, slot + lo, (hi - lo) * sizeof(float), cudaMemcpyHostToDevice,
+                                     (cudaStream_t)st),
+                     what) ||
+        !tyb_slot_consumed(t, layer, st, what))
+        return 0;
+    if (!rq) *dq = stage + 2 * TYB_ROW_FLOATS;
+    if (!rk) *dk = stage;
+    if (!rv) *dv = stage + TYB_ROW_FLOATS;
+    return 1;
+}
+
 void attention_decode_gqa(const float *q, const KVCache *cache, float *output, int layer_idx,
                           int kv_len, float scale)
 {
@@ -86,10 +127,20 @@ void attention_decode_gqa(const float *q, const KVCache *cache, float *output, i
         tyb_set_error("%s: kv_len %d out of range [0, %d]", what, kv_len, cache->max_seq_len);
         return;
     }
+    if (t->pending[layer_idx] >= 0 && t->pending[layer_idx] == kv_len - 1) {
+        /* The row kv_cache_append staged for this layer is the last one attended: append and
+         * attend in one launch (kernel/decoder.c:96-105), the row taken from its slot. */
+        const float *slot = tyb_row_slot(t, layer_idx);
+        t->pending[layer_idx] = -1;
+        decode_append_impl(q, slot, slot + TYB_ROW_FLOATS, (KVCache *)cache, output, layer_idx, scale, 0,
+                           KV_NUM_KV_HEADS, NULL, kv_len - 1, what);
+        return;
+    }
+    if (!tyb_flush_pending(t, layer_idx, what)) return;
     void *st = tyb_stream();
-    int qk = 0, ok = 0;
-    const float *dq = small_view(q, t->d_q, TYB_Q_FLOATS * sizeof(float), &qk, st, what);
-    if (!dq) return;
+    int ok = 0;
+    const float *dq = NULL, *unused_k, *unused_v;
+    if (kv_len > 0 && !stage_inputs(t, layer_idx, q, NULL, NULL, &dq, &unused_k, &unused_v, st, what)) return;
     float *dout = small_view(output, NULL, 0, &ok, st, what);
     if (ok < 0 || (ok == TYB_MEM_DEVICE && !dout)) return;
     if (ok == TYB_MEM_HOST) dout = t->d_out;
@@ -105,7 +156,7 @@ void attention_decode_gqa(const float *q, const KVCache *cache, float *output, i
         const tyb_seq_kv one = tyb_layer_rows(t, layer_idx, kv_len);
         const int early = tyb_prefetch_rows(cache, layer_idx, kv_len);
         if (!tyb_cuda_ok(decode_launch(dq, dout, NULL, one, 1, kv_len, t->dtype, scale, early, t->d_partials,
-                                       t->d_counters, qk != TYB_MEM_PINNED ? TYB_DEC_DEVICE_SMALL : 0, st),
+                                       t->d_counters, TYB_DEC_DEVICE_SMALL, st),
                          what))
             return;
         tyb_note_nowrite(st);
@@ -116,8 +167,8 @@ void attention_decode_gqa(const float *q, const KVCache *cache, float *output, i
                          what))
             return;
     }
-    /* Host buffers (pageable or page-locked): the call returns once the result is there. */
-    if (ok != TYB_MEM_DEVICE || qk != TYB_MEM_DEVICE) tyb_finish(st, what);
+    /* A host output (pageable or page-locked): the call returns once the result is there. */
+    if (ok != TYB_MEM_DEVICE) tyb_finish(st, what);
 }
 
 void attention_prefill_gqa(const float *q, const float *k, const float *v, float *output, int Sq,
@@ -206,6 +257,7 @@ void attention_chunked_prefill_gqa(const float *q, const KVCache *cache, float *
         tyb_set_error("%s: NULL q/output", what);
         return;
     }
+    if (!tyb_flush_pending(t, layer_idx, what)) return;
     void *st = tyb_stream();
     const size_t qb = (size_t)chunk_len * TYB_Q_FLOATS * sizeof(float);
     int qd = tyb_is_device_ptr(q), od = tyb_is_device_ptr(output);
@@ -261,7 +313,7 @@ int attention_decode_gqa_batched(const float *q, const KVCache *const *caches, c
     int dtype = -1, max_kv = 0, ok = 1;
     for (int b = 0; b < batch && ok; b++) {
         tyb_cache *t = tyb_cache_from(caches[b]);
-        if (!t) { ok = 0; break; }
+        if (!t || !tyb_flush_pending(t, layer_idx, what)) { ok = 0; break; }
         if (dtype >= 0 && t->dtype != dtype) {
             tyb_set_error("%s: caches mix element types", what);
             ok = 0;
@@ -336,8 +388,11 @@ int attention_decode_gqa_batched(const float *q, const KVCache *const *caches, c
 
 /* gather: NULL, or the connected output gather (the output is then the whole [16][128],
  * assembled from every rank's shard; see attn_gather_init). */
+/* pos_at: the row the new K/V go to, kv_len = pos_at + 1; -1 for cache->seq_len (then a deferred
+ * row of the layer is written first; >= 0 is the consumption of that row, staged by the caller). */
 static int decode_append_impl(const float *q, const float *k_new, const float *v_new, KVCache *cache, float *output,
-                              int layer_idx, float scale, int kvh0, int nkvh, const void *gather, const char *what)
+                              int layer_idx, float scale, int kvh0, int nkvh, const void *gather, int pos_at,
+                              const char *what)
 {
     tyb_cache *t = tyb_cache_from(cache);
     if (!t || !check_layer(layer_idx, what)) return 1;
@@ -345,18 +400,16 @@ static int decode_append_impl(const float *q, const float *k_new, const float *v
         tyb_set_error("%s: NULL q/k_new/v_new/output", what);
         return 1;
     }
-    const int pos = cache->seq_len;
+    if (pos_at < 0 && !tyb_flush_pending(t, layer_idx, what)) return 1;
+    const int pos = pos_at >= 0 ? pos_at : cache->seq_len;
     if (pos < 0 || pos >= cache->max_seq_len) {
         tyb_set_error("%s: row %d exceeds max_seq_len %d", what, pos, cache->max_seq_len);
         return 1;
     }
     void *st = tyb_stream();
-    int qk = 0, kk = 0, vk = 0, ok = 0;
-    const size_t row = TYB_ROW_FLOATS * sizeof(float);
-    const float *dq = small_view(q, t->d_q, TYB_Q_FLOATS * sizeof(float), &qk, st, what);
-    const float *dk = dq ? small_view(k_new, t->d_kv_stage, row, &kk, st, what) : NULL;
-    const float *dv = dk ? small_view(v_new, t->d_kv_stage + TYB_ROW_FLOATS, row, &vk, st, what) : NULL;
-    if (!dq || !dk || !dv) return 1;
+    int ok = 0;
+    const float *dq, *dk, *dv;
+    if (!stage_inputs(t, layer_idx, q, k_new, v_new, &dq, &dk, &dv, st, what)) return 1;
     float *dout = small_view(output, NULL, 0, &ok, st, what);
     /* rows of the query heads computed (all 16 when gathered from every rank) */
     const size_t out_floats = (size_t)2 * (gather ? KV_NUM_KV_HEADS : nkvh) * KV_HEAD_DIM;
@@ -365,11 +418,8 @@ static int decode_append_impl(const float *q, const float *k_new, const float *v
     const tyb_seq_kv one = tyb_layer_rows(t, layer_idx, pos + 1);
     const int early = tyb_prefetch_rows(cache, layer_idx, pos);
     if (!tyb_cuda_ok(tyb_decode_launch_heads(dq, dout, NULL, one, 1, pos + 1, t->dtype, scale, t->d_partials,
-                                             t->d_counters, dk, dv, early, kvh0, nkvh,
-                                             (qk != TYB_MEM_PINNED && kk != TYB_MEM_PINNED && vk != TYB_MEM_PINNED)
-                                                 ? TYB_DEC_DEVICE_SMALL
-                                                 : 0,
-                                             gather, st),
+                                             t->d_counters, dk, dv, early, kvh0, nkvh, TYB_DEC_DEVICE_SMALL, gather,
+                                             st),
                      what))
         return 1;
     if (gather && !tyb_cuda_ok(tyb_gather_wait_launch(dout, st), what)) return 1;
@@ -378,16 +428,16 @@ static int decode_append_impl(const float *q, const float *k_new, const float *v
                                                            cudaMemcpyDeviceToHost, (cudaStream_t)st),
                                            what))
         return 1;
-    /* Host buffers (pageable or page-locked): the call returns once the result is there. */
-    if (qk != TYB_MEM_DEVICE || kk != TYB_MEM_DEVICE || vk != TYB_MEM_DEVICE || ok != TYB_MEM_DEVICE)
-        return tyb_finish(st, what) ? 0 : 1;
+    /* A host output (pageable or page-locked): the call returns once the result is there.  Host
+     * inputs were copied before the launch (stage_inputs), so they need no wait. */
+    if (ok != TYB_MEM_DEVICE) return tyb_finish(st, what) ? 0 : 1;
     return 0;
 }
 
 int attention_decode_append_gqa(const float *q, const float *k_new, const float *v_new, KVCache *cache,
                                 float *output, int layer_idx, float scale)
 {
-    return decode_append_impl(q, k_new, v_new, cache, output, layer_idx, scale, 0, KV_NUM_KV_HEADS, NULL,
+    return decode_append_impl(q, k_new, v_new, cache, output, layer_idx, scale, 0, KV_NUM_KV_HEADS, NULL, -1,
                               "attention_decode_append_gqa");
 }
 
@@ -405,7 +455,7 @@ int attention_decode_append_gqa_heads(const float *q, const float *k_new, const 
 {
     const char *what = "attention_decode_append_gqa_heads";
     if (!check_heads(kv_head0, kv_heads, what)) return 1;
-    return decode_append_impl(q, k_new, v_new, cache, output, layer_idx, scale, kv_head0, kv_heads, NULL, what);
+    return decode_append_impl(q, k_new, v_new, cache, output, layer_idx, scale, kv_head0, kv_heads, NULL, -1, what);
 }
 
 int attn_gather_init(int rank, int world)
@@ -445,7 +495,7 @@ int attention_decode_append_gqa_gathered(const float *q, const float *k_new, con
         tyb_set_error("%s: the cache must hold BF16 rows", what);
         return 1;
     }
-    return decode_append_impl(q, k_new, v_new, cache, output, layer_idx, scale, kv_head0, kv_heads, g, what);
+    return decode_append_impl(q, k_new, v_new, cache, output, layer_idx, scale, kv_head0, kv_heads, g, -1, what);
 }
 
 int attention_decode_append_fused_gqa(const float *q_raw, const float *k_raw, const float *v_new,
@@ -465,6 +515,7 @@ int attention_decode_append_fused_gqa(const float *q_raw, const float *k_raw, co
         tyb_set_error("%s: row %d exceeds max_seq_len %d", what, pos, cache->max_seq_len);
         return 1;
     }
+    if (!tyb_flush_pending(t, layer_idx, what)) return 1;
     const void *ptrs[8] = {q_raw, k_raw, v_new, q_norm, k_norm, token_cos, token_sin, output};
     for (int i = 0; i < 8; i++) {
         const int d = ptrs[i] ? tyb_is_device_ptr(ptrs[i]) : 0;
@@ -513,6 +564,7 @@ static int prefill_fused_impl(const void *q_raw, const void *k_raw, const void *
         return 1;
     }
     if (seq_len == 0) return 0;
+    if (!tyb_flush_pending(t, layer_idx, what)) return 1;
     const void *ptrs[9] = {q_raw, k_raw, v_raw, q_norm, k_norm, token_cos, token_sin, output, NULL};
     for (int i = 0; i < 8; i++) {
         const int d = ptrs[i] ? tyb_is_device_ptr(ptrs[i]) : 0;

@@ -30,12 +30,32 @@ typedef struct {
     int device;              /* CUDA device current at allocation */
     size_t elem_bytes;       /* 4 or 2 */
     void *k_slab, *v_slab;   /* [28][8][max_seq][128] elements */
-    float *d_q;              /* [16][128] staging of a host query (decode) */
     float *d_out;            /* [16][128] staging of a host output (decode) */
-    float *d_kv_stage;       /* [2][max_seq][8][128] fp32 staging of host K/V rows */
+    float *d_kv_stage;       /* [2][max_seq][8][128] fp32 staging of host K/V rows (>= 16 KB); also the
+                              * device copy of a decode call's host inputs (one slot) */
     float *d_partials;       /* split-KV workspace of the decode kernel */
     unsigned int *d_counters;/* [8] split tickets, kept zero between launches */
+    /* Deferred single-row appends from host memory (kv_cache_append as kernel/decoder.c:96-100
+     * calls it): the row is copied here at once, and written to the cache by the next launch that
+     * touches its layer -- normally the attention_decode_gqa of the same step, which then appends
+     * and attends in one kernel. */
+    float *h_rows;           /* page-locked, device-mapped [28][4][1024]: per layer the staged K row, V
+                              * row, then room for a host query [16][128] copied beside them */
+    float *h_rows_dev;       /* its device view */
+    void *row_ev[KV_NUM_LAYERS]; /* cudaEvent_t: recorded after the launch that read the layer's slot */
+    int pending[KV_NUM_LAYERS];  /* row the layer's staged row goes to, or -1 */
 } tyb_cache;
+
+/* Writes (cache, layer)'s deferred row, if any, on the calling thread's stream; every path that
+ * reads or writes the layer's rows calls it first.  1 on success, else 0 with the error set. */
+int tyb_flush_pending(tyb_cache *t, int layer, const char *what);
+/* The layer's staging slot: K row [8][128], V row [8][128], query [16][128] (4096 floats). */
+#define TYB_SLOT_FLOATS (4 * TYB_ROW_FLOATS)
+static inline float *tyb_row_slot(const tyb_cache *t, int layer) { return t->h_rows + (size_t)layer * TYB_SLOT_FLOATS; }
+/* The slots (page-locked, device-mapped) and their events, set up on first use; 1 on success. */
+int tyb_slots_ready(tyb_cache *t, const char *what);
+/* Records the layer's "slot consumed" event after a launch that read the slot. */
+int tyb_slot_consumed(tyb_cache *t, int layer, void *stream, const char *what);
 
 /* The cache behind a KVCache*, or NULL (error set) if this library did not make it. */
 tyb_cache *tyb_cache_from(const KVCache *c);

@@ -35,11 +35,13 @@ static void cache_release(tyb_cache *t)
     if (!t) return;
     cudaFree(t->k_slab);
     cudaFree(t->v_slab);
-    cudaFree(t->d_q);
     cudaFree(t->d_out);
     cudaFree(t->d_kv_stage);
     cudaFree(t->d_partials);
     cudaFree(t->d_counters);
+    if (t->h_rows) cudaFreeHost(t->h_rows);
+    for (int l = 0; l < KV_NUM_LAYERS; l++)
+        if (t->row_ev[l]) cudaEventDestroy((cudaEvent_t)t->row_ev[l]);
     t->magic = 0;
     free(t);
 }
@@ -65,6 +67,7 @@ KVCache *kv_cache_alloc_ex(int max_seq_len, int kv_dtype)
     t->pub.max_seq_len = max_seq_len;
     t->pub.seq_len = 0;
     t->pub.rope_offset = 0;
+    for (int l = 0; l < KV_NUM_LAYERS; l++) t->pending[l] = -1;
     cudaGetDevice(&t->device);
     /* Kernels on this device may flag the status mirror from now on; without one (setup
      * failed) the blocking calls read the status word back each time instead. */
@@ -78,9 +81,10 @@ KVCache *kv_cache_alloc_ex(int max_seq_len, int kv_dtype)
     /* Any failure frees what was allocated and returns NULL (kernel/kv_cache.c:17-30). */
     int ok = tyb_dev_alloc(&t->k_slab, slab, "kv_cache_alloc: K slab") &&
              tyb_dev_alloc(&t->v_slab, slab, "kv_cache_alloc: V slab") &&
-             tyb_dev_alloc((void **)&t->d_q, TYB_Q_FLOATS * sizeof(float), "kv_cache_alloc: q") &&
              tyb_dev_alloc((void **)&t->d_out, TYB_Q_FLOATS * sizeof(float), "kv_cache_alloc: out") &&
-             tyb_dev_alloc((void **)&t->d_kv_stage, 2 * (size_t)max_seq_len * TYB_ROW_FLOATS * sizeof(float),
+             /* at least 16 KB: a deferred row with its query (TYB_SLOT_FLOATS) is staged here too */
+             tyb_dev_alloc((void **)&t->d_kv_stage,
+                           2 * (size_t)(max_seq_len < 2 ? 2 : max_seq_len) * TYB_ROW_FLOATS * sizeof(float),
                            "kv_cache_alloc: staging") &&
              tyb_dev_alloc((void **)&t->d_partials, part, "kv_cache_alloc: decode workspace") &&
              tyb_dev_alloc((void **)&t->d_counters, KV_NUM_KV_HEADS * sizeof(unsigned int),
@@ -119,7 +123,61 @@ void kv_cache_free(KVCache *c)
 
 void kv_cache_clear(KVCache *c)
 {
-    if (c) { c->seq_len = 0; c->rope_offset = 0; } /* kernel/kv_cache.c:48-51 */
+    if (!c) return;
+    tyb_cache *t = tyb_cache_from(c);
+    for (int l = 0; t && l < KV_NUM_LAYERS; l++) tyb_flush_pending(t, l, "kv_cache_clear");
+    c->seq_len = 0; /* kernel/kv_cache.c:48-51 */
+    c->rope_offset = 0;
+}
+
+/* The deferred-append staging (page-locked, mapped) and its per-layer events, on first use. */
+int tyb_slots_ready(tyb_cache *t, const char *what)
+{
+    if (t->h_rows) return 1;
+    void *p = NULL;
+    if (!tyb_host_alloc(&p, (size_t)KV_NUM_LAYERS * TYB_SLOT_FLOATS * sizeof(float),
+                        cudaHostAllocMapped | cudaHostAllocPortable, what))
+        return 0;
+    void *d = NULL;
+    if (!tyb_cuda_ok(cudaHostGetDevicePointer(&d, p, 0), what)) {
+        cudaFreeHost(p);
+        return 0;
+    }
+    for (int l = 0; l < KV_NUM_LAYERS; l++) {
+        cudaEvent_t ev;
+        if (!tyb_cuda_ok(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming), what)) {
+            for (int j = 0; j < l; j++) {
+                cudaEventDestroy((cudaEvent_t)t->row_ev[j]);
+                t->row_ev[j] = NULL;
+            }
+            cudaFreeHost(p);
+            return 0;
+        }
+        t->row_ev[l] = ev;
+    }
+    t->h_rows = (float *)p;
+    t->h_rows_dev = (float *)d;
+    return 1;
+}
+
+int tyb_slot_consumed(tyb_cache *t, int layer, void *stream, const char *what)
+{
+    return tyb_cuda_ok(cudaEventRecord((cudaEvent_t)t->row_ev[layer], (cudaStream_t)stream), what);
+}
+
+int tyb_flush_pending(tyb_cache *t, int layer, const char *what)
+{
+    const int pos = t->pending[layer];
+    if (pos < 0) return 1;
+    t->pending[layer] = -1;
+    void *st = tyb_stream();
+    const float *ks = t->h_rows_dev + (size_t)layer * TYB_SLOT_FLOATS; /* read over the bus */
+    void *kl = tyb_slab_head(t, t->k_slab, layer, 0), *vl = tyb_slab_head(t, t->v_slab, layer, 0);
+    if (!tyb_cuda_ok(tyb_kv_scatter_launch(ks, ks + TYB_ROW_FLOATS, kl, vl, t->pub.max_seq_len, pos, 1, t->dtype, st),
+                     what))
+        return 0;
+    tyb_note_write(&t->pub, layer, pos, st);
+    return tyb_slot_consumed(t, layer, st, what);
 }
 
 /* Rows [pos, pos+S) of `layer` from token-major k_new/v_new [S][8][128] fp32. */
@@ -144,6 +202,23 @@ static void append_rows(KVCache *c, int layer, const float *k_new, const float *
     }
     const int kd = tyb_is_device_ptr(k_new), vd = tyb_is_device_ptr(v_new);
     if (kd < 0 || vd < 0) return;
+    /* An earlier deferred row of this layer lands first (writes keep their order). */
+    if (!tyb_flush_pending(t, layer, what)) return;
+    if (S == 1 && !kd && !vd) {
+        /* One row from host memory, as kernel/decoder.c:96-100 appends each decode step: copied
+         * now into the layer's page-locked slot (the caller may reuse its buffers on return, as
+         * after the reference's memcpy), written to the cache by the next launch on this layer --
+         * attention_decode_gqa over seq_len + 1 rows appends and attends in one kernel. */
+        if (tyb_slots_ready(t, what)) {
+            if (!tyb_cuda_ok(cudaEventSynchronize((cudaEvent_t)t->row_ev[layer]), what)) return; /* slot free */
+            float *slot = tyb_row_slot(t, layer);
+            memcpy(slot, k_new, TYB_ROW_FLOATS * sizeof(float));
+            memcpy(slot + TYB_ROW_FLOATS, v_new, TYB_ROW_FLOATS * sizeof(float));
+            t->pending[layer] = pos;
+            return;
+        }
+        tyb_set_error(""); /* no page-locked slot: the row goes the direct way below */
+    }
     void *st = tyb_stream();
     const size_t bytes = (size_t)S * TYB_ROW_FLOATS * sizeof(float);
     const float *ks = k_new, *vs = v_new;
@@ -183,12 +258,18 @@ void kv_cache_advance(KVCache *c, int n)
     if (c->rope_offset > 0) c->rope_offset += n;
 }
 
+/* The rows behind these pointers include a deferred appended row once it is written: it is
+ * queued here, before the pointer is handed out. */
 const float *kv_cache_k(const KVCache *c, int layer, int head)
 {
+    tyb_cache *t = tyb_cache_from(c);
+    if (t && layer >= 0 && layer < KV_NUM_LAYERS) tyb_flush_pending(t, layer, "kv_cache_k");
     return c->layers[layer].heads[head].k; /* kernel/kv_cache.c:112-115 */
 }
 
 const float *kv_cache_v(const KVCache *c, int layer, int head)
 {
+    tyb_cache *t = tyb_cache_from(c);
+    if (t && layer >= 0 && layer < KV_NUM_LAYERS) tyb_flush_pending(t, layer, "kv_cache_v");
     return c->layers[layer].heads[head].v; /* kernel/kv_cache.c:117-120 */
 }
