@@ -130,11 +130,12 @@ int attention_decode_append_gqa_heads(const float *q, const float *k_new, const 
                                       int kv_head0, int kv_heads);
 
 /* Decode output gather over NVLink, without a collective library: attention_decode_append_gqa_heads
- * whose output is the whole [16][128] on every rank.  The CTA that finishes a head pair stores it
- * into every rank's exchange buffer (peer stores into memory mapped by CUDA IPC), the rank's last
- * one raises its flag there, and a one-block kernel waits (bounded; attn_last_error on timeout)
- * for all ranks' flags of the call and copies the result to `output`.  One rank per GPU on one
- * node, up to 8 ranks; every rank calls with the same layers in the same order.
+ * whose output is the whole [16][128] on every rank, in one launch.  The CTA that finishes a head
+ * pair stores it into every rank's exchange buffer (peer stores into memory mapped by CUDA IPC)
+ * and raises that head's flag there; the rank's last such CTA waits (bounded; attn_last_error on
+ * timeout) for all 8 heads' flags of the call and copies the result to `output`.  One rank per
+ * GPU on one node, up to 8 ranks; every rank calls with the same layers in the same order, and
+ * the ranks' KV-head ranges together cover the 8 heads.
  *   attn_gather_init(rank, world)   allocates this rank's exchange buffer on the current device
  *   attn_gather_handle(h)           writes its 64-byte CUDA IPC handle to h
  *   attn_gather_connect(handles)    handles: world x 64 bytes in rank order (exchanged by the

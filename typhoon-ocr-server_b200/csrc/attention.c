@@ -422,7 +422,6 @@ static int decode_append_impl(const float *q, const float *k_new, const float *v
                                              st),
                      what))
         return 1;
-    if (gather && !tyb_cuda_ok(tyb_gather_wait_launch(dout, st), what)) return 1;
     tyb_note_write(cache, layer_idx, pos, st);
     if (ok == TYB_MEM_HOST && !tyb_cuda_ok(cudaMemcpyAsync(output, dout, out_floats * sizeof(float),
                                                            cudaMemcpyDeviceToHost, (cudaStream_t)st),

@@ -88,7 +88,6 @@ int tyb_gather_init(int rank, int world);
 int tyb_gather_handle(void *handle_out);            /* 64-byte cudaIpcMemHandle_t */
 int tyb_gather_connect(const void *handles);         /* world x 64 bytes, rank order */
 const void *tyb_gather_dev(int *world, int *rank);   /* NULL until connected */
-int tyb_gather_wait_launch(float *out, void *stream);
 void tyb_gather_close(void);
 /* Encodes into `map` (a CUtensorMap: 128 bytes, 64-byte aligned) rows [0, rows) of the 8
  * heads of one layer's BF16 cache slab (head stride row_capacity rows) as a 3-D tensor

@@ -533,18 +533,19 @@ constexpr int kMmaStat = 64 + 256;  // floats: block maxima and sums [16][2] x 2
 // With the KV heads of one sequence split over N ranks, every rank needs the whole [16][128]
 // output of each decode call.  Instead of a separate collective per layer, the CTA that writes a
 // head pair's final output also stores it into every rank's exchange buffer (peer stores over
-// NVLink into memory mapped by CUDA IPC), and the last such CTA of the rank then raises the rank's
-// flag in every exchange buffer; a one-block wait kernel per rank waits for all ranks' flags
-// (bounded) and copies the assembled output to the caller.  Epochs (one per call, counted on
+// NVLink into memory mapped by CUDA IPC) and raises that head's flag there, after one
+// system-scope release fence.  The rank's last such CTA of the call (a device-scope ticket) then
+// waits, bounded, for all 8 heads' flags in its own buffer and copies the assembled output to the
+// caller -- inside the decode kernel, so a call is one launch.  Epochs (one per call, counted on
 // each rank) make the flags monotone, and the exchange buffer is double-buffered by epoch parity:
-// a rank can run at most one call ahead of another (its next wait needs the other's next
-// publication, which follows the other's current wait).
+// a rank can run at most one call ahead of another (its next call completes only once the other
+// has raised its flags of that call, which it does after completing the current one).
 
 constexpr int kGatherMaxRanks = 8;
 
 struct GatherBuf {                          // one per rank, in that rank's device memory
     float data[2][kHq][kD];                 // assembled outputs, by epoch parity
-    unsigned int flags[kGatherMaxRanks];    // flags[r]: last epoch rank r has published here
+    unsigned int flags[kHkv];               // flags[h]: last epoch whose head pair h is stored here
     unsigned int epoch;                     // calls this rank has completed (local)
     unsigned int done;                      // this rank's head pairs published in the current call
 };
@@ -562,39 +563,58 @@ __device__ __forceinline__ unsigned int ld_acquire_sys(const unsigned int* p)
     return v;
 }
 
-__device__ __forceinline__ void st_release_sys(unsigned int* p, unsigned int v)
+__device__ __forceinline__ void st_relaxed_sys(unsigned int* p, unsigned int v)
 {
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+    asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
-// Called by every thread of the CTA that has just written rows row0, row0 + 1 of this rank's
-// exchange slot data[epoch & 1]: copies them to the other ranks' slots and, for the rank's last
-// head pair of the call, raises the rank's flag everywhere (a system-scope acquire-release count
-// orders the peer stores of all the rank's CTAs before the flags).
-__device__ __forceinline__ void gather_publish(const GatherDev* g, int row0, int nkvh_local, unsigned int epoch)
+// Called by every thread of the CTA that has just written the rows of KV head kvh's query pair
+// into this rank's exchange slot data[epoch & 1]: stores them into every other rank's slot
+// (16-byte peer stores), then one system-scope release fence and the head's flag in every
+// buffer (plain relaxed stores: the fence orders the CTA's stores, made its own by the barrier,
+// before them).  The rank's last head pair of the call waits for all heads' flags in its own
+// buffer (bounded: a rank that never publishes raises TYB_STATUS_WAIT_TIMEOUT) and copies the
+// assembled [16][128] to `out`.
+__device__ __forceinline__ void gather_publish(const GatherDev* g, int kvh, int nkvh_local, unsigned int epoch,
+                                               float* out)
 {
+    __shared__ int s_last, s_fail;
     const int par = (int)(epoch & 1u);
+    GatherBuf* mine = g->buf[g->rank];
     __syncthreads();
-    const float* src = &g->buf[g->rank]->data[par][row0][0];
-    for (int i = threadIdx.x; i < 2 * kD; i += blockDim.x) {
-        const float v = src[i];
+    if (threadIdx.x < 2 * kD / 4) {
+        const float4 v = reinterpret_cast<const float4*>(&mine->data[par][kGroup * kvh][0])[threadIdx.x];
         for (int p = 0; p < g->world; p++)
-            if (p != g->rank) (&g->buf[p]->data[par][row0][0])[i] = v;
+            if (p != g->rank) reinterpret_cast<float4*>(&g->buf[p]->data[par][kGroup * kvh][0])[threadIdx.x] = v;
     }
     __syncthreads();
     if (threadIdx.x == 0) {
-        // Acquire-release at system scope: releases this CTA's peer stores (ordered by the barrier)
-        // and, for the last CTA, acquires the other CTAs' before the flags go out.
-        unsigned int old;
-        asm volatile("atom.acq_rel.sys.global.add.u32 %0, [%1], 1;"
-                     : "=r"(old)
-                     : "l"(&g->buf[g->rank]->done)
-                     : "memory");
-        if (old == (unsigned int)(nkvh_local - 1)) {
-            atomicExch(&g->buf[g->rank]->done, 0u);
-            for (int p = 0; p < g->world; p++) st_release_sys(&g->buf[p]->flags[g->rank], epoch);
+        asm volatile("fence.acq_rel.sys;" ::: "memory");
+        for (int p = 0; p < g->world; p++) st_relaxed_sys(&g->buf[p]->flags[kvh], epoch);
+        unsigned int t;
+        asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(t) : "l"(&mine->done) : "memory");
+        s_last = t == (unsigned int)(nkvh_local - 1);
+        if (s_last) mine->done = 0u;  // the next call's tickets come after this kernel has completed
+        s_fail = 0;
+    }
+    __syncthreads();
+    if (!s_last) return;
+    if (threadIdx.x < kHkv) {
+        const uint64_t t0 = globaltimer_ns();
+        while ((int)(ld_acquire_sys(&mine->flags[threadIdx.x]) - epoch) < 0) {
+            if (globaltimer_ns() - t0 > wait_limit_ns()) {
+                raise_status(TYB_STATUS_WAIT_TIMEOUT);
+                s_fail = 1;
+                break;
+            }
+            __nanosleep(32);
         }
     }
+    __syncthreads();
+    if (s_fail) return;
+    const float4* src = reinterpret_cast<const float4*>(&mine->data[par][0][0]);
+    for (int i = threadIdx.x; i < kHq * kD / 4; i += blockDim.x) reinterpret_cast<float4*>(out)[i] = __ldcg(src + i);
+    if (threadIdx.x == 0) mine->epoch = epoch;
 }
 
 struct DecodeMmaArgs {
@@ -1121,7 +1141,7 @@ __global__ void __launch_bounds__(NW * 32, 16 / NW)
             o_[0] = y0 * inv;
             o_[8] = y1 * inv;
         }
-        if (a.gather) gather_publish(a.gather, kGroup * kvh, gridDim.y, epoch);
+        if (a.gather) gather_publish(a.gather, kvh, gridDim.y, epoch, a.out);
         return;
     }
 
@@ -1151,7 +1171,7 @@ __global__ void __launch_bounds__(NW * 32, 16 / NW)
     if (!*last_flag) return;
     merge_records_direct(recs, nsplit, reinterpret_cast<float*>(Kt), out_pair);
     if (tid == 0) a.counters[b * kHkv + kvh] = 0u;
-    if (a.gather) gather_publish(a.gather, kGroup * kvh, gridDim.y, epoch);
+    if (a.gather) gather_publish(a.gather, kvh, gridDim.y, epoch, a.out);
 }
 
 // ---- streaming form: many waves (request batches, long sequences) ----------------------------
@@ -1453,7 +1473,7 @@ __global__ void __launch_bounds__(256, 2)
             o_[0] = y0 * inv;
             o_[8] = y1 * inv;
         }
-        if (a.gather) gather_publish(a.gather, kGroup * kvh, gridDim.y, epoch);
+        if (a.gather) gather_publish(a.gather, kvh, gridDim.y, epoch, a.out);
         return;
     }
     float* recs = a.partials + ((size_t)b * kHkv + kvh) * a.nsplit * kRec;  // a.nsplit: the record stride
@@ -1482,41 +1502,7 @@ __global__ void __launch_bounds__(256, 2)
     if (!*last_flag) return;
     merge_records_direct(recs, nspan, reinterpret_cast<float*>(smem), out_pair);
     if (tid == 0) a.counters[b * kHkv + kvh] = 0u;
-    if (a.gather) gather_publish(a.gather, kGroup * kvh, gridDim.y, epoch);
-}
-
-// Waits (bounded) until every rank has published this call's epoch into this rank's exchange
-// buffer, copies the assembled [16][128] output to `out`, and counts the call.  One block,
-// launched as a programmatic dependent of the decode kernel: it needs nothing of that kernel but
-// the flags (system-scope acquire), so it starts waiting at once, and it lets the next kernel's
-// CTAs launch at once (they wait for its completion in their own dependency wait).  The epoch it
-// reads was written by the previous call's wait kernel, complete before the decode kernel passed
-// its own dependency wait.
-__global__ void __launch_bounds__(256) gather_wait_kernel(const GatherDev* g, float* out)
-{
-    __shared__ int fail;
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-    GatherBuf* mine = g->buf[g->rank];
-    const unsigned int epoch = __ldcg(&mine->epoch) + 1u;
-    if (threadIdx.x == 0) fail = 0;
-    __syncthreads();
-    if (threadIdx.x < g->world) {
-        const uint64_t t0 = globaltimer_ns();
-        while ((int)(ld_acquire_sys(&mine->flags[threadIdx.x]) - epoch) < 0) {
-            if (globaltimer_ns() - t0 > wait_limit_ns()) {
-                raise_status(TYB_STATUS_WAIT_TIMEOUT);
-                fail = 1;
-                break;
-            }
-            __nanosleep(64);
-        }
-    }
-    __syncthreads();
-    if (fail) return;
-    const float* src = &mine->data[epoch & 1u][0][0];
-    for (int i = threadIdx.x; i < kHq * kD; i += blockDim.x) out[i] = __ldcg(src + i);
-    __syncthreads();
-    if (threadIdx.x == 0) mine->epoch = epoch;
+    if (a.gather) gather_publish(a.gather, kvh, gridDim.y, epoch, a.out);
 }
 
 // ---- host-side planning ----------------------------------------------------------------
@@ -2145,21 +2131,6 @@ extern "C" const void* tyb_gather_dev(int* world, int* rank)
     if (world) *world = g_gather.world;
     if (rank) *rank = g_gather.rank;
     return g_gather.dev;
-}
-
-extern "C" int tyb_gather_wait_launch(float* out, void* stream)
-{
-    if (!g_gather.connected) return (int)cudaErrorInvalidValue;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(1);
-    cfg.blockDim = dim3(256);
-    cfg.stream = (cudaStream_t)stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    return (int)cudaLaunchKernelEx(&cfg, gather_wait_kernel, (const GatherDev*)g_gather.dev, out);
 }
 
 extern "C" void tyb_gather_close(void)
