@@ -351,7 +351,7 @@ def time_long_context(pkg, lib, dctx, device, decode_steps=16):
     qn = 1.0 + 0.02 * torch.randn((D,), generator=gen, device=device)
     kn = 1.0 + 0.02 * torch.randn((D,), generator=gen, device=device)
     cos, sin = _rope_tables(pos, device)
-    part = torch.empty((2 * n, S, D), dtype=torch.bfloat16, device=device)
+    part = torch.empty((2 * n, S, D), dtype=torch.bfloat16, device=device) if world > 1 else None
     tokens = torch.empty((S, HQ, D), dtype=torch.bfloat16, device=device)
     cache = lib.kv_cache_alloc_ex(S + decode_steps + 8, pkg.ATTN_KV_BF16)
     if not cache:
@@ -362,14 +362,36 @@ def time_long_context(pkg, lib, dctx, device, decode_steps=16):
     lib.attn_set_stream(ctypes.c_void_p(stream.cuda_stream))
     vp = lambda t: ctypes.c_void_p(t.data_ptr())
 
+    # N > 1: the C-level shard set-up (IPC handles exchanged once, through torch.distributed);
+    # then no collective call on the data path.
+    grp = shard.ShardGroup(lib, max_tokens=S) if world > 1 else None
+    sharded_out = ctypes.c_void_p()
+
     def prefill():
+        """One GPU: attention_prefill_fused_gqa, token-major.  N GPUs: attention_prefill_fused_gqa_sharded,
+        whose epilogue stores every row into every rank's exchange slot (the assembled token-major
+        output, no all-gather call, no relayout)."""
+        cs.seq_len = 0
+        for layer in range(LAYERS):
+            if world > 1:
+                rc = lib.attention_prefill_fused_gqa_sharded(vp(q), vp(k), vp(v), pkg.ATTN_DT_BF16, vp(qn), vp(kn),
+                                                             vp(cos), vp(sin), cache, layer, S, scale, eps,
+                                                             ctypes.byref(sharded_out))
+            else:
+                rc = lib.attention_prefill_fused_gqa(vp(q), vp(k), vp(v), pkg.ATTN_DT_BF16, vp(qn), vp(kn), vp(cos),
+                                                     vp(sin), cache, layer, vp(tokens), pkg.ATTN_DT_BF16, S, scale, eps)
+            if rc:
+                raise RuntimeError(pkg.last_error(lib))
+
+    def prefill_nccl():
+        """For comparison (N > 1): head-major shards, NCCL all-gather, relayout."""
         cs.seq_len = 0
         for layer in range(LAYERS):
             if lib.attention_prefill_fused_gqa_heads(vp(q), vp(k), vp(v), pkg.ATTN_DT_BF16, vp(qn), vp(kn), vp(cos),
                                                      vp(sin), cache, layer, vp(part), pkg.ATTN_DT_BF16, S, scale,
                                                      eps, h0, n):
                 raise RuntimeError(pkg.last_error(lib))
-            full = shard.gather_heads(part) if world > 1 else part
+            full = shard.gather_heads(part)
             if lib.attn_heads_to_tokens(vp(full), vp(tokens), S, pkg.ATTN_DT_BF16):
                 raise RuntimeError(pkg.last_error(lib))
 
@@ -383,8 +405,8 @@ def time_long_context(pkg, lib, dctx, device, decode_steps=16):
         cs.seq_len = S + i
         for layer in range(LAYERS):
             if fused:  # the library's peer-store gather: the whole [16][128] output on every rank
-                rc = lib.attention_decode_append_gqa_gathered(vp(dq[layer]), vp(dk[layer]), vp(dv[layer]), cache,
-                                                              vp(dout), layer, scale, h0, n)
+                rc = lib.attention_decode_append_gqa_sharded(vp(dq[layer]), vp(dk[layer]), vp(dv[layer]), cache,
+                                                             vp(dout), layer, scale)
             else:      # one GPU: the shard is the whole output; else NCCL all-gather of the shards
                 rc = lib.attention_decode_append_gqa_heads(vp(dq[layer]), vp(dk[layer]), vp(dv[layer]), cache,
                                                            vp(dpart if world > 1 else dout), layer, scale, h0, n)
@@ -406,12 +428,16 @@ def time_long_context(pkg, lib, dctx, device, decode_steps=16):
 
     prefill()  # warm-up
     pf_ms = timed(prefill)
+    pf_nccl_ms = None
+    if world > 1:
+        prefill_nccl()
+        pf_nccl_ms = timed(prefill_nccl)
+        prefill()  # the sharded output of the last layer stays in its slot for the parity check
     # Decode: one graph per step (the step's kv_len is in the captured launch arguments),
     # captured on a side stream after an eager warm-up step (communicators set up).
     gstream = torch.cuda.Stream(device)
     gstream.wait_stream(stream)
     lib.attn_set_stream(ctypes.c_void_p(gstream.cuda_stream))
-    peers = shard.PeerGather(lib) if world > 1 else None
 
     def time_decode(fused):
         with torch.cuda.stream(gstream):
@@ -453,21 +479,22 @@ def time_long_context(pkg, lib, dctx, device, decode_steps=16):
         if world > 1:
             parity = long_context_parity(pkg, lib, dctx, device, decode_step, dout, gstream, dict(
                 q=q, k=k, v=v, qn=qn, kn=kn, cos=cos, sin=sin, dq=dq, dk=dk, dv=dv, S=S, steps=decode_steps,
-                tokens=tokens))
+                tokens=tokens, sharded_prefill=sharded_out.value))
     finally:
         torch.cuda.synchronize()
         dctx.barrier()
-        if peers is not None:
-            peers.close()
+        if grp is not None:
+            grp.close()
     lib.attn_set_stream(None)
     lib.kv_cache_free(cache)
     flops = LAYERS * 4.0 * D * HQ * S * (S + 1) / 2
     return {
         "workload": "config5: 32,768 tokens (30,000 vision 150x200 + 2,768 text), 28 layers, bf16, QK-RMSNorm + "
                     "M-RoPE fused; KV heads sharded over the GPUs; per layer the head outputs gathered on every "
-                    "rank (prefill: NCCL all-gather; decode: peer stores fused into the decode kernels)",
+                    "rank by peer stores fused into the prefill and decode kernels",
         "kv_heads_per_gpu": n,
         "prefill_ms": pf_ms, "prefill_tok_per_s": S / (pf_ms * 1e-3), "prefill_tflops": flops / (pf_ms * 1e-3) / 1e12,
+        "prefill_ms_nccl_allgather": pf_nccl_ms,
         "decode_us_per_step": dec_ms * 1e3 / decode_steps, "decode_steps": decode_steps,
         "parity": parity,
         "decode_gather": "peer stores over NVLink fused into the decode kernel (attention_decode_append_gqa_gathered)"
@@ -476,17 +503,21 @@ def time_long_context(pkg, lib, dctx, device, decode_steps=16):
         "decode_kv_len": f"{S + 1}..{S + decode_steps}",
         "allgather_bytes_per_layer": {"prefill": S * HQ * D * 2 if world > 1 else 0,
                                       "decode": HQ * D * 4 if world > 1 else 0},
-        "path": "prefill: attention_prefill_fused_gqa_heads + NCCL all_gather_into_tensor + attn_heads_to_tokens; "
-                "decode: attention_decode_append_gqa_gathered (N > 1) / attention_decode_append_gqa_heads",
+        "path": "N > 1: attn_shard_init once, then per layer attention_prefill_fused_gqa_sharded (output rows stored "
+                "into every rank's exchange buffer by the prefill epilogue) and attention_decode_append_gqa_sharded "
+                "(decode outputs gathered inside the decode kernel); prefill_ms_nccl_allgather: "
+                "attention_prefill_fused_gqa_heads + NCCL all_gather_into_tensor + attn_heads_to_tokens.  "
+                "N = 1: attention_prefill_fused_gqa, attention_decode_append_gqa_heads (all heads)",
     }
 
 
 def long_context_parity(pkg, lib, dctx, device, decode_step, dout, stream, d):
-    """What the sharded config-5 decode computes, checked after it was timed (N > 1): the last
+    """What the sharded config-5 path computes, checked after it was timed (N > 1): the last
     decode step once more through the fused peer-store gather and once through the NCCL
     all-gather -- bitwise equal on every rank -- and, on rank 0, against attention_decode_append_gqa
     over a full-head cache that went through the same prefill and decode steps on one GPU (the
-    same BF16 rows; the split-merge order differs, so within the FP32 bar).  Every rank takes the
+    same BF16 rows; the split-merge order differs, so within the FP32 bar); and rank 0's assembled
+    output of the sharded prefill (last layer) against attention_prefill_fused_gqa, bit for bit.  Every rank takes the
     same collective steps.  Returns a dict with the verdict and the errors."""
     import torch
     last = d["steps"] - 1
@@ -500,6 +531,7 @@ def long_context_parity(pkg, lib, dctx, device, decode_step, dout, stream, d):
         raise RuntimeError(pkg.last_error(lib))
     bitwise = bool(torch.equal(out_fused, out_nccl))
     e_max = e_rel = 0.0
+    prefill_bitwise = True
     if dctx.rank == 0:
         S, vp = d["S"], (lambda t: ctypes.c_void_p(t.data_ptr()))
         full = lib.kv_cache_alloc_ex(S + d["steps"] + 8, pkg.ATTN_KV_BF16)
@@ -515,6 +547,14 @@ def long_context_parity(pkg, lib, dctx, device, decode_step, dout, stream, d):
                                                    vp(d["kn"]), vp(d["cos"]), vp(d["sin"]), full, layer,
                                                    vp(d["tokens"]), pkg.ATTN_DT_BF16, S, scale, eps):
                     raise RuntimeError(pkg.last_error(lib))
+            torch.cuda.synchronize()
+            # the sharded prefill's assembled output (last layer) against the unsharded one
+            shp = torch.empty_like(d["tokens"])
+            cudart = ctypes.CDLL("libcudart.so.12")
+            cudart.cudaMemcpy.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int]
+            if cudart.cudaMemcpy(shp.data_ptr(), d["sharded_prefill"], shp.numel() * 2, 3):
+                raise RuntimeError("copy of the sharded prefill output failed")
+            prefill_bitwise = bool(torch.equal(shp, d["tokens"]))
             for i in range(d["steps"]):
                 cs.seq_len = S + i
                 for layer in range(LAYERS):
@@ -528,10 +568,11 @@ def long_context_parity(pkg, lib, dctx, device, decode_step, dout, stream, d):
         diff = (out_fused - ref).double()
         e_max = float(diff.abs().max())
         e_rel = float(diff.norm() / ref.double().norm())
-    ok_local = bitwise and e_max <= 2e-3 and e_rel <= 1e-3
+    ok_local = bitwise and prefill_bitwise and e_max <= 2e-3 and e_rel <= 1e-3
     ok_all = dctx.max(0.0 if ok_local else 1.0) == 0.0
     return {"pass": ok_all, "fused_vs_nccl_bitwise_all_ranks": dctx.max(0.0 if bitwise else 1.0) == 0.0,
             "rank0_vs_unsharded": {"max_abs": e_max, "rel_l2": e_rel, "tolerance": [2e-3, 1e-3]},
+            "rank0_sharded_prefill_vs_unsharded_bitwise": prefill_bitwise,
             "what": "layer 27 output of decode step kv_len " + str(d["S"] + d["steps"])}
 
 

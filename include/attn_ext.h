@@ -4,6 +4,8 @@
  * have no error channel, kernel/attention.h:11,26,39).
  */
 #pragma once
+#include <stddef.h>
+
 #include "kv_cache.h"
 
 #ifdef __cplusplus
@@ -150,6 +152,42 @@ int  attn_gather_connect(const void *handles);
 void attn_gather_close(void);
 int  attention_decode_append_gqa_gathered(const float *q, const float *k_new, const float *v_new, KVCache *cache,
                                           float *output, int layer_idx, float scale, int kv_head0, int kv_heads);
+
+/* ---- KV-head sharding set up from C (one rank per GPU on one node) ----------------------
+ * The pieces above, tied together without a collective library:
+ *
+ * attn_allgather_fn: an all-gather the caller supplies -- `bytes` bytes from every rank, written
+ * to recv in rank order (recv[r * bytes ..] = rank r's send) -- e.g. MPI_Allgather, a TCP store, or
+ * torch.distributed.  Called once, by attn_shard_init, for 128 bytes per rank.  0 on success.
+ *
+ * attn_shard_init(rank, nranks, max_tokens, allgather, user): rank `rank` of `nranks` (1, 2, 4
+ * or 8) owns KV heads [8 rank / nranks, 8 (rank + 1) / nranks).  Allocates on the current device
+ * the decode output exchange and a prefill output exchange for sequences of up to max_tokens
+ * tokens (2 x max_tokens x 4 KB: two BF16 slots), exchanges the CUDA IPC handles through
+ * `allgather` and maps every peer's buffers.  Every rank calls it, then makes the same calls in
+ * the same order.  0 on success.  attn_shard_close(): after all calls have completed.
+ * attn_shard_heads: this rank's KV heads.
+ *
+ * attention_prefill_fused_gqa_sharded: attention_prefill_fused_gqa_heads for this rank's KV heads
+ * (raw inputs as there; BF16 cache), whose tensor-core kernel stores every output row, token-major
+ * BF16, into the exchange buffer of EVERY rank (peer stores over NVLink from the epilogue that
+ * produces it) and returns once all ranks' rows are in place: *output receives this rank's
+ * device address of the assembled [seq_len][16][128] BF16 output, valid until the call after
+ * next (two slots).  seq_len <= max_tokens.  Calls count on the host: not for CUDA graph
+ * capture.  0 on success.
+ *
+ * attention_decode_append_gqa_sharded: attention_decode_append_gqa_gathered for this rank's KV
+ * heads (output [16][128] on every rank).  0 on success. */
+typedef int (*attn_allgather_fn)(const void *send, void *recv, size_t bytes, void *user);
+int  attn_shard_init(int rank, int nranks, int max_tokens, attn_allgather_fn allgather, void *user);
+void attn_shard_close(void);
+int  attn_shard_heads(int *kv_head0, int *kv_heads);
+int  attention_prefill_fused_gqa_sharded(const void *q_raw, const void *k_raw, const void *v_raw, int in_dtype,
+                                         const float *q_norm, const float *k_norm, const float *token_cos,
+                                         const float *token_sin, KVCache *cache, int layer_idx, int seq_len,
+                                         float scale, float eps, void **output);
+int  attention_decode_append_gqa_sharded(const float *q, const float *k_new, const float *v_new, KVCache *cache,
+                                         float *output, int layer_idx, float scale);
 
 /* Gathered head-major [16][seq_len][128] -> token-major [seq_len][16][128], in dtype
  * (ATTN_DT_F32 or ATTN_DT_BF16); device memory, queued on the library stream.  0 on success. */

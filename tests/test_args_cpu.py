@@ -102,3 +102,19 @@ def test_wait_limit_and_reserve_reject_bad_arguments(pl):
     assert "below" in _err(pkg, lib)
     assert lib.attn_workspace_reserve(-1, 0, 0) != 0
     assert "negative" in _err(pkg, lib)
+
+
+def test_shard_init_rejects_bad_arguments(pl):
+    import ctypes as C
+    pkg, lib = pl
+    cb = pkg.ALLGATHER_FN(lambda s, r, n, u: 0)
+    p = C.cast(cb, C.c_void_p)
+    lib.attn_clear_error()
+    assert lib.attn_shard_init(0, 3, 0, p, None) != 0  # 3 ranks do not divide the 8 KV heads
+    assert "nranks" in _err(pkg, lib)
+    assert lib.attn_shard_init(2, 2, 0, p, None) != 0
+    assert "rank" in _err(pkg, lib)
+    assert lib.attn_shard_init(0, 2, 0, None, None) != 0  # no exchange callback
+    assert "callback" in _err(pkg, lib)
+    assert lib.attn_shard_heads(None, None) != 0  # nothing set up
+    assert "attn_shard_init" in _err(pkg, lib)

@@ -130,7 +130,17 @@ _SIGNATURES = {
     "attn_gather_close": (None, []),
     "attention_decode_append_gqa_gathered": (ctypes.c_int, [_VP, _VP, _VP, _VP, _VP, ctypes.c_int, ctypes.c_float,
                                                             ctypes.c_int, ctypes.c_int]),
+    "attn_shard_init": (ctypes.c_int, [ctypes.c_int, ctypes.c_int, ctypes.c_int, _VP, _VP]),
+    "attn_shard_close": (None, []),
+    "attn_shard_heads": (ctypes.c_int, [_VP, _VP]),
+    "attention_prefill_fused_gqa_sharded": (ctypes.c_int, [_VP, _VP, _VP, ctypes.c_int, _VP, _VP, _VP, _VP, _VP,
+                                                           ctypes.c_int, ctypes.c_int, ctypes.c_float, ctypes.c_float,
+                                                           _VP]),
+    "attention_decode_append_gqa_sharded": (ctypes.c_int, [_VP, _VP, _VP, _VP, _VP, ctypes.c_int, ctypes.c_float]),
 }
+
+# The all-gather callback of attn_shard_init: (send, recv, bytes, user) -> 0 on success.
+ALLGATHER_FN = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p)
 
 
 def declared_symbols():

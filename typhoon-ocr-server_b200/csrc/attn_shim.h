@@ -111,6 +111,19 @@ int tyb_heads_to_tokens_launch(const void *src, void *dst, int S, int elem_bytes
 
 /* ---- tensor-core prefill (prefill_tc.cu) ---------------------------------------------- */
 
+/* Prefill output exchange of KV-head sharding (shard.c): every rank's buffer is a header of
+ * TYB_PX_HEADER_BYTES (flags[8]: the last call whose output rank r has stored here; then the
+ * rank's count of finished work items of the current call) followed by two token-major
+ * [max_tokens][16][128] BF16 slots, used by call parity.  The device table lists the buffers of
+ * all ranks (peers' through CUDA IPC). */
+#define TYB_PX_HEADER_BYTES 256
+typedef struct {
+    void *base[8];
+    int rank;
+    int world;
+    long long slot_elems; /* max_tokens * 16 * 128 */
+} tyb_prefill_x;
+
 /* Raw K/V rows [S][8][128] (fp32, or bf16 when in_bf16) -> BF16 cache rows [pos0, pos0+S) of
  * one layer (layout of tyb_seq_kv): K through RMSNorm(k_norm) and rotate_half M-RoPE with the
  * per-token cos/sin [S][64]; V as is.  KV heads [kvh0, kvh0 + nkvh) only. */
@@ -124,11 +137,13 @@ int tyb_kv_prep_launch(const void *k_raw, const void *v_raw, int in_bf16, const 
  * Output [Sq][16][128], or with out_head_major the shard [2 nkvh][Sq][128]; fp32 or bf16.
  * Launched as a programmatic dependent of the previous kernel in the stream, which must be the
  * tyb_kv_prep_launch of the same rows (it starts before that kernel completes; its TMA producer
- * waits for it before reading the cache). */
+ * waits for it before reading the cache).  * xchg_dev (device table, or NULL): the output rows go, token-major BF16, into slot (epoch & 1)
+ * of EVERY rank's exchange buffer instead of `out`, and the kernel returns only once all ranks'
+ * rows of call `epoch` are in this rank's buffer (bounded wait). */
 int tyb_prefill_tc_launch(const void *q, int q_bf16, const float *q_norm, const float *cos, const float *sin,
                           const void *k_cache, const void *v_cache, int row_capacity, void *out, int out_bf16,
                           int Sq, int pos_offset, float scale, float eps, int kvh0, int nkvh, int out_head_major,
-                          void *stream);
+                          const tyb_prefill_x *xchg_dev, unsigned int epoch, void *stream);
 
 /* ---- tensor-core prefill at the FP32 bar (prefill_tc32.cu) ----------------------------- */
 

@@ -67,6 +67,8 @@ struct PrefillTcArgs {
     int kvh0;              // KV heads [kvh0, kvh0 + nkvh) (and their query heads) are computed
     int nkvh;
     int out_head_major;    // output [2 nkvh][Sq][128] (a contiguous head shard) instead of [Sq][16][128]
+    const tyb_prefill_x* xchg;  // non-NULL: BF16 rows into every rank's exchange slot (KV-head sharding)
+    unsigned int epoch;    // the call's number (1, 2, ...): slot epoch & 1, flags compared to it
     unsigned int* status;  // the library's status word (tyb_status_word)
     unsigned int* mirror;  // its page-locked host mirror flag (tyb_status_mirror_device), or NULL
     unsigned long long wait_ns;  // limit of every bounded wait (tyb_wait_limit)
@@ -482,7 +484,23 @@ __global__ void __launch_bounds__(kPtThreads, 1)
             for (int c = 0; c < 4; c++) {
                 float v[32];
                 tmem_ld32(o_addr + c * 32, v);
-                if (tok < a.Sq) {
+                if (tok < a.Sq && a.xchg) {
+                    // Sharded: the row, token-major BF16, into this call's slot of every rank's
+                    // exchange buffer (peer stores over NVLink) -- the all-gather of the head
+                    // outputs done by the epilogue that produces them.
+                    uint4 u[4];
+#pragma unroll
+                    for (int i = 0; i < 32; i += 8)
+                        u[i / 8] = make_uint4(pack_bf16x2(v[i] * inv, v[i + 1] * inv), pack_bf16x2(v[i + 2] * inv, v[i + 3] * inv),
+                                              pack_bf16x2(v[i + 4] * inv, v[i + 5] * inv), pack_bf16x2(v[i + 6] * inv, v[i + 7] * inv));
+                    const size_t slot = (size_t)(a.epoch & 1u) * (size_t)a.xchg->slot_elems + ooff + c * 32;
+                    for (int p = 0; p < a.xchg->world; p++) {
+                        uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.xchg->base[p]) +
+                                                              TYB_PX_HEADER_BYTES / 2 + slot);
+#pragma unroll
+                        for (int i = 0; i < 4; i++) dst[i] = u[i];
+                    }
+                } else if (tok < a.Sq) {
                     if (a.out_bf16) {
                         __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(a.out) + ooff + c * 32;
 #pragma unroll
@@ -509,6 +527,39 @@ __global__ void __launch_bounds__(kPtThreads, 1)
     if (warp == 8) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem) : "memory");
+    }
+    if (a.xchg && tid == 0) {
+        // Sharded completion: one system-scope release fence makes this CTA's peer stores (its
+        // threads' own through the barrier above) visible before its count; the rank's last item
+        // raises the rank's flag in every buffer, then waits -- bounded -- for every rank's flag
+        // of this call in its own buffer.  The kernel ends once the assembled output is here.
+        unsigned int* hdr = static_cast<unsigned int*>(a.xchg->base[a.xchg->rank]);
+        asm volatile("fence.acq_rel.sys;" ::: "memory");
+        unsigned int t;
+        asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(t) : "l"(hdr + 8) : "memory");
+        if (t == gridDim.x - 1) {
+            hdr[8] = 0u;  // the next call's counts come after this kernel has completed
+            asm volatile("fence.acq_rel.sys;" ::: "memory");
+            for (int p = 0; p < a.xchg->world; p++) {
+                unsigned int* f = static_cast<unsigned int*>(a.xchg->base[p]) + a.xchg->rank;
+                asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(f), "r"(a.epoch) : "memory");
+            }
+            const uint64_t t0 = globaltimer_ns();
+            for (int r = 0; r < a.xchg->world; r++) {
+                unsigned int seen;
+                while (true) {
+                    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(seen) : "l"(hdr + r) : "memory");
+                    if ((int)(seen - a.epoch) >= 0) break;
+                    if (globaltimer_ns() - t0 > a.wait_ns) {
+                        atomicOr(a.status, TYB_STATUS_WAIT_TIMEOUT);
+                        flag_mirror(a.mirror);
+                        r = a.xchg->world;
+                        break;
+                    }
+                    __nanosleep(64);
+                }
+            }
+        }
     }
 }
 
@@ -640,7 +691,8 @@ extern "C" int tyb_kv_prep_launch(const void* k_raw, const void* v_raw, int in_b
 extern "C" int tyb_prefill_tc_launch(const void* q, int q_bf16, const float* q_norm, const float* cos,
                                      const float* sin, const void* k_cache, const void* v_cache, int row_capacity,
                                      void* out, int out_bf16, int Sq, int pos_offset, float scale, float eps,
-                                     int kvh0, int nkvh, int out_head_major, void* stream)
+                                     int kvh0, int nkvh, int out_head_major, const tyb_prefill_x* xchg_dev,
+                                     unsigned int epoch, void* stream)
 {
     if (Sq <= 0 || nkvh <= 0) return 0;
     // Once per device: the shared-memory opt-in, and a check that the kernel was compiled
@@ -677,6 +729,8 @@ extern "C" int tyb_prefill_tc_launch(const void* q, int q_bf16, const float* q_n
     a.kvh0 = kvh0;
     a.nkvh = nkvh;
     a.out_head_major = out_head_major;
+    a.xchg = xchg_dev;
+    a.epoch = epoch;
     a.status = tyb_status_word();
     if (!a.status) return (int)cudaErrorInvalidSymbol;
     a.mirror = tyb_status_mirror_device();

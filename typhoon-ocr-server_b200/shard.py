@@ -89,3 +89,44 @@ class PeerGather:
         if self.lib is not None:
             self.lib.attn_gather_close()
             self.lib = None
+
+
+class ShardGroup:
+    """attn_shard_init for the ranks of a torch.distributed group: the library's all-gather
+    callback is served by torch.distributed (any backend; host bytes).  Afterwards
+    attention_prefill_fused_gqa_sharded / attention_decode_append_gqa_sharded run this rank's KV
+    heads and leave the whole output on every rank, with no collective call.  close() after the
+    last call has completed.  (A C caller passes its own callback -- MPI, a TCP store, ...)"""
+
+    def __init__(self, lib, max_tokens, group=None):
+        import ctypes
+
+        import torch.distributed as dist
+
+        self.lib = lib
+        self.group = group
+        rank, world = dist.get_rank(group), dist.get_world_size(group)
+
+        def allgather(send, recv, nbytes, user):
+            try:
+                mine = ctypes.string_at(send, nbytes)
+                parts = [None] * world
+                dist.all_gather_object(parts, mine, group=group)
+                blob = b"".join(parts)
+                ctypes.memmove(recv, blob, len(blob))
+                return 0
+            except Exception:  # noqa: BLE001 -- reported to the library as a failed exchange
+                return 1
+
+        pkg = __import__(__name__.rsplit(".", 1)[0])
+        self._cb = pkg.ALLGATHER_FN(allgather)  # kept alive while the library may call it
+        if lib.attn_shard_init(rank, world, int(max_tokens), ctypes.cast(self._cb, ctypes.c_void_p), None):
+            raise RuntimeError((lib.attn_last_error() or b"").decode())
+        h0, n = ctypes.c_int(), ctypes.c_int()
+        lib.attn_shard_heads(ctypes.byref(h0), ctypes.byref(n))
+        self.kv_head0, self.kv_heads = h0.value, n.value
+
+    def close(self):
+        if self.lib is not None:
+            self.lib.attn_shard_close()
+            self.lib = None
