@@ -975,6 +975,8 @@ def run_case(case):
       prefill-small  4 passes of one config-3 layer (4,096 tokens) through attention_prefill_fused_gqa
       batched-small  4 request-batch launches (the streaming form) over 6 sequences of config 4's
                      seeded ragged list, alternating two layers (~230 MB of K/V: larger than L2)
+      prefill32-small 4 drop-in FP32 prefills (attention_prefill_gqa: kv_split_kernel +
+                     prefill_tc32_kernel) of 4,096 tokens, device buffers (64 MB of inputs)
     """
     import torch
     pkg = _pkg()
@@ -1026,6 +1028,19 @@ def run_case(case):
             lib.kv_cache_free(c)
         print(json.dumps({"case": case, "status": "ok"}))
         return
+    elif case == "prefill32-small":
+        S = 4096
+        q = torch.randn((S, HQ, D), generator=gen, device="cuda")
+        k = torch.randn((S, HKV, D), generator=gen, device="cuda")
+        v = torch.randn((S, HKV, D), generator=gen, device="cuda")
+        out = torch.empty_like(q)
+        for _ in range(4):
+            lib.attention_prefill_gqa(vp(q), vp(k), vp(v), vp(out), S, S, ctypes.c_float(pkg.SCALE), None, None, None,
+                                      None)
+        pkg.check(lib, "prefill32-small")
+        torch.cuda.synchronize()
+        print(json.dumps({"case": case, "status": "ok"}))
+        return
     elif case == "prefill-small":
         S = 4096
         q = (0.5 * torch.randn((S, HQ, D), generator=gen, device="cuda")).bfloat16()
@@ -1062,7 +1077,7 @@ def main():
     ap.add_argument("--prefill-pages", type=int, default=20)
     ap.add_argument("--long-context", type=int, default=1, help="run the config-5 section (1) or not (0)")
     ap.add_argument("--batched", type=int, default=1, help="run the config-4 section (1) or not (0)")
-    ap.add_argument("--case", choices=["decode-small", "prefill-small", "batched-small"],
+    ap.add_argument("--case", choices=["decode-small", "prefill-small", "batched-small", "prefill32-small"],
                     help="run a small fixed invocation of one kernel (for profiler captures) and exit")
     args = ap.parse_args()
     if args.case:
