@@ -29,8 +29,9 @@ pytestmark = pytest.mark.gpu
 SCALE = ctypes.c_float(0.08838834764831843)
 EPS = ctypes.c_float(1e-6)
 LAYER = 7
-# the tensor-core prefill against the oracle fed the same BF16-rounded operands
-TOL_TC_MAX, TOL_TC_REL = 1e-2, 4e-3
+# the tensor-core prefill against the oracle fed the same BF16-rounded operands (the bar of
+# test_prefill_tc_gpu.py; measured here 1.5e-3 / 1.2e-3)
+TOL_TC_MAX, TOL_TC_REL = 4e-3, 2.6e-3
 
 
 def _config1(pkg):

@@ -2,10 +2,13 @@
 M-RoPE fused, through attention_prefill_fused_gqa, against the oracle running the same chain
 (kernel/decoder.c:73-117: RMSNorm, M-RoPE, append, attention).
 
-Tolerances of the BF16 path (written here): against the oracle fed the same BF16-rounded
-normalised q, k and v, max-abs TOL_TC_MAX and rel-L2 TOL_TC_REL -- what remains is the BF16
-rounding of the softmax weights P before the P.V product and the order of FP32 sums;
-against the unrounded FP32 chain, the looser TOL_TC32_*.
+Tolerances of the BF16 path (written here), about twice the largest errors measured on a B200
+over these tests: against the oracle fed the same BF16-rounded normalised q, k and v, max-abs
+TOL_TC_MAX and rel-L2 TOL_TC_REL (measured at most 1.9e-3 / 1.3e-3 with FP32 output) -- what remains
+is the BF16 rounding of the softmax weights P before the P.V product and the order of FP32 sums --
+plus TOL_OUT_BF16_* when the output is rounded to BF16 too (measured at most 5.1e-3 / 2.0e-3 in all);
+against the unrounded FP32 chain, TOL_TC32_* (measured at most 7.5e-3 / 2.9e-3 with FP32 output,
+4.4e-3 / 3.0e-3 for config 3 with BF16 inputs and output).
 """
 
 import ctypes
@@ -21,8 +24,9 @@ from oracle import max_abs, rel_l2
 pytestmark = pytest.mark.gpu
 SCALE = ctypes.c_float(0.08838834764831843)
 EPS = ctypes.c_float(1e-6)
-TOL_TC_MAX, TOL_TC_REL = 1e-2, 4e-3
-TOL_TC32_MAX, TOL_TC32_REL = 5e-2, 1.5e-2
+TOL_TC_MAX, TOL_TC_REL = 4e-3, 2.6e-3
+TOL_OUT_BF16_MAX, TOL_OUT_BF16_REL = 6e-3, 1.6e-3
+TOL_TC32_MAX, TOL_TC32_REL = 1.5e-2, 6e-3
 
 
 def _inputs(pkg, S, seed, grid=None):
@@ -94,8 +98,11 @@ def test_fused_prefill_sizes(pkg, lib, oracle, S, in_bf16, out_bf16):
     finally:
         lib.kv_cache_free(h)
     exact, fp32, _ = _expect(oracle, q, k, v, qn, kn, cos, sin, in_bf16)
-    tol_max = TOL_TC_MAX + (1e-2 if out_bf16 else 0.0)  # one more BF16 rounding of the output
-    assert max_abs(out, exact) <= tol_max and rel_l2(out, exact) <= TOL_TC_REL + (4e-3 if out_bf16 else 0.0)
+    print(f"S={S} in_bf16={in_bf16} out_bf16={out_bf16}: vs rounded max {max_abs(out, exact):.3e} "
+          f"rel {rel_l2(out, exact):.3e}; vs fp32 max {max_abs(out, fp32):.3e} rel {rel_l2(out, fp32):.3e}")
+    tol_max = TOL_TC_MAX + (TOL_OUT_BF16_MAX if out_bf16 else 0.0)  # one more BF16 rounding of the output
+    tol_rel = TOL_TC_REL + (TOL_OUT_BF16_REL if out_bf16 else 0.0)
+    assert max_abs(out, exact) <= tol_max and rel_l2(out, exact) <= tol_rel
 
 
 @pytest.mark.parametrize("off,S", [(1, 1), (100, 30), (128, 128), (300, 200), (1000, 129)])
@@ -119,6 +126,7 @@ def test_fused_prefill_chunked(pkg, lib, oracle, off, S):
     ck = head_first(bf16_round(np.concatenate([k_old, kr])))
     cv = head_first(bf16_round(np.concatenate([v_old, v])))
     exact = oracle.chunked_prefill(bf16_round(qr), ck, cv, off)
+    print(f"chunked off={off} S={S}: max {max_abs(out, exact):.3e} rel {rel_l2(out, exact):.3e}")
     assert max_abs(out, exact) <= TOL_TC_MAX and rel_l2(out, exact) <= TOL_TC_REL
 
 
@@ -133,7 +141,9 @@ def test_fused_prefill_config3(pkg, lib, oracle):
     finally:
         lib.kv_cache_free(h)
     exact, fp32, _ = _expect(oracle, q, k, v, qn, kn, cos, sin, True)
-    assert max_abs(out, exact) <= TOL_TC_MAX + 1e-2 and rel_l2(out, exact) <= TOL_TC_REL + 4e-3
+    print(f"config3: vs rounded max {max_abs(out, exact):.3e} rel {rel_l2(out, exact):.3e}; "
+          f"vs fp32 max {max_abs(out, fp32):.3e} rel {rel_l2(out, fp32):.3e}")
+    assert max_abs(out, exact) <= TOL_TC_MAX + TOL_OUT_BF16_MAX and rel_l2(out, exact) <= TOL_TC_REL + TOL_OUT_BF16_REL
     assert max_abs(out, fp32) <= TOL_TC32_MAX and rel_l2(out, fp32) <= TOL_TC32_REL
 
 
