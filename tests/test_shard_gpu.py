@@ -64,7 +64,9 @@ def test_prefill_shards_equal_unsharded(pkg, lib, oracle, S, off):
         lib.kv_cache_free(h)
 
 
-@pytest.mark.parametrize("kv_len", [1, 700, 4097])
+# 20,000 and 33,000 rows: a head's splits merged by one CTA from L2 (8 heads), through shared
+# memory (33-64 records: 4 heads) and in two levels (more than 64: 1 and 2 heads)
+@pytest.mark.parametrize("kv_len", [1, 700, 4097, 20000, 33000])
 def test_decode_shards_equal_unsharded(pkg, lib, kv_len):
     shard = importlib.import_module(pkg.__name__ + ".shard")
     pos = kv_len - 1

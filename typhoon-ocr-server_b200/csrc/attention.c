@@ -156,7 +156,7 @@ void attention_decode_gqa(const float *q, const KVCache *cache, float *output, i
         const tyb_seq_kv one = tyb_layer_rows(t, layer_idx, kv_len);
         const int early = tyb_prefetch_rows(cache, layer_idx, kv_len);
         if (!tyb_cuda_ok(decode_launch(dq, dout, NULL, one, 1, kv_len, t->dtype, scale, early, t->d_partials,
-                                       t->d_counters, TYB_DEC_DEVICE_SMALL, st),
+                                       t->d_counters, TYB_DEC_DEVICE_SMALL | TYB_DEC_WIDE_COUNTERS, st),
                          what))
             return;
         tyb_note_nowrite(st);
@@ -418,7 +418,8 @@ static int decode_append_impl(const float *q, const float *k_new, const float *v
     const tyb_seq_kv one = tyb_layer_rows(t, layer_idx, pos + 1);
     const int early = tyb_prefetch_rows(cache, layer_idx, pos);
     if (!tyb_cuda_ok(tyb_decode_launch_heads(dq, dout, NULL, one, 1, pos + 1, t->dtype, scale, t->d_partials,
-                                             t->d_counters, dk, dv, early, kvh0, nkvh, TYB_DEC_DEVICE_SMALL, gather,
+                                             t->d_counters, dk, dv, early, kvh0, nkvh,
+                                             TYB_DEC_DEVICE_SMALL | TYB_DEC_WIDE_COUNTERS, gather,
                                              st),
                      what))
         return 1;

@@ -105,6 +105,11 @@ int tyb_decode_launch_batched(const float *q, float *out, const tyb_seq_kv *seqs
 /* flags of tyb_decode_launch_heads: q, k_new and v_new are device memory (not page-locked host
  * memory mapped into the device), so their L2 lines may be requested before the dependency wait. */
 #define TYB_DEC_DEVICE_SMALL 1
+/* flags: `counters` holds TYB_DEC_WIDE_COUNTER_WORDS zeroed words (8 head counters, then 32 group
+ * counters per KV head), so one sequence split over more than 32 CTAs per head is merged in two
+ * levels (groups of 16 records in parallel, then the group records). */
+#define TYB_DEC_WIDE_COUNTERS 2
+#define TYB_DEC_WIDE_COUNTER_WORDS (8 + 8 * 32)
 /* Relayout of a gathered head-major tensor [16][S][128] into token-major [S][16][128]
  * (elem_bytes 2 or 4). */
 int tyb_heads_to_tokens_launch(const void *src, void *dst, int S, int elem_bytes, void *stream);

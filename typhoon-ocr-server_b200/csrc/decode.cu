@@ -150,6 +150,7 @@ __device__ __forceinline__ bool merge_records(const float* recs, int nsplit, flo
         const int nb = min(cap, nsplit - j0);
         __syncthreads();  // the previous batch is consumed
         if (tid == 0) {
+            fence_proxy_async_smem();  // the region's earlier (generic) reads come before the copy's writes
             const uint32_t bytes = (uint32_t)nb * kRec * sizeof(float);
             mbar_arrive_expect_tx(bar, bytes);
             bulk_g2s(region, recs + (size_t)j0 * kRec, bytes, bar);
@@ -639,6 +640,7 @@ struct DecodeMmaArgs {
     unsigned int* counters;
     int kvh0;
     int prefetch_small;
+    int wide_counters;  // counters hold kHkv head counters then [kHkv][kGroupCounters] group counters
     const GatherDev* gather;  // non-NULL: outputs go to the exchange buffer and to every rank
     // Non-NULL q_norm: q and k_new arrive raw; RMSNorm(q_norm / k_norm, eps) and rotate_half
     // M-RoPE with the token's rope_cos / rope_sin [64] are applied on load (one sequence only).
@@ -768,8 +770,11 @@ __device__ __forceinline__ void split_pair(float x0, float x1, uint32_t& hi, uin
 // of each record, then accumulates it against the weights with four independent chains.  Loads
 // bypass L1 (.cg): the records were written by other CTAs, and the workspace by earlier launches.
 // wts: 2 * 32 + 4 floats of shared memory.  Every thread of the CTA calls it; writes
-// out[h * 128 + d].
-__device__ __forceinline__ void merge_records_direct(const float* recs, int nsplit, float* wts, float* out)
+// out[h * 128 + d].  step: records at recs + j * step * kRec.  rec_out non-NULL: the merge is
+// written as a record instead (running maxima and sums in the header, O unnormalised), for a
+// later merge of merges; it may be the first record read (all reads come first).
+__device__ __forceinline__ void merge_records_direct(const float* recs, int nsplit, float* wts, float* out,
+                                                     int step = 1, float* rec_out = nullptr)
 {
     const int tid = threadIdx.x;
     const int lane = tid & 31;
@@ -782,18 +787,18 @@ __device__ __forceinline__ void merge_records_direct(const float* recs, int nspl
     float O = 0.f;
     for (int j0 = 0; j0 < nsplit; j0 += 32) {
         const int nb = min(32, nsplit - j0);
-        const float* r = recs + (size_t)j0 * kRec;
+        const float* r = recs + (size_t)j0 * step * kRec;
         if (j0) __syncthreads();  // the previous batch's weights are consumed
         // Headers first: the weights (on the path to the output) need them.
         float mj = -INFINITY, lj = 0.f;
         if (warp < 2 && lane < nb) {
-            const float2 e = __ldcg(reinterpret_cast<const float2*>(r + (size_t)lane * kRec + 2 * warp));
+            const float2 e = __ldcg(reinterpret_cast<const float2*>(r + (size_t)lane * step * kRec + 2 * warp));
             mj = e.x;
             lj = e.y;
         }
         float ov[32];
 #pragma unroll
-        for (int j = 0; j < 32; j++) ov[j] = active && j < nb ? __ldcg(r + (size_t)j * kRec + 4 + h * kD + d) : 0.f;
+        for (int j = 0; j < 32; j++) ov[j] = active && j < nb ? __ldcg(r + (size_t)j * step * kRec + 4 + h * kD + d) : 0.f;
         if (warp < 2) {
             float mb = mj;
 #pragma unroll
@@ -821,8 +826,57 @@ __device__ __forceinline__ void merge_records_direct(const float* recs, int nspl
             O = (o4[0] + o4[1]) + (o4[2] + o4[3]);
         }
     }
+    if (rec_out) {
+        __syncthreads();  // every read of the records is done
+        if (warp < 2 && lane == 0) {
+            rec_out[2 * warp] = run;
+            rec_out[2 * warp + 1] = Lrun;
+        }
+        if (active) rec_out[4 + (size_t)h * kD + d] = O;
+        return;
+    }
     if (active) out[(size_t)h * kD + d] = O / alpha_s[2 + h];
 }
+
+// Merge of a head's records when more than 64 CTAs share it (kGroupRecs-record groups, each
+// merged into its first record by the group's last CTA -- the groups in parallel -- then the
+// group records merged by the last group).  Returns true in the CTA that produced the output.
+// Measured at 32K with one KV head (128 splits, one GPU, 28 layers): 234 us/step against 299 with
+// one CTA merging all 128 records; with 64 records the one-CTA merge through shared memory wins.
+// gcount: the head's group counters (zero between launches); hcount: its head counter.
+constexpr int kGroupRecs = 16;
+constexpr int kGroupCounters = 32;  // groups per head at most (512 records)
+__device__ __forceinline__ bool merge_two_level(float* recs, int n, int s, float* wts, float* out,
+                                                unsigned int* gcount, unsigned int* hcount, int* flag)
+{
+    const int tid = threadIdx.x;
+    const int grp = s / kGroupRecs;
+    const int gsize = min(kGroupRecs, n - grp * kGroupRecs);
+    const int ngroups = (n + kGroupRecs - 1) / kGroupRecs;
+    float* gfirst = recs + (size_t)grp * kGroupRecs * kRec;
+    if (tid == 0) {
+        unsigned int t;
+        asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(t) : "l"(&gcount[grp]) : "memory");
+        *flag = t == (unsigned int)(gsize - 1);
+    }
+    __syncthreads();
+    if (!*flag) return false;
+    merge_records_direct(gfirst, gsize, wts, nullptr, 1, gfirst);
+    __syncthreads();  // the group record is written
+    if (tid == 0) {
+        gcount[grp] = 0u;
+        unsigned int t;
+        asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(t) : "l"(hcount) : "memory");
+        *flag = t == (unsigned int)(ngroups - 1);
+    }
+    __syncthreads();
+    if (!*flag) return false;
+    merge_records_direct(recs, ngroups, wts, out, kGroupRecs);
+    if (tid == 0) *hcount = 0u;
+    return true;
+}
+
+
 
 // kQk: q and the new key row arrive raw and are normalised and rotated on load (DecodeMmaArgs).
 template <int NW, bool kQk = false>
@@ -1159,6 +1213,13 @@ __global__ void __launch_bounds__(NW * 32, 16 / NW)
         }
     }
     __syncthreads();
+    if (a.wide_counters && !a.seqs && nsplit > 64) {  // many splits of one sequence's head: merged in two levels
+        if (!merge_two_level(recs, nsplit, s, reinterpret_cast<float*>(Kt), out_pair,
+                             a.counters + kHkv + (size_t)kvh * kGroupCounters, &a.counters[kvh], last_flag))
+            return;
+        if (a.gather) gather_publish(a.gather, kvh, gridDim.y, epoch, a.out);
+        return;
+    }
     if (tid == 0) {
         unsigned int ticket;
         asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;"
@@ -1166,10 +1227,20 @@ __global__ void __launch_bounds__(NW * 32, 16 / NW)
                      : "l"(&a.counters[b * kHkv + kvh])
                      : "memory");
         *last_flag = ticket == (unsigned int)(nsplit - 1);
+        if (*last_flag && nsplit > 32) asm volatile("fence.proxy.async.global;" ::: "memory");  // read by a bulk copy
     }
     __syncthreads();
     if (!*last_flag) return;
-    merge_records_direct(recs, nsplit, reinterpret_cast<float*>(Kt), out_pair);
+    // Up to 32 records: plain L2 loads, one round trip.  More (sequences split over 33-128 CTAs per
+    // KV head, as when one long sequence's heads are spread over GPUs): one bulk copy of the
+    // records into the CTA's free tile space and the merge from shared memory -- a round trip
+    // per 32 records measured ~1.4 us each.
+    if (nsplit > 32) {
+        if (!merge_records(recs, nsplit, reinterpret_cast<float*>(Kt), (size_t)(Qa - Kt), &bars[2], stat, out_pair))
+            return;
+    } else {
+        merge_records_direct(recs, nsplit, reinterpret_cast<float*>(Kt), out_pair);
+    }
     if (tid == 0) a.counters[b * kHkv + kvh] = 0u;
     if (a.gather) gather_publish(a.gather, kvh, gridDim.y, epoch, a.out);
 }
@@ -1490,6 +1561,13 @@ __global__ void __launch_bounds__(256, 2)
         }
     }
     __syncthreads();
+    if (a.wide_counters && !a.seqs && nspan > 64) {  // as in decode_mma_kernel
+        if (!merge_two_level(recs, nspan, span, reinterpret_cast<float*>(smem), out_pair,
+                             a.counters + kHkv + (size_t)kvh * kGroupCounters, &a.counters[kvh], last_flag))
+            return;
+        if (a.gather) gather_publish(a.gather, kvh, gridDim.y, epoch, a.out);
+        return;
+    }
     if (tid == 0) {
         unsigned int ticket;
         asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;"
@@ -1497,10 +1575,16 @@ __global__ void __launch_bounds__(256, 2)
                      : "l"(&a.counters[b * kHkv + kvh])
                      : "memory");
         *last_flag = ticket == (unsigned int)(nspan - 1);
+        if (*last_flag && nspan > 32) asm volatile("fence.proxy.async.global;" ::: "memory");  // read by a bulk copy
     }
     __syncthreads();
     if (!*last_flag) return;
-    merge_records_direct(recs, nspan, reinterpret_cast<float*>(smem), out_pair);
+    if (nspan > 32) {  // as in decode_mma_kernel: many records through shared memory
+        if (!merge_records(recs, nspan, reinterpret_cast<float*>(smem), (size_t)(Qa - smem), &bars[4], stat, out_pair))
+            return;
+    } else {
+        merge_records_direct(recs, nspan, reinterpret_cast<float*>(smem), out_pair);
+    }
     if (tid == 0) a.counters[b * kHkv + kvh] = 0u;
     if (a.gather) gather_publish(a.gather, kvh, gridDim.y, epoch, a.out);
 }
@@ -1874,6 +1958,7 @@ static int launch_heads_impl(const float* q, float* out, const tyb_seq_kv* seqs_
         m.counters = counters;
         m.kvh0 = kvh0;
         m.prefetch_small = a.prefetch_small;
+        m.wide_counters = (flags & TYB_DEC_WIDE_COUNTERS) != 0;
         m.gather = static_cast<const GatherDev*>(gather);
         if (prep) {
             m.q_norm = prep->q_norm;
@@ -1911,7 +1996,8 @@ extern "C" int tyb_decode_launch_fused(const float* q_raw, float* out, tyb_seq_k
 {
     if (!prep) return (int)cudaErrorInvalidValue;
     return launch_heads_impl(q_raw, out, nullptr, one, 1, kv_len, TYB_BF16, scale, partials, counters, k_raw, v_new,
-                             prefetch_rows, 0, kHkv, TYB_DEC_DEVICE_SMALL, nullptr, prep, stream);
+                             prefetch_rows, 0, kHkv, TYB_DEC_DEVICE_SMALL | TYB_DEC_WIDE_COUNTERS, nullptr, prep,
+                             stream);
 }
 
 extern "C" int tyb_decode_launch_ex(const float* q, float* out, const tyb_seq_kv* seqs_dev, tyb_seq_kv one,

@@ -34,7 +34,7 @@ typedef struct {
     float *d_kv_stage;       /* [2][max_seq][8][128] fp32 staging of host K/V rows (>= 16 KB); also the
                               * device copy of a decode call's host inputs (one slot) */
     float *d_partials;       /* split-KV workspace of the decode kernel */
-    unsigned int *d_counters;/* [8] split tickets, kept zero between launches */
+    unsigned int *d_counters;/* split tickets: 8 per head, then 32 group counters per head (TYB_DEC_WIDE_COUNTER_WORDS), kept zero between launches */
     /* Deferred single-row appends from host memory (kv_cache_append as kernel/decoder.c:96-100
      * calls it): the row is copied here at once, and written to the cache by the next launch that
      * touches its layer -- normally the attention_decode_gqa of the same step, which then appends

@@ -87,9 +87,9 @@ KVCache *kv_cache_alloc_ex(int max_seq_len, int kv_dtype)
                            2 * (size_t)(max_seq_len < 2 ? 2 : max_seq_len) * TYB_ROW_FLOATS * sizeof(float),
                            "kv_cache_alloc: staging") &&
              tyb_dev_alloc((void **)&t->d_partials, part, "kv_cache_alloc: decode workspace") &&
-             tyb_dev_alloc((void **)&t->d_counters, KV_NUM_KV_HEADS * sizeof(unsigned int),
+             tyb_dev_alloc((void **)&t->d_counters, TYB_DEC_WIDE_COUNTER_WORDS * sizeof(unsigned int),
                            "kv_cache_alloc: counters") &&
-             tyb_cuda_ok(cudaMemset(t->d_counters, 0, KV_NUM_KV_HEADS * sizeof(unsigned int)),
+             tyb_cuda_ok(cudaMemset(t->d_counters, 0, TYB_DEC_WIDE_COUNTER_WORDS * sizeof(unsigned int)),
                          "kv_cache_alloc: counters memset");
     if (!ok) {
         cache_release(t);
