@@ -26,10 +26,10 @@
 /* flags: TYB_DEC_DEVICE_SMALL when q is device memory (not a mapped page-locked host buffer). */
 static int decode_launch(const float *q, float *out, const tyb_seq_kv *seqs_dev, tyb_seq_kv one, int batch,
                          int max_kv, int dtype, float scale, int prefetch_rows, float *partials,
-                         unsigned int *counters, int flags, void *st)
+                         unsigned int *counters, int flags, const float *inl, void *st)
 {
     return tyb_decode_launch_heads(q, out, seqs_dev, one, batch, max_kv, dtype, scale, partials, counters, NULL, NULL,
-                                   prefetch_rows, 0, KV_NUM_KV_HEADS, flags, NULL, st);
+                                   prefetch_rows, 0, KV_NUM_KV_HEADS, flags, NULL, inl, st);
 }
 
 static int check_layer(int layer, const char *what)
@@ -75,6 +75,46 @@ static float *small_view(const float *p, float *stage, size_t bytes, int *kind, 
 static int decode_append_impl(const float *q, const float *k_new, const float *v_new, KVCache *cache, float *output,
                               int layer_idx, float scale, int kvh0, int nkvh, const void *gather, int pos_at,
                               const char *what);
+
+/* Host inputs of a one-sequence decode call as the launch's parameter block: when q and, for an
+ * append, k_new / v_new are all host memory (page-locked or not), they are copied into the layer's
+ * page-locked slot [K row][V row][q] and *inl is the slot, which the launch reads as its
+ * parameters -- the inputs reach the GPU with the launch, with no copy queued ahead of it (k_new /
+ * v_new may already be the slot's own rows: a deferred append).  *inl = NULL when any input is
+ * device memory (stage_inputs then).  1 on success, else 0 with the error set. */
+static int inline_inputs(tyb_cache *t, int layer, const float *q, const float *k_new, const float *v_new,
+                         const float **inl, const char *what)
+{
+    *inl = NULL;
+    const int rq = tyb_is_device_ptr(q);
+    const int rk = k_new ? tyb_is_device_ptr(k_new) : 0, rv = v_new ? tyb_is_device_ptr(v_new) : 0;
+    if (rq < 0 || rk < 0 || rv < 0) return 0;
+    if (rq || rk || rv) return 1;
+    if (!tyb_slots_ready(t, what)) return 0;
+    float *slot = tyb_row_slot(t, layer);
+    /* an earlier launch may still read the slot through its mapping (a deferred row's write) */
+    if (!tyb_cuda_ok(cudaEventSynchronize((cudaEvent_t)t->row_ev[layer]), what)) return 0;
+    if (k_new && k_new != slot) memcpy(slot, k_new, TYB_ROW_FLOATS * sizeof(float));
+    if (v_new && v_new != slot + TYB_ROW_FLOATS) memcpy(slot + TYB_ROW_FLOATS, v_new, TYB_ROW_FLOATS * sizeof(float));
+    memcpy(slot + 2 * TYB_ROW_FLOATS, q, TYB_Q_FLOATS * sizeof(float));
+    *inl = slot;
+    return 1;
+}
+
+/* A host output of a one-sequence decode call, `n` floats: stored by the kernel through a device
+ * mapping -- the caller's page-locked buffer in place, a pageable one by way of the cache's
+ * page-locked staging (copied out after the wait) -- and marked unwritten first, so the call
+ * can wait for the words themselves (tyb_wait_output).  Sets *dout (the device view) and *hout
+ * (the host side the call waits on); 1 on success. */
+static int host_output(tyb_cache *t, float *output, float *dout_mapped, int kind, size_t n, float **dout,
+                       float **hout, const char *what)
+{
+    if (!tyb_slots_ready(t, what)) return 0;
+    *hout = kind == TYB_MEM_PINNED ? output : t->h_out;
+    *dout = kind == TYB_MEM_PINNED ? dout_mapped : t->h_out_dev;
+    tyb_mark_unwritten(*hout, n);
+    return 1;
+}
 
 /* The single-token inputs of a decode call -- q [16][128] and, for an append, k_new / v_new
  * [8][128] (NULL when absent) -- on the device.  Device buffers are used in place.  Host buffers
@@ -139,11 +179,18 @@ void attention_decode_gqa(const float *q, const KVCache *cache, float *output, i
     if (!tyb_flush_pending(t, layer_idx, what)) return;
     void *st = tyb_stream();
     int ok = 0;
-    const float *dq = NULL, *unused_k, *unused_v;
-    if (kv_len > 0 && !stage_inputs(t, layer_idx, q, NULL, NULL, &dq, &unused_k, &unused_v, st, what)) return;
+    const float *inl = NULL, *dq = q, *unused_k, *unused_v;
+    float *hout = NULL;
+    if (kv_len > 0 && !inline_inputs(t, layer_idx, q, NULL, NULL, &inl, what)) return;
+    if (kv_len > 0 && !inl && !stage_inputs(t, layer_idx, q, NULL, NULL, &dq, &unused_k, &unused_v, st, what))
+        return;
     float *dout = small_view(output, NULL, 0, &ok, st, what);
-    if (ok < 0 || (ok == TYB_MEM_DEVICE && !dout)) return;
-    if (ok == TYB_MEM_HOST) dout = t->d_out;
+    if (ok < 0 || (ok != TYB_MEM_HOST && !dout)) return;
+    if (kv_len > 0 && ok != TYB_MEM_DEVICE) {
+        if (!host_output(t, output, dout, ok, TYB_Q_FLOATS, &dout, &hout, what)) return;
+    } else if (ok == TYB_MEM_HOST) {
+        dout = t->d_out;
+    }
     if (kv_len == 0) {
         /* The reference's loops do not run and the output stays zeroed (:186-190). */
         if (ok == TYB_MEM_PINNED) {
@@ -156,10 +203,16 @@ void attention_decode_gqa(const float *q, const KVCache *cache, float *output, i
         const tyb_seq_kv one = tyb_layer_rows(t, layer_idx, kv_len);
         const int early = tyb_prefetch_rows(cache, layer_idx, kv_len);
         if (!tyb_cuda_ok(decode_launch(dq, dout, NULL, one, 1, kv_len, t->dtype, scale, early, t->d_partials,
-                                       t->d_counters, TYB_DEC_DEVICE_SMALL | TYB_DEC_WIDE_COUNTERS, st),
+                                       t->d_counters, TYB_DEC_DEVICE_SMALL | TYB_DEC_WIDE_COUNTERS, inl, st),
                          what))
             return;
         tyb_note_nowrite(st);
+        if (hout) {
+            /* host output: wait for its words, not for the launch */
+            if (tyb_wait_output(hout, TYB_Q_FLOATS, st, what) && ok == TYB_MEM_HOST)
+                memcpy(output, t->h_out, TYB_Q_FLOATS * sizeof(float));
+            return;
+        }
     }
     if (ok == TYB_MEM_HOST) {
         if (!tyb_cuda_ok(cudaMemcpyAsync(output, dout, TYB_Q_FLOATS * sizeof(float), cudaMemcpyDeviceToHost,
@@ -375,7 +428,7 @@ int attention_decode_gqa_batched(const float *q, const KVCache *const *caches, c
         tyb_seq_kv none;
         memset(&none, 0, sizeof none);
         if (!tyb_cuda_ok(decode_launch(dq, dout, ddesc, none, batch, max_kv, dtype, scale, 0, part, cnt,
-                                       TYB_DEC_DEVICE_SMALL, st),
+                                       TYB_DEC_DEVICE_SMALL, NULL, st),
                          what))
             return 1;
     }
@@ -408,22 +461,34 @@ static int decode_append_impl(const float *q, const float *k_new, const float *v
     }
     void *st = tyb_stream();
     int ok = 0;
-    const float *dq, *dk, *dv;
-    if (!stage_inputs(t, layer_idx, q, k_new, v_new, &dq, &dk, &dv, st, what)) return 1;
+    const float *inl = NULL, *dq = q, *dk = k_new, *dv = v_new;
+    float *hout = NULL;
+    if (!gather && !inline_inputs(t, layer_idx, q, k_new, v_new, &inl, what)) return 1;
+    if (!inl && !stage_inputs(t, layer_idx, q, k_new, v_new, &dq, &dk, &dv, st, what)) return 1;
     float *dout = small_view(output, NULL, 0, &ok, st, what);
     /* rows of the query heads computed (all 16 when gathered from every rank) */
     const size_t out_floats = (size_t)2 * (gather ? KV_NUM_KV_HEADS : nkvh) * KV_HEAD_DIM;
     if (ok < 0 || (ok != TYB_MEM_HOST && !dout)) return 1;
-    if (ok == TYB_MEM_HOST) dout = t->d_out;
+    if (!gather && ok != TYB_MEM_DEVICE) {
+        if (!host_output(t, output, dout, ok, out_floats, &dout, &hout, what)) return 1;
+    } else if (ok == TYB_MEM_HOST) {
+        dout = t->d_out;
+    }
     const tyb_seq_kv one = tyb_layer_rows(t, layer_idx, pos + 1);
     const int early = tyb_prefetch_rows(cache, layer_idx, pos);
     if (!tyb_cuda_ok(tyb_decode_launch_heads(dq, dout, NULL, one, 1, pos + 1, t->dtype, scale, t->d_partials,
                                              t->d_counters, dk, dv, early, kvh0, nkvh,
-                                             TYB_DEC_DEVICE_SMALL | TYB_DEC_WIDE_COUNTERS, gather,
+                                             TYB_DEC_DEVICE_SMALL | TYB_DEC_WIDE_COUNTERS, gather, inl,
                                              st),
                      what))
         return 1;
     tyb_note_write(cache, layer_idx, pos, st);
+    if (hout) {
+        /* host output: wait for its words, not for the launch */
+        if (!tyb_wait_output(hout, out_floats, st, what)) return 1;
+        if (ok == TYB_MEM_HOST) memcpy(output, t->h_out, out_floats * sizeof(float));
+        return 0;
+    }
     if (ok == TYB_MEM_HOST && !tyb_cuda_ok(cudaMemcpyAsync(output, dout, out_floats * sizeof(float),
                                                            cudaMemcpyDeviceToHost, (cudaStream_t)st),
                                            what))

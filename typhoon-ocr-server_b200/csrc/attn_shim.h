@@ -67,10 +67,14 @@ int tyb_decode_launch_ex(const float *q, float *out, const tyb_seq_kv *seqs_dev,
                          void *stream);
 /* tyb_decode_launch_ex for KV heads [kvh0, kvh0 + nkvh) only; `out` points at the row of query
  * head 2 kvh0 (the shard's rows [2 nkvh][128] are contiguous). */
+/* inl: NULL, or for one sequence (no gather, no QK prep) a page-locked slot [K row 1024][V row 1024]
+ * [q 2048] floats whose contents are passed as the launch's own parameters: the kernel then reads
+ * q, and the appended row when k_new is non-NULL, from there (q / k_new / v_new are not
+ * dereferenced). */
 int tyb_decode_launch_heads(const float *q, float *out, const tyb_seq_kv *seqs_dev, tyb_seq_kv one, int batch,
                             int max_kv_len, int kv_dtype, float scale, float *partials, unsigned int *counters,
                             const float *k_new, const float *v_new, int prefetch_rows, int kvh0, int nkvh,
-                            int flags, const void *gather, void *stream);
+                            int flags, const void *gather, const float *inl, void *stream);
 /* QK-RMSNorm (q_norm / k_norm, eps) and rotate_half M-RoPE with one token's cos / sin [64],
  * applied by the decode kernels on load: all device memory. */
 typedef struct {

@@ -27,6 +27,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <type_traits>
 
 #include "common.cuh"
 #include "host_internal.h"
@@ -61,6 +62,34 @@ struct DecodeArgs {
     int kvh0;  // KV heads [kvh0, kvh0 + gridDim.y); out points at query head 2 kvh0's row
     int prefetch_small;  // q, k_new, v_new are device memory: ask L2 for their lines early
 };
+
+// Decode inputs carried in the launch's own parameters (kernel parameter space holds up to 32 KB):
+// the appended K and V rows [8][128] and the query [16][128] of a call whose inputs are host
+// memory, in the layout of the cache's page-locked per-layer slot they are staged in.  They reach
+// the GPU with the launch itself, so no copy is queued ahead of the kernel.  Read through the
+// parameter's address (hence __grid_constant__; 16-byte aligned for the vector loads).
+struct __align__(16) DecodeInline {
+    float k[kHkv * kD];
+    float v[kHkv * kD];
+    float q[kHq * kD];
+};
+struct DecodeNoInline {  // the inputs are device memory, read through the argument pointers
+    int unused;
+};
+template <typename In>
+constexpr bool kIsInline = std::is_same<In, DecodeInline>::value;
+
+// The query / new-row sources of a launch: the argument pointers, or the parameter copies (k and
+// v only when the call appends a row: the argument pointers then only say whether it does).
+__device__ __forceinline__ void inline_inputs(const DecodeNoInline&, const float*&, const float*&, const float*&) {}
+__device__ __forceinline__ void inline_inputs(const DecodeInline& in, const float*& q, const float*& k,
+                                              const float*& v)
+{
+    q = in.q;
+    if (k) k = in.k;
+    if (v) v = in.v;
+}
+
 
 __device__ __forceinline__ float fast_exp2(float x)
 {
@@ -203,8 +232,8 @@ __device__ __forceinline__ bool merge_records(const float* recs, int nsplit, flo
     return true;
 }
 
-template <typename T>
-__global__ void __launch_bounds__(kDecThreads, 2) decode_split_kernel(const DecodeArgs a)
+template <typename T, typename In>
+__global__ void __launch_bounds__(kDecThreads, 2) decode_split_kernel(const DecodeArgs a, const __grid_constant__ In in)
 {
     extern __shared__ __align__(128) unsigned char smem[];
     const int s = blockIdx.x;
@@ -223,6 +252,10 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_split_kernel(const Deco
     uint64_t* bars = reinterpret_cast<uint64_t*>(stat + 24);  // K rows, V rows, merge records
     int* last_flag = reinterpret_cast<int*>(bars + 3);
     float* red = reinterpret_cast<float*>(kreg);  // [16][2][128], after the scores
+    const float* q_src = a.q;
+    const float* k_src = a.k_new;
+    const float* v_src = a.v_new;
+    inline_inputs(in, q_src, k_src, v_src);
 
     // Split geometry.  The new token's row (fused append) never comes from the cache.
     int kv_len = 0, nsplit = 0, r0 = 0, nrows = 0, tma_rows = 0;
@@ -269,13 +302,13 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_split_kernel(const Deco
     // L2, which the later loads read) and takes the DRAM latency off the path after the wait.
     // Plain prefetch instructions, one 128-byte line per lane: q of the two heads (8 lines),
     // then the new K and V rows (4 lines each) in the CTA that appends them.
-    if (a.prefetch_small && warp == 1) {
+    if (!kIsInline<In> && a.prefetch_small && warp == 1) {
         const float* line = nullptr;
         if (lane < 8) {
-            line = a.q + ((size_t)b * kHq + kGroup * kvh) * kD + lane * 32;
-        } else if (lane < 16 && !a.seqs && a.k_new && kv_len - 1 >= r0 && kv_len - 1 < r0 + nrows) {
+            line = q_src + ((size_t)b * kHq + kGroup * kvh) * kD + lane * 32;
+        } else if (lane < 16 && !a.seqs && k_src && kv_len - 1 >= r0 && kv_len - 1 < r0 + nrows) {
             const size_t off = ((size_t)b * kHkv + kvh) * kD + (lane & 3) * 32;
-            line = (lane < 12 ? a.k_new : a.v_new) + off;
+            line = (lane < 12 ? k_src : v_src) + off;
         }
         if (line) asm volatile("prefetch.global.L2 [%0];" ::"l"(line));
     }
@@ -312,7 +345,7 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_split_kernel(const Deco
     const int part = lane & 7;
     float q0[16], q1[16];
     {
-        const float* qb = a.q + (size_t)b * kHq * kD + (size_t)(kGroup * kvh) * kD;
+        const float* qb = q_src + (size_t)b * kHq * kD + (size_t)(kGroup * kvh) * kD;
         load_query16<T>(qb, part, q0);
         load_query16<T>(qb + kD, part, q1);
     }
@@ -323,8 +356,8 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_split_kernel(const Deco
     float nk[8], nv[8];
     if (has_new && tid < 16) {
         const size_t off = ((size_t)b * kHkv + kvh) * kD + tid * 8;
-        load8(a.k_new + off, nk);
-        load8(a.v_new + off, nv);
+        load8(k_src + off, nk);
+        load8(v_src + off, nv);
         store8(const_cast<T*>(kh) + (size_t)(kv_len - 1) * kD + tid * 8, nk);
         store8(const_cast<T*>(vh) + (size_t)(kv_len - 1) * kD + tid * 8, nv);
         store8(Ks + (size_t)(kv_len - 1 - r0) * kD + tid * 8, nk);
@@ -879,11 +912,11 @@ __device__ __forceinline__ bool merge_two_level(float* recs, int n, int s, float
 
 
 // kQk: q and the new key row arrive raw and are normalised and rotated on load (DecodeMmaArgs).
-template <int NW, bool kQk = false>
+template <int NW, bool kQk, typename In>
 __global__ void __launch_bounds__(NW * 32, 16 / NW)
     decode_mma_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
                       const __grid_constant__ CUtensorMap tmk16, const __grid_constant__ CUtensorMap tmv16,
-                      const DecodeMmaArgs a)
+                      const DecodeMmaArgs a, const __grid_constant__ In in)
 {
     extern __shared__ unsigned char smem_raw[];
     unsigned char* smem =
@@ -908,7 +941,11 @@ __global__ void __launch_bounds__(NW * 32, 16 / NW)
     const uint32_t kt_u32 = smem_u32(Kt), vt_u32 = smem_u32(Vt);
 
     const int b = blockIdx.z;
-    const float* qb = a.q + (size_t)b * kHq * kD;
+    const float* q_src = a.q;
+    const float* k_src = a.k_new;
+    const float* v_src = a.v_new;
+    inline_inputs(in, q_src, k_src, v_src);
+    const float* qb = q_src + (size_t)b * kHq * kD;
     int kv_len = a.kv_len;
     int nsplit = a.nsplit;
     const CUtensorMap* mk = &tmk;
@@ -964,12 +1001,12 @@ __global__ void __launch_bounds__(NW * 32, 16 / NW)
     const bool has_new = !a.seqs && a.k_new && kv_len - 1 >= r0 && kv_len - 1 < r0 + nrows;
     // q and the appended row may be written by the previous kernel: read after the wait, but
     // their L2 lines requested now (plain prefetches, one 128-byte line per lane).
-    if (a.prefetch_small && warp == 1) {
+    if (!kIsInline<In> && a.prefetch_small && warp == 1) {
         const float* line = nullptr;
         if (lane < 8)
             line = qb + (size_t)(kGroup * kvh) * kD + lane * 32;
         else if (lane < 16 && has_new)
-            line = (lane < 12 ? a.k_new : a.v_new) + (size_t)kvh * kD + (lane & 3) * 32;
+            line = (lane < 12 ? k_src : v_src) + (size_t)kvh * kD + (lane & 3) * 32;
         if (line) asm volatile("prefetch.global.L2 [%0];" ::"l"(line));
     }
     pdl_wait();
@@ -1013,8 +1050,8 @@ __global__ void __launch_bounds__(NW * 32, 16 / NW)
     if (new_thread) {
         const int i = tid - 64;
         const size_t off = (size_t)kvh * kD + i * 8;
-        load8(a.k_new + off, nk);
-        load8(a.v_new + off, nv);
+        load8(k_src + off, nk);
+        load8(v_src + off, nv);
         if (kQk) qk_prep_row8(nk, i, a.k_norm, a.rope_cos, a.rope_sin, a.eps);  // raw k: normed, rotated
         const size_t row = ((size_t)kvh * a.row_capacity + (kv_len - 1)) * kD + i * 8;
         store8(a.k + row, nk);
@@ -1265,10 +1302,10 @@ __host__ __device__ constexpr size_t decode_stream_smem_bytes()
     return 1024 + 4 * kStTile + 4 * kStPitch + 4 * kQaPitch + 32 * sizeof(float) + 5 * sizeof(uint64_t) + 16;
 }
 
-template <bool kQk = false>  // as in decode_mma_kernel
+template <bool kQk, typename In>  // as in decode_mma_kernel
 __global__ void __launch_bounds__(256, 2)
     decode_stream_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
-                         const DecodeMmaArgs a)
+                         const DecodeMmaArgs a, const __grid_constant__ In in)
 {
     extern __shared__ unsigned char smem_raw[];
     unsigned char* smem =
@@ -1289,7 +1326,11 @@ __global__ void __launch_bounds__(256, 2)
     int* last_flag = reinterpret_cast<int*>(bars + 5);
     const uint32_t base_u32 = smem_u32(smem);  // K0 K1 V0 V1 tiles, kStTile apart
 
-    const float* qb = a.q + (size_t)b * kHq * kD;
+    const float* q_src = a.q;
+    const float* k_src = a.k_new;
+    const float* v_src = a.v_new;
+    inline_inputs(in, q_src, k_src, v_src);
+    const float* qb = q_src + (size_t)b * kHq * kD;
     int kv_len = a.kv_len;
     const CUtensorMap* mk = &tmk;
     const CUtensorMap* mv = &tmv;
@@ -1301,7 +1342,7 @@ __global__ void __launch_bounds__(256, 2)
         fence_proxy_async_smem();
     }
     __syncthreads();
-    if (a.prefetch_small && warp == 1 && lane < 8)
+    if (!kIsInline<In> && a.prefetch_small && warp == 1 && lane < 8)
         asm volatile("prefetch.global.L2 [%0];" ::"l"(qb + (size_t)(kGroup * kvh) * kD + lane * 32));
     // One sequence: the tiles of the first two stages are requested before the dependency wait
     // when the previous kernel wrote none of their cache rows (rows of a box past them are masked
@@ -1388,8 +1429,8 @@ __global__ void __launch_bounds__(256, 2)
     if (new_thread) {
         const int i = tid - 64;
         const size_t off = (size_t)kvh * kD + i * 8;
-        load8(a.k_new + off, nk);
-        load8(a.v_new + off, nv);
+        load8(k_src + off, nk);
+        load8(v_src + off, nv);
         if (kQk) qk_prep_row8(nk, i, a.k_norm, a.rope_cos, a.rope_sin, a.eps);  // raw k: normed, rotated
         const size_t row = ((size_t)kvh * a.row_capacity + (kv_len - 1)) * kD + i * 8;
         store8(a.k + row, nk);
@@ -1624,7 +1665,7 @@ static int blocks_per_sm(int chunk)
     const int i = chunk / 16;
     if (!cache[i]) {
         int n = 0;
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, decode_split_kernel<T>, kDecThreads,
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, decode_split_kernel<T, DecodeNoInline>, kDecThreads,
                                                           decode_smem_bytes<T>(chunk)) != cudaSuccess ||
             n <= 0)
             n = 1;
@@ -1639,8 +1680,11 @@ static bool set_smem_attr()
     static bool done[kMaxDevices];
     const int dev = cur_dev();
     if (!done[dev]) {
-        if (cudaFuncSetAttribute(decode_split_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)decode_smem_bytes<T>(DecodeTile<T>::kMaxChunk)) != cudaSuccess)
+        const int bytes = (int)decode_smem_bytes<T>(DecodeTile<T>::kMaxChunk);
+        if (cudaFuncSetAttribute(decode_split_kernel<T, DecodeNoInline>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 bytes) != cudaSuccess ||
+            cudaFuncSetAttribute(decode_split_kernel<T, DecodeInline>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 bytes) != cudaSuccess)
             return false;
         done[dev] = true;
     }
@@ -1670,7 +1714,7 @@ static void plan(int batch, int max_kv_len, int* chunk_rows, int* nsplit, int nk
 }
 
 template <typename T>
-static int launch_decode(const DecodeArgs& a, int batch, int nkvh, void* stream)
+static int launch_decode(const DecodeArgs& a, int batch, int nkvh, const void* inl, void* stream)
 {
     if (!set_smem_attr<T>()) return (int)cudaGetLastError();
     cudaLaunchConfig_t cfg = {};
@@ -1683,7 +1727,11 @@ static int launch_decode(const DecodeArgs& a, int batch, int nkvh, void* stream)
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return (int)cudaLaunchKernelEx(&cfg, decode_split_kernel<T>, a);
+    if (inl) {  // the parameter block is read from the host slot by the launch itself
+        void* args[2] = {const_cast<DecodeArgs*>(&a), const_cast<void*>(inl)};
+        return (int)cudaLaunchKernelExC(&cfg, (const void*)decode_split_kernel<T, DecodeInline>, args);
+    }
+    return (int)cudaLaunchKernelEx(&cfg, decode_split_kernel<T, DecodeNoInline>, a, DecodeNoInline{});
 }
 
 // Tensor maps of a layer's K and V slabs (all row_capacity rows, boxes of `chunk` rows), kept in
@@ -1785,16 +1833,13 @@ static int set_mma_smem_attr()
     const int dev = cur_dev();
     if (!done[dev]) {
         const int mma_smem = (int)decode_mma_smem_bytes(kMmaMaxChunk), st_smem = (int)decode_stream_smem_bytes();
-        cudaError_t e = cudaFuncSetAttribute(decode_mma_kernel<8, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             mma_smem);
-        if (e == cudaSuccess)
-            e = cudaFuncSetAttribute(decode_mma_kernel<8, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, mma_smem);
-        if (e == cudaSuccess)
-            e = cudaFuncSetAttribute(decode_stream_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     st_smem);
-        if (e == cudaSuccess)
-            e = cudaFuncSetAttribute(decode_stream_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     st_smem);
+        const cudaFuncAttribute dyn = cudaFuncAttributeMaxDynamicSharedMemorySize;
+        cudaError_t e = cudaFuncSetAttribute(decode_mma_kernel<8, false, DecodeNoInline>, dyn, mma_smem);
+        if (e == cudaSuccess) e = cudaFuncSetAttribute(decode_mma_kernel<8, true, DecodeNoInline>, dyn, mma_smem);
+        if (e == cudaSuccess) e = cudaFuncSetAttribute(decode_mma_kernel<8, false, DecodeInline>, dyn, mma_smem);
+        if (e == cudaSuccess) e = cudaFuncSetAttribute(decode_stream_kernel<false, DecodeNoInline>, dyn, st_smem);
+        if (e == cudaSuccess) e = cudaFuncSetAttribute(decode_stream_kernel<true, DecodeNoInline>, dyn, st_smem);
+        if (e == cudaSuccess) e = cudaFuncSetAttribute(decode_stream_kernel<false, DecodeInline>, dyn, st_smem);
         if (e != cudaSuccess) return (int)e;
         done[dev] = true;
     }
@@ -1803,7 +1848,7 @@ static int set_mma_smem_attr()
 
 // The tensor-core form for one sequence with a BF16 cache.  Splits as planned for
 // decode_split_kernel<bf16> (same record count, so the callers' workspaces fit).
-static int launch_decode_mma(DecodeMmaArgs a, const tyb_seq_kv& one, int nkvh, void* stream)
+static int launch_decode_mma(DecodeMmaArgs a, const tyb_seq_kv& one, int nkvh, const void* inl, void* stream)
 {
     const int e = set_mma_smem_attr();
     if (e) return e;
@@ -1821,12 +1866,20 @@ static int launch_decode_mma(DecodeMmaArgs a, const tyb_seq_kv& one, int nkvh, v
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    if (a.q_norm) return (int)cudaLaunchKernelEx(&cfg, decode_mma_kernel<8, true>, mk, mv, mk16, mv16, a);
-    return (int)cudaLaunchKernelEx(&cfg, decode_mma_kernel<8, false>, mk, mv, mk16, mv16, a);
+    if (inl) {  // the parameter block is read from the host slot by the launch itself
+        if (a.q_norm) return (int)cudaErrorInvalidValue;
+        void* args[6] = {&mk, &mv, &mk16, &mv16, &a, const_cast<void*>(inl)};
+        return (int)cudaLaunchKernelExC(&cfg, (const void*)decode_mma_kernel<8, false, DecodeInline>, args);
+    }
+    if (a.q_norm)
+        return (int)cudaLaunchKernelEx(&cfg, decode_mma_kernel<8, true, DecodeNoInline>, mk, mv, mk16, mv16, a,
+                                       DecodeNoInline{});
+    return (int)cudaLaunchKernelEx(&cfg, decode_mma_kernel<8, false, DecodeNoInline>, mk, mv, mk16, mv16, a,
+                                   DecodeNoInline{});
 }
 
 static int launch_stream(const DecodeMmaArgs& a, const CUtensorMap& mk, const CUtensorMap& mv, int nkvh, int batch,
-                         void* stream)
+                         const void* inl, void* stream)
 {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.nsplit, nkvh, batch);
@@ -1838,8 +1891,14 @@ static int launch_stream(const DecodeMmaArgs& a, const CUtensorMap& mk, const CU
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    if (a.q_norm) return (int)cudaLaunchKernelEx(&cfg, decode_stream_kernel<true>, mk, mv, a);
-    return (int)cudaLaunchKernelEx(&cfg, decode_stream_kernel<false>, mk, mv, a);
+    if (inl) {
+        if (a.q_norm) return (int)cudaErrorInvalidValue;
+        void* args[4] = {const_cast<CUtensorMap*>(&mk), const_cast<CUtensorMap*>(&mv), const_cast<DecodeMmaArgs*>(&a),
+                         const_cast<void*>(inl)};
+        return (int)cudaLaunchKernelExC(&cfg, (const void*)decode_stream_kernel<false, DecodeInline>, args);
+    }
+    if (a.q_norm) return (int)cudaLaunchKernelEx(&cfg, decode_stream_kernel<true, DecodeNoInline>, mk, mv, a, DecodeNoInline{});
+    return (int)cudaLaunchKernelEx(&cfg, decode_stream_kernel<false, DecodeNoInline>, mk, mv, a, DecodeNoInline{});
 }
 
 }  // namespace tyb
@@ -1886,7 +1945,7 @@ extern "C" int tyb_decode_launch_batched(const float* q, float* out, const tyb_s
     a.counters = counters;
     a.prefetch_small = 1;
     a.gather = nullptr;
-    return launch_stream(a, m0, m1, kHkv, batch, stream);
+    return launch_stream(a, m0, m1, kHkv, batch, nullptr, stream);
 }
 
 extern "C" void tyb_decode_plan(int batch, int max_kv_len, int kv_dtype, int* chunk_rows, int* nsplit)
@@ -1907,9 +1966,12 @@ extern "C" size_t tyb_decode_partial_floats(int batch, int nsplit)
 static int launch_heads_impl(const float* q, float* out, const tyb_seq_kv* seqs_dev, tyb_seq_kv one, int batch,
                              int max_kv_len, int kv_dtype, float scale, float* partials, unsigned int* counters,
                              const float* k_new, const float* v_new, int prefetch_rows, int kvh0, int nkvh,
-                             int flags, const void* gather, const tyb_qk_prep* prep, void* stream)
+                             int flags, const void* gather, const tyb_qk_prep* prep, const float* inl, void* stream)
 {
     if (gather && (kv_dtype != TYB_BF16 || seqs_dev || batch != 1)) return (int)cudaErrorInvalidValue;
+    // Inputs in the parameter block: one sequence, no gather, raw-pointer decode (not the QK-norm form)
+    if (inl && (seqs_dev || batch != 1 || gather || prep)) return (int)cudaErrorInvalidValue;
+    if (inl) flags &= ~TYB_DEC_DEVICE_SMALL;
     // QK-RMSNorm + M-RoPE on load: the tensor-core forms for one sequence (BF16 cache) only
     if (prep && (kv_dtype != TYB_BF16 || seqs_dev || batch != 1 || !prep->q_norm || !prep->k_norm ||
                  !prep->cos || !prep->sin))
@@ -1967,27 +2029,27 @@ static int launch_heads_impl(const float* q, float* out, const tyb_seq_kv* seqs_
             m.rope_sin = prep->sin;
             m.eps = prep->eps;
         }
-        if (one_wave(1, max_kv_len, nkvh)) return launch_decode_mma(m, one, nkvh, stream);
+        if (one_wave(1, max_kv_len, nkvh)) return launch_decode_mma(m, one, nkvh, inl, stream);
         const int e = set_mma_smem_attr();
         if (e) return e;
         CUtensorMap mk, mv;
         if (!slab_maps(one, kStRows, &mk, &mv)) return (int)cudaErrorInvalidValue;
         m.seqs = nullptr;
         m.maps = nullptr;
-        return launch_stream(m, mk, mv, nkvh, 1, stream);
+        return launch_stream(m, mk, mv, nkvh, 1, inl, stream);
     }
-    if (kv_dtype == TYB_BF16) return launch_decode<__nv_bfloat16>(a, batch, nkvh, stream);
-    return launch_decode<float>(a, batch, nkvh, stream);
+    if (kv_dtype == TYB_BF16) return launch_decode<__nv_bfloat16>(a, batch, nkvh, inl, stream);
+    return launch_decode<float>(a, batch, nkvh, inl, stream);
 }
 
 extern "C" int tyb_decode_launch_heads(const float* q, float* out, const tyb_seq_kv* seqs_dev, tyb_seq_kv one,
                                        int batch, int max_kv_len, int kv_dtype, float scale, float* partials,
                                        unsigned int* counters, const float* k_new, const float* v_new,
                                        int prefetch_rows, int kvh0, int nkvh, int flags, const void* gather,
-                                       void* stream)
+                                       const float* inl, void* stream)
 {
     return launch_heads_impl(q, out, seqs_dev, one, batch, max_kv_len, kv_dtype, scale, partials, counters, k_new,
-                             v_new, prefetch_rows, kvh0, nkvh, flags, gather, nullptr, stream);
+                             v_new, prefetch_rows, kvh0, nkvh, flags, gather, nullptr, inl, stream);
 }
 
 extern "C" int tyb_decode_launch_fused(const float* q_raw, float* out, tyb_seq_kv one, int kv_len, float scale,
@@ -1997,7 +2059,7 @@ extern "C" int tyb_decode_launch_fused(const float* q_raw, float* out, tyb_seq_k
     if (!prep) return (int)cudaErrorInvalidValue;
     return launch_heads_impl(q_raw, out, nullptr, one, 1, kv_len, TYB_BF16, scale, partials, counters, k_raw, v_new,
                              prefetch_rows, 0, kHkv, TYB_DEC_DEVICE_SMALL | TYB_DEC_WIDE_COUNTERS, nullptr, prep,
-                             stream);
+                             nullptr, stream);
 }
 
 extern "C" int tyb_decode_launch_ex(const float* q, float* out, const tyb_seq_kv* seqs_dev, tyb_seq_kv one,
@@ -2006,7 +2068,7 @@ extern "C" int tyb_decode_launch_ex(const float* q, float* out, const tyb_seq_kv
                                     int prefetch_rows, void* stream)
 {
     return tyb_decode_launch_heads(q, out, seqs_dev, one, batch, max_kv_len, kv_dtype, scale, partials, counters,
-                                   k_new, v_new, prefetch_rows, 0, kHkv, 0, nullptr, stream);
+                                   k_new, v_new, prefetch_rows, 0, kHkv, 0, nullptr, nullptr, stream);
 }
 
 extern "C" int tyb_decode_launch(const float* q, float* out, const tyb_seq_kv* seqs_dev, tyb_seq_kv one,

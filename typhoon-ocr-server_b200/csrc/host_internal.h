@@ -40,10 +40,15 @@ typedef struct {
      * touches its layer -- normally the attention_decode_gqa of the same step, which then appends
      * and attends in one kernel. */
     float *h_rows;           /* page-locked, device-mapped [28][4][1024]: per layer the staged K row, V
-                              * row, then room for a host query [16][128] copied beside them */
+                              * row, then room for a host query [16][128] copied beside them (the
+                              * parameter block of a decode launch from host inputs) */
     float *h_rows_dev;       /* its device view */
     void *row_ev[KV_NUM_LAYERS]; /* cudaEvent_t: recorded after the launch that read the layer's slot */
     int pending[KV_NUM_LAYERS];  /* row the layer's staged row goes to, or -1 */
+    /* In the same page-locked block, after the slots: the [16][128] output staging of a pageable
+     * host output (written by the decode kernel through its device view, copied out after the
+     * call's wait). */
+    float *h_out, *h_out_dev;
 } tyb_cache;
 
 /* Writes (cache, layer)'s deferred row, if any, on the calling thread's stream; every path that
@@ -51,6 +56,15 @@ typedef struct {
 int tyb_flush_pending(tyb_cache *t, int layer, const char *what);
 /* The layer's staging slot: K row [8][128], V row [8][128], query [16][128] (4096 floats). */
 #define TYB_SLOT_FLOATS (4 * TYB_ROW_FLOATS)
+/* The page-locked block: the 28 slots, then the output staging. */
+#define TYB_PINNED_FLOATS ((size_t)KV_NUM_LAYERS * TYB_SLOT_FLOATS + TYB_Q_FLOATS)
+/* Host output of a blocking decode call, stored by the kernel through a device mapping: filled
+ * with TYB_UNWRITTEN before the launch (tyb_mark_unwritten), then tyb_wait_output waits until no
+ * word holds it (or for the stream when a status bit is raised or the stream goes idle first);
+ * 1 on success, else 0 with the error set. */
+#define TYB_UNWRITTEN 0xFFFFFFFFu
+void tyb_mark_unwritten(float *out, size_t n);
+int tyb_wait_output(const float *out, size_t n, void *stream, const char *what);
 static inline float *tyb_row_slot(const tyb_cache *t, int layer) { return t->h_rows + (size_t)layer * TYB_SLOT_FLOATS; }
 /* The slots (page-locked, device-mapped) and their events, set up on first use; 1 on success. */
 int tyb_slots_ready(tyb_cache *t, const char *what);

@@ -135,9 +135,9 @@ int tyb_slots_ready(tyb_cache *t, const char *what)
 {
     if (t->h_rows) return 1;
     void *p = NULL;
-    if (!tyb_host_alloc(&p, (size_t)KV_NUM_LAYERS * TYB_SLOT_FLOATS * sizeof(float),
-                        cudaHostAllocMapped | cudaHostAllocPortable, what))
+    if (!tyb_host_alloc(&p, TYB_PINNED_FLOATS * sizeof(float), cudaHostAllocMapped | cudaHostAllocPortable, what))
         return 0;
+    memset(p, 0, TYB_PINNED_FLOATS * sizeof(float));
     void *d = NULL;
     if (!tyb_cuda_ok(cudaHostGetDevicePointer(&d, p, 0), what)) {
         cudaFreeHost(p);
@@ -157,6 +157,9 @@ int tyb_slots_ready(tyb_cache *t, const char *what)
     }
     t->h_rows = (float *)p;
     t->h_rows_dev = (float *)d;
+    const size_t out_at = (size_t)KV_NUM_LAYERS * TYB_SLOT_FLOATS;
+    t->h_out = t->h_rows + out_at;
+    t->h_out_dev = t->h_rows_dev + out_at;
     return 1;
 }
 

@@ -314,3 +314,32 @@ int tyb_finish(void *stream, const char *what)
 }
 
 int attn_sync(void) { return tyb_finish(g_stream, "attn_sync") ? 0 : 1; }
+
+/* A blocking decode call with a host output returns once the output is there, not once the
+ * launch has retired: measured on a B200 (4K-row BF16 decode, page-locked buffers), a host
+ * waiting in cudaStreamSynchronize saw the launch complete ~3 us after a host polling the output
+ * saw the last word land.  The output is filled with TYB_UNWRITTEN before the launch -- a NaN
+ * whose sign bit is set, which GPU arithmetic never produces (it returns the canonical NaN
+ * 0x7FFFFFFF) -- and each word is written once by the kernel with a 16-byte store, so the call
+ * waits until no word holds the pattern.  No fence or flag is needed in the kernel: the words
+ * themselves are the signal.  Every 1024 rounds the stream is queried: if it went idle (or
+ * failed) first, or a kernel raised a status bit, the full synchronisation reports the outcome. */
+void tyb_mark_unwritten(float *out, size_t n)
+{
+    unsigned int *w = (unsigned int *)out;
+    for (size_t i = 0; i < n; i++) w[i] = TYB_UNWRITTEN;
+}
+
+int tyb_wait_output(const float *out, size_t n, void *stream, const char *what)
+{
+    const unsigned int *w = (const unsigned int *)out;
+    volatile unsigned int *mirror = tyb_status_mirror_host();
+    size_t i = 0; /* words [0, i) are written */
+    for (unsigned long spin = 1;; spin++) {
+        while (i < n && __atomic_load_n(&w[i], __ATOMIC_ACQUIRE) != TYB_UNWRITTEN) i++;
+        if (mirror && *mirror) break;
+        if (i == n) return 1;
+        if ((spin & 1023u) == 0u && cudaStreamQuery((cudaStream_t)stream) != cudaErrorNotReady) break;
+    }
+    return tyb_finish(stream, what);
+}
