@@ -608,12 +608,12 @@ int attention_decode_append_fused_gqa(const float *q_raw, const float *k_raw, co
     return 0;
 }
 
-/* xchg_dev / epoch: the sharded form (tyb_prefill_sharded); NULL / 0 otherwise. */
+/* xchg_dev / xchg_maps / epoch: the sharded form (tyb_prefill_sharded); NULL / NULL / 0 otherwise. */
 static int prefill_fused_impl(const void *q_raw, const void *k_raw, const void *v_raw, int in_dtype,
                               const float *q_norm, const float *k_norm, const float *token_cos, const float *token_sin,
                               KVCache *cache, int layer_idx, void *output, int out_dtype, int seq_len, float scale,
                               float eps, int kvh0, int nkvh, int head_major, const tyb_prefill_x *xchg_dev,
-                              unsigned int epoch, const char *what)
+                              const void *xchg_maps, unsigned int epoch, const char *what)
 {
     tyb_cache *t = tyb_cache_from(cache);
     if (!t || !check_layer(layer_idx, what)) return 1;
@@ -651,7 +651,7 @@ static int prefill_fused_impl(const void *q_raw, const void *k_raw, const void *
     tyb_note_write(cache, layer_idx, pos0, st);
     if (!tyb_cuda_ok(tyb_prefill_tc_launch(q_raw, in_dtype == ATTN_DT_BF16, q_norm, token_cos, token_sin, kl, vl,
                                            cache->max_seq_len, output, out_dtype == ATTN_DT_BF16, seq_len, pos0, scale,
-                                           eps, kvh0, nkvh, head_major, xchg_dev, epoch, st),
+                                           eps, kvh0, nkvh, head_major, xchg_dev, xchg_maps, epoch, st),
                      what))
         return 1;
     tyb_note_nowrite(st);
@@ -664,7 +664,7 @@ int attention_prefill_fused_gqa(const void *q_raw, const void *k_raw, const void
                                 int seq_len, float scale, float eps)
 {
     return prefill_fused_impl(q_raw, k_raw, v_raw, in_dtype, q_norm, k_norm, token_cos, token_sin, cache, layer_idx,
-                              output, out_dtype, seq_len, scale, eps, 0, KV_NUM_KV_HEADS, 0, NULL, 0,
+                              output, out_dtype, seq_len, scale, eps, 0, KV_NUM_KV_HEADS, 0, NULL, NULL, 0,
                               "attention_prefill_fused_gqa");
 }
 
@@ -676,7 +676,7 @@ int attention_prefill_fused_gqa_heads(const void *q_raw, const void *k_raw, cons
     const char *what = "attention_prefill_fused_gqa_heads";
     if (!check_heads(kv_head0, kv_heads, what)) return 1;
     return prefill_fused_impl(q_raw, k_raw, v_raw, in_dtype, q_norm, k_norm, token_cos, token_sin, cache, layer_idx,
-                              output, out_dtype, seq_len, scale, eps, kv_head0, kv_heads, 1, NULL, 0, what);
+                              output, out_dtype, seq_len, scale, eps, kv_head0, kv_heads, 1, NULL, NULL, 0, what);
 }
 
 int attn_heads_to_tokens(const void *gathered, void *output, int seq_len, int dtype)
@@ -707,9 +707,9 @@ int attn_heads_to_tokens(const void *gathered, void *output, int seq_len, int dt
 int tyb_prefill_sharded(const void *q_raw, const void *k_raw, const void *v_raw, int in_dtype, const float *q_norm,
                         const float *k_norm, const float *token_cos, const float *token_sin, KVCache *cache,
                         int layer_idx, void *own_slot, int seq_len, float scale, float eps, int kv_head0, int kv_heads,
-                        const void *xchg_dev, unsigned int epoch, const char *what)
+                        const void *xchg_dev, const void *xchg_maps, unsigned int epoch, const char *what)
 {
     return prefill_fused_impl(q_raw, k_raw, v_raw, in_dtype, q_norm, k_norm, token_cos, token_sin, cache, layer_idx,
                               own_slot, ATTN_DT_BF16, seq_len, scale, eps, kv_head0, kv_heads, 0,
-                              (const tyb_prefill_x *)xchg_dev, epoch, what);
+                              (const tyb_prefill_x *)xchg_dev, xchg_maps, epoch, what);
 }

@@ -147,12 +147,19 @@ int tyb_kv_prep_launch(const void *k_raw, const void *v_raw, int in_bf16, const 
  * Launched as a programmatic dependent of the previous kernel in the stream, which must be the
  * tyb_kv_prep_launch of the same rows (it starts before that kernel completes; its TMA producer
  * waits for it before reading the cache).  * xchg_dev (device table, or NULL): the output rows go, token-major BF16, into slot (epoch & 1)
- * of EVERY rank's exchange buffer instead of `out`, and the kernel returns only once all ranks'
- * rows of call `epoch` are in this rank's buffer (bounded wait). */
+ * of EVERY rank's exchange buffer instead of `out` (TMA stores through xchg_maps, tyb_prefill_x_maps),
+ * and the kernel returns only once all ranks' rows of call `epoch` are in this rank's buffer
+ * (bounded wait). */
 int tyb_prefill_tc_launch(const void *q, int q_bf16, const float *q_norm, const float *cos, const float *sin,
                           const void *k_cache, const void *v_cache, int row_capacity, void *out, int out_bf16,
                           int Sq, int pos_offset, float scale, float eps, int kvh0, int nkvh, int out_head_major,
-                          const tyb_prefill_x *xchg_dev, unsigned int epoch, void *stream);
+                          const tyb_prefill_x *xchg_dev, const void *xchg_maps, unsigned int epoch, void *stream);
+/* The TMA tensor maps the sharded prefill stores its output tiles through (xchg_maps of
+ * tyb_prefill_tc_launch): one per rank over the two slots of that rank's exchange buffer
+ * (bases[p]: the buffer, as tyb_prefill_x.base), written to maps_out (8 x 128 bytes, 64-byte
+ * aligned).  0 on success. */
+#define TYB_PX_MAPS_BYTES (8 * 128)
+int tyb_prefill_x_maps(void *const *bases, int world, int max_tokens, void *maps_out);
 
 /* ---- tensor-core prefill at the FP32 bar (prefill_tc32.cu) ----------------------------- */
 

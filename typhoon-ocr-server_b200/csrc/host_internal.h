@@ -160,12 +160,13 @@ void tyb_note_nowrite(void *stream);
 int  tyb_prefetch_rows(const void *cache, int layer, int rows);
 
 /* The fused prefill of attention_prefill_fused_gqa_heads in its sharded form: output rows into
- * every rank's exchange slot (xchg_dev: the device tyb_prefill_x of shard.c; own_slot: this rank's
- * slot of call `epoch`, for the argument checks).  0 on success. */
+ * every rank's exchange slot (xchg_dev: the device tyb_prefill_x of shard.c, xchg_maps its
+ * tyb_prefill_x_maps; own_slot: this rank's slot of call `epoch`, for the argument checks).
+ * 0 on success. */
 int tyb_prefill_sharded(const void *q_raw, const void *k_raw, const void *v_raw, int in_dtype, const float *q_norm,
                         const float *k_norm, const float *token_cos, const float *token_sin, KVCache *cache,
                         int layer_idx, void *own_slot, int seq_len, float scale, float eps, int kv_head0, int kv_heads,
-                        const void *xchg_dev, unsigned int epoch, const char *what);
+                        const void *xchg_dev, const void *xchg_maps, unsigned int epoch, const char *what);
 
 /* Wait for `stream`, then check the device status word.  1 when all is well;
  * otherwise 0 with the error set. */

@@ -74,6 +74,14 @@ struct PrefillTcArgs {
     unsigned long long wait_ns;  // limit of every bounded wait (tyb_wait_limit)
 };
 
+// Sharded form: per rank, a 4-D map of its exchange slots {128 dims, 16 heads, max_tokens tokens,
+// 2 slots} (BF16, token-major), stored to in boxes of {64 dims, 1 head, 128 tokens, 1 slot} with
+// the 128-byte swizzle -- the layout of a query tile in shared memory.  Built once per set-up
+// (tyb_prefill_x_maps); unused otherwise.
+struct PrefillPeerMaps {
+    CUtensorMap m[8];
+};
+
 // Softmax weight split between the two exp2 units: of every four column pairs of an unmasked
 // tile, kPtEmuPairs are evaluated on the FMA pipe (exp2_fma2) and the rest on the MUFU.
 constexpr int kPtEmuPairs = 0;
@@ -231,10 +239,19 @@ __device__ __forceinline__ void load_queries(const PrefillTcArgs& a, unsigned ch
     }
 }
 
+// Barrier of the 128 softmax threads of head h (named barriers 1 and 2; 0 is __syncthreads).
+__device__ __forceinline__ void head_bar(int h)
+{
+    if (h == 0)
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+    else
+        asm volatile("bar.sync 2, 128;" ::: "memory");
+}
+
 // 384 threads (3 warpgroups) launched at 168 registers, split 200 / 200 / 96 by setmaxnreg.
 __global__ void __launch_bounds__(kPtThreads, 1)
     prefill_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
-                      const PrefillTcArgs a)
+                      const PrefillTcArgs a, const __grid_constant__ PrefillPeerMaps px)
 {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     // 1024-byte alignment is required by the 128-byte swizzle atoms.
@@ -253,6 +270,7 @@ __global__ void __launch_bounds__(kPtThreads, 1)
     uint64_t* q_full = bars + 14;   // Q0, Q1 written (256 arrivals)
     uint64_t* e_done = bars + 15;   // [2] per head: exponentials of the tile done (128 arrivals)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
+    int* store_fail = reinterpret_cast<int*>(bars + 18);  // [2] per head: its output tile is incomplete
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     // Longest items first: q-tile index descends with blockIdx.
@@ -278,6 +296,7 @@ __global__ void __launch_bounds__(kPtThreads, 1)
             mbar_init(q_full, kPtSoftmaxThreads);
             mbar_init(&e_done[0], kPtSoftmaxThreads / 2);
             mbar_init(&e_done[1], kPtSoftmaxThreads / 2);
+            store_fail[0] = store_fail[1] = 0;
             fence_barrier_init();
             fence_proxy_async_smem();
         }
@@ -473,7 +492,44 @@ __global__ void __launch_bounds__(kPtThreads, 1)
             mbar_arrive(&p_full[h]);
         }
         // Epilogue: O / l for this row.
-        if (ok && warp_wait(&pv_done[h], (uint32_t)(ntiles - 1) & 1u)) {
+        if (a.xchg) {
+            // Sharded: the row, BF16, into this head's query tile -- free, since the last QK of
+            // the head completed before its last P.V -- in the swizzled layout; then one thread
+            // per head sends the 128 x 128 tile to every rank's exchange slot with TMA stores
+            // (two 64-dimension boxes per rank), the all-gather of the head outputs done by the
+            // epilogue that produces them, in transfers of whole tiles.
+            const bool done = ok && warp_wait(&pv_done[h], (uint32_t)(ntiles - 1) & 1u);
+            if (!done) {
+                store_fail[h] = 1;
+            } else {
+                tc_fence_after();
+                const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+                unsigned char* tile = sQ + h * kPtTile;
+#pragma unroll
+                for (int c = 0; c < 4; c++) {
+                    float v[32];
+                    tmem_ld32(o_addr + c * 32, v);
+#pragma unroll
+                    for (int i = 0; i < 32; i += 8)
+                        *reinterpret_cast<uint4*>(tile + sw128_offset(r, c * 32 + i)) =
+                            make_uint4(pack_bf16x2(v[i] * inv, v[i + 1] * inv), pack_bf16x2(v[i + 2] * inv, v[i + 3] * inv),
+                                       pack_bf16x2(v[i + 4] * inv, v[i + 5] * inv), pack_bf16x2(v[i + 6] * inv, v[i + 7] * inv));
+                }
+            }
+            fence_proxy_async_smem();  // the tile is read by the TMA unit (async proxy)
+            head_bar(h);
+            if (lane == 0 && (warp & 3) == 0 && !store_fail[h]) {
+                const int slot = (int)(a.epoch & 1u), world = a.xchg->world;
+                const unsigned char* tile = sQ + h * kPtTile;
+#pragma unroll 1
+                for (int p = 0; p < world; p++) {
+                    tma_store_4d(&px.m[p], 0, kGroup * kvh + h, t0, slot, tile);
+                    tma_store_4d(&px.m[p], 64, kGroup * kvh + h, t0, slot, tile + kPtBox);
+                }
+                tma_store_drain();
+                asm volatile("fence.acq_rel.sys;" ::: "memory");
+            }
+        } else if (ok && warp_wait(&pv_done[h], (uint32_t)(ntiles - 1) & 1u)) {
             tc_fence_after();
             const int tok = t0 + r;
             const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
@@ -484,23 +540,7 @@ __global__ void __launch_bounds__(kPtThreads, 1)
             for (int c = 0; c < 4; c++) {
                 float v[32];
                 tmem_ld32(o_addr + c * 32, v);
-                if (tok < a.Sq && a.xchg) {
-                    // Sharded: the row, token-major BF16, into this call's slot of every rank's
-                    // exchange buffer (peer stores over NVLink) -- the all-gather of the head
-                    // outputs done by the epilogue that produces them.
-                    uint4 u[4];
-#pragma unroll
-                    for (int i = 0; i < 32; i += 8)
-                        u[i / 8] = make_uint4(pack_bf16x2(v[i] * inv, v[i + 1] * inv), pack_bf16x2(v[i + 2] * inv, v[i + 3] * inv),
-                                              pack_bf16x2(v[i + 4] * inv, v[i + 5] * inv), pack_bf16x2(v[i + 6] * inv, v[i + 7] * inv));
-                    const size_t slot = (size_t)(a.epoch & 1u) * (size_t)a.xchg->slot_elems + ooff + c * 32;
-                    for (int p = 0; p < a.xchg->world; p++) {
-                        uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.xchg->base[p]) +
-                                                              TYB_PX_HEADER_BYTES / 2 + slot);
-#pragma unroll
-                        for (int i = 0; i < 4; i++) dst[i] = u[i];
-                    }
-                } else if (tok < a.Sq) {
+                if (tok < a.Sq) {
                     if (a.out_bf16) {
                         __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(a.out) + ooff + c * 32;
 #pragma unroll
@@ -674,6 +714,26 @@ extern "C" int tyb_encode_rows_map(void* map, const void* base, int rows, int ro
     return make_rows_map(static_cast<CUtensorMap*>(map), base, rows, row_capacity, box_rows) ? 0 : 1;
 }
 
+extern "C" int tyb_prefill_x_maps(void* const* bases, int world, int max_tokens, void* maps_out)
+{
+    EncodeTiledFn fn = encode_fn();
+    if (!fn || world < 1 || world > 8 || max_tokens <= 0) return (int)cudaErrorInvalidValue;
+    CUtensorMap* maps = static_cast<CUtensorMap*>(maps_out);
+    memset(maps, 0, sizeof(PrefillPeerMaps));
+    const cuuint64_t dims[4] = {(cuuint64_t)kD, (cuuint64_t)kHq, (cuuint64_t)max_tokens, 2};
+    const cuuint64_t strides[3] = {(cuuint64_t)kD * 2, (cuuint64_t)kHq * kD * 2, (cuuint64_t)max_tokens * kHq * kD * 2};
+    const cuuint32_t box[4] = {64, 1, (cuuint32_t)(max_tokens < kPtRows ? max_tokens : kPtRows), 1};
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    for (int p = 0; p < world; p++) {
+        void* slots = static_cast<unsigned char*>(bases[p]) + TYB_PX_HEADER_BYTES;
+        if (fn(&maps[p], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, slots, dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return (int)cudaErrorInvalidValue;
+    }
+    return 0;
+}
+
 extern "C" int tyb_kv_prep_launch(const void* k_raw, const void* v_raw, int in_bf16, const float* k_norm,
                                   const float* cos, const float* sin, void* k_dst, void* v_dst, int row_capacity,
                                   int pos0, int S, float eps, int kvh0, int nkvh, void* stream)
@@ -692,9 +752,10 @@ extern "C" int tyb_prefill_tc_launch(const void* q, int q_bf16, const float* q_n
                                      const float* sin, const void* k_cache, const void* v_cache, int row_capacity,
                                      void* out, int out_bf16, int Sq, int pos_offset, float scale, float eps,
                                      int kvh0, int nkvh, int out_head_major, const tyb_prefill_x* xchg_dev,
-                                     unsigned int epoch, void* stream)
+                                     const void* xchg_maps, unsigned int epoch, void* stream)
 {
     if (Sq <= 0 || nkvh <= 0) return 0;
+    if (xchg_dev && !xchg_maps) return (int)cudaErrorInvalidValue;
     // Once per device: the shared-memory opt-in, and a check that the kernel was compiled
     // for the launch register count its setmaxnreg split is sized against (a split above
     // the launch's registers would never be granted).
@@ -754,5 +815,10 @@ extern "C" int tyb_prefill_tc_launch(const void* q, int q_bf16, const float* q_n
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return (int)cudaLaunchKernelEx(&cfg, prefill_tc_kernel, mk, mv, a);
+    PrefillPeerMaps px;
+    if (xchg_maps)
+        memcpy(&px, xchg_maps, sizeof px);
+    else
+        memset(&px, 0, sizeof px);
+    return (int)cudaLaunchKernelEx(&cfg, prefill_tc_kernel, mk, mv, a, px);
 }

@@ -27,6 +27,8 @@ static struct {
     void *px;                /* this rank's prefill exchange buffer (device) */
     void *peer_px[8];        /* every rank's, mapped (own at `rank`) */
     tyb_prefill_x *px_dev;   /* device copy of the table */
+    /* the TMA maps of every rank's slots the prefill stores its output tiles through */
+    unsigned char px_maps[TYB_PX_MAPS_BYTES] __attribute__((aligned(64)));
     unsigned int px_epoch;   /* sharded prefill calls made (host count; the kernel gets it) */
 } g_sh;
 
@@ -120,7 +122,8 @@ int attn_shard_init(int rank, int nranks, int max_tokens, attn_allgather_fn allg
             table.base[p] = g_sh.peer_px[p];
         }
         ok = ok && tyb_dev_alloc((void **)&g_sh.px_dev, sizeof table, "attn_shard_init: exchange table") &&
-             tyb_cuda_ok(cudaMemcpy(g_sh.px_dev, &table, sizeof table, cudaMemcpyHostToDevice), what);
+             tyb_cuda_ok(cudaMemcpy(g_sh.px_dev, &table, sizeof table, cudaMemcpyHostToDevice), what) &&
+             tyb_cuda_ok(tyb_prefill_x_maps(table.base, nranks, max_tokens, g_sh.px_maps), what);
     }
     free(all);
     free(dec);
@@ -180,7 +183,7 @@ int attention_prefill_fused_gqa_sharded(const void *q_raw, const void *k_raw, co
         return 0;
     }
     if (tyb_prefill_sharded(q_raw, k_raw, v_raw, in_dtype, q_norm, k_norm, token_cos, token_sin, cache, layer_idx,
-                            slot, seq_len, scale, eps, h0, n, g_sh.px_dev, epoch, what))
+                            slot, seq_len, scale, eps, h0, n, g_sh.px_dev, g_sh.px_maps, epoch, what))
         return 1;
     g_sh.px_epoch = epoch;
     *output = slot;

@@ -135,6 +135,25 @@ __device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* m
         : "memory");
 }
 
+// TMA tensor store: a 4-D box from shared memory to global memory (a peer's, over NVLink, in the
+// sharded prefill), as part of this thread's bulk async-group.
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, int c0, int c1, int c2, int c3, const void* smem_src)
+{
+    asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(smem_u32(smem_src)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+                 : "memory");
+}
+
+// Completion of this thread's bulk async-group stores: the writes are performed, then ordered
+// (async proxy -> generic proxy) before this thread's later release.
+__device__ __forceinline__ void tma_store_drain()
+{
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+    asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
 // Shared-memory matrix descriptor (sm_100 format, version 1) for a 128-byte-swizzled tile.
 //   K-major operands (Q, K, P): 8-row core groups 1024 B apart (SBO); LBO unused (1).
 //   MN-major operand (V): 64-element atoms along N are `lbo` bytes apart; SBO = 1024 B.
