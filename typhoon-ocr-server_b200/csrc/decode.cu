@@ -567,19 +567,22 @@ constexpr int kMmaStat = 64 + 256;  // floats: block maxima and sums [16][2] x 2
 // With the KV heads of one sequence split over N ranks, every rank needs the whole [16][128]
 // output of each decode call.  Instead of a separate collective per layer, the CTA that writes a
 // head pair's final output also stores it into every rank's exchange buffer (peer stores over
-// NVLink into memory mapped by CUDA IPC) and raises that head's flag there, after one
-// system-scope release fence.  The rank's last such CTA of the call (a device-scope ticket) then
-// waits, bounded, for all 8 heads' flags in its own buffer and copies the assembled output to the
-// caller -- inside the decode kernel, so a call is one launch.  Epochs (one per call, counted on
-// each rank) make the flags monotone, and the exchange buffer is double-buffered by epoch parity:
-// a rank can run at most one call ahead of another (its next call completes only once the other
-// has raised its flags of that call, which it does after completing the current one).
+// NVLink into memory mapped by CUDA IPC), each value as one 64-bit word that carries the call's
+// epoch beside the value's bits: a word is single-copy atomic, so a reader that sees the epoch
+// sees the value, and no fence or flag is needed.  The rank's last such CTA of the call (a
+// device-scope ticket) then polls, bounded, the 16 x 128 words of its own buffer until each
+// carries the epoch and writes the values to the caller -- inside the decode kernel, so a call is
+// one launch.  Epochs (one per call, counted on each rank) grow by one per call, and the words
+// are double-buffered by epoch parity: a rank can run at most one call ahead of another (its next
+// call completes only once the other has stored its words of that call, which it does after
+// completing the current one), so a word of two calls back is never taken for the current one.
+// (The first form raised one flag per head after a system-scope release fence, ~2 us per call.)
 
 constexpr int kGatherMaxRanks = 8;
 
 struct GatherBuf {                          // one per rank, in that rank's device memory
-    float data[2][kHq][kD];                 // assembled outputs, by epoch parity
-    unsigned int flags[kHkv];               // flags[h]: last epoch whose head pair h is stored here
+    unsigned long long words[2][kHq][kD];   // by epoch parity: (epoch << 32) | the value's bits
+    float stage[kHq][kD];                   // this rank's head pairs' outputs before they are sent
     unsigned int epoch;                     // calls this rank has completed (local)
     unsigned int done;                      // this rank's head pairs published in the current call
 };
@@ -602,53 +605,62 @@ __device__ __forceinline__ void st_relaxed_sys(unsigned int* p, unsigned int v)
     asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
+__device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long* p, unsigned long long v)
+{
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned long long* p)
+{
+    unsigned long long v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
 // Called by every thread of the CTA that has just written the rows of KV head kvh's query pair
-// into this rank's exchange slot data[epoch & 1]: stores them into every other rank's slot
-// (16-byte peer stores), then one system-scope release fence and the head's flag in every
-// buffer (plain relaxed stores: the fence orders the CTA's stores, made its own by the barrier,
-// before them).  The rank's last head pair of the call waits for all heads' flags in its own
-// buffer (bounded: a rank that never publishes raises TYB_STATUS_WAIT_TIMEOUT) and copies the
-// assembled [16][128] to `out`.
+// into this rank's stage: stores them, as epoch-carrying words, into slot epoch & 1 of every
+// rank's buffer (its own included).  The rank's last head pair of the call (a device-scope
+// ticket among this rank's CTAs) then reads all 16 x 128 words of its own slot, each polled until
+// it carries the epoch (bounded: a rank that never publishes raises TYB_STATUS_WAIT_TIMEOUT), and
+// writes the assembled [16][128] to `out`.
 __device__ __forceinline__ void gather_publish(const GatherDev* g, int kvh, int nkvh_local, unsigned int epoch,
                                                float* out)
 {
     __shared__ int s_last, s_fail;
     const int par = (int)(epoch & 1u);
     GatherBuf* mine = g->buf[g->rank];
-    __syncthreads();
-    if (threadIdx.x < 2 * kD / 4) {
-        const float4 v = reinterpret_cast<const float4*>(&mine->data[par][kGroup * kvh][0])[threadIdx.x];
-        for (int p = 0; p < g->world; p++)
-            if (p != g->rank) reinterpret_cast<float4*>(&g->buf[p]->data[par][kGroup * kvh][0])[threadIdx.x] = v;
+    __syncthreads();  // the head pair's rows are in the stage
+    if (threadIdx.x < 2 * kD) {
+        const int i = kGroup * kvh * kD + threadIdx.x;  // element of [16][128]
+        const unsigned long long w =
+            ((unsigned long long)epoch << 32) | __float_as_uint((&mine->stage[0][0])[i]);
+        for (int p = 0; p < g->world; p++) st_relaxed_sys_u64(&g->buf[p]->words[par][0][0] + i, w);
     }
-    __syncthreads();
     if (threadIdx.x == 0) {
-        asm volatile("fence.acq_rel.sys;" ::: "memory");
-        for (int p = 0; p < g->world; p++) st_relaxed_sys(&g->buf[p]->flags[kvh], epoch);
         unsigned int t;
-        asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(t) : "l"(&mine->done) : "memory");
+        asm volatile("atom.relaxed.gpu.global.add.u32 %0, [%1], 1;" : "=r"(t) : "l"(&mine->done) : "memory");
         s_last = t == (unsigned int)(nkvh_local - 1);
         if (s_last) mine->done = 0u;  // the next call's tickets come after this kernel has completed
         s_fail = 0;
     }
     __syncthreads();
     if (!s_last) return;
-    if (threadIdx.x < kHkv) {
-        const uint64_t t0 = globaltimer_ns();
-        while ((int)(ld_acquire_sys(&mine->flags[threadIdx.x]) - epoch) < 0) {
+    const unsigned long long* src = &mine->words[par][0][0];
+    const uint64_t t0 = globaltimer_ns();
+    for (int i = threadIdx.x; i < kHq * kD && !s_fail; i += blockDim.x) {
+        unsigned long long w = ld_relaxed_sys_u64(src + i);
+        while ((unsigned int)(w >> 32) != epoch) {
             if (globaltimer_ns() - t0 > wait_limit_ns()) {
                 raise_status(TYB_STATUS_WAIT_TIMEOUT);
                 s_fail = 1;
                 break;
             }
-            __nanosleep(32);
+            w = ld_relaxed_sys_u64(src + i);
         }
+        out[i] = __uint_as_float((unsigned int)w);
     }
     __syncthreads();
-    if (s_fail) return;
-    const float4* src = reinterpret_cast<const float4*>(&mine->data[par][0][0]);
-    for (int i = threadIdx.x; i < kHq * kD / 4; i += blockDim.x) reinterpret_cast<float4*>(out)[i] = __ldcg(src + i);
-    if (threadIdx.x == 0) mine->epoch = epoch;
+    if (threadIdx.x == 0 && !s_fail) mine->epoch = epoch;
 }
 
 struct DecodeMmaArgs {
@@ -1222,7 +1234,7 @@ __global__ void __launch_bounds__(NW * 32, 16 / NW)
     float* out_pair = a.out + (size_t)b * kHq * kD + (size_t)(kGroup * (kvh - a.kvh0)) * kD;
     if (a.gather) {
         epoch = __ldcg(&a.gather->buf[a.gather->rank]->epoch) + 1u;
-        out_pair = &a.gather->buf[a.gather->rank]->data[epoch & 1u][kGroup * kvh][0];
+        out_pair = &a.gather->buf[a.gather->rank]->stage[kGroup * kvh][0];
     }
 
     if (nsplit == 1) {
@@ -1576,7 +1588,7 @@ __global__ void __launch_bounds__(256, 2)
     float* out_pair = a.out + (size_t)b * kHq * kD + (size_t)(kGroup * (kvh - a.kvh0)) * kD;
     if (a.gather) {
         epoch = __ldcg(&a.gather->buf[a.gather->rank]->epoch) + 1u;
-        out_pair = &a.gather->buf[a.gather->rank]->data[epoch & 1u][kGroup * kvh][0];
+        out_pair = &a.gather->buf[a.gather->rank]->stage[kGroup * kvh][0];
     }
     if (nspan == 1) {
         if (holder) {
