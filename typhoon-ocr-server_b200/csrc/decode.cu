@@ -610,11 +610,12 @@ __device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long* p, unsign
     asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 
-__device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned long long* p)
+// Two words with one 16-byte load; each word is validated on its own (its epoch), so the pair
+// need not be read at one instant.
+__device__ __forceinline__ void ld_relaxed_sys_u64x2(const unsigned long long* p, unsigned long long& a,
+                                                     unsigned long long& b)
 {
-    unsigned long long v;
-    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-    return v;
+    asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
 }
 
 // Called by every thread of the CTA that has just written the rows of KV head kvh's query pair
@@ -645,19 +646,31 @@ __device__ __forceinline__ void gather_publish(const GatherDev* g, int kvh, int 
     }
     __syncthreads();
     if (!s_last) return;
+    // Each thread reads 8 consecutive words with all its loads in flight at once, then re-reads
+    // until every one carries the epoch (polling one word at a time costs a round trip each).
     const unsigned long long* src = &mine->words[par][0][0];
     const uint64_t t0 = globaltimer_ns();
-    for (int i = threadIdx.x; i < kHq * kD && !s_fail; i += blockDim.x) {
-        unsigned long long w = ld_relaxed_sys_u64(src + i);
-        while ((unsigned int)(w >> 32) != epoch) {
-            if (globaltimer_ns() - t0 > wait_limit_ns()) {
+    for (int i0 = threadIdx.x * 8; i0 < kHq * kD; i0 += blockDim.x * 8) {
+        unsigned long long w[8];
+        bool all = false;
+        while (!all) {
+#pragma unroll
+            for (int k = 0; k < 8; k += 2) ld_relaxed_sys_u64x2(src + i0 + k, w[k], w[k + 1]);
+            all = true;
+#pragma unroll
+            for (int k = 0; k < 8; k++) all = all && (unsigned int)(w[k] >> 32) == epoch;
+            if (!all && globaltimer_ns() - t0 > wait_limit_ns()) {
                 raise_status(TYB_STATUS_WAIT_TIMEOUT);
                 s_fail = 1;
                 break;
             }
-            w = ld_relaxed_sys_u64(src + i);
         }
-        out[i] = __uint_as_float((unsigned int)w);
+        if (!all) break;
+        float4* o = reinterpret_cast<float4*>(out + i0);
+        o[0] = make_float4(__uint_as_float((unsigned int)w[0]), __uint_as_float((unsigned int)w[1]),
+                           __uint_as_float((unsigned int)w[2]), __uint_as_float((unsigned int)w[3]));
+        o[1] = make_float4(__uint_as_float((unsigned int)w[4]), __uint_as_float((unsigned int)w[5]),
+                           __uint_as_float((unsigned int)w[6]), __uint_as_float((unsigned int)w[7]));
     }
     __syncthreads();
     if (threadIdx.x == 0 && !s_fail) mine->epoch = epoch;
