@@ -93,7 +93,7 @@ static int inline_inputs(tyb_cache *t, int layer, const float *q, const float *k
     if (!tyb_slots_ready(t, what)) return 0;
     float *slot = tyb_row_slot(t, layer);
     /* an earlier launch may still read the slot through its mapping (a deferred row's write) */
-    if (!tyb_cuda_ok(cudaEventSynchronize((cudaEvent_t)t->row_ev[layer]), what)) return 0;
+    if (!tyb_slot_wait(t, layer, what)) return 0;
     if (k_new && k_new != slot) memcpy(slot, k_new, TYB_ROW_FLOATS * sizeof(float));
     if (v_new && v_new != slot + TYB_ROW_FLOATS) memcpy(slot + TYB_ROW_FLOATS, v_new, TYB_ROW_FLOATS * sizeof(float));
     memcpy(slot + 2 * TYB_ROW_FLOATS, q, TYB_Q_FLOATS * sizeof(float));
@@ -136,7 +136,7 @@ static int stage_inputs(tyb_cache *t, int layer, const float *q, const float *k_
     if (!tyb_slots_ready(t, what)) return 0;
     float *slot = tyb_row_slot(t, layer);
     /* the slot's previous contents have been read (a deferred row is already in place) */
-    if (!tyb_cuda_ok(cudaEventSynchronize((cudaEvent_t)t->row_ev[layer]), what)) return 0;
+    if (!tyb_slot_wait(t, layer, what)) return 0;
     if (!rk && k_new != slot) memcpy(slot, k_new, TYB_ROW_FLOATS * sizeof(float));
     if (!rv && v_new != slot + TYB_ROW_FLOATS) memcpy(slot + TYB_ROW_FLOATS, v_new, TYB_ROW_FLOATS * sizeof(float));
     if (!rq) memcpy(slot + 2 * TYB_ROW_FLOATS, q, TYB_Q_FLOATS * sizeof(float));

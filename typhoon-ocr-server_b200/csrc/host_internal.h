@@ -44,6 +44,7 @@ typedef struct {
                               * parameter block of a decode launch from host inputs) */
     float *h_rows_dev;       /* its device view */
     void *row_ev[KV_NUM_LAYERS]; /* cudaEvent_t: recorded after the launch that read the layer's slot */
+    unsigned char slot_read[KV_NUM_LAYERS]; /* row_ev recorded since the host last waited for it */
     int pending[KV_NUM_LAYERS];  /* row the layer's staged row goes to, or -1 */
     /* In the same page-locked block, after the slots: the [16][128] output staging of a pageable
      * host output (written by the decode kernel through its device view, copied out after the
@@ -70,6 +71,10 @@ static inline float *tyb_row_slot(const tyb_cache *t, int layer) { return t->h_r
 int tyb_slots_ready(tyb_cache *t, const char *what);
 /* Records the layer's "slot consumed" event after a launch that read the slot. */
 int tyb_slot_consumed(tyb_cache *t, int layer, void *stream, const char *what);
+/* Before the host rewrites the layer's slot: waits for the last launch that read it, if one has
+ * since the last wait (a launch that takes the slot as its parameter block copies it at the
+ * launch and records nothing).  1 on success. */
+int tyb_slot_wait(tyb_cache *t, int layer, const char *what);
 
 /* The cache behind a KVCache*, or NULL (error set) if this library did not make it. */
 tyb_cache *tyb_cache_from(const KVCache *c);

@@ -165,7 +165,17 @@ int tyb_slots_ready(tyb_cache *t, const char *what)
 
 int tyb_slot_consumed(tyb_cache *t, int layer, void *stream, const char *what)
 {
-    return tyb_cuda_ok(cudaEventRecord((cudaEvent_t)t->row_ev[layer], (cudaStream_t)stream), what);
+    if (!tyb_cuda_ok(cudaEventRecord((cudaEvent_t)t->row_ev[layer], (cudaStream_t)stream), what)) return 0;
+    t->slot_read[layer] = 1;
+    return 1;
+}
+
+int tyb_slot_wait(tyb_cache *t, int layer, const char *what)
+{
+    if (!t->slot_read[layer]) return 1;
+    if (!tyb_cuda_ok(cudaEventSynchronize((cudaEvent_t)t->row_ev[layer]), what)) return 0;
+    t->slot_read[layer] = 0;
+    return 1;
 }
 
 int tyb_flush_pending(tyb_cache *t, int layer, const char *what)
@@ -213,7 +223,7 @@ static void append_rows(KVCache *c, int layer, const float *k_new, const float *
          * after the reference's memcpy), written to the cache by the next launch on this layer --
          * attention_decode_gqa over seq_len + 1 rows appends and attends in one kernel. */
         if (tyb_slots_ready(t, what)) {
-            if (!tyb_cuda_ok(cudaEventSynchronize((cudaEvent_t)t->row_ev[layer]), what)) return; /* slot free */
+            if (!tyb_slot_wait(t, layer, what)) return; /* slot free */
             float *slot = tyb_row_slot(t, layer);
             memcpy(slot, k_new, TYB_ROW_FLOATS * sizeof(float));
             memcpy(slot + TYB_ROW_FLOATS, v_new, TYB_ROW_FLOATS * sizeof(float));
