@@ -662,13 +662,15 @@ def time_e2e(pkg, lib, cache, steps, device):
     qp, op, kp, vp = q.data_ptr(), out.data_ptr(), kn.data_ptr(), vn.data_ptr()
     cs = pkg.cache_struct(cache)
 
+    # per-layer buffer addresses, as a decoder loop holds them (the argtypes convert the ints)
+    args = [(qp + layer * HQ * D * 4, kp + layer * HKV * D * 4, vp + layer * HKV * D * 4, op + layer * HQ * D * 4)
+            for layer in range(LAYERS)]
+    fn = lib.attention_decode_append_gqa
+
     def one(step):
         cs.seq_len = kv_len_of(step) - 1
-        for layer in range(LAYERS):
-            lib.attention_decode_append_gqa(ctypes.c_void_p(qp + layer * HQ * D * 4),
-                                            ctypes.c_void_p(kp + layer * HKV * D * 4),
-                                            ctypes.c_void_p(vp + layer * HKV * D * 4), cache,
-                                            ctypes.c_void_p(op + layer * HQ * D * 4), layer, scale)
+        for layer, (ql, kl, vl, ol) in enumerate(args):
+            fn(ql, kl, vl, cache, ol, layer, scale)
 
     for s in range(5):
         one(s)
@@ -701,11 +703,15 @@ def time_decode_dropin(pkg, lib, cache, steps):
     scale = ctypes.c_float(pkg.SCALE)
     cs = pkg.cache_struct(cache)
 
+    sq, sk, sv, sattn = s.q, s.k, s.v, s.attn  # the DecoderScratch pointers decoder.c passes
+    append, attend = lib.kv_cache_append, lib.attention_decode_gqa
+
     def one(step):
         cs.seq_len = kv_len_of(step) - 1
+        kv = cs.seq_len + 1
         for layer in range(LAYERS):
-            lib.kv_cache_append(cache, layer, s.k, s.v)
-            lib.attention_decode_gqa(s.q, cache, s.attn, layer, cs.seq_len + 1, scale)
+            append(cache, layer, sk, sv)
+            attend(sq, cache, sattn, layer, kv, scale)
         lib.kv_cache_advance(cache, 1)
 
     try:
