@@ -6,21 +6,23 @@
 // normalise, out = sum p*V) and, fused, kernel/kv_cache.c:53-65 (the new row written at
 // row seq_len first).  One CTA owns one (sequence, KV head, split of rows):
 //   1. the split's K and V rows are requested into shared memory by TMA on two mbarriers.
-//      Kernels are launched with programmatic dependent launch and the grid is planned to
-//      fill only half of the SM slots, so the next kernel's CTAs are resident early and
-//      request their rows BEFORE griddepcontrol.wait (only rows the host knows the
-//      previous launch did not write).  On B200 such copies were measured to complete only
-//      once the previous grid has finished (they land right after the wait returns), so
-//      what this saves is the request latency, not the transfer;
+//      Kernels are launched with programmatic dependent launch, so the next kernel's CTAs are
+//      resident early and request their rows BEFORE griddepcontrol.wait (only rows the host
+//      knows the previous launch did not write).  On B200 the completion of such copies is
+//      held until the previous grid has finished, but their data moves meanwhile: at 4K the
+//      K tile lands ~0.5 us after the wait returns, against ~2.6 us of HBM time for a layer;
 //   2. after the wait: the query (and the new row, written to the cache and into its
 //      slot), scores of both query heads, max and exp2 per head;
 //   3. p.V for both heads from the same V bytes (GQA pair read once);
 //   4. the split's (max, sum, unnormalised o) goes to a workspace record; the CTA that
-//      takes the last ticket merges all records, pulled into shared memory by bulk
-//      copies, and writes the output.  No second launch.
-// Two kernels implement it: decode_mma_kernel (one sequence, BF16 cache: the contractions on
-// the tensor cores through mma.sync, tiles by TMA tensor copies) and decode_split_kernel<T>
-// (FP32 caches and request batches: CUDA-core dot products, tiles by 1-D bulk copies).
+//      takes the last ticket merges all records (up to 32 with plain L2 loads, 33-64 pulled
+//      into shared memory by bulk copies, more in two levels of groups) and writes the
+//      output.  No second launch.
+// Three kernels implement it: decode_mma_kernel (one sequence whose splits fit one wave, BF16
+// cache: the contractions on the tensor cores through mma.sync, tiles by TMA tensor copies),
+// decode_stream_kernel (longer sequences and request batches, BF16: each CTA streams a span of
+// rows in double-buffered stages with an online softmax) and decode_split_kernel<T> (FP32
+// caches: CUDA-core dot products, tiles by 1-D bulk copies).
 // Bandwidth-bound: 2 * kv_len * 128 * sizeof(T) bytes per (sequence, KV head).
 #include <cuda.h>
 
