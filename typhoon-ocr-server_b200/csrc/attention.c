@@ -117,11 +117,13 @@ static int host_output(tyb_cache *t, float *output, float *dout_mapped, int kind
 }
 
 /* The single-token inputs of a decode call -- q [16][128] and, for an append, k_new / v_new
- * [8][128] (NULL when absent) -- on the device.  Device buffers are used in place.  Host buffers
- * (page-locked or not) are copied now into the layer's page-locked slot of the cache, so the
- * caller may reuse them on return, and the slot reaches the device in ONE copy, into the cache's
- * staging area, ahead of the kernel: the splits then read L2 instead of each fetching the query
- * over the bus.  k_new / v_new may already be the slot's own rows (a deferred append).
+ * [8][128] (NULL when absent) -- on the device, when they cannot all travel as the launch's
+ * parameter block (inline_inputs: some are device memory, some host memory, or the output is
+ * gathered from every rank).  Device buffers are used in place.  Host buffers (page-locked or
+ * not) are copied now into the layer's page-locked slot of the cache, so the caller may reuse
+ * them on return, and the slot reaches the device in ONE copy, into the cache's staging area,
+ * ahead of the kernel: the splits then read L2 instead of each fetching the query over the bus.
+ * k_new / v_new may already be the slot's own rows (a deferred append).
  * 1 on success, else 0 with the error set. */
 static int stage_inputs(tyb_cache *t, int layer, const float *q, const float *k_new, const float *v_new,
                         const float **dq, const float **dk, const float **dv, void *st, const char *what)
