@@ -12,8 +12,10 @@
  *                                                             -> decode.cu, fused
  *
  * Host buffers are copied to the device on the library stream and results copied back,
- * and then the call waits: the reference's calls block until done.  Device buffers are
- * used in place and the call returns once the work is queued.
+ * and then the call waits: the reference's calls block until done.  The single-token decode
+ * calls take host inputs as the launch's parameter block instead (inline_inputs) and return
+ * once their host output's words are written (host_output, tyb_wait_output).  Device buffers
+ * are used in place and the call returns once the work is queued.
  */
 #include <cuda_runtime_api.h>
 #include <stdlib.h>
