@@ -133,9 +133,10 @@ int attention_decode_append_gqa_heads(const float *q, const float *k_new, const 
 
 /* Decode output gather over NVLink, without a collective library: attention_decode_append_gqa_heads
  * whose output is the whole [16][128] on every rank, in one launch.  The CTA that finishes a head
- * pair stores it into every rank's exchange buffer (peer stores into memory mapped by CUDA IPC)
- * and raises that head's flag there; the rank's last such CTA waits (bounded; attn_last_error on
- * timeout) for all 8 heads' flags of the call and copies the result to `output`.  One rank per
+ * pair stores it into every rank's exchange buffer (peer stores into memory mapped by CUDA IPC),
+ * each value as a 64-bit word carrying the call's number; the rank's last such CTA reads the
+ * 16 x 128 words of its own buffer, each until it carries the call's number (bounded;
+ * attn_last_error on timeout), and writes the values to `output`.  One rank per
  * GPU on one node, up to 8 ranks; every rank calls with the same layers in the same order, and
  * the ranks' KV-head ranges together cover the 8 heads.
  *   attn_gather_init(rank, world)   allocates this rank's exchange buffer on the current device
@@ -169,8 +170,8 @@ int  attention_decode_append_gqa_gathered(const float *q, const float *k_new, co
  * attn_shard_heads: this rank's KV heads.
  *
  * attention_prefill_fused_gqa_sharded: attention_prefill_fused_gqa_heads for this rank's KV heads
- * (raw inputs as there; BF16 cache), whose tensor-core kernel stores every output row, token-major
- * BF16, into the exchange buffer of EVERY rank (peer stores over NVLink from the epilogue that
+ * (raw inputs as there; BF16 cache), whose tensor-core kernel stores every output tile, token-major
+ * BF16, into the exchange buffer of EVERY rank (TMA stores over NVLink from the epilogue that
  * produces it) and returns once all ranks' rows are in place: *output receives this rank's
  * device address of the assembled [seq_len][16][128] BF16 output, valid until the call after
  * next (two slots).  seq_len <= max_tokens.  Calls count on the host: not for CUDA graph

@@ -14,15 +14,18 @@
 //   * all 8 softmax warps load the raw queries, RMSNorm + rotate them in registers and store
 //     them as BF16 into shared memory in the 128-byte-swizzled K-major layout the tensor core
 //     reads (Q0, Q1: 128 x 128 each);
-//   * one thread of warp 8 streams K and V tiles (128 keys x 128 dims, BF16) from the cache
-//     with TMA tensor copies (SWIZZLE_128B; rows past the attended length are zero-filled) and
-//     issues the MMAs: S_h = Q_h . K^T into TMEM, later O_h += P_h . V into TMEM;
+//   * one thread of warp 9 streams K and V tiles (128 keys x 128 dims, BF16) from the cache
+//     with TMA tensor copies (SWIZZLE_128B; rows past the attended length are zero-filled), and
+//     one thread of warp 8 issues the MMAs: S_h = Q_h . K^T into TMEM, later O_h += P_h . V
+//     into TMEM, the two heads' MMAs alternating;
 //   * softmax warp w owns TMEM lane (row) 32*(w%4)+lane of head w/4: it reads its S row with
 //     tcgen05.ld, applies the causal mask and the online softmax (base 2), rescales its O row
-//     in TMEM, and writes P as BF16 into shared memory (same swizzled layout) for the P.V MMA;
-//   * the epilogue reads O, divides by the row sum and writes the output rows.
-// TMEM: S0 | S1 | O0 | O1, 128 columns each (all 512).  Shared memory: Q0 Q1 P0 P1 K V, 32 KB
-// each.  Every mbarrier wait is bounded; a timed-out CTA raises the status word, leaves its
+//     in TMEM when the running maximum moves, and writes P as BF16 pairs into TMEM over its S
+//     row, where the P.V MMA reads it;
+//   * the epilogue reads O, divides by the row sum and writes the output rows (or, sharded,
+//     the output tiles to every rank).
+// TMEM: S0 | S1 | O0 | O1, 128 columns each (all 512).  Shared memory: Q0 Q1, K stages 0-1,
+// V stages 0-1, 32 KB each.  Every mbarrier wait is bounded; a timed-out CTA raises the status word, leaves its
 // loops, frees its TMEM and returns.
 #include <cuda.h>
 

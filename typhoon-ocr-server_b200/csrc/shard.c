@@ -10,7 +10,8 @@
  * exchanged through a caller-supplied all-gather callback, so any transport the caller already
  * has (MPI, a TCP store, NCCL over a host-staged buffer, torch.distributed) will do and the
  * library links no collective library.  After that, no collective call is needed: the kernels
- * store their outputs into every rank's buffer over NVLink and synchronise through flags.
+ * store their outputs into every rank's buffer over NVLink -- the prefill raising a flag per
+ * rank once its tiles are stored, the decode sending values that carry the call's number.
  */
 #include <cuda_runtime_api.h>
 #include <stdlib.h>
