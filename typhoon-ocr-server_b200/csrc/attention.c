@@ -78,12 +78,13 @@ static int decode_append_impl(const float *q, const float *k_new, const float *v
                               int layer_idx, float scale, int kvh0, int nkvh, const void *gather, int pos_at,
                               const char *what);
 
-/* Host inputs of a one-sequence decode call as the launch's parameter block: when q and, for an
- * append, k_new / v_new are all host memory (page-locked or not), they are copied into the layer's
- * page-locked slot [K row][V row][q] and *inl is the slot, which the launch reads as its
- * parameters -- the inputs reach the GPU with the launch, with no copy queued ahead of it (k_new /
- * v_new may already be the slot's own rows: a deferred append).  *inl = NULL when any input is
- * device memory (stage_inputs then).  1 on success, else 0 with the error set. */
+/* Host inputs of a one-sequence decode call: when q and, for an append, k_new / v_new are all
+ * host memory (page-locked or not), they are copied into the layer's page-locked slot
+ * [K row][V row][q] and *inl is the slot's query, which the launch takes as its parameter block
+ * -- the query reaches the GPU with the launch, with no copy queued ahead of it -- while the
+ * kernel reads the new row through the slot's device mapping (k_new / v_new may already be the
+ * slot's own rows: a deferred append).  *inl = NULL when any input is device memory
+ * (stage_inputs then).  1 on success, else 0 with the error set. */
 static int inline_inputs(tyb_cache *t, int layer, const float *q, const float *k_new, const float *v_new,
                          const float **inl, const char *what)
 {
@@ -99,7 +100,7 @@ static int inline_inputs(tyb_cache *t, int layer, const float *q, const float *k
     if (k_new && k_new != slot) memcpy(slot, k_new, TYB_ROW_FLOATS * sizeof(float));
     if (v_new && v_new != slot + TYB_ROW_FLOATS) memcpy(slot + TYB_ROW_FLOATS, v_new, TYB_ROW_FLOATS * sizeof(float));
     memcpy(slot + 2 * TYB_ROW_FLOATS, q, TYB_Q_FLOATS * sizeof(float));
-    *inl = slot;
+    *inl = slot + 2 * TYB_ROW_FLOATS;
     return 1;
 }
 
@@ -467,6 +468,7 @@ static int decode_append_impl(const float *q, const float *k_new, const float *v
     int ok = 0;
     const float *inl = NULL, *dq = q, *dk = k_new, *dv = v_new;
     float *hout = NULL;
+    int flags = TYB_DEC_DEVICE_SMALL | TYB_DEC_WIDE_COUNTERS;
     if (!gather && !inline_inputs(t, layer_idx, q, k_new, v_new, &inl, what)) return 1;
     if (!inl && !stage_inputs(t, layer_idx, q, k_new, v_new, &dq, &dk, &dv, st, what)) return 1;
     float *dout = small_view(output, NULL, 0, &ok, st, what);
@@ -478,12 +480,22 @@ static int decode_append_impl(const float *q, const float *k_new, const float *v
     } else if (ok == TYB_MEM_HOST) {
         dout = t->d_out;
     }
+    if (inl && hout) {
+        /* a blocking call: the query as the parameter block, the new row read through the slot's
+         * device mapping (the output is written after it is read, so the slot is free on return) */
+        const float *slot_dev = t->h_rows_dev + (size_t)layer_idx * TYB_SLOT_FLOATS;
+        dk = slot_dev;
+        dv = slot_dev + TYB_ROW_FLOATS;
+    } else if (inl) {
+        /* returns before the kernel runs: the whole slot as the parameter block (nothing on the
+         * device reads the slot, so the host may rewrite it at once) */
+        inl -= 2 * TYB_ROW_FLOATS;
+        flags |= TYB_DEC_INLINE_ROW;
+    }
     const tyb_seq_kv one = tyb_layer_rows(t, layer_idx, pos + 1);
     const int early = tyb_prefetch_rows(cache, layer_idx, pos);
     if (!tyb_cuda_ok(tyb_decode_launch_heads(dq, dout, NULL, one, 1, pos + 1, t->dtype, scale, t->d_partials,
-                                             t->d_counters, dk, dv, early, kvh0, nkvh,
-                                             TYB_DEC_DEVICE_SMALL | TYB_DEC_WIDE_COUNTERS, gather, inl,
-                                             st),
+                                             t->d_counters, dk, dv, early, kvh0, nkvh, flags, gather, inl, st),
                      what))
         return 1;
     tyb_note_write(cache, layer_idx, pos, st);

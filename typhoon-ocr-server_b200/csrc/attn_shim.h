@@ -67,10 +67,10 @@ int tyb_decode_launch_ex(const float *q, float *out, const tyb_seq_kv *seqs_dev,
                          void *stream);
 /* tyb_decode_launch_ex for KV heads [kvh0, kvh0 + nkvh) only; `out` points at the row of query
  * head 2 kvh0 (the shard's rows [2 nkvh][128] are contiguous). */
-/* inl: NULL, or for one sequence (no gather, no QK prep) a page-locked slot [K row 1024][V row 1024]
- * [q 2048] floats whose contents are passed as the launch's own parameters: the kernel then reads
- * q, and the appended row when k_new is non-NULL, from there (q / k_new / v_new are not
- * dereferenced). */
+/* inl: NULL, or for one sequence (no gather, no QK prep) host memory passed as the launch's own
+ * parameters: a copy of q [16][128], the kernel reading q from there (q is not dereferenced);
+ * with TYB_DEC_INLINE_ROW in flags, a page-locked slot [K row 1024][V row 1024][q 2048] floats,
+ * the kernel reading q and the appended row from there (q / k_new / v_new not dereferenced). */
 int tyb_decode_launch_heads(const float *q, float *out, const tyb_seq_kv *seqs_dev, tyb_seq_kv one, int batch,
                             int max_kv_len, int kv_dtype, float scale, float *partials, unsigned int *counters,
                             const float *k_new, const float *v_new, int prefetch_rows, int kvh0, int nkvh,
@@ -114,6 +114,8 @@ int tyb_decode_launch_batched(const float *q, float *out, const tyb_seq_kv *seqs
  * levels (groups of 16 records in parallel, then the group records). */
 #define TYB_DEC_WIDE_COUNTERS 2
 #define TYB_DEC_WIDE_COUNTER_WORDS (8 + 8 * 32)
+/* flags: `inl` is the whole slot [K row][V row][q] (see tyb_decode_launch_heads). */
+#define TYB_DEC_INLINE_ROW 4
 /* Relayout of a gathered head-major tensor [16][S][128] into token-major [S][16][128]
  * (elem_bytes 2 or 4). */
 int tyb_heads_to_tokens_launch(const void *src, void *dst, int S, int elem_bytes, void *stream);

@@ -65,12 +65,25 @@ struct DecodeArgs {
     int prefetch_small;  // q, k_new, v_new are device memory: ask L2 for their lines early
 };
 
-// Decode inputs carried in the launch's own parameters (kernel parameter space holds up to 32 KB):
-// the appended K and V rows [8][128] and the query [16][128] of a call whose inputs are host
-// memory, in the layout of the cache's page-locked per-layer slot they are staged in.  They reach
-// the GPU with the launch itself, so no copy is queued ahead of the kernel.  Read through the
-// parameter's address (hence __grid_constant__; 16-byte aligned for the vector loads).
+// Inputs of a call whose inputs are host memory, carried in the launch's own parameters (kernel
+// parameter space holds up to 32 KB): they reach the GPU with the launch itself, so no copy is
+// queued ahead of the kernel.  Read through the parameter's address (hence __grid_constant__;
+// 16-byte aligned for the vector loads).  Two forms:
+//   DecodeInline     the query [16][128] only, for a call that blocks on a host output: the
+//                    appended K/V row, read by one CTA per KV head only, comes through the
+//                    device mapping of the page-locked slot it is staged in (k_new / v_new) --
+//                    0.6 us less per blocking call than a 16 KB block (the launch copies and
+//                    uploads half the bytes), and the output is written after the row is read,
+//                    so the slot is free when the call returns;
+//   DecodeInlineRow  the slot's whole contents, K row, V row, query (16 KB), for a call that
+//                    returns before its kernel has run (a device output): nothing on the device
+//                    reads the slot, so the host may rewrite it at once (with the row read
+//                    through the mapping, the slot's next writer had to wait for the launch:
+//                    10.2 against 7.1 us per call back to back).
 struct __align__(16) DecodeInline {
+    float q[kHq * kD];
+};
+struct __align__(16) DecodeInlineRow {
     float k[kHkv * kD];
     float v[kHkv * kD];
     float q[kHq * kD];
@@ -79,12 +92,17 @@ struct DecodeNoInline {  // the inputs are device memory, read through the argum
     int unused;
 };
 template <typename In>
-constexpr bool kIsInline = std::is_same<In, DecodeInline>::value;
+constexpr bool kIsInline = !std::is_same<In, DecodeNoInline>::value;
 
 // The query / new-row sources of a launch: the argument pointers, or the parameter copies (k and
-// v only when the call appends a row: the argument pointers then only say whether it does).
+// v only in DecodeInlineRow, and when the call appends a row: the argument pointers then only say
+// whether it does).
 __device__ __forceinline__ void inline_inputs(const DecodeNoInline&, const float*&, const float*&, const float*&) {}
-__device__ __forceinline__ void inline_inputs(const DecodeInline& in, const float*& q, const float*& k,
+__device__ __forceinline__ void inline_inputs(const DecodeInline& in, const float*& q, const float*&, const float*&)
+{
+    q = in.q;
+}
+__device__ __forceinline__ void inline_inputs(const DecodeInlineRow& in, const float*& q, const float*& k,
                                               const float*& v)
 {
     q = in.q;
@@ -1712,6 +1730,8 @@ static bool set_smem_attr()
         if (cudaFuncSetAttribute(decode_split_kernel<T, DecodeNoInline>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  bytes) != cudaSuccess ||
             cudaFuncSetAttribute(decode_split_kernel<T, DecodeInline>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 bytes) != cudaSuccess ||
+            cudaFuncSetAttribute(decode_split_kernel<T, DecodeInlineRow>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  bytes) != cudaSuccess)
             return false;
         done[dev] = true;
@@ -1742,7 +1762,7 @@ static void plan(int batch, int max_kv_len, int* chunk_rows, int* nsplit, int nk
 }
 
 template <typename T>
-static int launch_decode(const DecodeArgs& a, int batch, int nkvh, const void* inl, void* stream)
+static int launch_decode(const DecodeArgs& a, int batch, int nkvh, const void* inl, bool inl_row, void* stream)
 {
     if (!set_smem_attr<T>()) return (int)cudaGetLastError();
     cudaLaunchConfig_t cfg = {};
@@ -1757,7 +1777,10 @@ static int launch_decode(const DecodeArgs& a, int batch, int nkvh, const void* i
     cfg.numAttrs = 1;
     if (inl) {  // the parameter block is read from the host slot by the launch itself
         void* args[2] = {const_cast<DecodeArgs*>(&a), const_cast<void*>(inl)};
-        return (int)cudaLaunchKernelExC(&cfg, (const void*)decode_split_kernel<T, DecodeInline>, args);
+        return (int)cudaLaunchKernelExC(&cfg,
+                                        inl_row ? (const void*)decode_split_kernel<T, DecodeInlineRow>
+                                                : (const void*)decode_split_kernel<T, DecodeInline>,
+                                        args);
     }
     return (int)cudaLaunchKernelEx(&cfg, decode_split_kernel<T, DecodeNoInline>, a, DecodeNoInline{});
 }
@@ -1865,9 +1888,11 @@ static int set_mma_smem_attr()
         cudaError_t e = cudaFuncSetAttribute(decode_mma_kernel<8, false, DecodeNoInline>, dyn, mma_smem);
         if (e == cudaSuccess) e = cudaFuncSetAttribute(decode_mma_kernel<8, true, DecodeNoInline>, dyn, mma_smem);
         if (e == cudaSuccess) e = cudaFuncSetAttribute(decode_mma_kernel<8, false, DecodeInline>, dyn, mma_smem);
+        if (e == cudaSuccess) e = cudaFuncSetAttribute(decode_mma_kernel<8, false, DecodeInlineRow>, dyn, mma_smem);
         if (e == cudaSuccess) e = cudaFuncSetAttribute(decode_stream_kernel<false, DecodeNoInline>, dyn, st_smem);
         if (e == cudaSuccess) e = cudaFuncSetAttribute(decode_stream_kernel<true, DecodeNoInline>, dyn, st_smem);
         if (e == cudaSuccess) e = cudaFuncSetAttribute(decode_stream_kernel<false, DecodeInline>, dyn, st_smem);
+        if (e == cudaSuccess) e = cudaFuncSetAttribute(decode_stream_kernel<false, DecodeInlineRow>, dyn, st_smem);
         if (e != cudaSuccess) return (int)e;
         done[dev] = true;
     }
@@ -1876,7 +1901,8 @@ static int set_mma_smem_attr()
 
 // The tensor-core form for one sequence with a BF16 cache.  Splits as planned for
 // decode_split_kernel<bf16> (same record count, so the callers' workspaces fit).
-static int launch_decode_mma(DecodeMmaArgs a, const tyb_seq_kv& one, int nkvh, const void* inl, void* stream)
+static int launch_decode_mma(DecodeMmaArgs a, const tyb_seq_kv& one, int nkvh, const void* inl, bool inl_row,
+                             void* stream)
 {
     const int e = set_mma_smem_attr();
     if (e) return e;
@@ -1897,7 +1923,10 @@ static int launch_decode_mma(DecodeMmaArgs a, const tyb_seq_kv& one, int nkvh, c
     if (inl) {  // the parameter block is read from the host slot by the launch itself
         if (a.q_norm) return (int)cudaErrorInvalidValue;
         void* args[6] = {&mk, &mv, &mk16, &mv16, &a, const_cast<void*>(inl)};
-        return (int)cudaLaunchKernelExC(&cfg, (const void*)decode_mma_kernel<8, false, DecodeInline>, args);
+        return (int)cudaLaunchKernelExC(&cfg,
+                                        inl_row ? (const void*)decode_mma_kernel<8, false, DecodeInlineRow>
+                                                : (const void*)decode_mma_kernel<8, false, DecodeInline>,
+                                        args);
     }
     if (a.q_norm)
         return (int)cudaLaunchKernelEx(&cfg, decode_mma_kernel<8, true, DecodeNoInline>, mk, mv, mk16, mv16, a,
@@ -1907,7 +1936,7 @@ static int launch_decode_mma(DecodeMmaArgs a, const tyb_seq_kv& one, int nkvh, c
 }
 
 static int launch_stream(const DecodeMmaArgs& a, const CUtensorMap& mk, const CUtensorMap& mv, int nkvh, int batch,
-                         const void* inl, void* stream)
+                         const void* inl, bool inl_row, void* stream)
 {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.nsplit, nkvh, batch);
@@ -1923,7 +1952,10 @@ static int launch_stream(const DecodeMmaArgs& a, const CUtensorMap& mk, const CU
         if (a.q_norm) return (int)cudaErrorInvalidValue;
         void* args[4] = {const_cast<CUtensorMap*>(&mk), const_cast<CUtensorMap*>(&mv), const_cast<DecodeMmaArgs*>(&a),
                          const_cast<void*>(inl)};
-        return (int)cudaLaunchKernelExC(&cfg, (const void*)decode_stream_kernel<false, DecodeInline>, args);
+        return (int)cudaLaunchKernelExC(&cfg,
+                                        inl_row ? (const void*)decode_stream_kernel<false, DecodeInlineRow>
+                                                : (const void*)decode_stream_kernel<false, DecodeInline>,
+                                        args);
     }
     if (a.q_norm) return (int)cudaLaunchKernelEx(&cfg, decode_stream_kernel<true, DecodeNoInline>, mk, mv, a, DecodeNoInline{});
     return (int)cudaLaunchKernelEx(&cfg, decode_stream_kernel<false, DecodeNoInline>, mk, mv, a, DecodeNoInline{});
@@ -1973,7 +2005,7 @@ extern "C" int tyb_decode_launch_batched(const float* q, float* out, const tyb_s
     a.counters = counters;
     a.prefetch_small = 1;
     a.gather = nullptr;
-    return launch_stream(a, m0, m1, kHkv, batch, nullptr, stream);
+    return launch_stream(a, m0, m1, kHkv, batch, nullptr, false, stream);
 }
 
 extern "C" void tyb_decode_plan(int batch, int max_kv_len, int kv_dtype, int* chunk_rows, int* nsplit)
@@ -2000,6 +2032,7 @@ static int launch_heads_impl(const float* q, float* out, const tyb_seq_kv* seqs_
     // Inputs in the parameter block: one sequence, no gather, raw-pointer decode (not the QK-norm form)
     if (inl && (seqs_dev || batch != 1 || gather || prep)) return (int)cudaErrorInvalidValue;
     if (inl) flags &= ~TYB_DEC_DEVICE_SMALL;
+    const bool inl_row = (flags & TYB_DEC_INLINE_ROW) != 0;
     // QK-RMSNorm + M-RoPE on load: the tensor-core forms for one sequence (BF16 cache) only
     if (prep && (kv_dtype != TYB_BF16 || seqs_dev || batch != 1 || !prep->q_norm || !prep->k_norm ||
                  !prep->cos || !prep->sin))
@@ -2057,17 +2090,17 @@ static int launch_heads_impl(const float* q, float* out, const tyb_seq_kv* seqs_
             m.rope_sin = prep->sin;
             m.eps = prep->eps;
         }
-        if (one_wave(1, max_kv_len, nkvh)) return launch_decode_mma(m, one, nkvh, inl, stream);
+        if (one_wave(1, max_kv_len, nkvh)) return launch_decode_mma(m, one, nkvh, inl, inl_row, stream);
         const int e = set_mma_smem_attr();
         if (e) return e;
         CUtensorMap mk, mv;
         if (!slab_maps(one, kStRows, &mk, &mv)) return (int)cudaErrorInvalidValue;
         m.seqs = nullptr;
         m.maps = nullptr;
-        return launch_stream(m, mk, mv, nkvh, 1, inl, stream);
+        return launch_stream(m, mk, mv, nkvh, 1, inl, inl_row, stream);
     }
-    if (kv_dtype == TYB_BF16) return launch_decode<__nv_bfloat16>(a, batch, nkvh, inl, stream);
-    return launch_decode<float>(a, batch, nkvh, inl, stream);
+    if (kv_dtype == TYB_BF16) return launch_decode<__nv_bfloat16>(a, batch, nkvh, inl, inl_row, stream);
+    return launch_decode<float>(a, batch, nkvh, inl, inl_row, stream);
 }
 
 extern "C" int tyb_decode_launch_heads(const float* q, float* out, const tyb_seq_kv* seqs_dev, tyb_seq_kv one,
