@@ -185,59 +185,67 @@ __device__ __forceinline__ float row_exp(const float (&s)[kPtKeys], int lim, flo
 }
 
 // Query rows of one item into shared memory: RMSNorm(q_norm) + rotate_half M-RoPE, rounded to
-// BF16, in the 128-byte-swizzled K-major layout of the QK MMA.  Warp w handles head w / 4 and
-// tokens 32 (w % 4) .. +32; lane l holds dims [4l, 4l + 4) mod 64 of the lower (l < 16) or
-// upper half.  All loads of eight rows go out before any is used (rows past Sq read row Sq - 1
-// and are zeroed), so that their latencies overlap.
+// BF16, in the 128-byte-swizzled K-major layout of the QK MMA.  Warp w handles tokens 16w .. +16
+// of the item, both query heads of each (they share the token's cos/sin), eight tokens at a
+// time; lane l holds dims [4l, 4l + 4) mod 64 of the lower (l < 16) or upper half.  All loads of
+// the eight tokens go out before any is used (tokens past Sq read token Sq - 1 and are zeroed),
+// so that their latencies overlap: two round trips to memory per warp.
 template <bool kBf16>
 __device__ __forceinline__ void load_queries(const PrefillTcArgs& a, unsigned char* sQ, int t0, int kvh, int warp,
                                              int lane)
 {
-    const int h = warp >> 2;
     const float4 w = *reinterpret_cast<const float4*>(a.q_norm + 4 * lane);
     const int jr = 4 * (lane & 15);  // rotary frequency index of this lane's first dim
 #pragma unroll 1
-    for (int i0 = 0; i0 < 32; i0 += 8) {
-        float x[8][4];
+    for (int i0 = 0; i0 < 16; i0 += 8) {
+        float x[8][kGroup][4];
         float4 cv[8], sn[8];
 #pragma unroll
         for (int u = 0; u < 8; u++) {
-            const int tok = min(t0 + 32 * (warp & 3) + i0 + u, a.Sq - 1);
-            const size_t off = ((size_t)tok * kHq + kGroup * kvh + h) * kD + 4 * lane;
-            if (kBf16) {
-                const uint2 q2 = __ldg(reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(a.q) + off));
-                const float2 f0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&q2.x));
-                const float2 f1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&q2.y));
-                x[u][0] = f0.x; x[u][1] = f0.y; x[u][2] = f1.x; x[u][3] = f1.y;
-            } else {
-                const float4 f = __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(a.q) + off));
-                x[u][0] = f.x; x[u][1] = f.y; x[u][2] = f.z; x[u][3] = f.w;
+            const int tok = min(t0 + 16 * warp + i0 + u, a.Sq - 1);
+#pragma unroll
+            for (int hh = 0; hh < kGroup; hh++) {
+                const size_t off = ((size_t)tok * kHq + kGroup * kvh + hh) * kD + 4 * lane;
+                if (kBf16) {
+                    const uint2 q2 = __ldg(reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(a.q) + off));
+                    const float2 f0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&q2.x));
+                    const float2 f1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&q2.y));
+                    x[u][hh][0] = f0.x; x[u][hh][1] = f0.y; x[u][hh][2] = f1.x; x[u][hh][3] = f1.y;
+                } else {
+                    const float4 f = __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(a.q) + off));
+                    x[u][hh][0] = f.x; x[u][hh][1] = f.y; x[u][hh][2] = f.z; x[u][hh][3] = f.w;
+                }
             }
             cv[u] = __ldg(reinterpret_cast<const float4*>(a.cos + (size_t)tok * 64 + jr));
             sn[u] = __ldg(reinterpret_cast<const float4*>(a.sin + (size_t)tok * 64 + jr));
         }
 #pragma unroll
         for (int u = 0; u < 8; u++) {
-            const int r = 32 * (warp & 3) + i0 + u;
+            const int r = 16 * warp + i0 + u;
             const bool live = t0 + r < a.Sq;
-            float ss = x[u][0] * x[u][0] + x[u][1] * x[u][1] + x[u][2] * x[u][2] + x[u][3] * x[u][3];
-#pragma unroll
-            for (int o = 16; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-            const float rs = live ? rsqrtf(ss * (1.f / kD) + a.eps) : 0.f;
-            const float y[4] = {x[u][0] * rs * w.x, x[u][1] * rs * w.y, x[u][2] * rs * w.z, x[u][3] * rs * w.w};
-            // rotate_half: lane l < 16 holds dims [4l, 4l+4), lane l+16 the partner dims + 64.
-            float partner[4];
-#pragma unroll
-            for (int e = 0; e < 4; e++) partner[e] = __shfl_xor_sync(0xffffffffu, y[e], 16);
             const float c4[4] = {cv[u].x, cv[u].y, cv[u].z, cv[u].w};
             const float s4[4] = {sn[u].x, sn[u].y, sn[u].z, sn[u].w};
-            float z[4];
 #pragma unroll
-            for (int e = 0; e < 4; e++)
-                z[e] = lane < 16 ? y[e] * c4[e] - partner[e] * s4[e]   // x[j] c - x[j+64] s
-                                 : y[e] * c4[e] + partner[e] * s4[e];  // x[j+64] c + x[j] s
-            const uint2 packed = make_uint2(pack_bf16x2(z[0], z[1]), pack_bf16x2(z[2], z[3]));
-            *reinterpret_cast<uint2*>(sQ + h * kPtTile + sw128_offset(r, 4 * lane)) = packed;
+            for (int hh = 0; hh < kGroup; hh++) {
+                float ss = x[u][hh][0] * x[u][hh][0] + x[u][hh][1] * x[u][hh][1] + x[u][hh][2] * x[u][hh][2] +
+                           x[u][hh][3] * x[u][hh][3];
+#pragma unroll
+                for (int o = 16; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+                const float rs = live ? rsqrtf(ss * (1.f / kD) + a.eps) : 0.f;
+                const float y[4] = {x[u][hh][0] * rs * w.x, x[u][hh][1] * rs * w.y, x[u][hh][2] * rs * w.z,
+                                    x[u][hh][3] * rs * w.w};
+                // rotate_half: lane l < 16 holds dims [4l, 4l+4), lane l+16 the partner dims + 64.
+                float partner[4];
+#pragma unroll
+                for (int e = 0; e < 4; e++) partner[e] = __shfl_xor_sync(0xffffffffu, y[e], 16);
+                float z[4];
+#pragma unroll
+                for (int e = 0; e < 4; e++)
+                    z[e] = lane < 16 ? y[e] * c4[e] - partner[e] * s4[e]   // x[j] c - x[j+64] s
+                                     : y[e] * c4[e] + partner[e] * s4[e];  // x[j+64] c + x[j] s
+                const uint2 packed = make_uint2(pack_bf16x2(z[0], z[1]), pack_bf16x2(z[2], z[3]));
+                *reinterpret_cast<uint2*>(sQ + hh * kPtTile + sw128_offset(r, 4 * lane)) = packed;
+            }
         }
     }
 }
@@ -405,8 +413,8 @@ __global__ void __launch_bounds__(kPtThreads, 1)
     } else {
         asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kPtSoftmaxRegs));
         // ---- queries: RMSNorm(q_norm) + rotate_half M-RoPE, BF16, swizzled into Q0/Q1 ----------
-        // Warps 0-7 (warp w: head w / 4, tokens 32 (w % 4) ..+32), while the producer already
-        // streams the first K/V tiles.
+        // Warps 0-7 (warp w: tokens 16w .. +16, both heads), while the producer already streams
+        // the first K/V tiles.
         {
             if (a.q_bf16) load_queries<true>(a, sQ, t0, kvh, warp, lane);
             else load_queries<false>(a, sQ, t0, kvh, warp, lane);
