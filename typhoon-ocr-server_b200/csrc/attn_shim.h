@@ -137,7 +137,8 @@ typedef struct {
 
 /* Raw K/V rows [S][8][128] (fp32, or bf16 when in_bf16) -> BF16 cache rows [pos0, pos0+S) of
  * one layer (layout of tyb_seq_kv): K through RMSNorm(k_norm) and rotate_half M-RoPE with the
- * per-token cos/sin [S][64]; V as is.  KV heads [kvh0, kvh0 + nkvh) only. */
+ * per-token cos/sin [S][64]; V as is.  KV heads [kvh0, kvh0 + nkvh) only.  A programmatic
+ * dependent of the previous kernel in the stream (it waits for it before reading anything). */
 int tyb_kv_prep_launch(const void *k_raw, const void *v_raw, int in_bf16, const float *k_norm, const float *cos,
                        const float *sin, void *k_dst, void *v_dst, int row_capacity, int pos0, int S, float eps,
                        int kvh0, int nkvh, void *stream);
@@ -148,7 +149,8 @@ int tyb_kv_prep_launch(const void *k_raw, const void *v_raw, int in_bf16, const 
  * Output [Sq][16][128], or with out_head_major the shard [2 nkvh][Sq][128]; fp32 or bf16.
  * Launched as a programmatic dependent of the previous kernel in the stream, which must be the
  * tyb_kv_prep_launch of the same rows (it starts before that kernel completes; its TMA producer
- * waits for it before reading the cache).  * xchg_dev (device table, or NULL): the output rows go, token-major BF16, into slot (epoch & 1)
+ * waits for it before reading the cache, and then lets the next kernel in the stream launch).
+ * xchg_dev (device table, or NULL): the output rows go, token-major BF16, into slot (epoch & 1)
  * of EVERY rank's exchange buffer instead of `out` (TMA stores through xchg_maps, tyb_prefill_x_maps),
  * and the kernel returns only once all ranks' rows of call `epoch` are in this rank's buffer
  * (bounded wait). */

@@ -328,9 +328,14 @@ __global__ void __launch_bounds__(kPtThreads, 1)
             // ---- TMA producer (one thread): K and V double-buffered, each stage refilled as soon
             // as the MMAs of the tile two back have read it.  The kernel may start while the
             // previous kernel in the stream (kv_prep, which writes the rows read here) still runs:
-            // this thread, the only reader of those rows, waits for it first.
+            // this thread, the only reader of those rows, waits for it first.  Past that wait the
+            // CTA lets the next kernel in the stream launch (the next layer's kv_prep, or a decode
+            // step): it starts once every CTA of this grid has started and passed the wait -- no
+            // CTA of this grid is left waiting for an SM, and kv_prep has completed -- and it
+            // waits for this grid before reading anything.
             if (lane == 0) {
                 asm volatile("griddepcontrol.wait;" ::: "memory");
+                asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
                 for (int j = 0; j < ntiles; j++) {
                     const int st = j & 1;
                     const uint32_t fpar = (uint32_t)((j - 2) >> 1) & 1u;
@@ -617,7 +622,11 @@ __global__ void __launch_bounds__(kPtThreads, 1)
 
 // ---- K/V append with QK-RMSNorm + M-RoPE on K ------------------------------------------------
 // One warp per (token, KV head): RMSNorm(k_norm) + rotate_half with the token's cos/sin, K and V
-// written as BF16 into cache rows pos0 + t (layout of tyb_seq_kv).
+// written as BF16 into cache rows pos0 + t (layout of tyb_seq_kv).  Launched as a programmatic
+// dependent of the previous kernel in the stream: every CTA waits for it before reading anything,
+// and only then lets the attention kernel that follows launch -- so that when that kernel's CTAs
+// start (reading q, q_norm, cos and sin before their own wait), everything before this kernel has
+// completed.
 __global__ void kv_prep_kernel(const void* __restrict__ k_raw, const void* __restrict__ v_raw, int in_bf16,
                                const float* __restrict__ k_norm, const float* __restrict__ cosv,
                                const float* __restrict__ sinv, __nv_bfloat16* __restrict__ k_dst,
@@ -625,8 +634,7 @@ __global__ void kv_prep_kernel(const void* __restrict__ k_raw, const void* __res
                                int kvh0, int nkvh)
 {
     const int lane = threadIdx.x & 31;
-    // The attention kernel that follows may launch now; it waits for this grid before reading
-    // the rows written here.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const long long nwarps = (long long)gridDim.x * (blockDim.x >> 5);
     const float4 w = *reinterpret_cast<const float4*>(k_norm + 4 * lane);
@@ -754,10 +762,18 @@ extern "C" int tyb_kv_prep_launch(const void* k_raw, const void* v_raw, int in_b
     const int threads = 256;
     long long blocks = ((long long)S * nkvh + threads / 32 - 1) / (threads / 32);
     if (blocks > 148LL * 16) blocks = 148LL * 16;
-    kv_prep_kernel<<<(unsigned)blocks, threads, 0, (cudaStream_t)stream>>>(
-        k_raw, v_raw, in_bf16, k_norm, cos, sin, static_cast<__nv_bfloat16*>(k_dst), static_cast<__nv_bfloat16*>(v_dst),
-        row_capacity, pos0, S, eps, kvh0, nkvh);
-    return (int)cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)blocks);
+    cfg.blockDim = dim3(threads);
+    cfg.stream = (cudaStream_t)stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return (int)cudaLaunchKernelEx(&cfg, kv_prep_kernel, k_raw, v_raw, in_bf16, k_norm, cos, sin,
+                                   static_cast<__nv_bfloat16*>(k_dst), static_cast<__nv_bfloat16*>(v_dst), row_capacity,
+                                   pos0, S, eps, kvh0, nkvh);
 }
 
 extern "C" int tyb_prefill_tc_launch(const void* q, int q_bf16, const float* q_norm, const float* cos,
@@ -813,10 +829,10 @@ extern "C" int tyb_prefill_tc_launch(const void* q, int q_bf16, const float* q_n
         return (int)cudaErrorInvalidValue;
     // Programmatic dependent launch: the CTAs may start (TMEM, barriers, the query prologue) while
     // kv_prep finishes; the TMA producer waits for it before reading the cache rows.  This needs
-    // kv_prep to be the previous kernel in the stream, launched without the attribute (so that
-    // everything before it, e.g. whatever produced q, q_norm, cos and sin, has completed): the
-    // only caller launches the two back to back.  The outputs are written after the wait (the
-    // epilogue follows the P.V of every tile, which follows the K/V loads).
+    // kv_prep to be the previous kernel in the stream, which lets it launch only after all its CTAs
+    // have waited for everything before it (so that whatever produced q, q_norm, cos and sin has
+    // completed): the only caller launches the two back to back.  The outputs are written after
+    // the wait (the epilogue follows the P.V of every tile, which follows the K/V loads).
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)(a.n_qtiles * nkvh));
     cfg.blockDim = dim3(kPtThreads);
