@@ -13,21 +13,23 @@ __device__ unsigned int g_status = 0u;
 __device__ unsigned int* g_status_mirror = nullptr;
 __device__ unsigned long long g_wait_limit_ns = kWaitLimitNs;
 
+static_assert(kD / 8 == 16 && kHkv == 8, "kv_scatter_kernel's index shifts");
+
 template <typename TDst>
 __global__ void kv_scatter_kernel(const float* __restrict__ k_src, const float* __restrict__ v_src,
                                   TDst* __restrict__ k_dst, TDst* __restrict__ v_dst,
                                   int row_capacity, int pos0, int S)
 {
-    // One thread per (tensor, token, head, 8-element group): 2 * S * 8 * 16 threads.
-    const long long n = 2LL * S * kHkv * (kD / 8);
-    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
-         i += (long long)gridDim.x * blockDim.x) {
-        const int c = (int)(i % (kD / 8));
-        const long long th = i / (kD / 8);
-        const int h = (int)(th % kHkv);
-        const long long tt = th / kHkv;
-        const int t = (int)(tt % S);
-        const int which = (int)(tt / S);
+    // One thread per (tensor, token, head, 8-element group): 2 * S * 8 * 16 threads (< 2^27: 32-bit
+    // indices, the division by S once per element group).
+    const int n = 2 * S * kHkv * (kD / 8);
+    for (int i = (int)(blockIdx.x * blockDim.x + threadIdx.x); i < n; i += (int)(gridDim.x * blockDim.x)) {
+        const int c = i & (kD / 8 - 1);
+        const int th = i >> 4;  // i / (kD / 8)
+        const int h = th & (kHkv - 1);
+        const int tt = th >> 3;  // th / kHkv
+        const int which = tt >= S;
+        const int t = tt - which * S;
         const float* src = (which ? v_src : k_src) + ((size_t)t * kHkv + h) * kD + 8 * c;
         TDst* dst = (which ? v_dst : k_dst) + ((size_t)h * row_capacity + pos0 + t) * kD + 8 * c;
         float x[8];
@@ -46,6 +48,7 @@ extern "C" int tyb_kv_scatter_launch(const float* k_src, const float* v_src, voi
 {
     if (S <= 0) return 0;
     const long long n = 2LL * S * kHkv * (kD / 8);
+    if (n >= (1LL << 31)) return (int)cudaErrorInvalidValue;
     const int threads = 256;
     long long blocks = (n + threads - 1) / threads;
     if (blocks > 148LL * 16) blocks = 148LL * 16;

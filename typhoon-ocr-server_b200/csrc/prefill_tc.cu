@@ -636,13 +636,14 @@ __global__ void kv_prep_kernel(const void* __restrict__ k_raw, const void* __res
     const int lane = threadIdx.x & 31;
     asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-    const long long nwarps = (long long)gridDim.x * (blockDim.x >> 5);
+    // 32-bit indices (S * nkvh < 2^21): a 64-bit division per row cost more issue slots than the
+    // row's arithmetic.
+    const int nwarps = (int)gridDim.x * (int)(blockDim.x >> 5);
     const float4 w = *reinterpret_cast<const float4*>(k_norm + 4 * lane);
     const float w4[4] = {w.x, w.y, w.z, w.w};
     const int jr = 4 * (lane & 15);
-    for (long long wi = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); wi < (long long)S * nkvh;
-         wi += nwarps) {
-        const int t = (int)(wi / nkvh), hh = kvh0 + (int)(wi % nkvh);
+    for (int wi = (int)blockIdx.x * (int)(blockDim.x >> 5) + (int)(threadIdx.x >> 5); wi < S * nkvh; wi += nwarps) {
+        const int t = wi / nkvh, hh = kvh0 + (wi - t * nkvh);
         const size_t off = ((size_t)t * kHkv + hh) * kD + 4 * lane;
         float x[4], v4[4];
         if (in_bf16) {
