@@ -229,6 +229,94 @@ void attention_decode_gqa(const float *q, const KVCache *cache, float *output, i
     if (ok != TYB_MEM_DEVICE) tyb_finish(st, what);
 }
 
+/* ---- pipelined drop-in prefill from host buffers ----------------------------------------
+ * kernel/decoder.c:106-117 calls attention_prefill_gqa with host q/k/v/output: 64 MB in and 32 MB
+ * out per 4K-token layer over PCIe, against ~0.25 ms of tensor-core work.  Done in order, the
+ * call is three copies, the kernels, then the copy back.  Here the rows go in chunks (multiples
+ * of the 128-row query tile): chunk c's queries and K/V rows are copied in on one stream while
+ * chunk c - 1 is split and attended (causal: its queries see only rows up to its own) on the
+ * library's stream, and its output rows go back on a third stream -- the inbound and outbound
+ * copies overlap each other and the kernels.  The output of a chunk is written over its staged
+ * queries (each query tile is read before its output is written, by the same CTA), so the
+ * staging needs no more room than the serial path.  Streams and events: per thread and device,
+ * made on first use and kept until exit. */
+#define TYB_PIPE_DEVICES 64
+static _Thread_local cudaStream_t g_pipe_in[TYB_PIPE_DEVICES], g_pipe_out[TYB_PIPE_DEVICES];
+static _Thread_local cudaEvent_t g_pipe_ev[TYB_PIPE_DEVICES][4]; /* start, in, done, out */
+
+static int pipe_ready(int dev, const char *what)
+{
+    if (g_pipe_in[dev]) return 1;
+    cudaStream_t a = NULL, b = NULL;
+    cudaEvent_t e[4] = {NULL, NULL, NULL, NULL};
+    int ok = tyb_cuda_ok(cudaStreamCreateWithFlags(&a, cudaStreamNonBlocking), what) &&
+             tyb_cuda_ok(cudaStreamCreateWithFlags(&b, cudaStreamNonBlocking), what);
+    for (int i = 0; ok && i < 4; i++) ok = tyb_cuda_ok(cudaEventCreateWithFlags(&e[i], cudaEventDisableTiming), what);
+    if (!ok) {
+        if (a) cudaStreamDestroy(a);
+        if (b) cudaStreamDestroy(b);
+        for (int i = 0; i < 4; i++)
+            if (e[i]) cudaEventDestroy(e[i]);
+        return 0;
+    }
+    g_pipe_out[dev] = b;
+    for (int i = 0; i < 4; i++) g_pipe_ev[dev][i] = e[i];
+    g_pipe_in[dev] = a;
+    return 1;
+}
+
+/* q/k/v/output host buffers of S rows (S keys), sq: device staging of the queries (>= S rows),
+ * so: of the raw K then V rows (2 x S rows), ksp / vsp: the hi|lo BF16 pairs.  1 on success. */
+static int prefill_pipelined(const float *q, const float *k, const float *v, float *output, int S, float scale,
+                             float *sq, float *so, unsigned char *ksp, unsigned char *vsp, void *st, const char *what)
+{
+    int dev = 0;
+    if (!tyb_cuda_ok(cudaGetDevice(&dev), what)) return 0;
+    if (dev < 0 || dev >= TYB_PIPE_DEVICES) {
+        tyb_set_error("%s: device %d out of range", what, dev);
+        return 0;
+    }
+    if (!pipe_ready(dev, what)) return 0;
+    cudaStream_t in = g_pipe_in[dev], out = g_pipe_out[dev], cs = (cudaStream_t)st;
+    cudaEvent_t *ev = g_pipe_ev[dev];
+    const size_t kb = (size_t)S * TYB_ROW_FLOATS * sizeof(float);
+    /* about eight chunks, at least 512 rows each, whole query tiles */
+    int chunk = ((S + 7) / 8 + 127) / 128 * 128;
+    if (chunk < 512) chunk = 512;
+    /* Both copy streams start after the work already queued on the library's stream. */
+    int ok = tyb_cuda_ok(cudaEventRecord(ev[0], cs), what) && tyb_cuda_ok(cudaStreamWaitEvent(in, ev[0], 0), what) &&
+             tyb_cuda_ok(cudaStreamWaitEvent(out, ev[0], 0), what);
+    for (int r0 = 0; ok && r0 < S; r0 += chunk) {
+        const int n = S - r0 < chunk ? S - r0 : chunk;
+        const size_t qo = (size_t)r0 * TYB_Q_FLOATS, ko = (size_t)r0 * TYB_ROW_FLOATS;
+        const size_t qn = (size_t)n * TYB_Q_FLOATS * sizeof(float), kn = (size_t)n * TYB_ROW_FLOATS * sizeof(float);
+        float *sk = so + ko, *sv = so + kb / sizeof(float) + ko;
+        ok = tyb_cuda_ok(cudaMemcpyAsync(sk, k + ko, kn, cudaMemcpyHostToDevice, in), what) &&
+             tyb_cuda_ok(cudaMemcpyAsync(sv, v + ko, kn, cudaMemcpyHostToDevice, in), what) &&
+             tyb_cuda_ok(cudaMemcpyAsync(sq + qo, q + qo, qn, cudaMemcpyHostToDevice, in), what) &&
+             tyb_cuda_ok(cudaEventRecord(ev[1], in), what) && tyb_cuda_ok(cudaStreamWaitEvent(cs, ev[1], 0), what) &&
+             tyb_cuda_ok(tyb_kv_split_rows_launch(sk, sv, TYB_ROW_FLOATS, KV_HEAD_DIM, n, r0, S, ksp, ksp + kb / 2, vsp,
+                                                  vsp + kb / 2, st),
+                         what) &&
+             tyb_cuda_ok(tyb_prefill_tc32_launch(sq + qo, sq + qo, n, r0, r0 + n, ksp, ksp + kb / 2, vsp, vsp + kb / 2, S,
+                                                 scale, st),
+                         what) &&
+             tyb_cuda_ok(cudaEventRecord(ev[2], cs), what) && tyb_cuda_ok(cudaStreamWaitEvent(out, ev[2], 0), what) &&
+             tyb_cuda_ok(cudaMemcpyAsync(output + qo, sq + qo, qn, cudaMemcpyDeviceToHost, out), what);
+    }
+    /* The library's stream resumes after the last copy back (later work may reuse the staging). */
+    const int joined = tyb_cuda_ok(cudaEventRecord(ev[3], out), what) &&
+                       tyb_cuda_ok(cudaStreamWaitEvent(cs, ev[3], 0), what);
+    if (!ok || !joined) {
+        /* nothing queued may outlive the call: the copies name the caller's buffers */
+        cudaStreamSynchronize(in);
+        cudaStreamSynchronize(out);
+        return 0;
+    }
+    tyb_note_nowrite(st);
+    return tyb_finish(st, what);
+}
+
 void attention_prefill_gqa(const float *q, const float *k, const float *v, float *output, int Sq,
                            int Sk, float scale, float *q_hm, float *k_hm, float *v_hm, float *o_hm)
 {
@@ -280,6 +368,12 @@ void attention_prefill_gqa(const float *q, const float *k, const float *v, float
     if (o_stage) so = (o_hm && tyb_registry_size(o_hm) >= o_stage) ? o_hm : (float *)tyb_workspace(TYB_WS_OUT, o_stage);
     if ((!qd && !sq) || !ksp || !vsp || (o_stage && !so)) return;
 
+    /* All four in host memory and every query row seeing its own key (Sk >= Sq): chunks of rows
+     * stream in and out while the kernels run (prefill_pipelined). */
+    if (!qd && !kd && !vd && !od && kv_rows == Sq && Sq >= 2 * 512 && sq) {
+        prefill_pipelined(q, k, v, output, Sq, scale, sq, so, ksp, vsp, st, what);
+        return;
+    }
     const float *dq = to_device(q, sq, qb, &qd, st, what);
     const float *dk = to_device(k, so, kb, &kd, st, what);
     const float *dv = dk ? to_device(v, so + (kd ? 0 : kb / sizeof(float)), kb, &vd, st, what) : NULL;

@@ -172,6 +172,10 @@ int tyb_prefill_x_maps(void *const *bases, int world, int max_tokens, void *maps
  * hi = bf16(x), lo = bf16(x - hi). */
 int tyb_kv_split_launch(const float *k, const float *v, long long row_stride, long long head_stride, int n,
                         void *k_hi, void *k_lo, void *v_hi, void *v_lo, void *stream);
+/* As tyb_kv_split_launch, with the n rows going to rows [row0, row0 + n) of [8][cap][128] arrays
+ * (the chunks of a pipelined split). */
+int tyb_kv_split_rows_launch(const float *k, const float *v, long long row_stride, long long head_stride, int n,
+                             int row0, int cap, void *k_hi, void *k_lo, void *v_hi, void *v_lo, void *stream);
 
 /* Causal attention of Sq queries q [Sq][16][128] fp32 (already normalised and rotated) into
  * out [Sq][16][128] fp32: query i sees keys k <= pos_offset + i with k < total_kv (>= 1).  K and

@@ -348,9 +348,10 @@ __global__ void __launch_bounds__(kT32Threads, 1)
 // ---- K/V split pass ---------------------------------------------------------------------------
 // Rows [0, n) of the 8 KV heads of K and V, FP32 with element (head h, row r, dim d) at
 // base + r * row_stride + h * head_stride + d, written as hi = bf16(x) and lo = bf16(x - hi) into
-// head-first [8][n][128] BF16 arrays.  One thread per 4 dims of a row of K and of V.
+// rows row0 + r of head-first [8][cap][128] BF16 arrays.  One thread per 4 dims of a row of K and
+// of V.
 __global__ void kv_split_kernel(const float* __restrict__ k, const float* __restrict__ v, long long row_stride,
-                                long long head_stride, int n, __nv_bfloat16* __restrict__ kh,
+                                long long head_stride, int n, int row0, int cap, __nv_bfloat16* __restrict__ kh,
                                 __nv_bfloat16* __restrict__ kl, __nv_bfloat16* __restrict__ vh,
                                 __nv_bfloat16* __restrict__ vl)
 {
@@ -363,7 +364,7 @@ __global__ void kv_split_kernel(const float* __restrict__ k, const float* __rest
         const int hh = (int)(rh % kHkv);
         const int r = (int)(rh / kHkv);
         const size_t src = (size_t)r * row_stride + (size_t)hh * head_stride + 4 * q4;
-        const size_t dst = ((size_t)hh * n + r) * kD + 4 * q4;
+        const size_t dst = ((size_t)hh * cap + row0 + r) * kD + 4 * q4;
         const float4 xk = __ldg(reinterpret_cast<const float4*>(k + src));
         const float4 xv = __ldg(reinterpret_cast<const float4*>(v + src));
         auto split4 = [](const float4 x, __nv_bfloat16* hi, __nv_bfloat16* lo, size_t off) {
@@ -383,17 +384,24 @@ __global__ void kv_split_kernel(const float* __restrict__ k, const float* __rest
 
 using namespace tyb;
 
-extern "C" int tyb_kv_split_launch(const float* k, const float* v, long long row_stride, long long head_stride, int n,
-                                   void* kh, void* kl, void* vh, void* vl, void* stream)
+extern "C" int tyb_kv_split_rows_launch(const float* k, const float* v, long long row_stride, long long head_stride,
+                                        int n, int row0, int cap, void* kh, void* kl, void* vh, void* vl, void* stream)
 {
     if (n <= 0) return 0;
+    if (row0 < 0 || row0 + n > cap) return (int)cudaErrorInvalidValue;
     const int threads = 256;
     long long blocks = ((long long)n * kHkv * 32 + threads - 1) / threads;
     if (blocks > 148LL * 8) blocks = 148LL * 8;
     kv_split_kernel<<<(unsigned)blocks, threads, 0, (cudaStream_t)stream>>>(
-        k, v, row_stride, head_stride, n, static_cast<__nv_bfloat16*>(kh), static_cast<__nv_bfloat16*>(kl),
+        k, v, row_stride, head_stride, n, row0, cap, static_cast<__nv_bfloat16*>(kh), static_cast<__nv_bfloat16*>(kl),
         static_cast<__nv_bfloat16*>(vh), static_cast<__nv_bfloat16*>(vl));
     return (int)cudaGetLastError();
+}
+
+extern "C" int tyb_kv_split_launch(const float* k, const float* v, long long row_stride, long long head_stride, int n,
+                                   void* kh, void* kl, void* vh, void* vl, void* stream)
+{
+    return tyb_kv_split_rows_launch(k, v, row_stride, head_stride, n, 0, n, kh, kl, vh, vl, stream);
 }
 
 extern "C" int tyb_prefill_tc32_launch(const float* q, float* out, int Sq, int pos_offset, int total_kv,
