@@ -19,12 +19,16 @@
 //     one thread of warp 8 issues the MMAs: S_h = Q_h . K^T into TMEM, later O_h += P_h . V
 //     into TMEM, the two heads' MMAs alternating;
 //   * softmax warp w owns TMEM lane (row) 32*(w%4)+lane of head w/4: it reads its S row with
-//     tcgen05.ld, applies the causal mask and the online softmax (base 2), rescales its O row
-//     in TMEM when the running maximum moves, and writes P as BF16 pairs into TMEM over its S
-//     row, where the P.V MMA reads it;
+//     tcgen05.ld (which frees S for the other head's next QK), applies the causal mask and the
+//     online softmax (base 2), rescales its O row in TMEM when the running maximum moves, and
+//     writes P as BF16 pairs into its head's P columns of TMEM, where the P.V MMA reads it;
 //   * the epilogue reads O, divides by the row sum and writes the output rows (or, sharded,
 //     the output tiles to every rank).
-// TMEM: S0 | S1 | O0 | O1, 128 columns each (all 512).  Shared memory: Q0 Q1, K stages 0-1,
+// TMEM: S (128 columns, the two heads in turn) | P0 | P1 (64 each) | O0 | O1 (128 each): all 512.
+// With one S buffer that each head's softmax releases as soon as it has read it, a head's next QK
+// needs no wait for its P.V (P has columns of its own), so the QK -> softmax -> P.V chain of a
+// head no longer sets the period: 2.39 -> 2.31 ms per config-3 page against an S per head with P
+// written over it.  Shared memory: Q0 Q1, K stages 0-1,
 // V stages 0-1, 32 KB each.  Every mbarrier wait is bounded; a timed-out CTA raises the status word, leaves its
 // loops, frees its TMEM and returns.
 #include <cuda.h>
@@ -45,8 +49,8 @@ constexpr int kPtThreads = kPtSoftmaxThreads + 128;  // + warpgroup 2: warp 8 MM
 // shares fit the launch's registers (checked against the compiled count before launching),
 // and a warp of each warpgroup shares every sub-partition's 512 registers per lane.
 constexpr int kPtLaunchRegs = 168;
-constexpr int kPtIssueRegs = 96;
-constexpr int kPtSoftmaxRegs = 200;
+constexpr int kPtIssueRegs = 112;
+constexpr int kPtSoftmaxRegs = 192;
 static_assert(kPtSoftmaxThreads * kPtSoftmaxRegs + 128 * kPtIssueRegs <= kPtThreads * kPtLaunchRegs,
               "register split exceeds the launch allocation");
 static_assert(2 * kPtSoftmaxRegs + kPtIssueRegs <= 512, "register split exceeds a sub-partition");
@@ -259,7 +263,7 @@ __device__ __forceinline__ void head_bar(int h)
         asm volatile("bar.sync 2, 128;" ::: "memory");
 }
 
-// 384 threads (3 warpgroups) launched at 168 registers, split 200 / 200 / 96 by setmaxnreg.
+// 384 threads (3 warpgroups) launched at 168 registers, split 192 / 192 / 112 by setmaxnreg.
 __global__ void __launch_bounds__(kPtThreads, 1)
     prefill_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
                       const PrefillTcArgs a, const __grid_constant__ PrefillPeerMaps px)
@@ -279,7 +283,8 @@ __global__ void __launch_bounds__(kPtThreads, 1)
     uint64_t* p_full = bars + 10;   // [2] per head: P written, O rescaled (128 arrivals)
     uint64_t* pv_done = bars + 12;  // [2] per head: P.V of the tile finished
     uint64_t* q_full = bars + 14;   // Q0, Q1 written (256 arrivals)
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
+    uint64_t* s_free = bars + 15;   // [2] per head: the softmax has loaded S (128 arrivals)
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);  // (bars 15-16: s_free)
     int* store_fail = reinterpret_cast<int*>(bars + 18);  // [2] per head: its output tile is incomplete
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -300,6 +305,7 @@ __global__ void __launch_bounds__(kPtThreads, 1)
                 mbar_init(&s_full[i], 1);
                 mbar_init(&p_full[i], kPtSoftmaxThreads / 2);
                 mbar_init(&pv_done[i], 1);
+                mbar_init(&s_free[i], kPtSoftmaxThreads / 2);
                 mbar_init(&k_full[i], 1);
                 mbar_init(&k_free[i], 1);
             }
@@ -366,15 +372,15 @@ __global__ void __launch_bounds__(kPtThreads, 1)
     #pragma unroll
                     for (int kk = 0; kk < 8; kk++) {
                         const uint32_t off = ((kk >> 2) * kPtBox + (kk & 3) * 32) >> 4;
-                        tc_mma(tmem + h * 128, dq + off, dk + off, idesc_qk, kk > 0);
+                        tc_mma(tmem, dq + off, dk + off, idesc_qk, kk > 0);
                     }
                     tc_commit(&s_full[h]);
                 };
-                auto pv = [&](int h, int j) {  // O_h += P_h . V(j), P_h (BF16) in S_h's first 64 columns
+                auto pv = [&](int h, int j) {  // O_h += P_h . V(j), P_h (BF16) in TMEM columns 128 + 64 h
                     const uint64_t dv = (j & 1) ? dv1 : dv0;
     #pragma unroll
                     for (int kk = 0; kk < 8; kk++)
-                        tc_mma_ts(tmem + 256 + h * 128, tmem + h * 128 + kk * 8, dv + ((kk * 16 * 128) >> 4), idesc_pv,
+                        tc_mma_ts(tmem + 256 + h * 128, tmem + 128 + h * 64 + kk * 8, dv + ((kk * 16 * 128) >> 4), idesc_pv,
                                   (j > 0 || kk > 0));
                     tc_commit(&pv_done[h]);
                 };
@@ -383,11 +389,16 @@ __global__ void __launch_bounds__(kPtThreads, 1)
                     tc_fence_after();
                     return ok;
                 };
-                // The tensor pipe runs this thread's MMAs in issue order: P_h of tile j (in S_h's
-                // columns) is read by P.V(h, j) before QK(h, j + 1) overwrites S_h.
+                // One S buffer (TMEM columns 0-127) for both heads, free as soon as the softmax has
+                // loaded it; P_h in columns 128 + 64 h.  So QK(h, j + 1) does not wait for P.V(h, j):
+                // head 0's next S is computed once head 1 has loaded its S of tile j, and the P.V of
+                // a head follows its P.  (The softmax writes P_h(j + 1) once P.V(h, j) is done.)
                 bool ok = wait(q_full, 0) && wait(&k_full[0], 0);
                 if (ok) {
                     qk(0, 0);
+                    ok = wait(&s_free[0], 0);
+                }
+                if (ok) {
                     qk(1, 0);
                     tc_commit(&k_free[0]);
                 }
@@ -395,22 +406,24 @@ __global__ void __launch_bounds__(kPtThreads, 1)
                     const uint32_t par = (uint32_t)j & 1u;
                     const bool more = j + 1 < ntiles;
                     const int nst = (j + 1) & 1;
+                    if (more) {
+                        ok = wait(&s_free[1], par) && wait(&k_full[nst], (uint32_t)((j + 1) >> 1) & 1u);
+                        if (!ok) break;
+                        qk(0, j + 1);
+                    }
                     ok = wait(&p_full[0], par) && wait(&v_full[j & 1], (uint32_t)(j >> 1) & 1u);
                     if (!ok) break;
                     pv(0, j);
                     if (more) {
-                        ok = wait(&k_full[nst], (uint32_t)((j + 1) >> 1) & 1u);
+                        ok = wait(&s_free[0], (uint32_t)(j + 1) & 1u);
                         if (!ok) break;
-                        qk(0, j + 1);
+                        qk(1, j + 1);
+                        tc_commit(&k_free[nst]);
                     }
                     ok = wait(&p_full[1], par);
                     if (!ok) break;
                     pv(1, j);
                     tc_commit(&v_free[j & 1]);
-                    if (more) {
-                        qk(1, j + 1);
-                        tc_commit(&k_free[nst]);
-                    }
                 }
             }
             __syncwarp();
@@ -431,7 +444,8 @@ __global__ void __launch_bounds__(kPtThreads, 1)
         const int h = warp >> 2;
         const int r = 32 * (warp & 3) + lane;  // row = TMEM lane = token t0 + r
         const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
-        const uint32_t s_addr = tmem + lane_base + h * 128;
+        const uint32_t s_addr = tmem + lane_base;                 // S: one buffer, both heads
+        const uint32_t p_addr = tmem + lane_base + 128 + h * 64;  // P_h (BF16 pairs)
         const uint32_t o_addr = tmem + lane_base + 256 + h * 128;
         const int qpos = a.pos_offset + t0 + r;
         const int qmin = a.pos_offset + t0;  // first query position of the item
@@ -452,6 +466,16 @@ __global__ void __launch_bounds__(kPtThreads, 1)
             tc_fence_after();
             float sv[kPtKeys];  // this row of S
             tmem_ld128(s_addr, sv);
+            tc_fence_before();
+            mbar_arrive(&s_free[h]);  // S may take the other head's next tile
+            // P_h is the previous P.V's operand until that P.V completes.
+            if (j > 0) {
+                if (!warp_wait(&pv_done[h], (uint32_t)(j - 1) & 1u)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+            }
             // Causal mask (key k visible to query qpos iff k <= qpos, and k < total_kv) --
             // only tiles that reach past the item's first query or the attended length need it.
             const int k0 = j * kPtKeys;
@@ -460,14 +484,12 @@ __global__ void __launch_bounds__(kPtThreads, 1)
             // The two heads' passes run when their S is ready, sharing the exponential unit (a
             // warp of each per sub-partition).  Making them take turns on it (head 0's tile j
             // after head 1's tile j - 1) measured 1.5 % slower per page.
-            // P of this tile overwrites P of the previous one in TMEM: the previous P.V has
-            // completed, since the commit that signalled this S tracks every earlier MMA.
             if (j == 0) {
                 // First tile: the row maximum starts the running one (every row sees key 0).
                 m_run = (masked ? row_max<true>(sv, lim) : row_max<false>(sv, lim)) * a.scale_log2;
                 const float neg_m = m_run == -INFINITY ? 0.f : -m_run;
-                l_run = masked ? row_exp<true, false>(sv, lim, a.scale_log2, neg_m, s_addr, nullptr)
-                               : row_exp<false, false>(sv, lim, a.scale_log2, neg_m, s_addr, nullptr);
+                l_run = masked ? row_exp<true, false>(sv, lim, a.scale_log2, neg_m, p_addr, nullptr)
+                               : row_exp<false, false>(sv, lim, a.scale_log2, neg_m, p_addr, nullptr);
             } else {
                 // Later tiles: the running maximum moves only when the tile's exceeds it by more
                 // than 2^8; below that the stale one stays (P <= 256: exact in BF16's range and
@@ -477,8 +499,8 @@ __global__ void __launch_bounds__(kPtThreads, 1)
                 // row's new maximum (the same P as taking the tile maximum first: 2.50 against
                 // 2.55 ms per page, the separate maximum pass gone from almost every tile).
                 float xmax;
-                float rowsum = masked ? row_exp<true, true>(sv, lim, a.scale_log2, -m_run, s_addr, &xmax)
-                                      : row_exp<false, true>(sv, lim, a.scale_log2, -m_run, s_addr, &xmax);
+                float rowsum = masked ? row_exp<true, true>(sv, lim, a.scale_log2, -m_run, p_addr, &xmax)
+                                      : row_exp<false, true>(sv, lim, a.scale_log2, -m_run, p_addr, &xmax);
                 const bool move = xmax > 8.f;
                 float m_new = m_run, alpha = 1.f;
                 if (__any_sync(0xffffffffu, move)) {
@@ -486,8 +508,8 @@ __global__ void __launch_bounds__(kPtThreads, 1)
                         m_new = m_run + xmax;
                         alpha = pt_exp2(m_run - m_new);
                     }
-                    rowsum = masked ? row_exp<true, false>(sv, lim, a.scale_log2, -m_new, s_addr, nullptr)
-                                    : row_exp<false, false>(sv, lim, a.scale_log2, -m_new, s_addr, nullptr);
+                    rowsum = masked ? row_exp<true, false>(sv, lim, a.scale_log2, -m_new, p_addr, nullptr)
+                                    : row_exp<false, false>(sv, lim, a.scale_log2, -m_new, p_addr, nullptr);
                 }
                 // O rescale: the TMEM accesses are warp-collective, so the warp takes the branch
                 // if any of its rows moved (the others multiply by 1).
