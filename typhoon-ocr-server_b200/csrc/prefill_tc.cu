@@ -16,8 +16,8 @@
 //     reads (Q0, Q1: 128 x 128 each);
 //   * one thread of warp 9 streams K and V tiles (128 keys x 128 dims, BF16) from the cache
 //     with TMA tensor copies (SWIZZLE_128B; rows past the attended length are zero-filled), and
-//     one thread of warp 8 issues the MMAs: S_h = Q_h . K^T into TMEM, later O_h += P_h . V
-//     into TMEM, the two heads' MMAs alternating;
+//     one thread of warp 8 issues the MMAs: S = Q_h . K^T into TMEM (the heads in turn), later
+//     O_h += P_h . V into TMEM;
 //   * softmax warp w owns TMEM lane (row) 32*(w%4)+lane of head w/4: it reads its S row with
 //     tcgen05.ld (which frees S for the other head's next QK), applies the causal mask and the
 //     online softmax (base 2), rescales its O row in TMEM when the running maximum moves, and
@@ -366,7 +366,7 @@ __global__ void __launch_bounds__(kPtThreads, 1)
                 const uint64_t dq0 = umma_desc(smem_u32(sQ), 16), dq1 = umma_desc(smem_u32(sQ) + kPtTile, 16);
                 const uint64_t dk0 = umma_desc(smem_u32(sK), 16), dk1 = umma_desc(smem_u32(sK) + kPtTile, 16);
                 const uint64_t dv0 = umma_desc(smem_u32(sV), kPtBox), dv1 = umma_desc(smem_u32(sV) + kPtTile, kPtBox);
-                auto qk = [&](int h, int j) {  // S_h = Q_h . K(j)^T
+                auto qk = [&](int h, int j) {  // S = Q_h . K(j)^T (the shared S buffer)
                     const uint64_t dq = h ? dq1 : dq0;
                     const uint64_t dk = (j & 1) ? dk1 : dk0;
     #pragma unroll
