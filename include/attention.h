@@ -35,7 +35,10 @@ void attention_decode_gqa(
  * k, v [Sk][8][128] (fp32), output [Sq][16][128].  Query i attends keys 0..i (< Sk).
  * q_hm/k_hm/v_hm/o_hm: the reference reserved them for a zero-copy path; here, when
  * they are device buffers of the DecoderScratch sizes, they stage host inputs and the
- * output on the device; otherwise (NULL or host memory) an internal workspace does. */
+ * output on the device; otherwise (NULL or host memory) an internal workspace does.  With
+ * q/k/v/output all in host memory and Sk >= Sq >= 1024, the rows cross the bus in chunks that
+ * overlap the kernels and each other (two copy streams of the calling thread); the call still
+ * returns once the output is written. */
 void attention_prefill_gqa(
     const float  *q,
     const float  *k,
